@@ -1,0 +1,235 @@
+/*
+ * sla_b200.h -- C ABI of libsla_b200.so, the sm_100a (B200) iterative-solve
+ * hot path behind torch-sla's `pytorch` backend.
+ *
+ * Conventions
+ *   - Every pointer argument named as "device" is CUDA device memory owned by
+ *     the caller (the Python layer allocates it through PyTorch's caching
+ *     allocator). The library never frees caller memory and never calls
+ *     cudaMalloc on the solve path: scratch space is a caller-provided
+ *     workspace whose size is returned by the matching *_workspace() query.
+ *   - All work is enqueued on the caller's stream (`sla_stream_t` is a
+ *     cudaStream_t). Functions that must return a host value produced on the
+ *     device (coalesced nnz, iteration counts) synchronise that stream.
+ *   - Return value: 0 = OK; > 0 = numerical outcome (not converged,
+ *     breakdown); < 0 = error (invalid argument, CUDA/NCCL error, timeout).
+ *   - dtype codes: SLA_F32 (float) and SLA_F64 (double). Index arrays are
+ *     int32 (local problem sizes stay below 2^31), COO inputs are int64 as in
+ *     torch-sla.
+ *
+ * Each entry point cites the torch-sla function whose work it replaces
+ * (paths relative to the torch-sla source tree).
+ */
+#ifndef SLA_B200_H
+#define SLA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *sla_stream_t; /* identical to cudaStream_t */
+
+enum { SLA_F32 = 0, SLA_F64 = 1 };
+
+enum {
+  SLA_OK = 0,
+  SLA_NOT_CONVERGED = 1,   /* maxiter reached (torch-sla warns)            */
+  SLA_BREAKDOWN = 2,       /* BiCGStab rho / t.t / omega guard fired        */
+  SLA_ERR_INVALID = -1,    /* bad argument (sizes, dtype, null pointer)     */
+  SLA_ERR_CUDA = -2,       /* a CUDA runtime call failed                    */
+  SLA_ERR_NCCL = -3,       /* an NCCL call failed                           */
+  SLA_ERR_TIMEOUT = -4,    /* a bounded device-side wait gave up            */
+  SLA_ERR_UNSUPPORTED = -5,/* shape outside the supported envelope          */
+  SLA_ERR_WORKSPACE = -6,  /* workspace smaller than *_workspace() asked    */
+  SLA_ERR_INDEX = -7       /* a COO index lies outside the matrix shape     */
+};
+
+/* Jacobi rules: how a diagonal d turns into the inverse used by M^{-1}. */
+enum {
+  SLA_JACOBI_EPS = 0,     /* 1/d, d := 1 where |d| < 100*eps(dtype)
+                             (backends/pytorch_backend.py:221-235)          */
+  SLA_JACOBI_CLAMP = 1,   /* 1/max(d, 1e-30)  (distributed/solve.py:95-115) */
+  SLA_JACOBI_NONZERO = 2  /* |d| > 0 ? 1/d : 1 (pytorch_backend.py:2611-2614)*/
+};
+
+/* Solver path selection for sla_pcg (flags argument). */
+enum {
+  SLA_PCG_AUTO = 0,        /* persistent kernel for small systems, else streamed */
+  SLA_PCG_STREAMED = 1,    /* two fused kernels per iteration                     */
+  SLA_PCG_PERSISTENT = 2   /* one cooperative launch for the whole solve          */
+};
+
+/* SELL-32 (SELL-C-sigma with C = 32, sigma = 1) matrix view. Slice s holds
+ * 32 consecutive row slots; entry j of slot l sits at
+ * slice_ptr[s] + 32*j + l. Padding entries have col == -1. */
+typedef struct {
+  int64_t n_slots;           /* row slots covered by this view               */
+  int64_t n_slices;          /* ceil(n_slots / 32)                           */
+  const int32_t *slice_ptr;  /* device [n_slices + 1]                        */
+  const int32_t *col;        /* device [slice_ptr[n_slices]]                 */
+  const void *val;           /* device, same length, dtype T                 */
+  const int32_t *row_ids;    /* device [n_slots] row of each slot, or NULL
+                                when slot i is row i                          */
+} sla_sell_t;
+
+typedef struct {
+  int64_t iterations;        /* torch-sla's iteration count convention       */
+  double residual;           /* recursive residual norm at exit              */
+  int32_t status;            /* SLA_OK / SLA_NOT_CONVERGED / SLA_BREAKDOWN    */
+  int32_t reason;            /* solver-specific detail, 0 if none            */
+} sla_solve_info_t;
+
+/* ------------------------------------------------------------------ misc */
+int sla_abi_version(void);
+const char *sla_status_string(int status);
+/* Kernels this library has launched in this process (all devices). */
+int64_t sla_kernel_launch_count(void);
+/* Per-kernel-class device time (ms) and launch count gathered while
+ * sampling is on; class 0 is the SpMV-bearing kernel of the running solver. */
+int sla_profile_enable(int enable, int sample_every);
+int sla_profile_read(int kernel_class, double *total_ms, int64_t *launches);
+
+/* ------------------------------------------------------------ COO -> CSR */
+/* Replaces CachedSparseMatrix.__init__'s sparse_coo_tensor(...).to_sparse_csr()
+ * (backends/pytorch_backend.py:114-152) and the int32 CSR of shard_matvec
+ * (distributed/matvec.py:271-294): sorts by (row, col), sums duplicates in
+ * input order, emits int32 CSR. Optional outputs: src_index[t] = input
+ * position of the t-th sorted entry, seg_ptr[e] = first sorted position of
+ * CSR entry e (seg_ptr has nnz_out + 1 entries). Synchronises `stream`. */
+int sla_csr_build_workspace(int64_t n_rows, int64_t nnz, size_t *bytes);
+int sla_csr_build(int dtype, const int64_t *row, const int64_t *col,
+                  const void *val, int64_t nnz, int64_t n_rows, int64_t n_cols,
+                  int32_t *rowptr, int32_t *colind, void *vals,
+                  int64_t *src_index, int32_t *seg_ptr, int64_t *nnz_out,
+                  void *workspace, size_t workspace_bytes, sla_stream_t stream);
+
+/* ------------------------------------------------------------- SELL-32 */
+/* Layout of a SELL-32 view over the CSR rows listed in row_ids (or rows
+ * 0..n_slots-1). Writes slice_ptr and returns the padded entry count. */
+int sla_sell_layout_workspace(int64_t n_slots, size_t *bytes);
+int sla_sell_layout(const int32_t *rowptr, const int32_t *row_ids,
+                    int64_t n_slots, int32_t *slice_ptr, int64_t *padded_out,
+                    void *workspace, size_t workspace_bytes,
+                    sla_stream_t stream);
+int sla_sell_fill(int dtype, const int32_t *rowptr, const int32_t *colind,
+                  const void *vals, const int32_t *row_ids, int64_t n_slots,
+                  const int32_t *slice_ptr, int32_t *sell_col, void *sell_val,
+                  sla_stream_t stream);
+
+/* Inverse diagonal for Jacobi (pytorch_backend.py:167-174, 221-235;
+ * distributed/solve.py:95-115). Rows without a stored diagonal use d = 0. */
+int sla_jacobi_inverse(int dtype, const int32_t *rowptr, const int32_t *colind,
+                       const void *vals, int64_t n_rows, int rule, void *dinv,
+                       sla_stream_t stream);
+
+/* ---------------------------------------------------------------- SpMV */
+/* y[row] = sum_j A[row, j] x[j] for every slot of A (torch.mv in
+ * CachedSparseMatrix.matvec, pytorch_backend.py:154-161; SparseTensor @ x,
+ * sparse_tensor/matmul.py:10-85). */
+int sla_spmv(int dtype, const sla_sell_t *A, const void *x, void *y,
+             sla_stream_t stream);
+
+/* g[k] = -sum_c a[row[k]*K + c] * b[col[k]*K + c] for every COO entry k,
+ * repeated for `batch` independent problems laid out back to back: the
+ * adjoint's value gradient (linear_solve.py:321-323,
+ * batch_solve.py:138). a has n_a*K entries per problem, b has n_b*K. */
+int sla_coo_value_grad(int dtype, const int64_t *row, const int64_t *col,
+                       int64_t nnz, const void *a, const void *b,
+                       int64_t n_a, int64_t n_b, int64_t K, int64_t batch,
+                       void *g, sla_stream_t stream);
+
+/* ------------------------------------------------------------- Krylov */
+/* Jacobi-PCG / CG with torch-sla's stopping rule: stop at the start of
+ * iteration i when (r,r) < max(atol, rtol*||b||)^2, iterations = i
+ * (pcg_solve_optimized, pytorch_backend.py:1262-1362). dinv == NULL selects
+ * preconditioner='none'. x holds the initial guess when x_is_guess != 0. */
+int sla_pcg_workspace(int dtype, int64_t n, size_t *bytes);
+int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b,
+            void *x, int x_is_guess, double atol, double rtol,
+            int64_t maxiter, int flags, void *workspace,
+            size_t workspace_bytes, sla_solve_info_t *info,
+            sla_stream_t stream);
+
+/* Jacobi-PBiCGStab with torch-sla's half-step / full-step stopping tests and
+ * 1e-30 breakdown guards (pbicgstab_solve, pytorch_backend.py:1508-1596). */
+int sla_bicgstab_workspace(int dtype, int64_t n, size_t *bytes);
+int sla_bicgstab(int dtype, const sla_sell_t *A, const void *dinv,
+                 const void *b, void *x, int x_is_guess, double atol,
+                 double rtol, int64_t maxiter, void *workspace,
+                 size_t workspace_bytes, sla_solve_info_t *info,
+                 sla_stream_t stream);
+
+/* B Jacobi-PCG solves sharing one CSR pattern, values interleaved
+ * [nnz][B] (batched_cg_same_pattern, pytorch_backend.py:2575-2638): stops
+ * when every ||R_b|| <= max(atol, rtol*||b_b||). b and x are [B][n]. */
+int sla_batched_values(int dtype, const void *val_batch, int64_t batch,
+                       int64_t nnz_coo, const int64_t *src_index,
+                       const int32_t *seg_ptr, int64_t nnz_csr, void *out,
+                       sla_stream_t stream);
+int sla_batched_cg_workspace(int dtype, int64_t n, int64_t batch,
+                             size_t *bytes);
+int sla_batched_cg(int dtype, const int32_t *rowptr, const int32_t *colind,
+                   const void *vals_interleaved, int64_t n, int64_t batch,
+                   const void *b, void *x, double atol, double rtol,
+                   int64_t maxiter, void *workspace, size_t workspace_bytes,
+                   sla_solve_info_t *info, sla_stream_t stream);
+
+/* -------------------------------------------------- row-sharded (NCCL) */
+/* Opaque NCCL communicator management (one process per GPU). */
+int sla_comm_unique_id(unsigned char id[128]);
+int sla_comm_init(void **comm, int nranks, const unsigned char id[128],
+                  int rank);
+int sla_comm_destroy(void *comm);
+
+/* Halo plan of one rank (partition.py:317-423 send/recv maps). Local vector
+ * layout is [owned | halo]; neighbours ascend by rank id. */
+typedef struct {
+  int32_t n_neighbors;
+  const int32_t *neighbor_rank;  /* host [n_neighbors]                        */
+  const int64_t *send_offset;    /* host [n_neighbors + 1] into send_index    */
+  const int64_t *recv_offset;    /* host [n_neighbors + 1] into the recv buf  */
+  const int32_t *send_index;     /* device: owned local rows to send          */
+  const int32_t *halo_src;       /* device [n_halo]: recv-buffer position of
+                                    halo slot h, or NULL when identity        */
+  int64_t n_owned;
+  int64_t n_halo;
+} sla_halo_plan_t;
+
+/* halo_exchange (distributed/matvec.py:26-93): fills x_local[n_owned:]. */
+int sla_halo_exchange(void *comm, const sla_halo_plan_t *plan, int dtype,
+                      void *x_local, void *sendbuf, void *recvbuf,
+                      sla_stream_t stream);
+/* shard_matvec (distributed/matvec.py:235-303): y_owned = A_local x_local,
+ * halo exchange overlapped with the interior rows. x_local has n_owned +
+ * n_halo entries; its halo part is overwritten. */
+int sla_shard_spmv(void *comm, const sla_halo_plan_t *plan, int dtype,
+                   const sla_sell_t *A_interior, const sla_sell_t *A_boundary,
+                   void *x_local, void *y_owned, void *sendbuf, void *recvbuf,
+                   sla_stream_t stream);
+/* cg_shard / bicgstab_shard (distributed/solve.py:279-436): stopping test
+ * every `check_every` iterations, one fused allreduce per reduction point. */
+int sla_shard_krylov_workspace(int dtype, int64_t n_owned, int64_t n_halo,
+                               int64_t n_send, size_t *bytes);
+int sla_shard_cg(void *comm_halo, void *comm_reduce,
+                 const sla_halo_plan_t *plan, int dtype,
+                 const sla_sell_t *A_interior, const sla_sell_t *A_boundary,
+                 const void *dinv, const void *b, void *x, double atol,
+                 double rtol, int64_t maxiter, int64_t check_every,
+                 void *workspace, size_t workspace_bytes,
+                 sla_solve_info_t *info, sla_stream_t stream);
+int sla_shard_bicgstab(void *comm_halo, void *comm_reduce,
+                       const sla_halo_plan_t *plan, int dtype,
+                       const sla_sell_t *A_interior,
+                       const sla_sell_t *A_boundary, const void *dinv,
+                       const void *b, void *x, double atol, double rtol,
+                       int64_t maxiter, int64_t check_every, void *workspace,
+                       size_t workspace_bytes, sla_solve_info_t *info,
+                       sla_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SLA_B200_H */

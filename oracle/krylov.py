@@ -1,0 +1,322 @@
+"""CPU restatement of torch-sla's Krylov hot path (test infrastructure only).
+
+Each function names the torch-sla source lines whose algorithm it restates.
+All arithmetic uses the PyTorch CPU ops the reference uses, in the same
+order, so iteration counts and residual histories match the reference.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+
+# --------------------------------------------------------------- matrices
+def csr(val, row, col, shape):
+    """COO -> torch sparse CSR, coalescing duplicates
+    (backends/pytorch_backend.py:138-142)."""
+    idx = torch.stack([row.to(torch.int64), col.to(torch.int64)])
+    return torch.sparse_coo_tensor(idx, val, tuple(shape)).to_sparse_csr()
+
+
+def diagonal(val, row, col, n):
+    """Sum of the diagonal COO entries (pytorch_backend.py:167-174)."""
+    d = torch.zeros(n, dtype=val.dtype)
+    m = row == col
+    d.scatter_add_(0, row[m].to(torch.int64), val[m])
+    return d
+
+
+def jacobi_inverse(d, rule: str):
+    """'eps' (pytorch_backend.py:221-235), 'clamp' (distributed/solve.py:95-115),
+    'nonzero' (pytorch_backend.py:2611-2614)."""
+    if rule == "eps":
+        eps = torch.finfo(d.dtype).eps * 100
+        return 1.0 / torch.where(torch.abs(d) < eps, torch.ones_like(d), d)
+    if rule == "clamp":
+        return 1.0 / d.clamp_min(1e-30)
+    if rule == "nonzero":
+        return torch.where(d.abs() > 0, 1.0 / d, torch.ones_like(d))
+    raise ValueError(rule)
+
+
+def spmv(val, row, col, shape, x):
+    """y = A x on the coalesced CSR (torch.mv, pytorch_backend.py:161)."""
+    return torch.mv(csr(val, row, col, shape), x)
+
+
+# ---------------------------------------------------------------- PCG
+def pcg(val, row, col, shape, b, *, x0=None, atol=1e-10, rtol=1e-6, maxiter=10000,
+        precond="jacobi"):
+    """pcg_solve_fused + pcg_solve_optimized (pytorch_backend.py:1262-1362,
+    1466-1501). Returns (x, iterations, residual, converged)."""
+    A = csr(val, row, col, shape)
+    n = shape[0]
+    dinv = None if precond == "none" else jacobi_inverse(diagonal(val, row, col, n), "eps")
+    apply_m = (lambda v: v) if dinv is None else (lambda v: dinv * v)
+    if x0 is None:
+        x = torch.zeros(n, dtype=b.dtype)
+        r = b.clone()
+    else:
+        x = x0.clone()
+        r = b - torch.mv(A, x)
+    z = apply_m(r).clone()
+    p = z.clone()
+    rz = torch.vdot(r, z)
+    tol_sq = max(atol, rtol * torch.norm(b).item()) ** 2
+    for i in range(maxiter):
+        rr = torch.vdot(r, r).real
+        if rr.item() < tol_sq:  # start-of-iteration test
+            return x, i, rr.sqrt().item(), True
+        Ap = torch.mv(A, p)
+        alpha = rz / torch.vdot(p, Ap)
+        x.addcmul_(alpha, p)
+        r.addcmul_(-alpha, Ap)
+        z = apply_m(r).clone()
+        rz_next = torch.vdot(r, z)
+        beta = rz_next / rz
+        p.mul_(beta).add_(z)
+        rz = rz_next
+    res = torch.norm(r).item()
+    return x, maxiter, res, res < math.sqrt(tol_sq)
+
+
+def csr_diagonal(A):
+    """Diagonal of a torch CPU CSR matrix."""
+    crow, colv, vals = A.crow_indices(), A.col_indices(), A.values()
+    rows = torch.repeat_interleave(torch.arange(A.shape[0]), crow[1:] - crow[:-1])
+    d = torch.zeros(A.shape[0], dtype=vals.dtype)
+    m = rows == colv
+    d.index_add_(0, rows[m], vals[m])
+    return d
+
+
+def pcg_iterations(A, b, dinv, iterations=None, budget_s=None):
+    """Timed CPU sample: the loop body of pcg_solve_optimized
+    (pytorch_backend.py:1317-1354) on a prebuilt CSR, for a fixed number of
+    iterations or until `budget_s` seconds have passed. Returns the count."""
+    import time
+    x = torch.zeros_like(b)
+    r = b.clone()
+    z = (dinv * r).clone()
+    p = z.clone()
+    rz = torch.vdot(r, z)
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        if iterations is not None and done >= iterations:
+            break
+        if budget_s is not None and done > 0 and time.perf_counter() - t0 > budget_s:
+            break
+        torch.vdot(r, r).real.item()
+        Ap = torch.mv(A, p)
+        alpha = rz / torch.vdot(p, Ap)
+        x.addcmul_(alpha, p)
+        r.addcmul_(-alpha, Ap)
+        z.copy_(dinv * r)
+        rz_next = torch.vdot(r, z)
+        p.mul_(rz_next / rz).add_(z)
+        rz = rz_next
+        done += 1
+    return done
+
+
+# ----------------------------------------------------------- BiCGStab
+def pbicgstab(val, row, col, shape, b, *, x0=None, atol=1e-10, rtol=1e-6, maxiter=10000,
+              precond="jacobi"):
+    """pbicgstab_solve (pytorch_backend.py:1508-1596). Returns
+    (x, iterations, residual, exit) with exit in {'converged_half',
+    'converged', 'rho', 'tt', 'omega', 'maxiter'}; breakdowns and maxiter
+    report `maxiter` iterations, as the reference does."""
+    A = csr(val, row, col, shape)
+    n = shape[0]
+    dinv = None if precond == "none" else jacobi_inverse(diagonal(val, row, col, n), "eps")
+    apply_m = (lambda v: v) if dinv is None else (lambda v: dinv * v)
+    if x0 is None:
+        x = torch.zeros(n, dtype=b.dtype)
+        r = b.clone()
+    else:
+        x = x0.clone()
+        r = b - torch.mv(A, x)
+    rhat = r.clone()
+    one = torch.tensor(1.0, dtype=b.dtype)
+    rho_prev, alpha, omega = one, one, one
+    v = torch.zeros(n, dtype=b.dtype)
+    p = torch.zeros(n, dtype=b.dtype)
+    bn = torch.norm(b)
+    if bn == 0:
+        bn = 1.0
+    tol = max(atol, rtol * bn)
+    residual = torch.norm(r).item()
+    how = "maxiter"
+    for i in range(maxiter):
+        rho = torch.vdot(rhat, r)
+        if abs(rho.item()) < 1e-30:
+            how = "rho"
+            break
+        beta = (rho / rho_prev) * (alpha / omega)
+        p = r + beta * (p - omega * v)
+        ph = apply_m(p)
+        v = torch.mv(A, ph)
+        alpha = rho / torch.vdot(rhat, v)
+        s = r - alpha * v
+        sn = torch.norm(s).item()
+        if sn < tol:
+            return x + alpha * ph, i + 1, sn, "converged_half"
+        sh = apply_m(s)
+        t = torch.mv(A, sh)
+        tt = torch.vdot(t, t).real
+        if tt < 1e-30:
+            x = x + alpha * ph
+            how = "tt"
+            break
+        omega = torch.vdot(t, s) / tt
+        x = x + alpha * ph + omega * sh
+        r = s - omega * t
+        residual = torch.norm(r).item()
+        if residual < tol:
+            return x, i + 1, residual, "converged"
+        if abs(omega.item()) < 1e-30:
+            how = "omega"
+            break
+        rho_prev = rho
+    return x, maxiter, residual, how
+
+
+# ------------------------------------------------------ batched CG
+def batched_cg_same_pattern(val_batch, row, col, shape, b_batch, *, atol=1e-10, rtol=1e-6,
+                            maxiter=10000):
+    """batched_cg_same_pattern (pytorch_backend.py:2575-2638). Returns
+    (X [B, n], iterations executed)."""
+    n = shape[0]
+    Bn = val_batch.shape[0]
+    row = row.to(torch.int64)
+    col = col.to(torch.int64)
+
+    def matvec(X):
+        Y = torch.zeros(Bn, n, dtype=val_batch.dtype)
+        Y.index_add_(1, row, val_batch * X[:, col])
+        return Y
+
+    D = torch.zeros(Bn, n, dtype=val_batch.dtype)
+    dm = row == col
+    D.index_add_(1, row[dm], val_batch[:, dm])
+    Dinv = torch.where(D.abs() > 0, 1.0 / D, torch.ones_like(D))
+    X = torch.zeros(Bn, n, dtype=val_batch.dtype)
+    R = b_batch.clone()
+    Z = Dinv * R
+    P = Z.clone()
+    rz = (R * Z).sum(dim=1)
+    tol = torch.clamp(rtol * torch.linalg.vector_norm(b_batch, dim=1).clamp_min(1e-30), min=atol)
+    tiny = torch.tensor(1e-30, dtype=val_batch.dtype)
+    it = 0
+    for it in range(1, maxiter + 1):
+        AP = matvec(P)
+        pAp = (P * AP).sum(dim=1)
+        alpha = rz / torch.where(pAp.abs() > 0, pAp, tiny)
+        X = X + alpha.unsqueeze(1) * P
+        R = R - alpha.unsqueeze(1) * AP
+        if bool((torch.linalg.vector_norm(R, dim=1) <= tol).all()):
+            break
+        Z = Dinv * R
+        rz_next = (R * Z).sum(dim=1)
+        beta = rz_next / torch.where(rz.abs() > 0, rz, tiny)
+        P = Z + beta.unsqueeze(1) * P
+        rz = rz_next
+    return X, it
+
+
+# -------------------------------------------------------- adjoints
+def adjoint(val, row, col, shape, u, gradu, *, method="cg", atol=1e-10, rtol=1e-10,
+            maxiter=10000, precond="jacobi"):
+    """SparseLinearSolvePyTorch.backward (linear_solve.py:303-324):
+    A^T gradb = gradu on the swapped pattern, gradval = -gradb[row]*u[col]."""
+    fn = pcg if method == "cg" else pbicgstab
+    gradb = fn(val, col, row, (shape[1], shape[0]), gradu, atol=atol, rtol=rtol,
+               maxiter=maxiter, precond=precond)[0]
+    gradval = -gradb[row.to(torch.int64)] * u[col.to(torch.int64)]
+    return gradval, gradb
+
+
+def batched_adjoint(val_batch, row, col, shape, u_batch, gradu_batch, *, atol=1e-10, rtol=1e-6,
+                    maxiter=10000):
+    """BatchSparseLinearSolveSameLayout.backward, CG branch (batch_solve.py:133-139)."""
+    gradb = batched_cg_same_pattern(val_batch, col, row, (shape[1], shape[0]), gradu_batch,
+                                    atol=atol, rtol=rtol, maxiter=maxiter)[0]
+    gradval = -gradb[:, row.to(torch.int64)] * u_batch[:, col.to(torch.int64)]
+    return gradval, gradb
+
+
+# ----------------------------------------------- Shard(0) control flow
+def cg_shard(val, row, col, shape, b, *, atol=1e-10, rtol=0.0, maxiter=1000, precond="jacobi",
+             check_every=10):
+    """cg_shard (distributed/solve.py:279-350) on the global vectors: the
+    row-sharded solve computes the same recurrences, only its dot products are
+    summed per rank first. Jacobi uses the clamp rule of make_preconditioner.
+    Returns (x, iterations)."""
+    A = csr(val, row, col, shape)
+    n = shape[0]
+    dinv = None if precond in (None, "none") else jacobi_inverse(diagonal(val, row, col, n), "clamp")
+    apply_m = (lambda v: v) if dinv is None else (lambda v: dinv * v)
+    x = torch.zeros_like(b)
+    r = b - torch.mv(A, x)
+    z = apply_m(r)
+    p = z.clone()
+    rs = torch.dot(r, z)
+    tol = max(atol, rtol * float(torch.dot(b, b).sqrt().item()))
+    iters = maxiter
+    for k in range(maxiter):
+        Ap = torch.mv(A, p)
+        alpha = rs / torch.dot(p, Ap)
+        torch.addcmul(x, alpha, p, value=1.0, out=x)
+        torch.addcmul(r, alpha, Ap, value=-1.0, out=r)
+        z = apply_m(r)
+        rr, rs_next = torch.dot(r, r), torch.dot(r, z)
+        if k % check_every == 0 and float(rr.sqrt().item()) < tol:
+            iters = k + 1
+            break
+        p.mul_(rs_next / rs).add_(z)
+        rs = rs_next
+    return x, iters
+
+
+def bicgstab_shard(val, row, col, shape, b, *, atol=1e-10, rtol=0.0, maxiter=1000,
+                   precond="jacobi", check_every=10):
+    """bicgstab_shard (distributed/solve.py:356-436) on the global vectors.
+    Returns (x, iterations)."""
+    A = csr(val, row, col, shape)
+    n = shape[0]
+    dinv = None if precond in (None, "none") else jacobi_inverse(diagonal(val, row, col, n), "clamp")
+    apply_m = (lambda v: v) if dinv is None else (lambda v: dinv * v)
+    x = torch.zeros_like(b)
+    r = b - torch.mv(A, x)
+    rhat = r.clone()
+    rho = alpha = omega = torch.tensor(1.0, dtype=b.dtype)
+    p = torch.zeros_like(b)
+    v = torch.zeros_like(b)
+    tol = max(atol, rtol * float(torch.dot(b, b).sqrt().item()))
+    for k in range(maxiter):
+        rho_k = torch.dot(rhat, r)
+        p = r.clone() if k == 0 else r + (rho_k / rho) * (alpha / omega) * (p - omega * v)
+        ph = apply_m(p)
+        v = torch.mv(A, ph)
+        alpha = rho_k / torch.dot(rhat, v)
+        s = r - alpha * v
+        ss = torch.dot(s, s)
+        if k % check_every == 0 and float(ss.sqrt().item()) < tol:
+            return x + alpha * ph, k + 1
+        sh = apply_m(s)
+        t = torch.mv(A, sh)
+        # shard_matvec returns a view of one cached output buffer
+        # (distributed/matvec.py:296-303), so computing t overwrites v: the
+        # next iteration's p-update reads t where the textbook reads v.
+        v = t
+        omega = torch.dot(t, s) / torch.dot(t, t)
+        x = x + alpha * ph + omega * sh
+        r = s - omega * t
+        if k % check_every == 0:
+            rn = float(torch.dot(r, r).sqrt().item())
+            if rn < tol or math.isnan(rn):
+                return x, k + 1
+        rho = rho_k
+    return x, maxiter

@@ -1,0 +1,153 @@
+"""Device-resident int32 CSR and SELL-32 views built by libsla_b200.
+
+`DeviceCSR` replaces the COO -> CSR conversion that torch-sla's
+`CachedSparseMatrix` performs on every solve
+(backends/pytorch_backend.py:114-152); the conversion, the SELL-32 layout
+used by the solver kernels and the Jacobi diagonal are all built on the GPU.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib as L
+
+
+class Sell:
+    """SELL-32 view (slice pointers, padded columns/values) of some CSR rows."""
+
+    def __init__(self, slice_ptr, col, val, n_slots, row_ids=None):
+        self.slice_ptr, self.col, self.val, self.row_ids = slice_ptr, col, val, row_ids
+        self.n_slots = int(n_slots)
+        self.n_slices = (self.n_slots + 31) // 32
+        self.view = L.SellView(self.n_slots, self.n_slices, L.ptr(slice_ptr), L.ptr(col),
+                               L.ptr(val), L.ptr(row_ids))
+
+    def ref(self):
+        return ctypes.byref(self.view)
+
+    @property
+    def padded_nnz(self) -> int:
+        return int(self.col.numel())
+
+
+class DeviceCSR:
+    """int32 CSR of a COO matrix, with duplicates summed in input order.
+
+    keep_map=True also keeps `src_index` (input position of each sorted
+    entry) and `seg_ptr` (sorted-entry range of each CSR entry), which the
+    batched solver uses to gather per-matrix values.
+    """
+
+    def __init__(self, val, row, col, shape, *, keep_map: bool = False, dtype=None):
+        n_rows, n_cols = int(shape[0]), int(shape[1])
+        dev = L.require_cuda(row, col, val)
+        if val is not None:
+            dtype = val.dtype
+            val = val.contiguous()
+        self.dtype = dtype
+        self.code = L.dtype_code(dtype)
+        self.device = dev
+        self.shape = (n_rows, n_cols)
+        row = row.to(device=dev, dtype=torch.int64).contiguous()
+        col = col.to(device=dev, dtype=torch.int64).contiguous()
+        nnz = int(row.numel())
+        if col.numel() != nnz or (val is not None and val.numel() != nnz):
+            raise ValueError("torch_sla_b200: row, col and values must have the same length")
+        lib = L.lib()
+        need = ctypes.c_size_t(0)
+        L.check("sla_csr_build_workspace", lib.sla_csr_build_workspace(n_rows, nnz, ctypes.byref(need)))
+        ws = L.workspace(need.value, dev)
+        rowptr = torch.empty(n_rows + 1, dtype=torch.int32, device=dev)
+        colind = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
+        vals = torch.empty(max(nnz, 1), dtype=dtype, device=dev)
+        src = torch.empty(max(nnz, 1), dtype=torch.int64, device=dev) if keep_map else None
+        seg = torch.empty(nnz + 1, dtype=torch.int32, device=dev) if keep_map else None
+        out = ctypes.c_int64(0)
+        L.check("sla_csr_build", lib.sla_csr_build(
+            self.code, L.ptr(row), L.ptr(col), L.ptr(val), nnz, n_rows, n_cols, L.ptr(rowptr),
+            L.ptr(colind), L.ptr(vals) if val is not None else None, L.ptr(src), L.ptr(seg),
+            ctypes.byref(out), L.ptr(ws), ws.numel(), L.stream_handle(dev)))
+        self.nnz = int(out.value)
+        self.rowptr = rowptr
+        self.colind = colind[: self.nnz]
+        self.vals = vals[: self.nnz] if val is not None else None
+        self.src_index = src[:nnz] if keep_map else None
+        self.seg_ptr = seg[: self.nnz + 1] if keep_map else None
+        self._sell = None
+
+    # ------------------------------------------------------------------ SELL
+    def sell(self, row_ids: torch.Tensor | None = None, values: torch.Tensor | None = None) -> Sell:
+        """SELL-32 view of all rows (row_ids=None) or of the listed rows."""
+        if row_ids is None and values is None and self._sell is not None:
+            return self._sell
+        vals = self.vals if values is None else values
+        if vals is None:
+            raise ValueError("torch_sla_b200: SELL view needs matrix values")
+        lib = L.lib()
+        dev = self.device
+        n_slots = self.shape[0] if row_ids is None else int(row_ids.numel())
+        if row_ids is not None:
+            row_ids = row_ids.to(device=dev, dtype=torch.int32).contiguous()
+        n_slices = (n_slots + 31) // 32
+        slice_ptr = torch.empty(n_slices + 1, dtype=torch.int32, device=dev)
+        need = ctypes.c_size_t(0)
+        L.check("sla_sell_layout_workspace", lib.sla_sell_layout_workspace(n_slots, ctypes.byref(need)))
+        ws = L.workspace(need.value, dev)
+        padded = ctypes.c_int64(0)
+        stream = L.stream_handle(dev)
+        L.check("sla_sell_layout", lib.sla_sell_layout(
+            L.ptr(self.rowptr), L.ptr(row_ids), n_slots, L.ptr(slice_ptr), ctypes.byref(padded),
+            L.ptr(ws), ws.numel(), stream))
+        scol = torch.empty(max(padded.value, 1), dtype=torch.int32, device=dev)
+        sval = torch.empty(max(padded.value, 1), dtype=self.dtype, device=dev)
+        L.check("sla_sell_fill", lib.sla_sell_fill(
+            self.code, L.ptr(self.rowptr), L.ptr(self.colind), L.ptr(vals), L.ptr(row_ids), n_slots,
+            L.ptr(slice_ptr), L.ptr(scol), L.ptr(sval), stream))
+        s = Sell(slice_ptr, scol, sval, n_slots, row_ids)
+        if row_ids is None and values is None:
+            self._sell = s
+        return s
+
+    # --------------------------------------------------------------- helpers
+    def jacobi_inverse(self, rule: int, n_rows: int | None = None) -> torch.Tensor:
+        n = self.shape[0] if n_rows is None else int(n_rows)
+        dinv = torch.empty(max(n, 1), dtype=self.dtype, device=self.device)[:n]
+        L.check("sla_jacobi_inverse", L.lib().sla_jacobi_inverse(
+            self.code, L.ptr(self.rowptr), L.ptr(self.colind), L.ptr(self.vals), n, rule,
+            L.ptr(dinv), L.stream_handle(self.device)))
+        return dinv
+
+    def diagonal(self) -> torch.Tensor:
+        rows = torch.repeat_interleave(
+            torch.arange(self.shape[0], device=self.device),
+            (self.rowptr[1:] - self.rowptr[:-1]).to(torch.int64))
+        mask = rows == self.colind.to(torch.int64)
+        d = torch.zeros(self.shape[0], dtype=self.dtype, device=self.device)
+        d.index_add_(0, rows[mask], self.vals[mask])
+        return d
+
+    def matvec(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        return spmv(self.sell(), x, self.shape[0], out)
+
+
+def spmv(sell: Sell, x: torch.Tensor, n_out: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty(n_out, dtype=x.dtype, device=x.device)
+    L.check("sla_spmv", L.lib().sla_spmv(L.dtype_code(x.dtype), sell.ref(), L.ptr(x), L.ptr(out),
+                                         L.stream_handle(x.device)))
+    return out
+
+
+def coo_value_grad(row, col, a, b, n_a, n_b, K=1, batch=1) -> torch.Tensor:
+    """g[k] = -sum_c a[row[k], c] * b[col[k], c] (per batch member)."""
+    nnz = int(row.numel())
+    a = a.contiguous()
+    b = b.contiguous()
+    g = torch.empty((batch, nnz) if batch > 1 else (nnz,), dtype=a.dtype, device=a.device)
+    L.check("sla_coo_value_grad", L.lib().sla_coo_value_grad(
+        L.dtype_code(a.dtype), L.ptr(row), L.ptr(col), nnz, L.ptr(a), L.ptr(b), n_a, n_b, K,
+        batch, L.ptr(g), L.stream_handle(a.device)))
+    return g

@@ -1,0 +1,298 @@
+"""B200 (sm_100a) implementation of torch-sla's `pytorch` iterative backend.
+
+Same function names, signatures, return conventions and warnings as
+torch_sla/backends/pytorch_backend.py, restricted to the hot path: CG and
+BiCGStab with the 'jacobi' / 'none' preconditioners, the CSR cache and the
+batched same-pattern CG. Every solve runs in libsla_b200 kernels on the GPU;
+CPU tensors raise (there is no CPU fallback).
+"""
+from __future__ import annotations
+
+import ctypes
+import warnings
+from typing import Callable, NamedTuple, Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from .. import _lib as L
+from .._csr import DeviceCSR, coo_value_grad
+
+__all__ = [
+    "SolveResult", "CachedSparseMatrix", "JacobiPreconditioner", "IdentityPreconditioner",
+    "jacobi_preconditioner", "get_preconditioner", "pcg_solve_optimized", "pcg_solve_fused",
+    "pbicgstab_solve", "pytorch_solve", "batched_cg_same_pattern", "last_solve_info",
+]
+
+
+class SolveResult(NamedTuple):
+    """Result of an iterative solve (pytorch_backend.py:35-40)."""
+    x: Tensor
+    num_iters: int
+    residual: float
+    converged: bool
+
+
+_LAST_INFO: dict = {}
+
+
+def last_solve_info() -> dict:
+    """Iterations / residual / status of the most recent solve on this process."""
+    return dict(_LAST_INFO)
+
+
+def _record(kind: str, info: L.SolveInfo) -> None:
+    _LAST_INFO.clear()
+    _LAST_INFO.update(kind=kind, iterations=int(info.iterations), residual=float(info.residual),
+                      status=int(info.status), reason=int(info.reason))
+
+
+class CachedSparseMatrix:
+    """GPU CSR cache of a COO matrix (pytorch_backend.py:107-215).
+
+    The COO -> CSR conversion, the SELL-32 view the solver kernels read and
+    the diagonal are built by libsla_b200 on the device.
+    """
+
+    def __init__(self, val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int],
+                 use_rcm: bool = False):
+        if use_rcm:
+            raise NotImplementedError("torch_sla_b200: RCM reordering is not part of the B200 path")
+        L.dtype_code(val.dtype)
+        self.val, self.row, self.col = val, row, col
+        self.shape = (int(shape[0]), int(shape[1]))
+        self.device = val.device
+        self.dtype = val.dtype
+        self.n = self.shape[0]
+        self.use_rcm = False
+        self.csr = DeviceCSR(val, row, col, self.shape)
+        self._diag = None
+
+    def matvec(self, x: Tensor) -> Tensor:
+        """Sparse matrix-vector product y = A @ x."""
+        L.require_cuda(x)
+        return self.csr.matvec(x.to(self.dtype))
+
+    matvec_reordered = matvec
+
+    @property
+    def diagonal(self) -> Tensor:
+        if self._diag is None:
+            self._diag = self.csr.diagonal()
+        return self._diag
+
+    def sell(self):
+        return self.csr.sell()
+
+
+class JacobiPreconditioner:
+    """M^{-1} = diag(A)^{-1} with |d| < 100 eps -> 1 (pytorch_backend.py:221-235).
+
+    Callable like the reference's closure; the fused solver kernels read
+    `dinv` directly instead of calling it.
+    """
+
+    def __init__(self, A: CachedSparseMatrix):
+        self.dinv = A.csr.jacobi_inverse(L.SLA_JACOBI_EPS)
+
+    def __call__(self, r: Tensor) -> Tensor:
+        return self.dinv * r
+
+
+class IdentityPreconditioner:
+    """preconditioner='none' (pytorch_backend.py:916-917)."""
+    dinv = None
+
+    def __call__(self, r: Tensor) -> Tensor:
+        return r
+
+
+def jacobi_preconditioner(A: CachedSparseMatrix) -> JacobiPreconditioner:
+    return JacobiPreconditioner(A)
+
+
+def get_preconditioner(A: CachedSparseMatrix, name: str = "jacobi",
+                       mixed_precision: bool = False, method: str = "cg"):
+    """'jacobi' and 'none' (pytorch_backend.py:855-929). 'auto' resolves to
+    'jacobi', the only preconditioner of the B200 path."""
+    if mixed_precision:
+        raise NotImplementedError("torch_sla_b200: mixed-precision preconditioning is not "
+                                  "part of the B200 path")
+    if name is None or name == "none":
+        return IdentityPreconditioner()
+    if name in ("jacobi", "auto"):
+        return jacobi_preconditioner(A)
+    raise NotImplementedError(
+        f"torch_sla_b200: preconditioner {name!r} is not implemented on the B200 path "
+        "(available: jacobi, none)")
+
+
+def _as_dinv(preconditioner, A: CachedSparseMatrix):
+    if preconditioner is None:
+        return jacobi_preconditioner(A).dinv
+    if isinstance(preconditioner, (JacobiPreconditioner, IdentityPreconditioner)):
+        return preconditioner.dinv
+    raise NotImplementedError("torch_sla_b200: the fused kernels accept the preconditioners "
+                              "built by get_preconditioner ('jacobi', 'none') only")
+
+
+def _pcg_core(A: CachedSparseMatrix, b: Tensor, x0, dinv, atol, rtol, maxiter, flags=0):
+    L.require_cuda(b, x0)
+    if b.dim() != 1 or b.shape[0] != A.n:
+        raise ValueError(f"torch_sla_b200: b must have shape [{A.n}]")
+    b = b.to(A.dtype).contiguous()
+    sell = A.sell()
+    lib = L.lib()
+    need = ctypes.c_size_t(0)
+    L.check("sla_pcg_workspace", lib.sla_pcg_workspace(A.csr.code, A.n, ctypes.byref(need)))
+    ws = L.workspace(need.value, A.device)
+    x = x0.to(A.dtype).clone().contiguous() if x0 is not None else torch.empty_like(b)
+    info = L.SolveInfo()
+    st = lib.sla_pcg(A.csr.code, sell.ref(), L.ptr(dinv), L.ptr(b), L.ptr(x),
+                     int(x0 is not None), float(atol), float(rtol), int(maxiter), int(flags),
+                     L.ptr(ws), ws.numel(), ctypes.byref(info), L.stream_handle(A.device))
+    L.check("sla_pcg", st)
+    _record("pcg", info)
+    return x, info
+
+
+def pcg_solve_optimized(A: CachedSparseMatrix, b: Tensor, x0: Optional[Tensor] = None,
+                        atol: float = 1e-10, rtol: float = 1e-6, maxiter: int = 10000,
+                        preconditioner: Callable[[Tensor], Tensor] = None,
+                        check_interval: int = 50) -> SolveResult:
+    """Jacobi-PCG with the start-of-iteration stopping test
+    (pytorch_backend.py:1262-1362), fused into two kernels per iteration."""
+    dinv = _as_dinv(preconditioner, A)
+    x, info = _pcg_core(A, b, x0, dinv, atol, rtol, maxiter)
+    converged = info.status == L.SLA_OK
+    if not converged:
+        warnings.warn(f"PCG did not converge in {maxiter} iterations "
+                      f"(residual={info.residual:.2e})")
+    return SolveResult(x, int(info.iterations), float(info.residual), converged)
+
+
+def pcg_solve_fused(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int], b: Tensor,
+                    x0: Optional[Tensor] = None, atol: float = 1e-10, rtol: float = 1e-6,
+                    maxiter: int = 10000, preconditioner: str = "auto") -> SolveResult:
+    """CSR build + preconditioner + PCG (pytorch_backend.py:1466-1501)."""
+    A = CachedSparseMatrix(val, row, col, shape)
+    M = get_preconditioner(A, preconditioner, method="cg")
+    return pcg_solve_optimized(A, b, x0=x0, atol=atol, rtol=rtol, maxiter=maxiter, preconditioner=M)
+
+
+def _bicgstab_core(A: CachedSparseMatrix, b: Tensor, x0, dinv, atol, rtol, maxiter):
+    L.require_cuda(b, x0)
+    b = b.to(A.dtype).contiguous()
+    lib = L.lib()
+    need = ctypes.c_size_t(0)
+    L.check("sla_bicgstab_workspace", lib.sla_bicgstab_workspace(A.csr.code, A.n, ctypes.byref(need)))
+    ws = L.workspace(need.value, A.device)
+    x = x0.to(A.dtype).clone().contiguous() if x0 is not None else torch.empty_like(b)
+    info = L.SolveInfo()
+    st = lib.sla_bicgstab(A.csr.code, A.sell().ref(), L.ptr(dinv), L.ptr(b), L.ptr(x),
+                          int(x0 is not None), float(atol), float(rtol), int(maxiter), L.ptr(ws),
+                          ws.numel(), ctypes.byref(info), L.stream_handle(A.device))
+    L.check("sla_bicgstab", st)
+    _record("bicgstab", info)
+    return x, info
+
+
+def pbicgstab_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int], b: Tensor,
+                    x0: Optional[Tensor] = None, atol: float = 1e-10, rtol: float = 1e-6,
+                    maxiter: int = 10000, preconditioner: str = "auto") -> Tuple[Tensor, int, float]:
+    """Jacobi-PBiCGStab (pytorch_backend.py:1508-1596); returns (x, iters, residual)."""
+    A = CachedSparseMatrix(val, row, col, shape)
+    M = get_preconditioner(A, preconditioner, method="bicgstab")
+    x, info = _bicgstab_core(A, b, x0, M.dinv, atol, rtol, maxiter)
+    if info.reason == 3:
+        warnings.warn("PBiCGStab: rho became too small")
+    if info.status != L.SLA_OK:
+        warnings.warn(f"PBiCGStab did not converge in {maxiter} iterations "
+                      f"(residual={info.residual:.2e})")
+    return x, int(info.iterations), float(info.residual)
+
+
+def pytorch_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int], b: Tensor,
+                  method: str = "cg", atol: float = 1e-10, rtol: float = 1e-6,
+                  maxiter: int = 10000, x0: Optional[Tensor] = None,
+                  preconditioner: str = "jacobi", mixed_precision: bool = False) -> Tensor:
+    """Method switch of the pytorch backend (pytorch_backend.py:2224-2337)."""
+    L.require_cuda(val, b)
+    if method == "cg":
+        if b.dim() == 2:
+            raise NotImplementedError("torch_sla_b200: multi-RHS CG (b of shape [n, K]) is "
+                                      "not implemented yet; solve the columns one by one")
+        if mixed_precision and val.dtype == torch.float32:
+            raise NotImplementedError("torch_sla_b200: mixed-precision PCG is not part of the "
+                                      "B200 path")
+        return pcg_solve_fused(val, row, col, shape, b, x0=x0, atol=atol, rtol=rtol,
+                               maxiter=maxiter, preconditioner=preconditioner).x
+    if method == "bicgstab":
+        if b.dim() == 2:
+            cols = [pbicgstab_solve(val, row, col, shape, b[:, k], x0=None, atol=atol, rtol=rtol,
+                                    maxiter=maxiter, preconditioner=preconditioner)[0]
+                    for k in range(b.shape[1])]
+            return torch.stack(cols, dim=1)
+        return pbicgstab_solve(val, row, col, shape, b, x0=x0, atol=atol, rtol=rtol,
+                               maxiter=maxiter, preconditioner=preconditioner)[0]
+    if method in ("gmres", "minres", "lsqr", "lsmr"):
+        raise NotImplementedError(f"torch_sla_b200: method {method!r} is outside the B200 "
+                                  "hot path (cg, bicgstab)")
+    raise ValueError(f"Unknown method: {method}. Available: cg, bicgstab, gmres, minres, lsqr, lsmr")
+
+
+# ----------------------------------------------------------------- batched
+_MAX_BATCH = 1024
+
+
+def batched_cg_same_pattern_info(val_batch: Tensor, row: Tensor, col: Tensor,
+                                 shape: Tuple[int, int], b_batch: Tensor, atol: float = 1e-10,
+                                 rtol: float = 1e-6, maxiter: int = 10000):
+    """batched_cg_same_pattern plus the solver info of the (last) chunk."""
+    m, n = shape
+    assert m == n, "CG requires square systems"
+    L.require_cuda(val_batch, b_batch)
+    code = L.dtype_code(val_batch.dtype)
+    Bn = int(val_batch.shape[0])
+    dev = val_batch.device
+    csr = DeviceCSR(None, row.to(dev), col.to(dev), (n, n), keep_map=True, dtype=val_batch.dtype)
+    lib = L.lib()
+    stream = L.stream_handle(dev)
+    X = torch.empty(Bn, n, dtype=val_batch.dtype, device=dev)
+    info = L.SolveInfo()
+    # Members are coupled only through the "all converged" test; batches
+    # beyond the kernel's 1024 lanes run as independent chunks.
+    for s0 in range(0, Bn, _MAX_BATCH):
+        vb = val_batch[s0:s0 + _MAX_BATCH].contiguous()
+        bb = b_batch[s0:s0 + _MAX_BATCH].to(val_batch.dtype).contiguous()
+        B = int(vb.shape[0])
+        vals = torch.empty(max(csr.nnz * B, 1), dtype=val_batch.dtype, device=dev)
+        L.check("sla_batched_values", lib.sla_batched_values(
+            code, L.ptr(vb), B, int(vb.shape[1]), L.ptr(csr.src_index), L.ptr(csr.seg_ptr),
+            csr.nnz, L.ptr(vals), stream))
+        need = ctypes.c_size_t(0)
+        L.check("sla_batched_cg_workspace", lib.sla_batched_cg_workspace(code, n, B, ctypes.byref(need)))
+        ws = L.workspace(need.value, dev)
+        xo = X[s0:s0 + B]
+        st = lib.sla_batched_cg(code, L.ptr(csr.rowptr), L.ptr(csr.colind), L.ptr(vals), n, B,
+                                L.ptr(bb), L.ptr(xo), float(atol), float(rtol), int(maxiter),
+                                L.ptr(ws), ws.numel(), ctypes.byref(info), stream)
+        L.check("sla_batched_cg", st)
+    _record("batched_cg", info)
+    return X, info
+
+
+def batched_cg_same_pattern(val_batch: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int],
+                            b_batch: Tensor, atol: float = 1e-10, rtol: float = 1e-6,
+                            maxiter: int = 10000) -> Tensor:
+    """B Jacobi-PCG solves over one shared pattern (pytorch_backend.py:2575-2638)."""
+    return batched_cg_same_pattern_info(val_batch, row, col, shape, b_batch, atol, rtol, maxiter)[0]
+
+
+def value_gradient(row: Tensor, col: Tensor, gradb: Tensor, u: Tensor, n_rows: int,
+                   n_cols: int) -> Tensor:
+    """gradval = -gradb[row] * u[col] (summed over RHS columns when 2-D),
+    linear_solve.py:321-323."""
+    K = 1 if gradb.dim() == 1 else int(gradb.shape[1])
+    return coo_value_grad(row.to(torch.int64).contiguous(), col.to(torch.int64).contiguous(),
+                          gradb, u, n_rows, n_cols, K=K, batch=1)

@@ -1,0 +1,295 @@
+// Jacobi-preconditioned BiCGStab with the control flow of pbicgstab_solve
+// (backends/pytorch_backend.py:1508-1596): half-step exit on ||s|| < tol,
+// full-step exit on ||r|| < tol, breakdown exits on |rho| < 1e-30,
+// (t,t) < 1e-30 and |omega| < 1e-30 (those report maxiter iterations, as the
+// reference does after `break`).
+//
+// Three kernels per iteration; s = r - alpha v is never stored:
+//   K1  p = r + beta (p - omega v) (own rows and inside the gather),
+//       v = A M^{-1} p, partial (r_hat, v)          -> alpha
+//   K2  t = A M^{-1} (r - alpha v) (gather),
+//       partials (s,s), (t,t), (t,s)                -> exit mode / omega
+//   K3  x += alpha M^{-1} p [+ omega M^{-1} s], r = s - omega t,
+//       partials (r,r), (r_hat, r)                  -> convergence, next rho
+// HBM per iteration: 2 x matrix + 19 vector passes.
+#include "solver.cuh"
+
+namespace sla {
+
+struct BicgState {
+  double rho_old, rho_new, alpha, omega;
+  double tol, residual;
+  double ss, tt, ts;
+  long long iter, maxiter, iters_out;
+  int done;  // 0 running, 1 converged, 2 maxiter, 3 rho guard, 4 (t,t) guard, 5 omega guard
+  int mode;  // set by K2: 0 full step, 1 half-step convergence, 2 (t,t) breakdown
+  unsigned counter[4];
+};
+
+enum { bRunning = 0, bConverged = 1, bMaxiter = 2, bRho = 3, bTT = 4, bOmega = 5 };
+
+template <typename T, bool PREC>
+struct PGather {  // p_hat = M^{-1}(r + beta (p - omega v))
+  const T *r, *p, *v, *dinv;
+  T beta, omega;
+  __device__ __forceinline__ T pval(int32_t c) const {
+    T t = sub_rn(__ldg(p + c), mul_rn(omega, __ldg(v + c)));
+    return add_rn(__ldg(r + c), mul_rn(beta, t));
+  }
+  __device__ __forceinline__ T operator()(int32_t c) const {
+    T pc = pval(c);
+    return PREC ? mul_rn(__ldg(dinv + c), pc) : pc;
+  }
+};
+
+template <typename T, bool PREC>
+struct SGather {  // s_hat = M^{-1}(r - alpha v)
+  const T *r, *v, *dinv;
+  T alpha;
+  __device__ __forceinline__ T sval(int32_t c) const {
+    return sub_rn(__ldg(r + c), mul_rn(alpha, __ldg(v + c)));
+  }
+  __device__ __forceinline__ T operator()(int32_t c) const {
+    T sc = sval(c);
+    return PREC ? mul_rn(__ldg(dinv + c), sc) : sc;
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kBlock)
+bicg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *__restrict__ Ax,
+                 T *__restrict__ r, T *__restrict__ rhat, T *__restrict__ p, T *__restrict__ v,
+                 BicgState *st, double *partials, double atol, double rtol) {
+  __shared__ double smem[2 * kWarps];
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T bi = b[i];
+    T ri = Ax ? sub_rn(bi, Ax[i]) : bi;
+    if (!Ax) x[i] = T(0);
+    r[i] = ri;
+    rhat[i] = ri;
+    p[i] = T(0);
+    v[i] = T(0);
+    acc[0] += (double)ri * (double)ri;
+    acc[1] += (double)bi * (double)bi;
+  }
+  if (last_block_sum<2, kBlock>(acc, partials, &st->counter[0], smem) && threadIdx.x == 0) {
+    double bnorm = sqrt(acc[1]);
+    if (bnorm == 0.0) bnorm = 1.0;
+    st->tol = fmax(atol, rtol * bnorm);
+    st->residual = sqrt(acc[0]);
+    st->rho_old = 1.0;
+    st->alpha = 1.0;
+    st->omega = 1.0;
+    st->rho_new = acc[0];  // (r_hat, r) with r_hat = r
+    st->iter = 0;
+    if (st->maxiter <= 0) { st->done = bMaxiter; st->iters_out = st->maxiter; }
+    else if (fabs(acc[0]) < 1e-30) { st->done = bRho; st->iters_out = st->maxiter; }
+    else st->done = bRunning;
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T *__restrict__ p_old,
+        const T *__restrict__ v_old, const T *__restrict__ dinv, T *__restrict__ p_new,
+        T *__restrict__ v_new, BicgState *st, double *partials) {
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->done) return;
+  const double beta = (st->rho_new / st->rho_old) * (st->alpha / st->omega);
+  PGather<T, PREC> g{r, p_old, v_old, dinv, (T)beta, (T)st->omega};
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[1] = {0.0};
+  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
+    T sum = sell_row(A, s, lane, g);
+    int64_t row = s * 32 + lane;
+    if (row < A.n_slots) {
+      p_new[row] = g.pval((int32_t)row);
+      v_new[row] = sum;
+      acc[0] += (double)rhat[row] * (double)sum;
+    }
+  }
+  if (last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem) && threadIdx.x == 0)
+    st->alpha = st->rho_new / acc[0];
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+bicg_k2(Sell<T> A, const T *__restrict__ r, const T *__restrict__ v, const T *__restrict__ dinv,
+        T *__restrict__ t, BicgState *st, double *partials) {
+  __shared__ double smem[3 * kWarps];
+  if (*(volatile int *)&st->done) return;
+  SGather<T, PREC> g{r, v, dinv, (T)st->alpha};
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[3] = {0.0, 0.0, 0.0};
+  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
+    T sum = sell_row(A, s, lane, g);
+    int64_t row = s * 32 + lane;
+    if (row < A.n_slots) {
+      T si = g.sval((int32_t)row);
+      t[row] = sum;
+      acc[0] += (double)si * (double)si;
+      acc[1] += (double)sum * (double)sum;
+      acc[2] += (double)sum * (double)si;
+    }
+  }
+  if (last_block_sum<3, kBlock>(acc, partials, &st->counter[2], smem) && threadIdx.x == 0) {
+    st->ss = acc[0];
+    st->tt = acc[1];
+    st->ts = acc[2];
+    if (sqrt(acc[0]) < st->tol) {
+      st->mode = 1;
+      st->residual = sqrt(acc[0]);
+    } else if (acc[1] < 1e-30) {
+      st->mode = 2;
+    } else {
+      st->mode = 0;
+      st->omega = acc[2] / acc[1];
+    }
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+bicg_k3(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ rhat,
+        const T *__restrict__ p, const T *__restrict__ v, const T *__restrict__ t,
+        const T *__restrict__ dinv, BicgState *st, double *partials) {
+  __shared__ double smem[2 * kWarps];
+  if (*(volatile int *)&st->done) return;
+  const int mode = st->mode;
+  const T alpha = (T)st->alpha, omega = (T)st->omega;
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T ph = PREC ? mul_rn(dinv[i], p[i]) : p[i];
+    T xi = add_rn(x[i], mul_rn(alpha, ph));
+    if (mode == 0) {
+      T si = sub_rn(r[i], mul_rn(alpha, v[i]));
+      T sh = PREC ? mul_rn(dinv[i], si) : si;
+      xi = add_rn(xi, mul_rn(omega, sh));
+      T ri = sub_rn(si, mul_rn(omega, t[i]));
+      r[i] = ri;
+      acc[0] += (double)ri * (double)ri;
+      acc[1] += (double)rhat[i] * (double)ri;
+    }
+    x[i] = xi;
+  }
+  if (last_block_sum<2, kBlock>(acc, partials, &st->counter[3], smem) && threadIdx.x == 0) {
+    const long long it = st->iter + 1;
+    st->iter = it;
+    if (mode == 1) { st->done = bConverged; st->iters_out = it; return; }
+    if (mode == 2) { st->done = bTT; st->iters_out = st->maxiter; return; }
+    double res = sqrt(acc[0]);
+    st->residual = res;
+    if (res < st->tol) { st->done = bConverged; st->iters_out = it; return; }
+    if (fabs(st->omega) < 1e-30) { st->done = bOmega; st->iters_out = st->maxiter; return; }
+    if (it >= st->maxiter) { st->done = bMaxiter; st->iters_out = st->maxiter; return; }
+    st->rho_old = st->rho_new;
+    st->rho_new = acc[1];
+    if (fabs(acc[1]) < 1e-30) { st->done = bRho; st->iters_out = st->maxiter; }
+  }
+}
+
+static size_t bicg_ws_bytes(size_t elem, int64_t n) {
+  size_t G = (size_t)solver_grid();
+  return 7 * align_up(elem * (size_t)n) + 4 * align_up(4 * G * sizeof(double)) +
+         align_up(sizeof(BicgState));
+}
+
+template <typename T, bool PREC>
+static int bicg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool guess,
+                     double atol, double rtol, int64_t maxiter, void *ws, size_t ws_bytes,
+                     sla_solve_info_t *info, cudaStream_t s) {
+  Sell<T> A = make_sell<T>(Ad);
+  const int64_t n = A.n_slots;
+  Carver c(ws, ws_bytes);
+  T *r = c.take<T>(n), *rhat = c.take<T>(n), *pA = c.take<T>(n), *pB = c.take<T>(n);
+  T *vA = c.take<T>(n), *vB = c.take<T>(n), *t = c.take<T>(n);
+  const int G = solver_grid();
+  double *part[4];
+  for (int k = 0; k < 4; ++k) part[k] = c.take<double>(4 * (size_t)G);
+  BicgState *st = c.take<BicgState>(1);
+  if (!c.ok) return SLA_ERR_WORKSPACE;
+  BicgState init{};
+  init.maxiter = maxiter;
+  SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(BicgState), cudaMemcpyHostToDevice, s));
+  if (guess) SLA_TRY(spmv_launch<T>(Ad, x, t, s));
+  SLA_LAUNCH(bicg_init_kernel<T>, grid_for(n), kBlock, 0, s, n, b, x, guess ? t : nullptr, r, rhat,
+             pA, vA, st, part[0], atol, rtol);
+  SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
+    T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
+    T *v_old = (it & 1) ? vB : vA, *v_new = (it & 1) ? vA : vB;
+    cudaEvent_t ev;
+    profiler().begin(0, it, s, &ev);
+    SLA_LAUNCH((bicg_k1<T, PREC>), G, kBlock, 0, s, A, r, rhat, p_old, v_old, dinv, p_new, v_new,
+               st, part[1]);
+    profiler().end(0, s, ev);
+    profiler().begin(1, it, s, &ev);
+    SLA_LAUNCH((bicg_k2<T, PREC>), G, kBlock, 0, s, A, r, v_new, dinv, t, st, part[2]);
+    profiler().end(1, s, ev);
+    profiler().begin(2, it, s, &ev);
+    SLA_LAUNCH((bicg_k3<T, PREC>), G, kBlock, 0, s, n, x, r, rhat, p_new, v_new, t, dinv, st,
+               part[3]);
+    profiler().end(2, s, ev);
+    return SLA_OK;
+  }));
+  BicgState out;
+  SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(BicgState), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaStreamSynchronize(s));
+  profiler().resolve();
+  info->iterations = out.iters_out;
+  info->residual = out.residual;
+  info->reason = out.done;
+  info->status = out.done == bConverged ? SLA_OK
+                 : (out.done == bMaxiter ? SLA_NOT_CONVERGED : SLA_BREAKDOWN);
+  return info->status;
+}
+
+}  // namespace sla
+
+using namespace sla;
+
+extern "C" {
+
+int sla_bicgstab_workspace(int dtype, int64_t n, size_t *bytes) {
+  if (!bytes || n < 0 || (dtype != SLA_F32 && dtype != SLA_F64)) return SLA_ERR_INVALID;
+  *bytes = bicg_ws_bytes(dtype == SLA_F64 ? 8 : 4, n);
+  return SLA_OK;
+}
+
+int sla_bicgstab(int dtype, const sla_sell_t *A, const void *dinv, const void *b, void *x,
+                 int x_is_guess, double atol, double rtol, int64_t maxiter, void *workspace,
+                 size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
+  if (!sell_ok(A) || !b || !x || !info || A->row_ids) return SLA_ERR_INVALID;
+  if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
+  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
+  size_t need = 0;
+  SLA_TRY(sla_bicgstab_workspace(dtype, A->n_slots, &need));
+  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  cudaStream_t s = (cudaStream_t)stream;
+  bool g = x_is_guess != 0;
+  if (dtype == SLA_F64) {
+    if (dinv)
+      return bicg_impl<double, true>(A, (const double *)dinv, (const double *)b, (double *)x, g,
+                                     atol, rtol, maxiter, workspace, workspace_bytes, info, s);
+    return bicg_impl<double, false>(A, nullptr, (const double *)b, (double *)x, g, atol, rtol,
+                                    maxiter, workspace, workspace_bytes, info, s);
+  }
+  if (dtype == SLA_F32) {
+    if (dinv)
+      return bicg_impl<float, true>(A, (const float *)dinv, (const float *)b, (float *)x, g, atol,
+                                    rtol, maxiter, workspace, workspace_bytes, info, s);
+    return bicg_impl<float, false>(A, nullptr, (const float *)b, (float *)x, g, atol, rtol, maxiter,
+                                   workspace, workspace_bytes, info, s);
+  }
+  return SLA_ERR_INVALID;
+}
+
+}  // extern "C"

@@ -1,0 +1,341 @@
+// Jacobi-preconditioned CG (and plain CG when dinv == NULL) with the
+// stopping rule of pcg_solve_optimized (backends/pytorch_backend.py:1262-1362):
+// at the start of iteration i stop if (r,r) < max(atol, rtol*||b||)^2 and
+// report i iterations.
+//
+// Streamed path, two kernels per iteration (large systems):
+//   K_A  p_new = p_old*beta + M^{-1} r    (computed inside the SpMV gather)
+//        Ap = A p_new, write p_new and Ap, partial (p_new, Ap)
+//        last block: alpha = (r,z) / (p,Ap)
+//   K_B  x += alpha p ; r -= alpha Ap ; partial (r,r), (r, M^{-1} r)
+//        last block: beta, convergence / maxiter bookkeeping
+// HBM per iteration: matrix + 12 vector passes (r, dinv, p_old read and
+// p_new, Ap written by K_A; x, p, r, Ap, dinv read and x, r written by K_B).
+// The scalar recurrences stay on the device; the host polls a pinned flag
+// once per chunk of iterations with one chunk in flight.
+//
+// Persistent path (small systems, vectors L2-resident): the same two phases
+// in one cooperative launch separated by a bounded grid barrier.
+#include "solver.cuh"
+
+namespace sla {
+
+struct CgState {
+  double rz;
+  double rr;
+  double pAp;
+  double alpha;
+  double beta;
+  double tol_sq;
+  long long iter;
+  long long maxiter;
+  long long iters_out;
+  int done;  // 0 running, 1 converged, 2 maxiter, 3 non-finite, 4 timeout
+  int pad;
+  unsigned counter[4];
+  GridBarrier bar;
+};
+
+enum { kRunning = 0, kConverged = 1, kMaxiter = 2, kNonFinite = 3, kTimeout = 4 };
+
+template <typename T, bool PREC, bool COH>
+struct CgPGather {
+  const T *r;
+  const T *dinv;
+  const T *p_old;
+  T beta;
+  __device__ __forceinline__ T operator()(int32_t c) const {
+    T rc = COH ? ld_l2(r + c) : __ldg(r + c);
+    T pc = COH ? ld_l2(p_old + c) : __ldg(p_old + c);
+    T z = PREC ? mul_rn(__ldg(dinv + c), rc) : rc;
+    return add_rn(mul_rn(pc, beta), z);
+  }
+};
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+cg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *__restrict__ Ax,
+               const T *__restrict__ dinv, T *__restrict__ r, T *__restrict__ p_old, CgState *st,
+               double *partials, double atol, double rtol) {
+  __shared__ double smem[3 * kWarps];
+  double acc[3] = {0.0, 0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T bi = b[i];
+    T ri = Ax ? sub_rn(bi, Ax[i]) : bi;
+    if (!Ax) x[i] = T(0);
+    r[i] = ri;
+    p_old[i] = T(0);
+    T zi = PREC ? mul_rn(dinv[i], ri) : ri;
+    acc[0] += (double)ri * (double)ri;
+    acc[1] += (double)ri * (double)zi;
+    acc[2] += (double)bi * (double)bi;
+  }
+  if (last_block_sum<3, kBlock>(acc, partials, &st->counter[0], smem) && threadIdx.x == 0) {
+    st->rr = acc[0];
+    st->rz = acc[1];
+    double tol = fmax(atol, rtol * sqrt(acc[2]));
+    st->tol_sq = tol * tol;
+    st->beta = 0.0;
+    st->iter = 0;
+    if (acc[0] < st->tol_sq) { st->done = kConverged; st->iters_out = 0; }
+    else if (st->maxiter <= 0) { st->done = kMaxiter; st->iters_out = 0; }
+    else if (!isfinite(acc[0])) { st->done = kNonFinite; st->iters_out = st->maxiter; }
+    else st->done = kRunning;
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
+               const T *__restrict__ p_old, T *__restrict__ p_new, T *__restrict__ Ap, CgState *st,
+               double *partials) {
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->done) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  CgPGather<T, PREC, false> g{r, dinv, p_old, (T)st->beta};
+  double acc[1] = {0.0};
+  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
+    T sum = sell_row(A, s, lane, g);
+    int64_t row = s * 32 + lane;
+    if (row < A.n_slots) {
+      T pn = g((int32_t)row);
+      p_new[row] = pn;
+      Ap[row] = sum;
+      acc[0] += (double)pn * (double)sum;
+    }
+  }
+  if (last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem) && threadIdx.x == 0) {
+    st->pAp = acc[0];
+    st->alpha = st->rz / acc[0];
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
+                 const T *__restrict__ Ap, const T *__restrict__ dinv, CgState *st,
+                 double *partials) {
+  __shared__ double smem[2 * kWarps];
+  if (*(volatile int *)&st->done) return;
+  const T alpha = (T)st->alpha;
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T xi = add_rn(x[i], mul_rn(alpha, p[i]));
+    T ri = sub_rn(r[i], mul_rn(alpha, Ap[i]));
+    x[i] = xi;
+    r[i] = ri;
+    T zi = PREC ? mul_rn(dinv[i], ri) : ri;
+    acc[0] += (double)ri * (double)ri;
+    acc[1] += (double)ri * (double)zi;
+  }
+  if (last_block_sum<2, kBlock>(acc, partials, &st->counter[2], smem) && threadIdx.x == 0) {
+    const long long it = st->iter + 1;
+    st->iter = it;
+    st->rr = acc[0];
+    st->beta = acc[1] / st->rz;
+    st->rz = acc[1];
+    if (acc[0] < st->tol_sq) { st->done = kConverged; st->iters_out = it; }
+    else if (!isfinite(acc[0])) { st->done = kNonFinite; st->iters_out = st->maxiter; }
+    else if (it >= st->maxiter) { st->done = kMaxiter; st->iters_out = st->maxiter; }
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
+                     const T *__restrict__ dinv, T *pA, T *pB, T *__restrict__ Ap, CgState *st,
+                     double *partA, double *partB) {
+  __shared__ double smem[2 * kWarps];
+  if (*(volatile int *)&st->done) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  double rz = st->rz, rr = st->rr;
+  const double tol_sq = st->tol_sq;
+  const long long maxiter = st->maxiter;
+  double beta = 0.0;
+  T *p_old = pA, *p_new = pB;
+  int done = kMaxiter;
+  long long iters = maxiter;
+  for (long long k = 0; k < maxiter; ++k) {
+    // phase A: p_new = p_old*beta + M^{-1} r (fused into the gather), Ap = A p_new
+    CgPGather<T, PREC, true> g{r, dinv, p_old, (T)beta};
+    double a1[1] = {0.0};
+    for (int64_t s = warp; s < A.n_slices; s += nwarps) {
+      T sum = sell_row(A, s, lane, g);
+      int64_t row = s * 32 + lane;
+      if (row < n) {
+        T pn = g((int32_t)row);
+        p_new[row] = pn;
+        Ap[row] = sum;
+        a1[0] += (double)pn * (double)sum;
+      }
+    }
+    block_sum<1, kBlock>(a1, smem);
+    if (threadIdx.x == 0) partA[blockIdx.x] = a1[0];
+    if (!grid_sync(&st->bar)) { done = kTimeout; break; }
+    reduce_partials<1>(a1, partA, smem);
+    const T alpha = (T)(rz / a1[0]);
+    // phase B: x, r update and the two residual dots
+    double a2[2] = {0.0, 0.0};
+    for (int64_t i = tid; i < n; i += nthreads) {
+      T xi = add_rn(x[i], mul_rn(alpha, ld_l2(p_new + i)));
+      T ri = sub_rn(r[i], mul_rn(alpha, ld_l2(Ap + i)));
+      x[i] = xi;
+      r[i] = ri;
+      T zi = PREC ? mul_rn(dinv[i], ri) : ri;
+      a2[0] += (double)ri * (double)ri;
+      a2[1] += (double)ri * (double)zi;
+    }
+    block_sum<2, kBlock>(a2, smem);
+    if (threadIdx.x == 0) { partB[blockIdx.x] = a2[0]; partB[gridDim.x + blockIdx.x] = a2[1]; }
+    if (!grid_sync(&st->bar)) { done = kTimeout; break; }
+    reduce_partials<2>(a2, partB, smem);
+    rr = a2[0];
+    beta = a2[1] / rz;
+    rz = a2[1];
+    if (rr < tol_sq) { done = kConverged; iters = k + 1; break; }
+    if (!isfinite(rr)) { done = kNonFinite; iters = maxiter; break; }
+    T *t = p_old; p_old = p_new; p_new = t;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    st->rr = rr;
+    st->rz = rz;
+    st->done = done;
+    st->iters_out = iters;
+  }
+}
+
+static size_t cg_ws_bytes(size_t elem, int64_t n) {
+  size_t G = (size_t)solver_grid();
+  return 4 * align_up(elem * (size_t)n) + 2 * align_up(4 * G * sizeof(double)) +
+         align_up(sizeof(CgState));
+}
+
+template <typename T>
+int spmv_launch(const sla_sell_t *A, const void *x, void *y, cudaStream_t s);
+
+template <typename T, bool PREC>
+static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool guess,
+                    double atol, double rtol, int64_t maxiter, int flags, void *ws,
+                    size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
+  Sell<T> A = make_sell<T>(Ad);
+  const int64_t n = A.n_slots;
+  Carver c(ws, ws_bytes);
+  T *r = c.take<T>(n), *pA = c.take<T>(n), *pB = c.take<T>(n), *Ap = c.take<T>(n);
+  const int G = solver_grid();
+  double *part0 = c.take<double>(4 * (size_t)G), *part1 = c.take<double>(4 * (size_t)G);
+  CgState *st = c.take<CgState>(1);
+  if (!c.ok) return SLA_ERR_WORKSPACE;
+  CgState init{};
+  init.maxiter = maxiter;
+  SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
+  if (guess) SLA_TRY(spmv_launch<T>(Ad, x, Ap, s));
+  SLA_LAUNCH((cg_init_kernel<T, PREC>), grid_for(n), kBlock, 0, s, n, b, x, guess ? Ap : nullptr,
+             dinv, r, pA, st, part0, atol, rtol);
+
+  const DeviceInfo &dev = device_info();
+  bool persistent = false;
+  int coop_grid = 0;
+  if (flags != SLA_PCG_STREAMED && dev.coop) {
+    int per_sm = 0;
+    SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, cg_persistent_kernel<T, PREC>, kBlock, 0));
+    int want = (int)((n + kBlock - 1) / kBlock);
+    int cap = per_sm * dev.sm_count;
+    coop_grid = want < cap ? want : cap;
+    if (coop_grid < 1) coop_grid = 1;
+    bool small = n <= (int64_t)(1 << 20);
+    persistent = per_sm > 0 && (flags == SLA_PCG_PERSISTENT || small);
+  }
+  if (flags == SLA_PCG_PERSISTENT && !persistent) return SLA_ERR_UNSUPPORTED;
+
+  if (persistent) {
+    int64_t nn = n;
+    void *args[] = {&A, &nn, &x, &r, (void *)&dinv, &pA, &pB, &Ap, &st, &part0, &part1};
+    cudaEvent_t ev;
+    profiler().begin(0, 0, s, &ev);
+    SLA_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)cg_persistent_kernel<T, PREC>,
+                                             dim3(coop_grid), dim3(kBlock), args, 0, s));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    profiler().end(0, s, ev);
+  } else {
+    const int grid_a = G;
+    const int grid_b = G;
+    SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
+      T *p_old = (it & 1) ? pB : pA;
+      T *p_new = (it & 1) ? pA : pB;
+      cudaEvent_t ev;
+      profiler().begin(0, it, s, &ev);
+      SLA_LAUNCH((cg_spmv_kernel<T, PREC>), grid_a, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap,
+                 st, part0);
+      profiler().end(0, s, ev);
+      profiler().begin(1, it, s, &ev);
+      SLA_LAUNCH((cg_update_kernel<T, PREC>), grid_b, kBlock, 0, s, n, x, r, p_new, Ap, dinv, st,
+                 part1);
+      profiler().end(1, s, ev);
+      return SLA_OK;
+    }));
+  }
+  CgState out;
+  SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaStreamSynchronize(s));
+  profiler().resolve();
+  info->residual = sqrt(out.rr);
+  info->reason = out.done;
+  if (out.done == kTimeout) return SLA_ERR_TIMEOUT;
+  info->iterations = out.iters_out;
+  info->status = out.done == kConverged ? SLA_OK : SLA_NOT_CONVERGED;
+  return info->status;
+}
+
+}  // namespace sla
+
+using namespace sla;
+
+extern "C" {
+
+int sla_pcg_workspace(int dtype, int64_t n, size_t *bytes) {
+  if (!bytes || n < 0 || (dtype != SLA_F32 && dtype != SLA_F64)) return SLA_ERR_INVALID;
+  *bytes = cg_ws_bytes(dtype == SLA_F64 ? 8 : 4, n);
+  return SLA_OK;
+}
+
+int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b, void *x,
+            int x_is_guess, double atol, double rtol, int64_t maxiter, int flags, void *workspace,
+            size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
+  if (!sell_ok(A) || !b || !x || !info || A->row_ids) return SLA_ERR_INVALID;
+  if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
+  if (flags < 0 || flags > 2) return SLA_ERR_INVALID;
+  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
+  size_t need = 0;
+  SLA_TRY(sla_pcg_workspace(dtype, A->n_slots, &need));
+  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  cudaStream_t s = (cudaStream_t)stream;
+  bool g = x_is_guess != 0;
+  if (dtype == SLA_F64) {
+    if (dinv)
+      return pcg_impl<double, true>(A, (const double *)dinv, (const double *)b, (double *)x, g, atol,
+                                    rtol, maxiter, flags, workspace, workspace_bytes, info, s);
+    return pcg_impl<double, false>(A, nullptr, (const double *)b, (double *)x, g, atol, rtol,
+                                   maxiter, flags, workspace, workspace_bytes, info, s);
+  }
+  if (dtype == SLA_F32) {
+    if (dinv)
+      return pcg_impl<float, true>(A, (const float *)dinv, (const float *)b, (float *)x, g, atol,
+                                   rtol, maxiter, flags, workspace, workspace_bytes, info, s);
+    return pcg_impl<float, false>(A, nullptr, (const float *)b, (float *)x, g, atol, rtol, maxiter,
+                                  flags, workspace, workspace_bytes, info, s);
+  }
+  return SLA_ERR_INVALID;
+}
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// SELL-32 row kernels shared by the SpMV-bearing solver kernels.
+//
+// One warp owns one 32-slot slice; lane l owns slot l. Entry j of a slot sits
+// at slice_ptr[s] + 32*j + l, so the column/value loads of a warp are single
+// 128 B / 256 B transactions and the padded tail costs one predicated lane.
+// The gathered vector is produced by a functor so a solver can fuse the
+// vector update that precedes the SpMV (p = z + beta p, p_hat = M^{-1} p,
+// s_hat = M^{-1}(r - alpha v)) into the gather instead of a separate pass.
+#pragma once
+
+#include "common.cuh"
+
+namespace sla {
+
+template <typename T>
+struct Sell {
+  int64_t n_slots;
+  int64_t n_slices;
+  const int32_t *__restrict__ slice_ptr;
+  const int32_t *__restrict__ col;
+  const T *__restrict__ val;
+  const int32_t *__restrict__ row_ids;
+};
+
+template <typename T>
+inline Sell<T> make_sell(const sla_sell_t *A) {
+  Sell<T> s;
+  s.n_slots = A ? A->n_slots : 0;
+  s.n_slices = A ? A->n_slices : 0;
+  s.slice_ptr = A ? A->slice_ptr : nullptr;
+  s.col = A ? A->col : nullptr;
+  s.val = A ? (const T *)A->val : nullptr;
+  s.row_ids = A ? A->row_ids : nullptr;
+  return s;
+}
+
+inline bool sell_ok(const sla_sell_t *A) {
+  if (!A) return false;
+  if (A->n_slots < 0 || A->n_slices != (A->n_slots + 31) / 32) return false;
+  if (A->n_slices > 0 && (!A->slice_ptr || !A->col || !A->val)) return false;
+  return true;
+}
+
+// sum_j val[j] * g(col[j]) over the entries of this lane's slot.
+template <typename T, typename G>
+__device__ __forceinline__ T sell_row(const Sell<T> &A, int64_t slice, int lane, const G &g) {
+  const int32_t base = A.slice_ptr[slice];
+  const int width = (A.slice_ptr[slice + 1] - base) >> 5;
+  const int32_t *__restrict__ cp = A.col + base + lane;
+  const T *__restrict__ vp = A.val + base + lane;
+  T sum = T(0);
+  int j = 0;
+  for (; j + 4 <= width; j += 4) {
+    int32_t c[4];
+    T v[4], x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      c[u] = ld_stream(cp + 32 * (j + u));
+      v[u] = ld_stream(vp + 32 * (j + u));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) x[u] = c[u] >= 0 ? g(c[u]) : T(0);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) sum = fma(v[u], x[u], sum);
+  }
+  for (; j < width; ++j) {
+    int32_t c = ld_stream(cp + 32 * j);
+    T v = ld_stream(vp + 32 * j);
+    T x = c >= 0 ? g(c) : T(0);
+    sum = fma(v, x, sum);
+  }
+  return sum;
+}
+
+template <typename T>
+struct PlainGather {
+  const T *__restrict__ x;
+  __device__ __forceinline__ T operator()(int32_t c) const { return __ldg(x + c); }
+};
+
+}  // namespace sla

@@ -1,0 +1,119 @@
+// Standalone SELL-32 SpMV, the adjoint's COO value gradient and the
+// batched-value gather of the same-pattern solver.
+#include "sell.cuh"
+
+namespace sla {
+
+template <typename T>
+__global__ void __launch_bounds__(kBlock) spmv_kernel(Sell<T> A, const T *__restrict__ x,
+                                                      T *__restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  PlainGather<T> g{x};
+  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
+    T sum = sell_row(A, s, lane, g);
+    int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      int64_t row = A.row_ids ? A.row_ids[slot] : slot;
+      y[row] = sum;
+    }
+  }
+}
+
+template <typename T>
+int spmv_launch(const sla_sell_t *A, const void *x, void *y, cudaStream_t s) {
+  Sell<T> a = make_sell<T>(A);
+  if (a.n_slices == 0) return SLA_OK;
+  SLA_LAUNCH(spmv_kernel<T>, grid_for(a.n_slices * 32), kBlock, 0, s, a, (const T *)x, (T *)y);
+  return SLA_OK;
+}
+template int spmv_launch<float>(const sla_sell_t *, const void *, void *, cudaStream_t);
+template int spmv_launch<double>(const sla_sell_t *, const void *, void *, cudaStream_t);
+
+template <typename T>
+__global__ void coo_value_grad_kernel(const int64_t *__restrict__ row, const int64_t *__restrict__ col,
+                                      int64_t nnz, const T *__restrict__ a, const T *__restrict__ b,
+                                      int64_t n_a, int64_t n_b, int64_t K, int64_t batch,
+                                      T *__restrict__ g) {
+  int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; t < nnz * batch; t += stride) {
+    int64_t bi = t / nnz, k = t - bi * nnz;
+    const T *ab = a + bi * n_a * K + row[k] * K;
+    const T *bb = b + bi * n_b * K + col[k] * K;
+    T acc = mul_rn(-ab[0], bb[0]);
+    for (int64_t c = 1; c < K; ++c) acc = add_rn(acc, mul_rn(-ab[c], bb[c]));
+    g[t] = acc;
+  }
+}
+
+template <typename T>
+__global__ void batched_values_kernel(const T *__restrict__ vb, int64_t batch, int64_t nnz_coo,
+                                      const int64_t *__restrict__ src, const int32_t *__restrict__ seg,
+                                      int64_t nnz_csr, T *__restrict__ out) {
+  int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; t < nnz_csr * batch; t += stride) {
+    int64_t e = t / batch, bi = t - e * batch;
+    const T *v = vb + bi * nnz_coo;
+    int32_t s0 = seg[e], s1 = seg[e + 1];
+    T acc = v[src[s0]];
+    for (int32_t q = s0 + 1; q < s1; ++q) acc = add_rn(acc, v[src[q]]);
+    out[t] = acc;
+  }
+}
+
+}  // namespace sla
+
+using namespace sla;
+
+extern "C" {
+
+int sla_spmv(int dtype, const sla_sell_t *A, const void *x, void *y, sla_stream_t stream) {
+  if (!sell_ok(A) || (A->n_slots > 0 && (!x || !y))) return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SLA_F64) return spmv_launch<double>(A, x, y, s);
+  if (dtype == SLA_F32) return spmv_launch<float>(A, x, y, s);
+  return SLA_ERR_INVALID;
+}
+
+int sla_coo_value_grad(int dtype, const int64_t *row, const int64_t *col, int64_t nnz,
+                       const void *a, const void *b, int64_t n_a, int64_t n_b, int64_t K,
+                       int64_t batch, void *g, sla_stream_t stream) {
+  if (nnz < 0 || K < 1 || batch < 1 || n_a < 1 || n_b < 1) return SLA_ERR_INVALID;
+  if (nnz == 0) return SLA_OK;
+  if (!row || !col || !a || !b || !g) return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SLA_F64)
+    SLA_LAUNCH(coo_value_grad_kernel<double>, grid_for(nnz * batch), kBlock, 0, s, row, col, nnz,
+               (const double *)a, (const double *)b, n_a, n_b, K, batch, (double *)g);
+  else if (dtype == SLA_F32)
+    SLA_LAUNCH(coo_value_grad_kernel<float>, grid_for(nnz * batch), kBlock, 0, s, row, col, nnz,
+               (const float *)a, (const float *)b, n_a, n_b, K, batch, (float *)g);
+  else
+    return SLA_ERR_INVALID;
+  return SLA_OK;
+}
+
+int sla_batched_values(int dtype, const void *val_batch, int64_t batch, int64_t nnz_coo,
+                       const int64_t *src_index, const int32_t *seg_ptr, int64_t nnz_csr,
+                       void *out, sla_stream_t stream) {
+  if (batch < 1 || nnz_coo < 0 || nnz_csr < 0) return SLA_ERR_INVALID;
+  if (nnz_csr == 0) return SLA_OK;
+  if (!val_batch || !src_index || !seg_ptr || !out) return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SLA_F64)
+    SLA_LAUNCH(batched_values_kernel<double>, grid_for(nnz_csr * batch), kBlock, 0, s,
+               (const double *)val_batch, batch, nnz_coo, src_index, seg_ptr, nnz_csr,
+               (double *)out);
+  else if (dtype == SLA_F32)
+    SLA_LAUNCH(batched_values_kernel<float>, grid_for(nnz_csr * batch), kBlock, 0, s,
+               (const float *)val_batch, batch, nnz_coo, src_index, seg_ptr, nnz_csr,
+               (float *)out);
+  else
+    return SLA_ERR_INVALID;
+  return SLA_OK;
+}
+
+}  // extern "C"
