@@ -96,6 +96,32 @@ def matrix_bytes(nnz: int, n: int, V: int = 8) -> int:
     return nnz * (V + 4) + 4 * (n + 1)
 
 
+def e2e_run(args, v, r, c, b_host, sh, dev):
+    """pytorch_solve() with the COO matrix and b in pinned host memory; the
+    timed region holds the H2D copies, the CSR build, the solve and the D2H
+    copy of x."""
+    import torch_sla_b200 as T
+    from torch_sla_b200.backends import pytorch_backend as PB
+    vh, rh, ch = v.cpu().pin_memory(), r.cpu().pin_memory(), c.cpu().pin_memory()
+    bh = b_host.pin_memory()
+    h2d = vh.numel() * 8 + rh.numel() * 8 + ch.numel() * 8 + bh.numel() * 8
+    e_iters = 0
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e_steps = max(1, min(args.steps, 3))
+    e0.record()
+    for _ in range(e_steps):
+        vd, rd, cd, bd = (t.to(dev, non_blocking=True) for t in (vh, rh, ch, bh))
+        x = T.pytorch_solve(vd, rd, cd, sh, bd, method="cg", atol=0.0, rtol=RTOL,
+                            preconditioner="jacobi")
+        x.cpu()
+        e_iters += PB.last_solve_info()["iterations"]
+    e1.record()
+    torch.cuda.synchronize()
+    return e_iters, e0.elapsed_time(e1), e_steps, h2d
+
+
 def run_b200(args):
     import torch.distributed as dist
 
@@ -112,8 +138,9 @@ def run_b200(args):
     if world > 1:
         return run_b200_sharded(args, world, rank, local)
 
-    n = M ** 3
-    v, r, c, sh = P.poisson_3d_7pt(M, device=dev)
+    m = args.grid
+    n = m ** 3
+    v, r, c, sh = P.poisson_3d_7pt(m, device=dev)
     b_host = P.rhs_normal(n, SEED)
     b = b_host.to(dev)
     A = PB.CachedSparseMatrix(v, r, c, sh)
@@ -156,31 +183,16 @@ def run_b200(args):
     traffic = read_traffic("cg_spmv_kernel")
 
     # end to end through pytorch_solve with pinned host COO + b
-    vh, rh, ch = v.cpu().pin_memory(), r.cpu().pin_memory(), c.cpu().pin_memory()
-    bh = b_host.pin_memory()
-    h2d = vh.numel() * 8 + rh.numel() * 8 + ch.numel() * 8 + bh.numel() * 8
-    e_iters = 0
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e_steps = max(1, min(args.steps, 3))
-    e0.record()
-    for _ in range(e_steps):
-        vd, rd, cd, bd = (t.to(dev, non_blocking=True) for t in (vh, rh, ch, bh))
-        x = T.pytorch_solve(vd, rd, cd, sh, bd, method="cg", atol=0.0, rtol=RTOL,
-                            preconditioner="jacobi")
-        x_host = x.cpu()
-        e_iters += PB.last_solve_info()["iterations"]
-    e1.record()
-    torch.cuda.synchronize()
-    e_ms = e0.elapsed_time(e1)
+    e_iters, e_ms, e_steps, h2d = 0, float("nan"), 0, 0
+    if not args.no_e2e:
+        e_iters, e_ms, e_steps, h2d = e2e_run(args, v, r, c, b_host, sh, dev)
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "iterations/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic",
-        "config": {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [M, M, M], "n": n, "nnz": nnz,
+        "config": {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [m, m, m], "n": n, "nnz": nnz,
                    "rtol": RTOL, "b": "N(0,1) seed 1", "iterations_per_solve": iters // args.steps,
                    "format": "SELL-32 int32 (sigma=1)", "l2": "inputs larger than L2 (1.4 GB matrix)",
                    "parallelism": "single GPU"},
@@ -196,9 +208,10 @@ def run_b200(args):
                      "avg_launch_ms": round(ka_avg, 5), "sampled_launches": ka_n,
                      "update_kernel_avg_ms": round(kb_ms / max(kb_n, 1), 5),
                      "peak_kind": peak_kind},
-        "e2e": {"value": round(e_iters / (e_ms / 1e3), 2), "unit": "iterations/s",
+        "e2e": {"value": round(e_iters / (e_ms / 1e3), 2) if e_steps else None,
+                "unit": "iterations/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": n * 8,
-                "ms_per_step": round(e_ms / e_steps, 3), "steps": e_steps},
+                "ms_per_step": round(e_ms / e_steps, 3) if e_steps else None, "steps": e_steps},
         "gpu_launches": launches,
         "clocks": clk.summary(),
     }
@@ -243,7 +256,7 @@ def cpu_baseline(A_gpu=None, b_host=None, budget_s=15.0):
     it = K.pcg_iterations(Acpu, b_host, dinv, budget_s=budget_s)
     dt = time.perf_counter() - t0
     return {"value": round(it / dt, 3), "unit": "iterations/s", "cores": cores, "kind": "port",
-            "sample": f"{it} Jacobi-PCG iterations of the 256^3 7-point system (n={n}) with "
+            "sample": f"{it} Jacobi-PCG iterations of the same 7-point system (n={n}) with "
                       "torch CPU CSR mv/vdot/addcmul, as torch-sla's pytorch backend runs them"}
 
 
@@ -301,6 +314,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--grid", type=int, default=M, help="grid edge per GPU (default 256)")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

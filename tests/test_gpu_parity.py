@@ -185,13 +185,38 @@ def test_bicgstab_matches_reference(dev, golden, name):
     assert rel(x, case["x"]) < (1e-7 if it < kw["maxiter"] else 1e-10)
 
 
+def rounding_envelope(fn, *args, seeds=4, **kw):
+    """Iteration counts of the oracle under its own summation order and under
+    `seeds` permuted summation orders of every inner product: BiCGStab's
+    count moves by several iterations with the rounding of the dots alone
+    (convdiff 24^3: 63..70 around the reference's 67)."""
+    import oracle.krylov as KK
+    counts = [fn(*args, **kw)[1]]
+    orig = KK.torch.vdot
+    n = args[4].numel()
+    for s in range(seeds):
+        perm = torch.randperm(n, generator=torch.Generator().manual_seed(s))
+        KK.torch.vdot = lambda a, b, perm=perm: (a[perm] * b[perm]).sum()
+        try:
+            counts.append(fn(*args, **kw)[1])
+        finally:
+            KK.torch.vdot = orig
+    return min(counts), max(counts), counts[0]
+
+
 def test_bicgstab_vs_oracle_larger(dev):
     v, r, c, sh = P.convdiff_3d_upwind(24)
     b = P.rhs_uniform01(sh[0], 3)
-    xo, ito, _, how = K.pbicgstab(v, r, c, sh, b, atol=0.0, rtol=1e-8, precond="jacobi")
+    lo, hi, ito = rounding_envelope(K.pbicgstab, v, r, c, sh, b, atol=0.0, rtol=1e-8,
+                                    precond="jacobi")
+    xo = K.pbicgstab(v, r, c, sh, b, atol=0.0, rtol=1e-8, precond="jacobi")[0]
     x, it, res = T.pbicgstab_solve(*cu(v, r, c, dev=dev), sh, b.to(dev), atol=0.0, rtol=1e-8,
                                    preconditioner="jacobi")
-    assert iters_close(it, ito)
+    assert math.floor(0.97 * lo) <= it <= math.ceil(1.03 * hi), (it, lo, hi, ito)
+    # both stop at ||r|| < 1e-8 ||b||; the true residual confirms it
+    A = T.SparseTensor(*cu(v, r, c, dev=dev), sh)
+    bd = b.to(dev)
+    assert float((bd - A @ x).norm() / bd.norm()) < 2e-8
     assert rel(x, xo) < 1e-6
 
 
