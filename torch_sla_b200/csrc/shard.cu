@@ -1,0 +1,925 @@
+// Row-sharded (Shard(0)) SpMV and Krylov solvers over NCCL, one process per
+// GPU (distributed/matvec.py:26-93, 235-303; distributed/solve.py:279-436).
+//
+// Local vectors are laid out [owned | halo]. Per SpMV the owned rows that a
+// neighbour needs are packed (for the solvers: the search direction computed
+// on the fly, so the packed values are the ones the SpMV uses), exchanged with
+// grouped ncclSend/ncclRecv on a side stream, and the interior rows (no halo
+// column) run on the compute stream meanwhile; the boundary rows run after
+// the halo arrives. Dot products are summed per rank by the kernels'
+// last block and combined by one small ncclAllReduce per reduction point.
+// Stopping decisions are computed by every kernel from the allreduced values
+// (identical on all ranks), so every rank enqueues the same NCCL sequence.
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <thread>
+
+#include "solver.cuh"
+
+namespace sla {
+
+#define SLA_NCCL_TRY(expr)                                                          \
+  do {                                                                              \
+    ncclResult_t _r = (expr);                                                       \
+    if (_r != ncclSuccess) {                                                        \
+      fprintf(stderr, "[sla_b200] %s failed: %s\n", #expr, ncclGetErrorString(_r)); \
+      return SLA_ERR_NCCL;                                                          \
+    }                                                                               \
+  } while (0)
+
+struct Comm {
+  ncclComm_t nccl = nullptr;
+  int rank = 0, nranks = 1;
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_ready = nullptr, ev_halo = nullptr;
+};
+
+template <typename T> inline ncclDataType_t nccl_type();
+template <> inline ncclDataType_t nccl_type<double>() { return ncclFloat64; }
+template <> inline ncclDataType_t nccl_type<float>() { return ncclFloat32; }
+
+// Host-side bounded wait: a peer that stops answering turns into
+// SLA_ERR_TIMEOUT (after aborting the communicator) instead of a hang.
+constexpr double kWaitSeconds = 600.0;
+
+static int wait_bounded(cudaEvent_t ev, Comm *c) {
+  auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaEventQuery(ev);
+    if (e == cudaSuccess) return SLA_OK;
+    if (e != cudaErrorNotReady) {
+      fprintf(stderr, "[sla_b200] event wait failed: %s\n", cudaGetErrorString(e));
+      return SLA_ERR_CUDA;
+    }
+    ncclResult_t async = ncclSuccess;
+    if (c && c->nccl && ncclCommGetAsyncError(c->nccl, &async) == ncclSuccess &&
+        async != ncclSuccess && async != ncclInProgress) {
+      fprintf(stderr, "[sla_b200] NCCL async error: %s\n", ncclGetErrorString(async));
+      ncclCommAbort(c->nccl);
+      c->nccl = nullptr;
+      return SLA_ERR_NCCL;
+    }
+    double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (dt > kWaitSeconds) {
+      fprintf(stderr, "[sla_b200] shard solve: no progress for %.0f s, aborting communicator\n", dt);
+      if (c && c->nccl) { ncclCommAbort(c->nccl); c->nccl = nullptr; }
+      return SLA_ERR_TIMEOUT;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+static bool plan_ok(const sla_halo_plan_t *p) {
+  if (!p || p->n_owned < 0 || p->n_halo < 0 || p->n_neighbors < 0) return false;
+  if (p->n_neighbors > 0 && (!p->neighbor_rank || !p->send_offset || !p->recv_offset))
+    return false;
+  if (p->n_neighbors > 0 && p->recv_offset[p->n_neighbors] != p->n_halo) return false;
+  if (p->n_neighbors > 0 && p->send_offset[p->n_neighbors] > 0 && !p->send_index) return false;
+  return true;
+}
+
+static int64_t n_send(const sla_halo_plan_t *p) {
+  return p->n_neighbors > 0 ? p->send_offset[p->n_neighbors] : 0;
+}
+
+// Grouped send/recv of the packed halo on the side stream, ordered after
+// everything already enqueued on `s`.
+template <typename T>
+static int halo_enqueue(Comm *c, const sla_halo_plan_t *p, const T *sendbuf, T *recvbuf,
+                        cudaStream_t s) {
+  SLA_CUDA_TRY(cudaEventRecord(c->ev_ready, s));
+  SLA_CUDA_TRY(cudaStreamWaitEvent(c->side, c->ev_ready, 0));
+  if (p->n_neighbors > 0) {
+    SLA_NCCL_TRY(ncclGroupStart());
+    for (int i = 0; i < p->n_neighbors; ++i) {
+      const int64_t so = p->send_offset[i], sc = p->send_offset[i + 1] - so;
+      const int64_t ro = p->recv_offset[i], rc = p->recv_offset[i + 1] - ro;
+      if (sc > 0)
+        SLA_NCCL_TRY(ncclSend(sendbuf + so, (size_t)sc, nccl_type<T>(), p->neighbor_rank[i],
+                              c->nccl, c->side));
+      if (rc > 0)
+        SLA_NCCL_TRY(ncclRecv(recvbuf + ro, (size_t)rc, nccl_type<T>(), p->neighbor_rank[i],
+                              c->nccl, c->side));
+    }
+    SLA_NCCL_TRY(ncclGroupEnd());
+  }
+  SLA_CUDA_TRY(cudaEventRecord(c->ev_halo, c->side));
+  return SLA_OK;
+}
+
+template <typename T, typename V>
+__global__ void halo_pack_kernel(const int32_t *__restrict__ idx, int64_t n, V val,
+                                 T *__restrict__ out, const int *stopped) {
+  if (stopped && *(volatile const int *)stopped) return;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) out[i] = val(idx[i]);
+}
+
+template <typename T>
+__global__ void halo_unpack_kernel(const T *__restrict__ recv, const int32_t *__restrict__ src,
+                                   int64_t n_halo, T *__restrict__ dst, const int *stopped) {
+  if (stopped && *(volatile const int *)stopped) return;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n_halo; i += stride) dst[i] = recv[src ? src[i] : i];
+}
+
+template <typename T>
+struct LoadVal {
+  const T *x;
+  __device__ __forceinline__ T operator()(int32_t c) const { return x[c]; }
+};
+
+// Gather that reads owned columns through `inner` and halo columns from the
+// received buffer.
+template <typename T, typename Inner>
+struct HaloGather {
+  Inner inner;
+  const T *halo;
+  int32_t n_own;
+  __device__ __forceinline__ T operator()(int32_t c) const {
+    return c < n_own ? inner(c) : __ldg(halo + (c - n_own));
+  }
+};
+
+template <typename T, typename G>
+__global__ void __launch_bounds__(kBlock)
+shard_spmv_rows_kernel(Sell<T> A, G g, T *__restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
+    T sum = sell_row(A, s, lane, g);
+    int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) y[A.row_ids ? A.row_ids[slot] : slot] = sum;
+  }
+}
+
+// ================================================================ shard CG
+struct ShardState {
+  int stopped;
+  int pad;
+  long long iters;
+  double pap_int;        // interior-rows part of the local (p, Ap)
+  double part3[3];       // interior-rows parts of the local (s,s),(t,t),(t,s)
+  double alpha_prev, omega_prev;
+  unsigned counter[8];
+};
+
+// Reduction buffers (allreduced in place), doubles.
+struct CgRed {
+  double init[2];   // (r,z), (b,b)
+  double pap[1];    // (p, Ap)
+  double pad0;
+  double loc[2][2]; // per iteration parity: (r,r), (r,z)
+};
+
+__device__ __forceinline__ double cg_rz(const CgRed *R, long long k) {
+  return k == 0 ? R->init[0] : R->loc[(k - 1) & 1][1];
+}
+
+// p_new = p_old * beta + M^{-1} r  (distributed/solve.py:324-348 order)
+template <typename T, bool PREC>
+struct ShardP {
+  const T *r, *dinv, *p_old;
+  T beta;
+  __device__ __forceinline__ T operator()(int32_t c) const {
+    T z = PREC ? mul_rn(__ldg(dinv + c), __ldg(r + c)) : __ldg(r + c);
+    return add_rn(mul_rn(__ldg(p_old + c), beta), z);
+  }
+};
+
+__device__ __forceinline__ double cg_beta(const CgRed *R, long long k) {
+  return k == 0 ? 0.0 : cg_rz(R, k) / cg_rz(R, k - 1);
+}
+
+// Stop test of iteration k-1 evaluated at the start of iteration k
+// (the reference breaks after iteration k-1's updates, before its p update).
+__device__ __forceinline__ bool cg_stop(const CgRed *R, long long k, long long every, double tol) {
+  if (k == 0 || ((k - 1) % every) != 0) return false;
+  return sqrt(R->loc[(k - 1) & 1][0]) < tol;
+}
+
+__device__ __forceinline__ double cg_tol(const CgRed *R, double atol, double rtol) {
+  return fmax(atol, rtol * sqrt(R->init[1]));
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+shard_cg_init(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *__restrict__ dinv,
+              T *__restrict__ r, T *__restrict__ p_old, ShardState *st, CgRed *R,
+              double *partials) {
+  __shared__ double smem[2 * kWarps];
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T bi = b[i];
+    x[i] = T(0);
+    r[i] = bi;
+    p_old[i] = T(0);
+    T zi = PREC ? mul_rn(dinv[i], bi) : bi;
+    acc[0] += (double)bi * (double)zi;
+    acc[1] += (double)bi * (double)bi;
+  }
+  if (last_block_sum<2, kBlock>(acc, partials, &st->counter[0], smem) && threadIdx.x == 0) {
+    R->init[0] = acc[0];
+    R->init[1] = acc[1];
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void shard_cg_pack(const int32_t *__restrict__ idx, int64_t n, const T *r,
+                              const T *dinv, const T *p_old, T *__restrict__ out, ShardState *st,
+                              const CgRed *R, long long k, long long every, double atol,
+                              double rtol) {
+  if (*(volatile int *)&st->stopped) return;
+  if (cg_stop(R, k, every, cg_tol(R, atol, rtol))) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) { st->stopped = 1; st->iters = k; }
+    return;
+  }
+  ShardP<T, PREC> p{r, dinv, p_old, (T)cg_beta(R, k)};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) out[i] = p(idx[i]);
+}
+
+template <typename T, bool PREC, bool HALO>
+__global__ void __launch_bounds__(kBlock)
+shard_cg_spmv(Sell<T> A, int32_t n_own, const T *__restrict__ r, const T *__restrict__ dinv,
+              const T *__restrict__ p_old, const T *__restrict__ phalo, T *__restrict__ p_new,
+              T *__restrict__ Ap, ShardState *st, CgRed *R, double *partials, long long k) {
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  ShardP<T, PREC> inner{r, dinv, p_old, (T)cg_beta(R, k)};
+  HaloGather<T, ShardP<T, PREC>> g{inner, phalo, n_own};
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[1] = {0.0};
+  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
+    T sum = HALO ? sell_row(A, s, lane, g) : sell_row(A, s, lane, inner);
+    int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      int32_t row = A.row_ids[slot];
+      T pn = inner(row);
+      p_new[row] = pn;
+      Ap[row] = sum;
+      acc[0] += (double)pn * (double)sum;
+    }
+  }
+  if (last_block_sum<1, kBlock>(acc, partials, &st->counter[HALO ? 2 : 1], smem) &&
+      threadIdx.x == 0) {
+    if (!HALO) st->pap_int = acc[0];
+    else R->pap[0] = st->pap_int + acc[0];
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+shard_cg_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
+                const T *__restrict__ Ap, const T *__restrict__ dinv, ShardState *st, CgRed *R,
+                double *partials, long long k) {
+  __shared__ double smem[2 * kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  const T alpha = (T)(cg_rz(R, k) / R->pap[0]);
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    // torch.addcmul(x, alpha, p, value=1) / (r, alpha, Ap, value=-1)
+    T xi = add_rn(x[i], mul_rn(alpha, p[i]));
+    T ri = sub_rn(r[i], mul_rn(alpha, Ap[i]));
+    x[i] = xi;
+    r[i] = ri;
+    T zi = PREC ? mul_rn(dinv[i], ri) : ri;
+    acc[0] += (double)ri * (double)ri;
+    acc[1] += (double)ri * (double)zi;
+  }
+  if (last_block_sum<2, kBlock>(acc, partials, &st->counter[3], smem) && threadIdx.x == 0) {
+    R->loc[k & 1][0] = acc[0];
+    R->loc[k & 1][1] = acc[1];
+  }
+}
+
+// ========================================================== shard BiCGStab
+struct BiRed {
+  double init[2];   // (r,r) = (r_hat, r), (b,b)
+  double rv[1];     // (r_hat, v)
+  double pad0;
+  double stt[3];    // (s,s), (t,t), (t,s)
+  double pad1;
+  double rr[2][2];  // per iteration parity: (r,r), (r_hat, r)
+};
+
+__device__ __forceinline__ double bi_rho(const BiRed *R, long long k) {
+  return k == 0 ? R->init[0] : R->rr[(k - 1) & 1][1];
+}
+
+__device__ __forceinline__ double bi_tol(const BiRed *R, double atol, double rtol) {
+  return fmax(atol, rtol * sqrt(R->init[1]));
+}
+
+// Full-step stop test of iteration k-1, evaluated at the start of k.
+__device__ __forceinline__ bool bi_stop(const BiRed *R, long long k, long long every, double tol) {
+  if (k == 0 || ((k - 1) % every) != 0) return false;
+  double rn = sqrt(R->rr[(k - 1) & 1][0]);
+  return rn < tol || isnan(rn);
+}
+
+// p_hat = M^{-1}(r + beta (p - omega t_prev)). torch-sla's shard_matvec
+// returns a view of one cached buffer, so its v is overwritten by t before
+// the next p update reads it; t_prev is that value.
+template <typename T, bool PREC>
+struct BiP {
+  const T *r, *p, *tp, *dinv;
+  T beta, omega;
+  __device__ __forceinline__ T pval(int32_t c) const {
+    T u = sub_rn(__ldg(p + c), mul_rn(omega, __ldg(tp + c)));
+    return add_rn(__ldg(r + c), mul_rn(beta, u));
+  }
+  __device__ __forceinline__ T operator()(int32_t c) const {
+    T pc = pval(c);
+    return PREC ? mul_rn(__ldg(dinv + c), pc) : pc;
+  }
+};
+
+template <typename T, bool PREC>
+struct BiS {  // s_hat = M^{-1}(r - alpha v)
+  const T *r, *v, *dinv;
+  T alpha;
+  __device__ __forceinline__ T sval(int32_t c) const {
+    return sub_rn(__ldg(r + c), mul_rn(alpha, __ldg(v + c)));
+  }
+  __device__ __forceinline__ T operator()(int32_t c) const {
+    T sc = sval(c);
+    return PREC ? mul_rn(__ldg(dinv + c), sc) : sc;
+  }
+};
+
+__device__ __forceinline__ double bi_beta(const BiRed *R, const ShardState *st, long long k) {
+  if (k == 0) return 0.0;
+  double rho_prev = k == 1 ? R->init[0] : R->rr[(k - 2) & 1][1];
+  return (bi_rho(R, k) / rho_prev) * (st->alpha_prev / st->omega_prev);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kBlock)
+shard_bi_init(int64_t n, const T *__restrict__ b, T *__restrict__ x, T *__restrict__ r,
+              T *__restrict__ rhat, T *__restrict__ p, T *__restrict__ t, ShardState *st,
+              BiRed *R, double *partials) {
+  __shared__ double smem[2 * kWarps];
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T bi = b[i];
+    x[i] = T(0);
+    r[i] = bi;
+    rhat[i] = bi;
+    p[i] = T(0);
+    t[i] = T(0);
+    acc[0] += (double)bi * (double)bi;
+    acc[1] += (double)bi * (double)bi;
+  }
+  if (last_block_sum<2, kBlock>(acc, partials, &st->counter[0], smem) && threadIdx.x == 0) {
+    R->init[0] = acc[0];
+    R->init[1] = acc[1];
+    st->alpha_prev = 1.0;
+    st->omega_prev = 1.0;
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void shard_bi_pack1(const int32_t *__restrict__ idx, int64_t n, BiP<T, PREC> g0,
+                               T *__restrict__ out, ShardState *st, const BiRed *R, long long k,
+                               long long every, double atol, double rtol) {
+  if (*(volatile int *)&st->stopped) return;
+  if (bi_stop(R, k, every, bi_tol(R, atol, rtol))) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) { st->stopped = 1; st->iters = k; }
+    return;
+  }
+  BiP<T, PREC> g = g0;
+  g.beta = (T)bi_beta(R, st, k);
+  g.omega = (T)st->omega_prev;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) out[i] = g(idx[i]);
+}
+
+template <typename T, bool PREC, bool HALO>
+__global__ void __launch_bounds__(kBlock)
+shard_bi_k1(Sell<T> A, int32_t n_own, BiP<T, PREC> g0, const T *__restrict__ phalo,
+            const T *__restrict__ rhat, T *__restrict__ p_new, T *__restrict__ v, ShardState *st,
+            BiRed *R, double *partials, long long k) {
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  BiP<T, PREC> inner = g0;
+  inner.beta = (T)bi_beta(R, st, k);
+  inner.omega = (T)st->omega_prev;
+  HaloGather<T, BiP<T, PREC>> g{inner, phalo, n_own};
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[1] = {0.0};
+  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
+    T sum = HALO ? sell_row(A, s, lane, g) : sell_row(A, s, lane, inner);
+    int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      int32_t row = A.row_ids[slot];
+      p_new[row] = inner.pval(row);
+      v[row] = sum;
+      acc[0] += (double)rhat[row] * (double)sum;
+    }
+  }
+  if (last_block_sum<1, kBlock>(acc, partials, &st->counter[HALO ? 2 : 1], smem) &&
+      threadIdx.x == 0) {
+    if (!HALO) st->pap_int = acc[0];
+    else R->rv[0] = st->pap_int + acc[0];
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void shard_bi_pack2(const int32_t *__restrict__ idx, int64_t n, BiS<T, PREC> g0,
+                               T *__restrict__ out, ShardState *st, const BiRed *R, long long k) {
+  if (*(volatile int *)&st->stopped) return;
+  BiS<T, PREC> g = g0;
+  g.alpha = (T)(bi_rho(R, k) / R->rv[0]);
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) out[i] = g(idx[i]);
+}
+
+template <typename T, bool PREC, bool HALO>
+__global__ void __launch_bounds__(kBlock)
+shard_bi_k2(Sell<T> A, int32_t n_own, BiS<T, PREC> g0, const T *__restrict__ shalo,
+            T *__restrict__ t, ShardState *st, BiRed *R, double *partials, long long k) {
+  __shared__ double smem[3 * kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  BiS<T, PREC> inner = g0;
+  inner.alpha = (T)(bi_rho(R, k) / R->rv[0]);
+  HaloGather<T, BiS<T, PREC>> g{inner, shalo, n_own};
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[3] = {0.0, 0.0, 0.0};
+  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
+    T sum = HALO ? sell_row(A, s, lane, g) : sell_row(A, s, lane, inner);
+    int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      int32_t row = A.row_ids[slot];
+      T si = inner.sval(row);
+      t[row] = sum;
+      acc[0] += (double)si * (double)si;
+      acc[1] += (double)sum * (double)sum;
+      acc[2] += (double)sum * (double)si;
+    }
+  }
+  if (last_block_sum<3, kBlock>(acc, partials, &st->counter[HALO ? 4 : 3], smem) &&
+      threadIdx.x == 0) {
+    if (!HALO) {
+      st->part3[0] = acc[0]; st->part3[1] = acc[1]; st->part3[2] = acc[2];
+    } else {
+      R->stt[0] = st->part3[0] + acc[0];
+      R->stt[1] = st->part3[1] + acc[1];
+      R->stt[2] = st->part3[2] + acc[2];
+    }
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+shard_bi_k3(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ rhat,
+            const T *__restrict__ p, const T *__restrict__ v, const T *__restrict__ t,
+            const T *__restrict__ dinv, ShardState *st, BiRed *R, double *partials, long long k,
+            long long every, double atol, double rtol) {
+  __shared__ double smem[2 * kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  const double alpha_d = bi_rho(R, k) / R->rv[0];
+  const T alpha = (T)alpha_d;
+  const bool half = (k % every) == 0 && sqrt(R->stt[0]) < bi_tol(R, atol, rtol);
+  const double omega_d = R->stt[2] / R->stt[1];
+  const T omega = (T)omega_d;
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T ph = PREC ? mul_rn(dinv[i], p[i]) : p[i];
+    T xi = add_rn(x[i], mul_rn(alpha, ph));
+    if (!half) {
+      T si = sub_rn(r[i], mul_rn(alpha, v[i]));
+      T sh = PREC ? mul_rn(dinv[i], si) : si;
+      xi = add_rn(xi, mul_rn(omega, sh));
+      T ri = sub_rn(si, mul_rn(omega, t[i]));
+      r[i] = ri;
+      acc[0] += (double)ri * (double)ri;
+      acc[1] += (double)rhat[i] * (double)ri;
+    }
+    x[i] = xi;
+  }
+  if (last_block_sum<2, kBlock>(acc, partials, &st->counter[5], smem) && threadIdx.x == 0) {
+    if (half) {
+      st->stopped = 1;
+      st->iters = k + 1;
+    } else {
+      R->rr[k & 1][0] = acc[0];
+      R->rr[k & 1][1] = acc[1];
+      st->alpha_prev = alpha_d;
+      st->omega_prev = omega_d;
+    }
+  }
+}
+
+// ================================================================= drivers
+static size_t shard_ws_bytes(size_t elem, int64_t n_own, int64_t n_halo, int64_t n_snd) {
+  size_t G = (size_t)solver_grid();
+  return 6 * align_up(elem * (size_t)(n_own + 1)) + align_up(elem * (size_t)(n_snd + 1)) +
+         2 * align_up(elem * (size_t)(n_halo + 1)) + 6 * align_up(4 * G * sizeof(double)) +
+         align_up(sizeof(ShardState)) + align_up(sizeof(BiRed)) + align_up(sizeof(CgRed));
+}
+
+// Poll the sticky stop flag once per chunk, one chunk in flight; all ranks
+// see identical flags at identical points, so they stop enqueueing together.
+template <typename Body>
+static int shard_loop(Comm *c, int64_t maxiter, int64_t chunk, const int *d_stopped,
+                      cudaStream_t s, Body body) {
+  HostPoll &hp = host_poll();
+  SLA_TRY(hp.init());
+  int slot = 0;
+  bool pending[2] = {false, false};
+  for (int64_t k = 0; k < maxiter;) {
+    int64_t n = maxiter - k < chunk ? maxiter - k : chunk;
+    for (int64_t j = 0; j < n; ++j) SLA_TRY(body(k + j));
+    k += n;
+    SLA_CUDA_TRY(cudaMemcpyAsync(hp.flags + slot, d_stopped, sizeof(int), cudaMemcpyDeviceToHost, s));
+    SLA_CUDA_TRY(cudaEventRecord(hp.ev[slot], s));
+    pending[slot] = true;
+    int other = slot ^ 1;
+    if (pending[other]) {
+      SLA_TRY(wait_bounded(hp.ev[other], c));
+      pending[other] = false;
+      if (hp.flags[other] != 0) break;
+    }
+    slot = other;
+  }
+  return SLA_OK;
+}
+
+template <typename T, bool PREC>
+static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const sla_sell_t *Ai,
+                         const sla_sell_t *Ab, const T *dinv, const T *b, T *x, double atol,
+                         double rtol, int64_t maxiter, int64_t every, void *ws, size_t ws_bytes,
+                         sla_solve_info_t *info, cudaStream_t s) {
+  Sell<T> AI = make_sell<T>(Ai), AB = make_sell<T>(Ab);
+  const int64_t no = plan->n_owned, nh = plan->n_halo, ns = n_send(plan);
+  Carver c(ws, ws_bytes);
+  T *r = c.take<T>(no + 1), *pA = c.take<T>(no + 1), *pB = c.take<T>(no + 1);
+  T *Ap = c.take<T>(no + 1);
+  T *sendbuf = c.take<T>(ns + 1), *recvbuf = c.take<T>(nh + 1), *halo = c.take<T>(nh + 1);
+  const int G = solver_grid();
+  double *part[4];
+  for (int q = 0; q < 4; ++q) part[q] = c.take<double>(4 * (size_t)G);
+  ShardState *st = c.take<ShardState>(1);
+  CgRed *R = c.take<CgRed>(1);
+  if (!c.ok) return SLA_ERR_WORKSPACE;
+  ShardState init{};
+  SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(init), cudaMemcpyHostToDevice, s));
+  SLA_CUDA_TRY(cudaMemsetAsync(R, 0, sizeof(CgRed), s));
+  SLA_LAUNCH((shard_cg_init<T, PREC>), grid_for(no), kBlock, 0, s, no, b, x, dinv, r, pA, st, R,
+             part[0]);
+  SLA_NCCL_TRY(ncclAllReduce(R->init, R->init, 2, ncclFloat64, ncclSum, cr->nccl, s));
+  const T *hsrc = plan->halo_src ? halo : recvbuf;
+  SLA_TRY(shard_loop(cr, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
+    T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
+    if (ns > 0)
+      SLA_LAUNCH((shard_cg_pack<T, PREC>), grid_for(ns), kBlock, 0, s, plan->send_index, ns, r,
+                 dinv, p_old, sendbuf, st, R, (long long)k, (long long)every, atol, rtol);
+    else
+      SLA_LAUNCH((shard_cg_pack<T, PREC>), 1, 32, 0, s, plan->send_index, (int64_t)0, r, dinv,
+                 p_old, sendbuf, st, R, (long long)k, (long long)every, atol, rtol);
+    SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
+    cudaEvent_t ev;
+    profiler().begin(0, k, s, &ev);
+    SLA_LAUNCH((shard_cg_spmv<T, PREC, false>), G, kBlock, 0, s, AI, (int32_t)no, r, dinv, p_old,
+               hsrc, p_new, Ap, st, R, part[1], (long long)k);
+    profiler().end(0, s, ev);
+    SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
+    if (plan->halo_src && nh > 0)
+      SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
+                 halo, &st->stopped);
+    SLA_LAUNCH((shard_cg_spmv<T, PREC, true>), G, kBlock, 0, s, AB, (int32_t)no, r, dinv, p_old,
+               hsrc, p_new, Ap, st, R, part[2], (long long)k);
+    SLA_NCCL_TRY(ncclAllReduce(R->pap, R->pap, 1, ncclFloat64, ncclSum, cr->nccl, s));
+    profiler().begin(1, k, s, &ev);
+    SLA_LAUNCH((shard_cg_update<T, PREC>), G, kBlock, 0, s, no, x, r, p_new, Ap, dinv, st, R,
+               part[3], (long long)k);
+    profiler().end(1, s, ev);
+    SLA_NCCL_TRY(ncclAllReduce(R->loc[k & 1], R->loc[k & 1], 2, ncclFloat64, ncclSum, cr->nccl, s));
+    return SLA_OK;
+  }));
+  ShardState out;
+  CgRed red;
+  SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(out), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaMemcpyAsync(&red, R, sizeof(red), cudaMemcpyDeviceToHost, s));
+  cudaEvent_t done;
+  SLA_CUDA_TRY(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+  SLA_CUDA_TRY(cudaEventRecord(done, s));
+  int w = wait_bounded(done, cr);
+  cudaEventDestroy(done);
+  SLA_TRY(w);
+  profiler().resolve();
+  info->iterations = out.stopped ? out.iters : maxiter;
+  long long last = info->iterations - 1;
+  info->residual = last >= 0 ? sqrt(red.loc[last & 1][0]) : sqrt(red.init[0]);
+  info->status = out.stopped ? SLA_OK : SLA_NOT_CONVERGED;
+  info->reason = out.stopped;
+  return info->status;
+}
+
+template <typename T, bool PREC>
+static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const sla_sell_t *Ai,
+                         const sla_sell_t *Ab, const T *dinv, const T *b, T *x, double atol,
+                         double rtol, int64_t maxiter, int64_t every, void *ws, size_t ws_bytes,
+                         sla_solve_info_t *info, cudaStream_t s) {
+  Sell<T> AI = make_sell<T>(Ai), AB = make_sell<T>(Ab);
+  const int64_t no = plan->n_owned, nh = plan->n_halo, ns = n_send(plan);
+  Carver c(ws, ws_bytes);
+  T *r = c.take<T>(no + 1), *rhat = c.take<T>(no + 1), *pA = c.take<T>(no + 1);
+  T *pB = c.take<T>(no + 1), *v = c.take<T>(no + 1), *t = c.take<T>(no + 1);
+  T *sendbuf = c.take<T>(ns + 1), *recvbuf = c.take<T>(nh + 1), *halo = c.take<T>(nh + 1);
+  const int G = solver_grid();
+  double *part[6];
+  for (int q = 0; q < 6; ++q) part[q] = c.take<double>(4 * (size_t)G);
+  ShardState *st = c.take<ShardState>(1);
+  BiRed *R = c.take<BiRed>(1);
+  if (!c.ok) return SLA_ERR_WORKSPACE;
+  ShardState init{};
+  SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(init), cudaMemcpyHostToDevice, s));
+  SLA_CUDA_TRY(cudaMemsetAsync(R, 0, sizeof(BiRed), s));
+  SLA_LAUNCH(shard_bi_init<T>, grid_for(no), kBlock, 0, s, no, b, x, r, rhat, pA, t, st, R,
+             part[0]);
+  SLA_NCCL_TRY(ncclAllReduce(R->init, R->init, 2, ncclFloat64, ncclSum, cr->nccl, s));
+  const T *hsrc = plan->halo_src ? halo : recvbuf;
+  const unsigned pack_grid = ns > 0 ? (unsigned)grid_for(ns) : 1u;
+  SLA_TRY(shard_loop(cr, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
+    T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
+    BiP<T, PREC> gp{r, p_old, t, dinv, T(0), T(1)};
+    BiS<T, PREC> gs{r, v, dinv, T(0)};
+    // p_hat halo, then v = A p_hat
+    SLA_LAUNCH((shard_bi_pack1<T, PREC>), pack_grid, kBlock, 0, s, plan->send_index, ns, gp,
+               sendbuf, st, R, (long long)k, (long long)every, atol, rtol);
+    SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
+    cudaEvent_t ev;
+    profiler().begin(0, k, s, &ev);
+    SLA_LAUNCH((shard_bi_k1<T, PREC, false>), G, kBlock, 0, s, AI, (int32_t)no, gp, hsrc, rhat,
+               p_new, v, st, R, part[1], (long long)k);
+    profiler().end(0, s, ev);
+    SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
+    if (plan->halo_src && nh > 0)
+      SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
+                 halo, &st->stopped);
+    SLA_LAUNCH((shard_bi_k1<T, PREC, true>), G, kBlock, 0, s, AB, (int32_t)no, gp, hsrc, rhat,
+               p_new, v, st, R, part[2], (long long)k);
+    SLA_NCCL_TRY(ncclAllReduce(R->rv, R->rv, 1, ncclFloat64, ncclSum, cr->nccl, s));
+    // s_hat halo, then t = A s_hat
+    SLA_LAUNCH((shard_bi_pack2<T, PREC>), pack_grid, kBlock, 0, s, plan->send_index, ns, gs,
+               sendbuf, st, R, (long long)k);
+    SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
+    SLA_LAUNCH((shard_bi_k2<T, PREC, false>), G, kBlock, 0, s, AI, (int32_t)no, gs, hsrc, t, st, R,
+               part[3], (long long)k);
+    SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
+    if (plan->halo_src && nh > 0)
+      SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
+                 halo, &st->stopped);
+    SLA_LAUNCH((shard_bi_k2<T, PREC, true>), G, kBlock, 0, s, AB, (int32_t)no, gs, hsrc, t, st, R,
+               part[4], (long long)k);
+    SLA_NCCL_TRY(ncclAllReduce(R->stt, R->stt, 3, ncclFloat64, ncclSum, cr->nccl, s));
+    SLA_LAUNCH((shard_bi_k3<T, PREC>), G, kBlock, 0, s, no, x, r, rhat, p_new, v, t, dinv, st, R,
+               part[5], (long long)k, (long long)every, atol, rtol);
+    SLA_NCCL_TRY(ncclAllReduce(R->rr[k & 1], R->rr[k & 1], 2, ncclFloat64, ncclSum, cr->nccl, s));
+    return SLA_OK;
+  }));
+  ShardState out;
+  BiRed red;
+  SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(out), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaMemcpyAsync(&red, R, sizeof(red), cudaMemcpyDeviceToHost, s));
+  cudaEvent_t done;
+  SLA_CUDA_TRY(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+  SLA_CUDA_TRY(cudaEventRecord(done, s));
+  int w = wait_bounded(done, cr);
+  cudaEventDestroy(done);
+  SLA_TRY(w);
+  profiler().resolve();
+  info->iterations = out.stopped ? out.iters : maxiter;
+  long long last = info->iterations - 1;
+  info->residual = last >= 0 ? sqrt(red.rr[last & 1][0]) : sqrt(red.init[0]);
+  info->status = out.stopped ? SLA_OK : SLA_NOT_CONVERGED;
+  info->reason = out.stopped;
+  return info->status;
+}
+
+}  // namespace sla
+
+using namespace sla;
+
+extern "C" {
+
+int sla_comm_unique_id(unsigned char id[128]) {
+  if (!id) return SLA_ERR_INVALID;
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+  ncclUniqueId uid;
+  SLA_NCCL_TRY(ncclGetUniqueId(&uid));
+  memcpy(id, &uid, sizeof(uid));
+  return SLA_OK;
+}
+
+int sla_comm_init(void **comm, int nranks, const unsigned char id[128], int rank) {
+  if (!comm || !id || nranks < 1 || rank < 0 || rank >= nranks) return SLA_ERR_INVALID;
+  Comm *c = new Comm();
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclResult_t r = ncclCommInitRank(&c->nccl, nranks, uid, rank);
+  if (r != ncclSuccess) {
+    fprintf(stderr, "[sla_b200] ncclCommInitRank failed: %s\n", ncclGetErrorString(r));
+    delete c;
+    return SLA_ERR_NCCL;
+  }
+  c->rank = rank;
+  c->nranks = nranks;
+  if (cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->ev_ready, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&c->ev_halo, cudaEventDisableTiming) != cudaSuccess) {
+    ncclCommDestroy(c->nccl);
+    delete c;
+    return SLA_ERR_CUDA;
+  }
+  *comm = c;
+  return SLA_OK;
+}
+
+int sla_comm_destroy(void *comm) {
+  Comm *c = (Comm *)comm;
+  if (!c) return SLA_OK;
+  if (c->side) cudaStreamSynchronize(c->side);
+  if (c->nccl) ncclCommDestroy(c->nccl);
+  if (c->ev_ready) cudaEventDestroy(c->ev_ready);
+  if (c->ev_halo) cudaEventDestroy(c->ev_halo);
+  if (c->side) cudaStreamDestroy(c->side);
+  delete c;
+  return SLA_OK;
+}
+
+int sla_halo_exchange(void *comm, const sla_halo_plan_t *plan, int dtype, void *x_local,
+                      void *sendbuf, void *recvbuf, sla_stream_t stream) {
+  Comm *c = (Comm *)comm;
+  if (!c || !c->nccl || !plan_ok(plan) || !x_local) return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t ns = n_send(plan), nh = plan->n_halo, no = plan->n_owned;
+  if ((ns > 0 && !sendbuf) || (nh > 0 && !recvbuf)) return SLA_ERR_INVALID;
+  auto run = [&](auto tag) -> int {
+    using T = decltype(tag);
+    T *x = (T *)x_local;
+    if (ns > 0)
+      SLA_LAUNCH((halo_pack_kernel<T, LoadVal<T>>), grid_for(ns), kBlock, 0, s, plan->send_index,
+                 ns, LoadVal<T>{x}, (T *)sendbuf, (const int *)nullptr);
+    SLA_TRY(halo_enqueue<T>(c, plan, (const T *)sendbuf, (T *)recvbuf, s));
+    SLA_CUDA_TRY(cudaStreamWaitEvent(s, c->ev_halo, 0));
+    if (nh > 0)
+      SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, (const T *)recvbuf,
+                 plan->halo_src, nh, x + no, (const int *)nullptr);
+    return SLA_OK;
+  };
+  if (dtype == SLA_F64) return run(double(0));
+  if (dtype == SLA_F32) return run(float(0));
+  return SLA_ERR_INVALID;
+}
+
+int sla_shard_spmv(void *comm, const sla_halo_plan_t *plan, int dtype, const sla_sell_t *A_interior,
+                   const sla_sell_t *A_boundary, void *x_local, void *y_owned, void *sendbuf,
+                   void *recvbuf, sla_stream_t stream) {
+  Comm *c = (Comm *)comm;
+  if (!c || !c->nccl || !plan_ok(plan) || !x_local || !y_owned) return SLA_ERR_INVALID;
+  if (!sell_ok(A_interior) || !sell_ok(A_boundary)) return SLA_ERR_INVALID;
+  if ((A_interior->n_slots > 0 && !A_interior->row_ids) ||
+      (A_boundary->n_slots > 0 && !A_boundary->row_ids))
+    return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t ns = n_send(plan), nh = plan->n_halo, no = plan->n_owned;
+  if ((ns > 0 && !sendbuf) || (nh > 0 && !recvbuf)) return SLA_ERR_INVALID;
+  auto run = [&](auto tag) -> int {
+    using T = decltype(tag);
+    T *x = (T *)x_local;
+    Sell<T> AI = make_sell<T>(A_interior), AB = make_sell<T>(A_boundary);
+    if (ns > 0)
+      SLA_LAUNCH((halo_pack_kernel<T, LoadVal<T>>), grid_for(ns), kBlock, 0, s, plan->send_index,
+                 ns, LoadVal<T>{x}, (T *)sendbuf, (const int *)nullptr);
+    SLA_TRY(halo_enqueue<T>(c, plan, (const T *)sendbuf, (T *)recvbuf, s));
+    if (AI.n_slices > 0)
+      SLA_LAUNCH((shard_spmv_rows_kernel<T, PlainGather<T>>), grid_for(AI.n_slices * 32), kBlock,
+                 0, s, AI, PlainGather<T>{x}, (T *)y_owned);
+    SLA_CUDA_TRY(cudaStreamWaitEvent(s, c->ev_halo, 0));
+    if (nh > 0)
+      SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, (const T *)recvbuf,
+                 plan->halo_src, nh, x + no, (const int *)nullptr);
+    if (AB.n_slices > 0)
+      SLA_LAUNCH((shard_spmv_rows_kernel<T, PlainGather<T>>), grid_for(AB.n_slices * 32), kBlock,
+                 0, s, AB, PlainGather<T>{x}, (T *)y_owned);
+    return SLA_OK;
+  };
+  if (dtype == SLA_F64) return run(double(0));
+  if (dtype == SLA_F32) return run(float(0));
+  return SLA_ERR_INVALID;
+}
+
+int sla_shard_krylov_workspace(int dtype, int64_t n_owned, int64_t n_halo, int64_t n_send_,
+                               size_t *bytes) {
+  if (!bytes || n_owned < 0 || n_halo < 0 || n_send_ < 0) return SLA_ERR_INVALID;
+  if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
+  *bytes = shard_ws_bytes(dtype == SLA_F64 ? 8 : 4, n_owned, n_halo, n_send_);
+  return SLA_OK;
+}
+
+static int shard_args_ok(void *ch, void *cr, const sla_halo_plan_t *plan, const sla_sell_t *Ai,
+                         const sla_sell_t *Ab, const void *b, void *x, sla_solve_info_t *info,
+                         int64_t every) {
+  if (!ch || !cr || !((Comm *)ch)->nccl || !((Comm *)cr)->nccl) return SLA_ERR_INVALID;
+  if (!plan_ok(plan) || !sell_ok(Ai) || !sell_ok(Ab) || !info || every < 1) return SLA_ERR_INVALID;
+  if (plan->n_owned > 0 && (!b || !x)) return SLA_ERR_INVALID;
+  if ((Ai->n_slots > 0 && !Ai->row_ids) || (Ab->n_slots > 0 && !Ab->row_ids)) return SLA_ERR_INVALID;
+  if (Ai->n_slots + Ab->n_slots != plan->n_owned) return SLA_ERR_INVALID;
+  if (plan->n_owned + plan->n_halo >= INT32_MAX) return SLA_ERR_UNSUPPORTED;
+  return SLA_OK;
+}
+
+int sla_shard_cg(void *comm_halo, void *comm_reduce, const sla_halo_plan_t *plan, int dtype,
+                 const sla_sell_t *A_interior, const sla_sell_t *A_boundary, const void *dinv,
+                 const void *b, void *x, double atol, double rtol, int64_t maxiter,
+                 int64_t check_every, void *workspace, size_t workspace_bytes,
+                 sla_solve_info_t *info, sla_stream_t stream) {
+  SLA_TRY(shard_args_ok(comm_halo, comm_reduce, plan, A_interior, A_boundary, b, x, info,
+                        check_every));
+  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
+  size_t need = 0;
+  SLA_TRY(sla_shard_krylov_workspace(dtype, plan->n_owned, plan->n_halo, n_send(plan), &need));
+  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  Comm *ch = (Comm *)comm_halo, *cr = (Comm *)comm_reduce;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SLA_F64) {
+    if (dinv)
+      return shard_cg_impl<double, true>(ch, cr, plan, A_interior, A_boundary, (const double *)dinv,
+                                         (const double *)b, (double *)x, atol, rtol, maxiter,
+                                         check_every, workspace, workspace_bytes, info, s);
+    return shard_cg_impl<double, false>(ch, cr, plan, A_interior, A_boundary, nullptr,
+                                        (const double *)b, (double *)x, atol, rtol, maxiter,
+                                        check_every, workspace, workspace_bytes, info, s);
+  }
+  if (dtype == SLA_F32) {
+    if (dinv)
+      return shard_cg_impl<float, true>(ch, cr, plan, A_interior, A_boundary, (const float *)dinv,
+                                        (const float *)b, (float *)x, atol, rtol, maxiter,
+                                        check_every, workspace, workspace_bytes, info, s);
+    return shard_cg_impl<float, false>(ch, cr, plan, A_interior, A_boundary, nullptr,
+                                       (const float *)b, (float *)x, atol, rtol, maxiter,
+                                       check_every, workspace, workspace_bytes, info, s);
+  }
+  return SLA_ERR_INVALID;
+}
+
+int sla_shard_bicgstab(void *comm_halo, void *comm_reduce, const sla_halo_plan_t *plan, int dtype,
+                       const sla_sell_t *A_interior, const sla_sell_t *A_boundary,
+                       const void *dinv, const void *b, void *x, double atol, double rtol,
+                       int64_t maxiter, int64_t check_every, void *workspace,
+                       size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
+  SLA_TRY(shard_args_ok(comm_halo, comm_reduce, plan, A_interior, A_boundary, b, x, info,
+                        check_every));
+  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
+  size_t need = 0;
+  SLA_TRY(sla_shard_krylov_workspace(dtype, plan->n_owned, plan->n_halo, n_send(plan), &need));
+  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  Comm *ch = (Comm *)comm_halo, *cr = (Comm *)comm_reduce;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SLA_F64) {
+    if (dinv)
+      return shard_bi_impl<double, true>(ch, cr, plan, A_interior, A_boundary, (const double *)dinv,
+                                         (const double *)b, (double *)x, atol, rtol, maxiter,
+                                         check_every, workspace, workspace_bytes, info, s);
+    return shard_bi_impl<double, false>(ch, cr, plan, A_interior, A_boundary, nullptr,
+                                        (const double *)b, (double *)x, atol, rtol, maxiter,
+                                        check_every, workspace, workspace_bytes, info, s);
+  }
+  if (dtype == SLA_F32) {
+    if (dinv)
+      return shard_bi_impl<float, true>(ch, cr, plan, A_interior, A_boundary, (const float *)dinv,
+                                        (const float *)b, (float *)x, atol, rtol, maxiter,
+                                        check_every, workspace, workspace_bytes, info, s);
+    return shard_bi_impl<float, false>(ch, cr, plan, A_interior, A_boundary, nullptr,
+                                       (const float *)b, (float *)x, atol, rtol, maxiter,
+                                       check_every, workspace, workspace_bytes, info, s);
+  }
+  return SLA_ERR_INVALID;
+}
+
+}  // extern "C"
