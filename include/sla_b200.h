@@ -153,6 +153,27 @@ int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b,
             size_t workspace_bytes, sla_solve_info_t *info,
             sla_stream_t stream);
 
+/* Allocation-free variant of sla_pcg. It has no counterpart in torch-sla: it
+ * exists for callers that cannot allocate device memory at solve time -- a
+ * host application whose device memory is owned by another framework's pool,
+ * a plugin that must not call cudaMalloc (which can synchronise the device
+ * and fail under memory pressure), or a C/Fortran code with no allocator of
+ * its own. Its scratch vectors live in one file-scope device array of
+ * SLA_PCG_NOALLOC_SCRATCH_BYTES (16 MiB), held on every GPU that loads the
+ * library until the process exits; that fits n <= 500,000 rows in float64
+ * (1,000,000 in float32) on a 148-SM B200. Larger n returns
+ * SLA_ERR_UNSUPPORTED. The caller still provides A, dinv, b and x. The first
+ * call on a device resolves the array's device address on that device, so
+ * make that first call before any stream capture. All calls share the one
+ * array: calls that overlap on the GPU (other streams, other host threads)
+ * race and must be serialised by the caller. No cudaMalloc/cudaFree or other
+ * allocating routine is called. */
+#define SLA_PCG_NOALLOC_SCRATCH_BYTES (16u << 20)
+int sla_pcg_noalloc(int dtype, const sla_sell_t *A, const void *dinv,
+                    const void *b, void *x, int x_is_guess, double atol,
+                    double rtol, int64_t maxiter, int flags,
+                    sla_solve_info_t *info, sla_stream_t stream);
+
 /* Jacobi-PBiCGStab with torch-sla's half-step / full-step stopping tests and
  * 1e-30 breakdown guards (pbicgstab_solve, pytorch_backend.py:1508-1596). */
 int sla_bicgstab_workspace(int dtype, int64_t n, size_t *bytes);

@@ -68,6 +68,9 @@ _SIGNATURES = {
     "sla_pcg": (ctypes.c_int, [ctypes.c_int, _P(SellView), c_ptr, c_ptr, c_ptr, ctypes.c_int,
                                c_dbl, c_dbl, c_i64, ctypes.c_int, c_ptr, c_sz, _P(SolveInfo),
                                c_ptr]),
+    "sla_pcg_noalloc": (ctypes.c_int, [ctypes.c_int, _P(SellView), c_ptr, c_ptr, c_ptr,
+                                       ctypes.c_int, c_dbl, c_dbl, c_i64, ctypes.c_int,
+                                       _P(SolveInfo), c_ptr]),
     "sla_bicgstab_workspace": (ctypes.c_int, [ctypes.c_int, c_i64, _P(c_sz)]),
     "sla_bicgstab": (ctypes.c_int, [ctypes.c_int, _P(SellView), c_ptr, c_ptr, c_ptr,
                                     ctypes.c_int, c_dbl, c_dbl, c_i64, c_ptr, c_sz,

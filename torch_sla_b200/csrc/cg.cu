@@ -16,6 +16,8 @@
 //
 // Persistent path (small systems, vectors L2-resident): the same two phases
 // in one cooperative launch separated by a bounded grid barrier.
+#include <mutex>
+
 #include "solver.cuh"
 
 namespace sla {
@@ -297,6 +299,105 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
   return info->status;
 }
 
+// ------------------------------------------------- allocation-free variant
+// Scratch of sla_pcg_noalloc: one file-scope device array, present on every
+// GPU that loads the library. In host code the symbol is only a handle, never
+// a device address; the address is resolved per device with
+// cudaGetSymbolAddress and passed to the kernels.
+static __device__ __align__(256) unsigned char g_pcg_noalloc_scratch[SLA_PCG_NOALLOC_SCRATCH_BYTES];
+constexpr int kMaxDevices = 64;
+
+// Device address of the scratch array on the current device, resolved once
+// per device (the first call on a device does this set-up).
+static int noalloc_scratch(void **out) {
+  static std::mutex mu;
+  static void *addr[kMaxDevices] = {};
+  int dev = 0;
+  SLA_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return SLA_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_pcg_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      fprintf(stderr, "[sla_b200] cudaGetSymbolAddress(pcg scratch) failed: %s\n",
+              cudaGetErrorString(e));
+      return SLA_ERR_CUDA;
+    }
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return SLA_OK;
+}
+
+// Same kernels and launch shapes as pcg_impl; the convergence flag is polled
+// with a plain stream-ordered copy (no pinned buffer, no events).
+template <typename T, bool PREC>
+static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool guess,
+                            double atol, double rtol, int64_t maxiter, int flags, void *ws,
+                            size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
+  Sell<T> A = make_sell<T>(Ad);
+  const int64_t n = A.n_slots;
+  Carver c(ws, ws_bytes);
+  T *r = c.take<T>(n), *pA = c.take<T>(n), *pB = c.take<T>(n), *Ap = c.take<T>(n);
+  const int G = solver_grid();
+  double *part0 = c.take<double>(4 * (size_t)G), *part1 = c.take<double>(4 * (size_t)G);
+  CgState *st = c.take<CgState>(1);
+  if (!c.ok) return SLA_ERR_UNSUPPORTED;
+  CgState init{};
+  init.maxiter = maxiter;
+  SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
+  if (guess) SLA_TRY(spmv_launch<T>(Ad, x, Ap, s));
+  SLA_LAUNCH((cg_init_kernel<T, PREC>), grid_for(n), kBlock, 0, s, n, b, x, guess ? Ap : nullptr,
+             dinv, r, pA, st, part0, atol, rtol);
+  const DeviceInfo &dev = device_info();
+  bool persistent = false;
+  int coop_grid = 0;
+  if (flags != SLA_PCG_STREAMED && dev.coop) {
+    int per_sm = 0;
+    SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, cg_persistent_kernel<T, PREC>, kBlock, 0));
+    int want = (int)((n + kBlock - 1) / kBlock);
+    int cap = per_sm * dev.sm_count;
+    coop_grid = want < cap ? want : cap;
+    if (coop_grid < 1) coop_grid = 1;
+    persistent = per_sm > 0;
+  }
+  if (flags == SLA_PCG_PERSISTENT && !persistent) return SLA_ERR_UNSUPPORTED;
+  if (persistent) {
+    int64_t nn = n;
+    void *args[] = {&A, &nn, &x, &r, (void *)&dinv, &pA, &pB, &Ap, &st, &part0, &part1};
+    SLA_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)cg_persistent_kernel<T, PREC>,
+                                             dim3(coop_grid), dim3(kBlock), args, 0, s));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+  } else {
+    for (int64_t it = 0; it < maxiter;) {
+      int64_t chunk = maxiter - it < 8 ? maxiter - it : 8;
+      for (int64_t j = 0; j < chunk; ++j, ++it) {
+        T *p_old = (it & 1) ? pB : pA;
+        T *p_new = (it & 1) ? pA : pB;
+        SLA_LAUNCH((cg_spmv_kernel<T, PREC>), G, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap, st,
+                   part0);
+        SLA_LAUNCH((cg_update_kernel<T, PREC>), G, kBlock, 0, s, n, x, r, p_new, Ap, dinv, st,
+                   part1);
+      }
+      int done = 0;
+      SLA_CUDA_TRY(cudaMemcpyAsync(&done, &st->done, sizeof(int), cudaMemcpyDeviceToHost, s));
+      SLA_CUDA_TRY(cudaStreamSynchronize(s));
+      if (done) break;
+    }
+  }
+  CgState out;
+  SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaStreamSynchronize(s));
+  info->residual = sqrt(out.rr);
+  info->reason = out.done;
+  if (out.done == kTimeout) return SLA_ERR_TIMEOUT;
+  info->iterations = out.iters_out;
+  info->status = out.done == kConverged ? SLA_OK : SLA_NOT_CONVERGED;
+  return info->status;
+}
+
 }  // namespace sla
 
 using namespace sla;
@@ -336,6 +437,42 @@ int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b, voi
                                   flags, workspace, workspace_bytes, info, s);
   }
   return SLA_ERR_INVALID;
+}
+
+int sla_pcg_noalloc(int dtype, const sla_sell_t *A, const void *dinv, const void *b, void *x,
+                    int x_is_guess, double atol, double rtol, int64_t maxiter, int flags,
+                    sla_solve_info_t *info, sla_stream_t stream) {
+  if (!sell_ok(A) || !b || !x || !info || A->row_ids) return SLA_ERR_INVALID;
+  if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
+  if (flags < 0 || flags > 2) return SLA_ERR_INVALID;
+  if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
+  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
+  size_t need = cg_ws_bytes(dtype == SLA_F64 ? 8 : 4, A->n_slots);
+  if (need > (size_t)SLA_PCG_NOALLOC_SCRATCH_BYTES) {
+    fprintf(stderr,
+            "[sla_b200] sla_pcg_noalloc: n=%lld needs %zu scratch bytes, above the fixed "
+            "%u-byte device array; use sla_pcg with a caller workspace\n",
+            (long long)A->n_slots, need, (unsigned)SLA_PCG_NOALLOC_SCRATCH_BYTES);
+    return SLA_ERR_UNSUPPORTED;
+  }
+  void *ws = nullptr;
+  SLA_TRY(noalloc_scratch(&ws));
+  const size_t cap = SLA_PCG_NOALLOC_SCRATCH_BYTES;
+  cudaStream_t s = (cudaStream_t)stream;
+  bool g = x_is_guess != 0;
+  if (dtype == SLA_F64) {
+    if (dinv)
+      return pcg_noalloc_impl<double, true>(A, (const double *)dinv, (const double *)b,
+                                            (double *)x, g, atol, rtol, maxiter, flags, ws, cap,
+                                            info, s);
+    return pcg_noalloc_impl<double, false>(A, nullptr, (const double *)b, (double *)x, g, atol,
+                                           rtol, maxiter, flags, ws, cap, info, s);
+  }
+  if (dinv)
+    return pcg_noalloc_impl<float, true>(A, (const float *)dinv, (const float *)b, (float *)x, g,
+                                         atol, rtol, maxiter, flags, ws, cap, info, s);
+  return pcg_noalloc_impl<float, false>(A, nullptr, (const float *)b, (float *)x, g, atol, rtol,
+                                        maxiter, flags, ws, cap, info, s);
 }
 
 }  // extern "C"
