@@ -1,0 +1,61 @@
+"""The C-ABI library loads without a GPU and exports every entry point that
+include/sla_b200.h declares (no compute calls here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from torch_sla_b200 import _lib as L
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "sla_b200.h")
+
+
+def header_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^[a-z][\w\s\*]*?\b(sla_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_entry_points():
+    syms = header_symbols()
+    assert "sla_pcg" in syms and "sla_shard_cg" in syms and "sla_csr_build" in syms
+    assert len(syms) >= 28
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(L.LIB_PATH)
+    missing = [s for s in header_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_binding_table_matches_header():
+    assert set(L.declared_symbols()) == set(header_symbols())
+
+
+def test_status_strings_and_version():
+    lib = L.lib()
+    assert lib.sla_abi_version() == 1
+    assert lib.sla_status_string(L.SLA_ERR_UNSUPPORTED) == b"unsupported problem shape"
+    assert lib.sla_status_string(L.SLA_NOT_CONVERGED).startswith(b"did not converge")
+
+
+def test_invalid_arguments_are_rejected_before_any_device_work():
+    lib = L.lib()
+    info = L.SolveInfo()
+    assert lib.sla_pcg(1, None, None, None, None, 0, 0.0, 1e-8, 10, 0, None, 0,
+                       ctypes.byref(info), None) == L.SLA_ERR_INVALID
+    assert lib.sla_spmv(7, None, None, None, None) == L.SLA_ERR_INVALID
+    assert lib.sla_csr_build(1, None, None, None, 10, 0, 5, None, None, None, None, None,
+                             None, None, 0, None) == L.SLA_ERR_INVALID
+    assert lib.sla_shard_cg(None, None, None, 1, None, None, None, None, None, 0.0, 0.0, 1, 10,
+                            None, 0, ctypes.byref(info), None) == L.SLA_ERR_INVALID
+
+
+@pytest.mark.parametrize("n,nnz", [(10, 30), (1000, 7000)])
+def test_workspace_queries(n, nnz):
+    lib = L.lib()
+    need = ctypes.c_size_t(0)
+    assert lib.sla_csr_build_workspace(n, nnz, ctypes.byref(need)) == 0 and need.value > 0
+    assert lib.sla_sell_layout_workspace(n, ctypes.byref(need)) == 0 and need.value > 0
+    assert lib.sla_bicgstab_workspace(2, n, ctypes.byref(need)) == L.SLA_ERR_INVALID

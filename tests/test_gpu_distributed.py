@@ -1,0 +1,125 @@
+"""Row-sharded path on GPUs: one NCCL process per GPU. Checks the shard
+CG/BiCGStab against the reference's own DSparseTensor runs (golden_shard.pt:
+iterations and solutions), D @ x against the oracle SpMV, the halo exchange,
+and DSparseTensor.from_owned_rows against the oracle's global CG."""
+import datetime
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rel(a, b):
+    return float((a.double() - b.double()).abs().max() / b.double().abs().max().clamp_min(1e-300))
+
+
+def _worker(rank, world, port, out_dir):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    sys.path.insert(0, os.path.dirname(here))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    res = {}
+    try:
+        from conftest import case_inputs, load_golden
+        from oracle import krylov as K
+        import torch_sla_b200 as T
+        from torch_sla_b200 import problems as P
+        from torch_sla_b200.distributed import DSparseTensor, destroy_all, halo_exchange
+        from torch.distributed.device_mesh import init_device_mesh
+        mesh = init_device_mesh("cuda", (world,))
+        for name, case in load_golden("golden_shard.pt").items():
+            v, r, c, sh = case_inputs(case)
+            A = T.SparseTensor(v.to(dev), r.to(dev), c.to(dev), sh)
+            D = DSparseTensor.partition(A, mesh, partition_method="simple")
+            b_dt = D.scatter(case["b"].to(dev))
+            with T.SolverConfig(method=case["method"], atol=case["atol"], rtol=case["rtol"],
+                                maxiter=2000, preconditioner=case["precond"]):
+                x_dt = T.solve(D, b_dt)
+            x = x_dt.full_tensor().cpu()
+            y = (D @ b_dt).full_tensor().cpu()
+            y_ref = K.spmv(v, r, c, sh, case["b"])
+            plan = D._shard_plan()
+            part = D.partition_info
+            xl = torch.zeros(plan.n_owned + plan.n_halo, dtype=torch.float64, device=dev)
+            xl[: plan.n_owned] = case["b"].to(dev)[part.owned_nodes.to(dev)]
+            halo_exchange(D, xl)
+            halo_ok = torch.equal(xl[plan.n_owned:].cpu(), case["b"][part.halo_nodes])
+            res[name] = {"x": x, "iters": D._last_info["iterations"], "spmv_rel": _rel(y, y_ref),
+                         "halo_ok": halo_ok}
+        # owned-rows construction on a slab-partitioned 7-point grid
+        m = 12
+        dims = (m * world, m, m)
+        n = dims[0] * m * m
+        vr, rr_, cr = P.poisson_3d_7pt_rows(dims, rank * m, m, device=dev)
+        D2 = DSparseTensor.from_owned_rows(vr, rr_, cr, (n, n), mesh=mesh)
+        b = P.rhs_normal(n, 1)
+        x2 = D2.solve(D2.scatter(b.to(dev)), method="cg", preconditioner="jacobi", atol=0.0,
+                      rtol=1e-8, maxiter=5000)
+        vg, rg, cg_, sh = P.poisson_3d_7pt(dims)
+        xo, ito = K.cg_shard(vg, rg, cg_, sh, b, atol=0.0, rtol=1e-8, maxiter=5000,
+                             precond="jacobi")
+        res["owned_rows"] = {"rel": _rel(x2.full_tensor().cpu(), xo),
+                             "iters": D2._last_info["iterations"], "oracle_iters": ito}
+        destroy_all()
+    finally:
+        torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
+        dist.destroy_process_group()
+
+
+def _run(world, tmp_path):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(rk, world, port, str(tmp_path)))
+             for rk in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=600)
+    for p in procs:
+        if p.is_alive():
+            p.terminate()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return [torch.load(tmp_path / f"r{rk}.pt") for rk in range(world)]
+
+
+def _check(results, golden_shard):
+    for res in results:
+        for name, case in golden_shard.items():
+            got = res[name]
+            assert got["spmv_rel"] < 1e-13, (name, got["spmv_rel"])
+            assert got["halo_ok"], name
+            # stop tests run every 10 iterations: counts agree to that stride
+            slack = 10 if case["method"] == "bicgstab" else max(1, math.ceil(0.03 * case["iters"]))
+            assert abs(got["iters"] - case["iters"]) <= slack, (name, got["iters"], case["iters"])
+            assert _rel(got["x"], case["x"]) < 1e-6, name
+        o = res["owned_rows"]
+        assert o["iters"] == o["oracle_iters"] and o["rel"] < 1e-8, o
+
+
+def test_shard_solvers_one_gpu(tmp_path, golden_shard):
+    _check(_run(1, tmp_path), golden_shard)
+
+
+def test_shard_solvers_two_gpus(tmp_path, golden_shard):
+    _check(_run(2, tmp_path), golden_shard)

@@ -92,7 +92,7 @@ bicg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T 
 }
 
 template <typename T, bool PREC>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T *__restrict__ p_old,
         const T *__restrict__ v_old, const T *__restrict__ dinv, T *__restrict__ p_new,
         T *__restrict__ v_new, BicgState *st, double *partials) {
@@ -118,7 +118,7 @@ bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T 
 }
 
 template <typename T, bool PREC>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 bicg_k2(Sell<T> A, const T *__restrict__ r, const T *__restrict__ v, const T *__restrict__ dinv,
         T *__restrict__ t, BicgState *st, double *partials) {
   __shared__ double smem[3 * kWarps];
@@ -223,19 +223,22 @@ static int bicg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool
   if (guess) SLA_TRY(spmv_launch<T>(Ad, x, t, s));
   SLA_LAUNCH(bicg_init_kernel<T>, grid_for(n), kBlock, 0, s, n, b, x, guess ? t : nullptr, r, rhat,
              pA, vA, st, part[0], atol, rtol);
+  const int g1 = occupancy_grid((const void *)bicg_k1<T, PREC>);
+  const int g2 = occupancy_grid((const void *)bicg_k2<T, PREC>);
+  const int g3 = occupancy_grid((const void *)bicg_k3<T, PREC>);
   SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
     T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
     T *v_old = (it & 1) ? vB : vA, *v_new = (it & 1) ? vA : vB;
     cudaEvent_t ev;
     profiler().begin(0, it, s, &ev);
-    SLA_LAUNCH((bicg_k1<T, PREC>), G, kBlock, 0, s, A, r, rhat, p_old, v_old, dinv, p_new, v_new,
+    SLA_LAUNCH((bicg_k1<T, PREC>), g1, kBlock, 0, s, A, r, rhat, p_old, v_old, dinv, p_new, v_new,
                st, part[1]);
     profiler().end(0, s, ev);
     profiler().begin(1, it, s, &ev);
-    SLA_LAUNCH((bicg_k2<T, PREC>), G, kBlock, 0, s, A, r, v_new, dinv, t, st, part[2]);
+    SLA_LAUNCH((bicg_k2<T, PREC>), g2, kBlock, 0, s, A, r, v_new, dinv, t, st, part[2]);
     profiler().end(1, s, ev);
     profiler().begin(2, it, s, &ev);
-    SLA_LAUNCH((bicg_k3<T, PREC>), G, kBlock, 0, s, n, x, r, rhat, p_new, v_new, t, dinv, st,
+    SLA_LAUNCH((bicg_k3<T, PREC>), g3, kBlock, 0, s, n, x, r, rhat, p_new, v_new, t, dinv, st,
                part[3]);
     profiler().end(2, s, ev);
     return SLA_OK;

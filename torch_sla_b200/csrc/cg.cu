@@ -89,7 +89,7 @@ cg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *_
 }
 
 template <typename T, bool PREC>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
                const T *__restrict__ p_old, T *__restrict__ p_new, T *__restrict__ Ap, CgState *st,
                double *partials) {
@@ -116,7 +116,23 @@ cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
   }
 }
 
+template <typename T> struct Pair;
+template <> struct Pair<double> { using type = double2; };
+template <> struct Pair<float> { using type = float2; };
+
+// x += alpha p ; r -= alpha Ap (torch addcmul_ rounding) and the two dots.
 template <typename T, bool PREC>
+__device__ __forceinline__ void cg_axpy(T &xi, T &ri, T pi, T api, T di, T alpha, double (&acc)[2]) {
+  xi = add_rn(xi, mul_rn(alpha, pi));
+  ri = sub_rn(ri, mul_rn(alpha, api));
+  T zi = PREC ? mul_rn(di, ri) : ri;
+  acc[0] += (double)ri * (double)ri;
+  acc[1] += (double)ri * (double)zi;
+}
+
+// VEC: 2 elements per 16-byte (fp64) / 8-byte (fp32) access; only launched
+// when every vector is 16-byte aligned.
+template <typename T, bool PREC, bool VEC>
 __global__ void __launch_bounds__(kBlock)
 cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
                  const T *__restrict__ Ap, const T *__restrict__ dinv, CgState *st,
@@ -125,16 +141,35 @@ cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__res
   if (*(volatile int *)&st->done) return;
   const T alpha = (T)st->alpha;
   double acc[2] = {0.0, 0.0};
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (; i < n; i += stride) {
-    T xi = add_rn(x[i], mul_rn(alpha, p[i]));
-    T ri = sub_rn(r[i], mul_rn(alpha, Ap[i]));
-    x[i] = xi;
-    r[i] = ri;
-    T zi = PREC ? mul_rn(dinv[i], ri) : ri;
-    acc[0] += (double)ri * (double)ri;
-    acc[1] += (double)ri * (double)zi;
+  if (VEC) {
+    using V = typename Pair<T>::type;
+    const int64_t n2 = n >> 1;
+    for (int64_t i = tid; i < n2; i += stride) {
+      V xv = ((V *)x)[i], rv = ((V *)r)[i];
+      const V pv = __ldcs((const V *)p + i), av = __ldcs((const V *)Ap + i);
+      V dv = pv;
+      if (PREC) dv = __ldg((const V *)dinv + i);
+      cg_axpy<T, PREC>(xv.x, rv.x, pv.x, av.x, dv.x, alpha, acc);
+      cg_axpy<T, PREC>(xv.y, rv.y, pv.y, av.y, dv.y, alpha, acc);
+      ((V *)x)[i] = xv;
+      ((V *)r)[i] = rv;
+    }
+    if ((n & 1) && tid == 0) {
+      const int64_t i = n - 1;
+      T xi = x[i], ri = r[i];
+      cg_axpy<T, PREC>(xi, ri, p[i], Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
+      x[i] = xi;
+      r[i] = ri;
+    }
+  } else {
+    for (int64_t i = tid; i < n; i += stride) {
+      T xi = x[i], ri = r[i];
+      cg_axpy<T, PREC>(xi, ri, p[i], Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
+      x[i] = xi;
+      r[i] = ri;
+    }
   }
   if (last_block_sum<2, kBlock>(acc, partials, &st->counter[2], smem) && threadIdx.x == 0) {
     const long long it = st->iter + 1;
@@ -149,7 +184,7 @@ cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__res
 }
 
 template <typename T, bool PREC>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
                      const T *__restrict__ dinv, T *pA, T *pB, T *__restrict__ Ap, CgState *st,
                      double *partA, double *partB) {
@@ -270,8 +305,10 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
     g_launches.fetch_add(1, std::memory_order_relaxed);
     profiler().end(0, s, ev);
   } else {
-    const int grid_a = G;
-    const int grid_b = G;
+    const int grid_a = occupancy_grid((const void *)cg_spmv_kernel<T, PREC>);
+    const bool vec = aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv));
+    const int grid_b = vec ? occupancy_grid((const void *)cg_update_kernel<T, PREC, true>)
+                           : occupancy_grid((const void *)cg_update_kernel<T, PREC, false>);
     SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
       T *p_old = (it & 1) ? pB : pA;
       T *p_new = (it & 1) ? pA : pB;
@@ -281,8 +318,12 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
                  st, part0);
       profiler().end(0, s, ev);
       profiler().begin(1, it, s, &ev);
-      SLA_LAUNCH((cg_update_kernel<T, PREC>), grid_b, kBlock, 0, s, n, x, r, p_new, Ap, dinv, st,
-                 part1);
+      if (vec)
+        SLA_LAUNCH((cg_update_kernel<T, PREC, true>), grid_b, kBlock, 0, s, n, x, r, p_new, Ap,
+                   dinv, st, part1);
+      else
+        SLA_LAUNCH((cg_update_kernel<T, PREC, false>), grid_b, kBlock, 0, s, n, x, r, p_new, Ap,
+                   dinv, st, part1);
       profiler().end(1, s, ev);
       return SLA_OK;
     }));
@@ -376,10 +417,16 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
       for (int64_t j = 0; j < chunk; ++j, ++it) {
         T *p_old = (it & 1) ? pB : pA;
         T *p_new = (it & 1) ? pA : pB;
-        SLA_LAUNCH((cg_spmv_kernel<T, PREC>), G, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap, st,
-                   part0);
-        SLA_LAUNCH((cg_update_kernel<T, PREC>), G, kBlock, 0, s, n, x, r, p_new, Ap, dinv, st,
-                   part1);
+        SLA_LAUNCH((cg_spmv_kernel<T, PREC>), occupancy_grid((const void *)cg_spmv_kernel<T, PREC>),
+                   kBlock, 0, s, A, r, dinv, p_old, p_new, Ap, st, part0);
+        if (aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv)))
+          SLA_LAUNCH((cg_update_kernel<T, PREC, true>),
+                     occupancy_grid((const void *)cg_update_kernel<T, PREC, true>), kBlock, 0, s,
+                     n, x, r, p_new, Ap, dinv, st, part1);
+        else
+          SLA_LAUNCH((cg_update_kernel<T, PREC, false>),
+                     occupancy_grid((const void *)cg_update_kernel<T, PREC, false>), kBlock, 0, s,
+                     n, x, r, p_new, Ap, dinv, st, part1);
       }
       int done = 0;
       SLA_CUDA_TRY(cudaMemcpyAsync(&done, &st->done, sizeof(int), cudaMemcpyDeviceToHost, s));

@@ -85,9 +85,20 @@ inline int grid_for(int64_t work_items, int per_block = kBlock,
   return (int)(want < cap ? want : cap);
 }
 
-// Fixed grid of the solver kernels: deterministic reductions need the same
-// block count in every launch of one solve.
+// Upper bound of the solver grids (sizes the per-block partial buffers).
 inline int solver_grid() { return device_info().sm_count * 8; }
+
+// One wave of resident blocks of `fn` on the current device (cached per
+// kernel): grid-stride kernels get no tail wave, and the grid (hence the
+// reduction order) is the same in every launch.
+int occupancy_grid(const void *fn, int block = kBlock);
+
+// True when every pointer is 16-byte aligned (vectorised streaming paths).
+inline bool aligned16() { return true; }
+template <typename P, typename... R>
+inline bool aligned16(const P *p, R... rest) {
+  return (((uintptr_t)p) & 15u) == 0 && aligned16(rest...);
+}
 
 inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
 

@@ -1,6 +1,8 @@
 // Process-wide state of libsla_b200: launch counter, device properties,
 // kernel-time sampling and status strings.
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <unordered_map>
 
 #include "solver.cuh"
@@ -26,6 +28,27 @@ const DeviceInfo &device_info() {
   info.coop = coop != 0;
   if (info.sm_count <= 0) info.sm_count = 1;
   return cache.emplace(dev, info).first->second;
+}
+
+int occupancy_grid(const void *fn, int block) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void *, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_tuple(dev, fn, block);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, block, 0) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const int sms = device_info().sm_count;
+  int cap = sms * 8;
+  int grid = per_sm * sms;
+  if (grid > cap) grid = cap;
+  cache.emplace(key, grid);
+  return grid;
 }
 
 static thread_local HostPoll t_poll;

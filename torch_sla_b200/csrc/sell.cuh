@@ -41,6 +41,11 @@ inline bool sell_ok(const sla_sell_t *A) {
   return true;
 }
 
+// Entries per load batch: a batch issues all its column/value loads, then all
+// its gathers, so a row of up to kRowBatch entries costs one dependent
+// load -> gather round trip (7-point rows fit one batch, 27-point rows four).
+constexpr int kRowBatch = 8;
+
 // sum_j val[j] * g(col[j]) over the entries of this lane's slot.
 template <typename T, typename G>
 __device__ __forceinline__ T sell_row(const Sell<T> &A, int64_t slice, int lane, const G &g) {
@@ -49,28 +54,30 @@ __device__ __forceinline__ T sell_row(const Sell<T> &A, int64_t slice, int lane,
   const int32_t *__restrict__ cp = A.col + base + lane;
   const T *__restrict__ vp = A.val + base + lane;
   T sum = T(0);
-  int j = 0;
-  for (; j + 4 <= width; j += 4) {
-    int32_t c[4];
-    T v[4], x[4];
+  for (int j = 0; j < width; j += kRowBatch) {
+    int32_t c[kRowBatch];
+    T v[kRowBatch], x[kRowBatch];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      c[u] = ld_stream(cp + 32 * (j + u));
-      v[u] = ld_stream(vp + 32 * (j + u));
+    for (int u = 0; u < kRowBatch; ++u) {
+      if (j + u < width) {
+        c[u] = ld_stream(cp + 32 * (j + u));
+        v[u] = ld_stream(vp + 32 * (j + u));
+      } else {
+        c[u] = -1;
+        v[u] = T(0);
+      }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) x[u] = c[u] >= 0 ? g(c[u]) : T(0);
+    for (int u = 0; u < kRowBatch; ++u) x[u] = c[u] >= 0 ? g(c[u]) : T(0);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) sum = fma(v[u], x[u], sum);
-  }
-  for (; j < width; ++j) {
-    int32_t c = ld_stream(cp + 32 * j);
-    T v = ld_stream(vp + 32 * j);
-    T x = c >= 0 ? g(c) : T(0);
-    sum = fma(v, x, sum);
+    for (int u = 0; u < kRowBatch; ++u) sum = fma(v[u], x[u], sum);
   }
   return sum;
 }
+
+// Blocks per SM the SpMV-bearing kernels are compiled for (register cap):
+// enough warps to keep ~8 batched loads each in flight.
+constexpr int kSpmvMinBlocks = 4;
 
 template <typename T>
 struct PlainGather {

@@ -248,7 +248,7 @@ __global__ void shard_cg_pack(const int32_t *__restrict__ idx, int64_t n, const 
 }
 
 template <typename T, bool PREC, bool HALO>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 shard_cg_spmv(Sell<T> A, int32_t n_own, const T *__restrict__ r, const T *__restrict__ dinv,
               const T *__restrict__ p_old, const T *__restrict__ phalo, T *__restrict__ p_new,
               T *__restrict__ Ap, ShardState *st, CgRed *R, double *partials, long long k) {
@@ -411,7 +411,7 @@ __global__ void shard_bi_pack1(const int32_t *__restrict__ idx, int64_t n, BiP<T
 }
 
 template <typename T, bool PREC, bool HALO>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 shard_bi_k1(Sell<T> A, int32_t n_own, BiP<T, PREC> g0, const T *__restrict__ phalo,
             const T *__restrict__ rhat, T *__restrict__ p_new, T *__restrict__ v, ShardState *st,
             BiRed *R, double *partials, long long k) {
@@ -454,7 +454,7 @@ __global__ void shard_bi_pack2(const int32_t *__restrict__ idx, int64_t n, BiS<T
 }
 
 template <typename T, bool PREC, bool HALO>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 shard_bi_k2(Sell<T> A, int32_t n_own, BiS<T, PREC> g0, const T *__restrict__ shalo,
             T *__restrict__ t, ShardState *st, BiRed *R, double *partials, long long k) {
   __shared__ double smem[3 * kWarps];
@@ -592,6 +592,9 @@ static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
              part[0]);
   SLA_NCCL_TRY(ncclAllReduce(R->init, R->init, 2, ncclFloat64, ncclSum, cr->nccl, s));
   const T *hsrc = plan->halo_src ? halo : recvbuf;
+  const int gi = occupancy_grid((const void *)shard_cg_spmv<T, PREC, false>);
+  const int gb = occupancy_grid((const void *)shard_cg_spmv<T, PREC, true>);
+  const int gu = occupancy_grid((const void *)shard_cg_update<T, PREC>);
   SLA_TRY(shard_loop(cr, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
     T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
     if (ns > 0)
@@ -603,18 +606,18 @@ static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
     SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
     cudaEvent_t ev;
     profiler().begin(0, k, s, &ev);
-    SLA_LAUNCH((shard_cg_spmv<T, PREC, false>), G, kBlock, 0, s, AI, (int32_t)no, r, dinv, p_old,
+    SLA_LAUNCH((shard_cg_spmv<T, PREC, false>), gi, kBlock, 0, s, AI, (int32_t)no, r, dinv, p_old,
                hsrc, p_new, Ap, st, R, part[1], (long long)k);
     profiler().end(0, s, ev);
     SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
     if (plan->halo_src && nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
                  halo, &st->stopped);
-    SLA_LAUNCH((shard_cg_spmv<T, PREC, true>), G, kBlock, 0, s, AB, (int32_t)no, r, dinv, p_old,
+    SLA_LAUNCH((shard_cg_spmv<T, PREC, true>), gb, kBlock, 0, s, AB, (int32_t)no, r, dinv, p_old,
                hsrc, p_new, Ap, st, R, part[2], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->pap, R->pap, 1, ncclFloat64, ncclSum, cr->nccl, s));
     profiler().begin(1, k, s, &ev);
-    SLA_LAUNCH((shard_cg_update<T, PREC>), G, kBlock, 0, s, no, x, r, p_new, Ap, dinv, st, R,
+    SLA_LAUNCH((shard_cg_update<T, PREC>), gu, kBlock, 0, s, no, x, r, p_new, Ap, dinv, st, R,
                part[3], (long long)k);
     profiler().end(1, s, ev);
     SLA_NCCL_TRY(ncclAllReduce(R->loc[k & 1], R->loc[k & 1], 2, ncclFloat64, ncclSum, cr->nccl, s));
@@ -664,6 +667,11 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
   SLA_NCCL_TRY(ncclAllReduce(R->init, R->init, 2, ncclFloat64, ncclSum, cr->nccl, s));
   const T *hsrc = plan->halo_src ? halo : recvbuf;
   const unsigned pack_grid = ns > 0 ? (unsigned)grid_for(ns) : 1u;
+  const int g1i = occupancy_grid((const void *)shard_bi_k1<T, PREC, false>);
+  const int g1b = occupancy_grid((const void *)shard_bi_k1<T, PREC, true>);
+  const int g2i = occupancy_grid((const void *)shard_bi_k2<T, PREC, false>);
+  const int g2b = occupancy_grid((const void *)shard_bi_k2<T, PREC, true>);
+  const int g3 = occupancy_grid((const void *)shard_bi_k3<T, PREC>);
   SLA_TRY(shard_loop(cr, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
     T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
     BiP<T, PREC> gp{r, p_old, t, dinv, T(0), T(1)};
@@ -674,30 +682,30 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
     SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
     cudaEvent_t ev;
     profiler().begin(0, k, s, &ev);
-    SLA_LAUNCH((shard_bi_k1<T, PREC, false>), G, kBlock, 0, s, AI, (int32_t)no, gp, hsrc, rhat,
+    SLA_LAUNCH((shard_bi_k1<T, PREC, false>), g1i, kBlock, 0, s, AI, (int32_t)no, gp, hsrc, rhat,
                p_new, v, st, R, part[1], (long long)k);
     profiler().end(0, s, ev);
     SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
     if (plan->halo_src && nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
                  halo, &st->stopped);
-    SLA_LAUNCH((shard_bi_k1<T, PREC, true>), G, kBlock, 0, s, AB, (int32_t)no, gp, hsrc, rhat,
+    SLA_LAUNCH((shard_bi_k1<T, PREC, true>), g1b, kBlock, 0, s, AB, (int32_t)no, gp, hsrc, rhat,
                p_new, v, st, R, part[2], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->rv, R->rv, 1, ncclFloat64, ncclSum, cr->nccl, s));
     // s_hat halo, then t = A s_hat
     SLA_LAUNCH((shard_bi_pack2<T, PREC>), pack_grid, kBlock, 0, s, plan->send_index, ns, gs,
                sendbuf, st, R, (long long)k);
     SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
-    SLA_LAUNCH((shard_bi_k2<T, PREC, false>), G, kBlock, 0, s, AI, (int32_t)no, gs, hsrc, t, st, R,
+    SLA_LAUNCH((shard_bi_k2<T, PREC, false>), g2i, kBlock, 0, s, AI, (int32_t)no, gs, hsrc, t, st, R,
                part[3], (long long)k);
     SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
     if (plan->halo_src && nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
                  halo, &st->stopped);
-    SLA_LAUNCH((shard_bi_k2<T, PREC, true>), G, kBlock, 0, s, AB, (int32_t)no, gs, hsrc, t, st, R,
+    SLA_LAUNCH((shard_bi_k2<T, PREC, true>), g2b, kBlock, 0, s, AB, (int32_t)no, gs, hsrc, t, st, R,
                part[4], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->stt, R->stt, 3, ncclFloat64, ncclSum, cr->nccl, s));
-    SLA_LAUNCH((shard_bi_k3<T, PREC>), G, kBlock, 0, s, no, x, r, rhat, p_new, v, t, dinv, st, R,
+    SLA_LAUNCH((shard_bi_k3<T, PREC>), g3, kBlock, 0, s, no, x, r, rhat, p_new, v, t, dinv, st, R,
                part[5], (long long)k, (long long)every, atol, rtol);
     SLA_NCCL_TRY(ncclAllReduce(R->rr[k & 1], R->rr[k & 1], 2, ncclFloat64, ncclSum, cr->nccl, s));
     return SLA_OK;

@@ -5,7 +5,7 @@
 namespace sla {
 
 template <typename T>
-__global__ void __launch_bounds__(kBlock) spmv_kernel(Sell<T> A, const T *__restrict__ x,
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks) spmv_kernel(Sell<T> A, const T *__restrict__ x,
                                                       T *__restrict__ y) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -25,7 +25,7 @@ template <typename T>
 int spmv_launch(const sla_sell_t *A, const void *x, void *y, cudaStream_t s) {
   Sell<T> a = make_sell<T>(A);
   if (a.n_slices == 0) return SLA_OK;
-  SLA_LAUNCH(spmv_kernel<T>, grid_for(a.n_slices * 32), kBlock, 0, s, a, (const T *)x, (T *)y);
+  SLA_LAUNCH(spmv_kernel<T>, grid_for(a.n_slices * 32, kBlock, 4), kBlock, 0, s, a, (const T *)x, (T *)y);
   return SLA_OK;
 }
 template int spmv_launch<float>(const sla_sell_t *, const void *, void *, cudaStream_t);

@@ -126,6 +126,27 @@ def diffusion_2d_batched(batch: int, m: int, seed: int = 2, dtype=torch.float64,
             b.to(dtype=dtype, device=device))
 
 
+def poisson_3d_7pt_rows(dims, z0: int, nz_local: int, dtype=torch.float64, device="cpu"):
+    """Rows of the global 7-point Laplacian on dims = (nz, ny, nx) whose z lies
+    in [z0, z0 + nz_local), as COO with GLOBAL indices (diagonal first, then
+    the six neighbour blocks). Coalesces to the same rows as poisson_3d_7pt."""
+    nz, ny, nx = dims
+    sz = ny * nx
+    st = (sz, nx, 1)
+    p = torch.arange(nz_local * sz, device=device, dtype=torch.int64) + z0 * sz
+    coords = (p // sz, (p // nx) % ny, p % nx)
+    rows, cols, vals = [p], [p], [torch.full((p.numel(),), 6.0, dtype=dtype, device=device)]
+    for axis in range(3):
+        for step in (1, -1):
+            nb = coords[axis] + step
+            keep = (nb >= 0) & (nb < dims[axis])
+            src = p[keep]
+            rows.append(src)
+            cols.append(src + step * st[axis])
+            vals.append(torch.full((src.numel(),), -1.0, dtype=dtype, device=device))
+    return torch.cat(vals), torch.cat(rows), torch.cat(cols)
+
+
 # --------------------------------------------------------------- 27-point
 _OFFS13 = [(dz, dy, dx) for dz in (-1, 0, 1) for dy in (-1, 0, 1) for dx in (-1, 0, 1)
            if (dz, dy, dx) > (0, 0, 0)]
