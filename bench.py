@@ -1,20 +1,30 @@
 #!/usr/bin/env python
-"""Benchmark: fp64 Jacobi-PCG iterations/s on the 3-D 7-point Poisson system,
-256^3 unknowns per GPU (weak scaling across GPUs, z-slab row partition).
+"""Benchmark of the torch-sla iterative-solve hot path on B200.
 
-One step = one full solve to rtol 1e-8 from x0 = 0 (b ~ N(0,1), seed 1).
-value = CG iterations/s summed over GPUs (each GPU advances its 256^3 slab
-by one iteration per global iteration), with matrix and b resident in HBM;
-e2e = the same metric through the public call pytorch_solve() with the COO
-matrix and b in pinned host memory, copies included.
+Default workload (the one the headline metric is quoted on): fp64 Jacobi
+PCG on the 3-D 7-point Poisson system with 256^3 unknowns per GPU, b ~ N(0,1)
+seed 1, rtol 1e-8. One step = one full solve. At N GPUs the global grid is
+(256 N) x 256 x 256, row-partitioned into z-slabs (weak scaling); value =
+CG iterations/s x N (each GPU advances its 256^3 slab once per iteration),
+with the matrix and b resident in HBM; e2e = the same metric through the
+public API with host buffers and the copies inside the timed region.
+
+Other workloads (--workload): cg2d (2-D 256^2 plain CG, rtol 1e-10,
+persistent kernel), spmv (256^3 SpMV fp64 and fp32), batched (64 x 512^2
+same-pattern CG, rtol 1e-8, with backward), bicgstab (192^3 convection-
+diffusion, Jacobi BiCGStab), pcg27 (27-point variable-coefficient 256^3 per
+GPU).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                  [--workload pcg7|cg2d|spmv|batched|bicgstab|pcg27] [--grid M]
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
+import socket
 import statistics
 import subprocess
 import sys
@@ -26,12 +36,13 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
-M = 256          # grid edge per GPU
+M = 256
 RTOL = 1e-8
 SEED = 1
 METRIC = "fp64 Jacobi-PCG iterations/s (3-D 7-point Poisson, 256^3 unknowns per GPU)"
 
 
+# ------------------------------------------------------------------ helpers
 def peaks():
     try:
         with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
@@ -93,51 +104,64 @@ class Clocks:
 
 
 def matrix_bytes(nnz: int, n: int, V: int = 8) -> int:
+    """Algorithmic matrix bytes on int32 CSR."""
     return nnz * (V + 4) + 4 * (n + 1)
 
 
-def e2e_run(args, v, r, c, b_host, sh, dev):
-    """pytorch_solve() with the COO matrix and b in pinned host memory; the
-    timed region holds the H2D copies, the CSR build, the solve and the D2H
-    copy of x."""
-    import torch_sla_b200 as T
-    from torch_sla_b200.backends import pytorch_backend as PB
-    vh, rh, ch = v.cpu().pin_memory(), r.cpu().pin_memory(), c.cpu().pin_memory()
-    bh = b_host.pin_memory()
-    h2d = vh.numel() * 8 + rh.numel() * 8 + ch.numel() * 8 + bh.numel() * 8
-    e_iters = 0
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e_steps = max(1, min(args.steps, 3))
-    e0.record()
-    for _ in range(e_steps):
-        vd, rd, cd, bd = (t.to(dev, non_blocking=True) for t in (vh, rh, ch, bh))
-        x = T.pytorch_solve(vd, rd, cd, sh, bd, method="cg", atol=0.0, rtol=RTOL,
-                            preconditioner="jacobi")
-        x.cpu()
-        e_iters += PB.last_solve_info()["iterations"]
-    e1.record()
-    torch.cuda.synchronize()
-    return e_iters, e0.elapsed_time(e1), e_steps, h2d
+def read_traffic(kernel: str):
+    """Per-launch DRAM bytes of `kernel` at the full workload from the ncu
+    summary profiles/traffic.txt ('<kernel> <bytes>' lines)."""
+    try:
+        with open(os.path.join(HERE, "profiles", "traffic.txt")) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == kernel:
+                    return int(float(parts[1]))
+    except OSError:
+        pass
+    return None
 
 
-def run_b200(args):
-    import torch.distributed as dist
+def timed(fn, steps, dev, clocks_gpu):
+    """Run fn() `steps` times between synchronisations, CUDA events on the
+    current stream; returns (ms, results, clocks summary)."""
+    out = []
+    with Clocks(clocks_gpu) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        t0.record()
+        for _ in range(steps):
+            out.append(fn())
+        t1.record()
+        torch.cuda.synchronize(dev)
+    return t0.elapsed_time(t1), out, clk.summary()
 
-    import torch_sla_b200 as T
+
+def base_line(args, metric, value, unit, ms, n_gpus, dtype="f64", hib=True):
+    return {"metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": n_gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
+            "higher_is_better": hib, "scaling": "weak", "vs_baseline": None, "dtype": dtype,
+            "data": "synthetic"}
+
+
+def roofline(kernel, alg_bytes, ms_total, launches, traffic_key=None):
+    peak, kind = peaks()
+    avg = ms_total / max(launches, 1)
+    ach = alg_bytes / (avg / 1e3) / 1e9 if launches else None
+    return {"kernel": kernel, "bound": "hbm", "achieved": None if ach is None else round(ach, 1),
+            "peak": peak, "unit": "GB/s", "frac": None if ach is None else round(ach / peak, 4),
+            "traffic": read_traffic(traffic_key or kernel), "algorithmic_bytes": int(alg_bytes),
+            "avg_launch_ms": round(avg, 5), "sampled_launches": launches,
+            "peak_kind": "measured (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else kind}
+
+
+# ----------------------------------------------------- single-GPU workloads
+def wl_pcg7(args, dev, local):
+    """3-D 7-point Poisson 256^3, fp64 Jacobi PCG, rtol 1e-8."""
     from torch_sla_b200 import _lib as L
     from torch_sla_b200 import problems as P
     from torch_sla_b200.backends import pytorch_backend as PB
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        return run_b200_sharded(args, world, rank, local)
-
     m = args.grid
     n = m ** 3
     v, r, c, sh = P.poisson_3d_7pt(m, device=dev)
@@ -148,134 +172,405 @@ def run_b200(args):
     nnz = A.csr.nnz
 
     def solve_once():
-        x, info = PB._pcg_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000)
-        return info
+        return PB._pcg_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000)[1].iterations
 
     for _ in range(args.warmup):
         solve_once()
-    torch.cuda.synchronize()
     L.profile_enable(True, 8)
-    launches0 = L.launch_count()
-    iters = 0
-    with Clocks(local) as clk:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        t0.record()
-        for _ in range(args.steps):
-            info = solve_once()
-            iters += int(info.iterations)
-        t1.record()
-        torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1)
-    launches = L.launch_count() - launches0
+    l0 = L.launch_count()
+    ms, its, clk = timed(solve_once, args.steps, dev, local)
+    launches = L.launch_count() - l0
     ka_ms, ka_n = L.profile_read(0)
     kb_ms, kb_n = L.profile_read(1)
     L.profile_enable(False)
+    iters = sum(its)
     value = iters / (ms / 1e3)
-
-    # roofline of the dominant kernel (SpMV with the fused p update)
-    ka_bytes = matrix_bytes(nnz, n) + 5 * 8 * n
-    ka_avg = ka_ms / max(ka_n, 1)
-    peak, peak_kind = peaks()
-    achieved = ka_bytes / (ka_avg / 1e3) / 1e9 if ka_n else None
+    peak, kind = peaks()
     iter_bytes = matrix_bytes(nnz, n) + 13 * 8 * n
-    traffic = read_traffic("cg_spmv_kernel")
-
-    # end to end through pytorch_solve with pinned host COO + b
-    e_iters, e_ms, e_steps, h2d = 0, float("nan"), 0, 0
+    line = base_line(args, METRIC, value, "iterations/s", ms, 1)
+    line["config"] = {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [m, m, m], "n": n,
+                      "nnz": nnz, "rtol": RTOL, "b": "N(0,1) seed 1",
+                      "iterations_per_solve": iters // args.steps,
+                      "format": "SELL-32 int32 (sigma=1)",
+                      "l2": "inputs larger than L2 (1.4 GB matrix); no flush",
+                      "parallelism": "single GPU"}
+    line["roofline"] = roofline("cg_spmv_kernel", matrix_bytes(nnz, n) + 5 * 8 * n, ka_ms, ka_n)
+    line["roofline"]["update_kernel"] = {
+        "kernel": "cg_update_kernel", "avg_launch_ms": round(kb_ms / max(kb_n, 1), 5),
+        "achieved": round(7 * 8 * n / (kb_ms / max(kb_n, 1) / 1e3) / 1e9, 1) if kb_n else None}
+    line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
+                                  "achieved_gbs": round(iter_bytes * value / 1e9, 1),
+                                  "frac": round(iter_bytes * value / 1e9 / peak, 4),
+                                  "frac_of_8tbs": round(iter_bytes * value / 8e12, 4),
+                                  "bytes_formula": "12 nnz + 4 (N+1) + 13 * 8 N"}
     if not args.no_e2e:
-        e_iters, e_ms, e_steps, h2d = e2e_run(args, v, r, c, b_host, sh, dev)
-
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "iterations/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic",
-        "config": {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [m, m, m], "n": n, "nnz": nnz,
-                   "rtol": RTOL, "b": "N(0,1) seed 1", "iterations_per_solve": iters // args.steps,
-                   "format": "SELL-32 int32 (sigma=1)", "l2": "inputs larger than L2 (1.4 GB matrix)",
-                   "parallelism": "single GPU"},
-        "iteration_roofline": {"bytes_per_iter": iter_bytes,
-                               "achieved_gbs": round(iter_bytes * value / 1e9, 1),
-                               "frac": round(iter_bytes * value / 1e9 / peak, 4),
-                               "peak_kind": peak_kind},
-        "roofline": {"kernel": "cg_spmv_kernel", "bound": "hbm",
-                     "achieved": None if achieved is None else round(achieved, 1),
-                     "peak": peak, "unit": "GB/s",
-                     "frac": None if achieved is None else round(achieved / peak, 4),
-                     "traffic": traffic, "algorithmic_bytes": ka_bytes,
-                     "avg_launch_ms": round(ka_avg, 5), "sampled_launches": ka_n,
-                     "update_kernel_avg_ms": round(kb_ms / max(kb_n, 1), 5),
-                     "peak_kind": peak_kind},
-        "e2e": {"value": round(e_iters / (e_ms / 1e3), 2) if e_steps else None,
-                "unit": "iterations/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": n * 8,
-                "ms_per_step": round(e_ms / e_steps, 3) if e_steps else None, "steps": e_steps},
-        "gpu_launches": launches,
-        "clocks": clk.summary(),
-    }
+        line["e2e"] = e2e_pcg7(args, v, r, c, b_host, sh, dev)
+    line["gpu_launches"] = launches
+    line["clocks"] = clk
     if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(A_gpu=A, b_host=b_host, budget_s=args.cpu_seconds)
-    print(json.dumps(line), flush=True)
+        line["cpu_baseline"] = cpu_baseline_pcg(A, b_host, args.cpu_seconds)
+    return line
 
 
-def read_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` at the full workload, from the
-    committed ncu summary (profiles/traffic.txt: '<kernel> <bytes>')."""
-    path = os.path.join(HERE, "profiles", "traffic.txt")
-    try:
-        with open(path) as f:
-            for line in f:
-                parts = line.split()
-                if len(parts) >= 2 and parts[0] == kernel:
-                    return int(float(parts[1]))
-    except OSError:
-        pass
-    return None
+def e2e_pcg7(args, v, r, c, b_host, sh, dev):
+    """pytorch_solve() with the COO matrix and b in pinned host memory; the
+    timed region holds the H2D copies, the CSR build, the solve and the D2H
+    copy of x."""
+    import torch_sla_b200 as T
+    from torch_sla_b200.backends import pytorch_backend as PB
+    vh, rh, ch = v.cpu().pin_memory(), r.cpu().pin_memory(), c.cpu().pin_memory()
+    bh = b_host.pin_memory()
+    h2d = (vh.numel() + rh.numel() + ch.numel() + bh.numel()) * 8
+    steps = max(1, min(args.steps, 3))
+
+    def once():
+        vd, rd, cd, bd = (t.to(dev, non_blocking=True) for t in (vh, rh, ch, bh))
+        x = T.pytorch_solve(vd, rd, cd, sh, bd, method="cg", atol=0.0, rtol=RTOL,
+                            preconditioner="jacobi")
+        x.cpu()
+        return PB.last_solve_info()["iterations"]
+
+    ms, its, _ = timed(once, steps, dev, dev.index)
+    return {"value": round(sum(its) / (ms / 1e3), 3), "unit": "iterations/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": bh.numel() * 8,
+            "ms_per_step": round(ms / steps, 3), "steps": steps,
+            "api": "torch_sla_b200.pytorch_solve (COO from pinned host memory)"}
 
 
-def cpu_csr_from_device(A):
-    """torch CPU CSR (int64 indices, as torch-sla's to_sparse_csr builds)
-    of the device CSR: skips the ~40 s CPU COO sort at 256^3."""
-    csr = A.csr
+def cpu_csr_from_device(csr):
+    """torch CPU CSR (int64 indices, as torch-sla builds it) of a device CSR:
+    skips the ~40 s CPU COO sort of the 256^3 matrix."""
     return torch.sparse_csr_tensor(csr.rowptr.cpu().long(), csr.colind.cpu().long(),
                                    csr.vals.cpu(), csr.shape)
 
 
-def cpu_baseline(A_gpu=None, b_host=None, budget_s=15.0):
-    """Reference CPU path (the oracle: torch-sla's own ATen ops) on the host
-    cores, on a bounded number of PCG iterations of the same system."""
+def cpu_baseline_pcg(A, b_host, budget_s):
+    """The oracle (torch-sla's CPU ops) on the host cores, a bounded number of
+    PCG iterations of the same system."""
     from oracle import krylov as K
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    Acpu = cpu_csr_from_device(A_gpu)
-    n = Acpu.shape[0]
+    Acpu = cpu_csr_from_device(A.csr)
     dinv = K.jacobi_inverse(K.csr_diagonal(Acpu), "eps")
     t0 = time.perf_counter()
     it = K.pcg_iterations(Acpu, b_host, dinv, budget_s=budget_s)
     dt = time.perf_counter() - t0
     return {"value": round(it / dt, 3), "unit": "iterations/s", "cores": cores, "kind": "port",
-            "sample": f"{it} Jacobi-PCG iterations of the same 7-point system (n={n}) with "
-                      "torch CPU CSR mv/vdot/addcmul, as torch-sla's pytorch backend runs them"}
+            "sample": f"{it} Jacobi-PCG iterations of the same system (n={Acpu.shape[0]}) with "
+                      "torch CPU CSR mv / vdot / addcmul, torch-sla's pytorch-backend ops"}
 
 
+def wl_cg2d(args, dev, local):
+    """2-D 5-point 256^2, b ~ U(-1,1) seed 0, plain CG rtol 1e-10."""
+    from oracle import krylov as K
+    from torch_sla_b200 import _lib as L
+    from torch_sla_b200 import problems as P
+    from torch_sla_b200.backends import pytorch_backend as PB
+    v, r, c, sh = P.poisson_2d_5pt(256, device=dev)
+    b_host = P.rhs_uniform_pm1(sh[0], 0)
+    b = b_host.to(dev)
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+
+    def once():
+        return PB._pcg_core(A, b, None, None, 0.0, 1e-10, 10000)[1].iterations
+
+    for _ in range(args.warmup):
+        once()
+    l0 = L.launch_count()
+    ms, its, clk = timed(once, args.steps, dev, local)
+    line = base_line(args, "fp64 CG solve time (2-D 5-point Poisson 256^2, rtol 1e-10)",
+                     ms / args.steps, "ms/solve", ms, 1, hib=False)
+    line["config"] = {"workload": "cg_poisson2d_5pt_256", "n": sh[0], "nnz": A.csr.nnz,
+                      "iterations_per_solve": its[0], "preconditioner": "none",
+                      "kernel": "cg_persistent_kernel (one cooperative launch per solve)",
+                      "iterations_per_s": round(sum(its) / (ms / 1e3), 1)}
+    line["gpu_launches"] = L.launch_count() - l0
+    line["clocks"] = clk
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    vc, rc_, cc, shc = P.poisson_2d_5pt(256)
+    t0 = time.perf_counter()
+    _, it, _, _ = K.pcg(vc, rc_, cc, shc, b_host, atol=0.0, rtol=1e-10, precond="none")
+    dt = time.perf_counter() - t0
+    line["cpu_baseline"] = {"value": round(dt * 1e3, 2), "unit": "ms/solve", "cores": cores,
+                            "kind": "port", "sample": f"one full solve ({it} iterations)"}
+    return line
+
+
+def wl_spmv(args, dev, local):
+    """configs[1] SpMV sweep: y = A x on the 256^3 7-point matrix, fp64 and fp32."""
+    from torch_sla_b200 import problems as P
+    from torch_sla_b200._csr import DeviceCSR, spmv
+    res = {}
+    m = args.grid
+    n = m ** 3
+    peak, _ = peaks()
+    for dt, V in ((torch.float64, 8), (torch.float32, 4)):
+        v, r, c, sh = P.poisson_3d_7pt(m, dtype=dt, device=dev)
+        csr = DeviceCSR(v, r, c, sh)
+        sell = csr.sell()
+        del v, r, c
+        x = P.rhs_normal(n, SEED, dt).to(dev)
+        y = torch.empty_like(x)
+        reps = 50
+        for _ in range(5):
+            spmv(sell, x, n, y)
+        ms, _, clk = timed(lambda: spmv(sell, x, n, y), reps, dev, local)
+        alg = matrix_bytes(csr.nnz, n, V) + 2 * V * n
+        sec = ms / reps / 1e3
+        res["f64" if V == 8 else "f32"] = {"us_per_spmv": round(sec * 1e6, 2),
+                                          "achieved_gbs": round(alg / sec / 1e9, 1),
+                                          "frac": round(alg / sec / 1e9 / peak, 4),
+                                          "frac_of_8tbs": round(alg / sec / 8e12, 4),
+                                          "algorithmic_bytes": alg, "clocks": clk}
+        del csr, sell, x, y
+    line = base_line(args, "SpMV HBM GB/s (256^3 7-point, fp64)", res["f64"]["achieved_gbs"],
+                     "GB/s", res["f64"]["us_per_spmv"] / 1e3 * args.steps, 1)
+    line["config"] = {"workload": "spmv_poisson3d_7pt", "grid": [m, m, m], "sweep": res,
+                      "l2": "inputs larger than L2"}
+    return line
+
+
+def wl_batched(args, dev, local):
+    """64 x 512^2 variable-coefficient diffusion, batched CG
+    rtol 1e-8, forward + backward through spsolve_batch_same_layout."""
+    import torch_sla_b200 as T
+    from torch_sla_b200 import _lib as L
+    from torch_sla_b200 import problems as P
+    from torch_sla_b200.backends import pytorch_backend as PB
+    B, m = 64, 512
+    vb, r, c, sh, bb = P.diffusion_2d_batched(B, m, seed=2)
+    vb, r, c, bb = vb.to(dev), r.to(dev), c.to(dev), bb.to(dev)
+
+    def fwd():
+        PB.batched_cg_same_pattern(vb, r, c, sh, bb, atol=0.0, rtol=RTOL)
+        return PB.last_solve_info()["iterations"]
+
+    def fwd_bwd():
+        vg = vb.clone().requires_grad_(True)
+        bg = bb.clone().requires_grad_(True)
+        U = T.spsolve_batch_same_layout(vg, r, c, sh, bg, method="cg", atol=0.0, rtol=RTOL)
+        (U * U).sum().backward()
+        return 0
+
+    for _ in range(args.warmup):
+        fwd()
+    L.profile_enable(True, 8)
+    ms, its, clk = timed(fwd, args.steps, dev, local)
+    ka_ms, ka_n = L.profile_read(0)
+    L.profile_enable(False)
+    ms_fb, _, _ = timed(fwd_bwd, max(1, args.steps // 2), dev, local)
+    nnz = int(r.numel())
+    n = sh[0]
+    iters = sum(its)
+    value = iters / (ms / 1e3)
+    iter_bytes = B * nnz * 8 + 4 * nnz + 4 * (n + 1) + 13 * B * 8 * n
+    peak, _ = peaks()
+    line = base_line(args, "fp64 batched Jacobi-PCG iterations/s (64 x 512^2 diffusion)", value,
+                     "iterations/s", ms, 1)
+    line["config"] = {"workload": "batched_cg_diffusion2d", "batch": B, "grid": [m, m],
+                      "iterations_per_solve": iters // args.steps, "rtol": RTOL,
+                      "forward_backward_ms": round(ms_fb / max(1, args.steps // 2), 2),
+                      "layout": "values [nnz][B], vectors [n][B]"}
+    line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
+                                  "achieved_gbs": round(iter_bytes * value / 1e9, 1),
+                                  "frac": round(iter_bytes * value / 1e9 / peak, 4)}
+    line["roofline"] = roofline("batch_spmv_kernel",
+                                B * nnz * 8 + 4 * nnz + 4 * (n + 1) + 5 * B * 8 * n, ka_ms, ka_n)
+    line["clocks"] = clk
+    return line
+
+
+def wl_bicgstab(args, dev, local):
+    """192^3 upwind convection-diffusion, Jacobi BiCGStab rtol 1e-8."""
+    from torch_sla_b200 import _lib as L
+    from torch_sla_b200 import problems as P
+    from torch_sla_b200.backends import pytorch_backend as PB
+    m = 192
+    v, r, c, sh = P.convdiff_3d_upwind(m, device=dev)
+    b = P.rhs_uniform01(sh[0], 3).to(dev)
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    Mj = PB.get_preconditioner(A, "jacobi")
+    nnz, n = A.csr.nnz, sh[0]
+
+    def once():
+        return PB._bicgstab_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000)[1].iterations
+
+    for _ in range(args.warmup):
+        once()
+    L.profile_enable(True, 8)
+    ms, its, clk = timed(once, args.steps, dev, local)
+    k1_ms, k1_n = L.profile_read(0)
+    L.profile_enable(False)
+    iters = sum(its)
+    value = iters / (ms / 1e3)
+    iter_bytes = 2 * matrix_bytes(nnz, n) + 25 * 8 * n
+    peak, _ = peaks()
+    line = base_line(args, "fp64 Jacobi-BiCGStab iterations/s (192^3 convection-diffusion)",
+                     value, "iterations/s", ms, 1)
+    line["config"] = {"workload": "bicgstab_convdiff3d_192", "n": n, "nnz": nnz, "rtol": RTOL,
+                      "iterations_per_solve": iters // args.steps}
+    line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
+                                  "achieved_gbs": round(iter_bytes * value / 1e9, 1),
+                                  "frac": round(iter_bytes * value / 1e9 / peak, 4),
+                                  "bytes_formula": "2 (12 nnz + 4 (N+1)) + 25 * 8 N"}
+    line["roofline"] = roofline("bicg_k1", matrix_bytes(nnz, n) + 6 * 8 * n, k1_ms, k1_n)
+    line["clocks"] = clk
+    return line
+
+
+WORKLOADS = {"pcg7": wl_pcg7, "cg2d": wl_cg2d, "spmv": wl_spmv, "batched": wl_batched,
+             "bicgstab": wl_bicgstab}
+
+
+# ------------------------------------------------------------ N GPUs
+def sharded_rows(workload, m, world, rank, dev):
+    from torch_sla_b200 import problems as P
+    dims = (m * world, m, m)
+    if workload == "pcg27":
+        v, r, c = P.stencil27_rows(dims, rank * m, m, seed=4, device=dev)
+    elif workload == "bicgstab":
+        v, r, c = P.convdiff_3d_upwind_rows(m, rank * m, m, device=dev, nz=m * world)
+    else:
+        v, r, c = P.poisson_3d_7pt_rows(dims, rank * m, m, device=dev)
+    return v, r, c, dims
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def run_sharded(args, world, rank, local):
+    """N GPUs, one process each: rank k owns z-slab k (partition_simple), its
+    shard built from its own rows only; NCCL halo + allreduces."""
+    import torch.distributed as dist
+    from torch_sla_b200 import _lib as L
+    from torch_sla_b200 import problems as P
+    from torch_sla_b200.distributed import DSparseTensor, destroy_all
+
+    dev = torch.device("cuda", local)
+    if "MASTER_ADDR" not in os.environ:  # single process outside torchrun
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()), RANK="0",
+                          WORLD_SIZE="1")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    wl = args.workload if args.workload in ("pcg7", "pcg27", "bicgstab") else "pcg7"
+    m = 192 if wl == "bicgstab" and args.grid == M else args.grid
+    n_loc = m ** 3
+    v, r, c, dims = sharded_rows(wl, m, world, rank, dev)
+    n_glob = dims[0] * dims[1] * dims[2]
+    D = DSparseTensor.from_owned_rows(v, r, c, (n_glob, n_glob), rank=rank, world=world)
+    del v, r, c
+    gen = P.rhs_uniform01 if wl == "bicgstab" else P.rhs_normal
+    seed = 3 if wl == "bicgstab" else (4 if wl == "pcg27" else SEED)
+    b_full = gen(n_glob, seed)
+    b_host = b_full[rank * n_loc:(rank + 1) * n_loc].clone().pin_memory()
+    del b_full
+    b = b_host.to(dev)
+    plan = D._shard_plan()
+    nnz = plan.csr.nnz
+    method = "bicgstab" if wl == "bicgstab" else "cg"
+
+    def once(bb=None):
+        x = D.solve_distributed_shard(b if bb is None else bb, method=method,
+                                      preconditioner="jacobi", atol=0.0, rtol=RTOL,
+                                      maxiter=100000)
+        return x, D._last_info["iterations"]
+
+    for _ in range(args.warmup):
+        once()
+    torch.cuda.synchronize()
+    dist.barrier()
+    L.profile_enable(True, 8)
+    l0 = L.launch_count()
+    ms_local, outs, clk = timed(lambda: once()[1], args.steps, dev, local)
+    dist.barrier()
+    launches = L.launch_count() - l0
+    ka_ms, ka_n = L.profile_read(0)
+    L.profile_enable(False)
+    t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    iters = sum(outs)
+    value = iters * world / (ms / 1e3)
+
+    e_steps = max(1, min(args.steps, 3))
+    dist.barrier()
+
+    def e2e_once():
+        x, it = once(b_host.to(dev, non_blocking=True))
+        x.cpu()
+        return it
+    e_ms_local, e_its, _ = timed(e2e_once, e_steps, dev, local)
+    te = torch.tensor([e_ms_local], dtype=torch.float64, device=dev)
+    dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e_ms = float(te.item())
+
+    V = 8
+    interior_frac = plan.sell_int.n_slots / max(n_loc, 1)
+    mat = matrix_bytes(nnz, n_loc)
+    if method == "cg":
+        metric = (METRIC if wl == "pcg7" else
+                  "fp64 Jacobi-PCG iterations/s (3-D 27-point, 256^3 unknowns per GPU)")
+        ka_bytes = (mat + 5 * V * n_loc) * interior_frac
+        iter_bytes = mat + 13 * V * n_loc
+        kname = "shard_cg_spmv"
+    else:
+        metric = "fp64 Jacobi-BiCGStab iterations/s (convection-diffusion, 192^3 per GPU)"
+        ka_bytes = (mat + 6 * V * n_loc) * interior_frac
+        iter_bytes = 2 * mat + 25 * V * n_loc
+        kname = "shard_bi_k1"
+    peak, _ = peaks()
+    if rank == 0:
+        line = base_line(args, metric, value, "iterations/s", ms, world)
+        line["config"] = {"workload": {"pcg7": "jacobi_pcg_poisson3d_7pt",
+                                       "pcg27": "jacobi_pcg_stencil27",
+                                       "bicgstab": "bicgstab_convdiff3d"}[wl],
+                          "grid": list(dims), "n": n_glob, "n_per_gpu": n_loc,
+                          "nnz_per_gpu": nnz, "rtol": RTOL,
+                          "iterations_per_solve": iters // args.steps,
+                          "partition": "z-slabs (partition_simple), one-layer halos",
+                          "halo_bytes_per_neighbour": m * m * V, "check_every": 10,
+                          "format": "SELL-32 int32 (sigma=1)", "l2": "inputs larger than L2",
+                          "parallelism": f"row-sharded x{world} (NCCL send/recv + allreduce)"}
+        line["iteration_roofline"] = {"bytes_per_iter_per_gpu": iter_bytes,
+                                      "achieved_gbs_per_gpu":
+                                          round(iter_bytes * value / world / 1e9, 1),
+                                      "frac": round(iter_bytes * value / world / 1e9 / peak, 4)}
+        line["roofline"] = roofline(f"{kname} (interior rows)", ka_bytes, ka_ms, ka_n, kname)
+        line["e2e"] = {"value": round(sum(e_its) * world / (e_ms / 1e3), 3),
+                       "unit": "iterations/s", "h2d_bytes_per_step": n_loc * V * world,
+                       "d2h_bytes_per_step": n_loc * V * world,
+                       "ms_per_step": round(e_ms / e_steps, 3), "steps": e_steps,
+                       "api": "DSparseTensor.solve_distributed_shard, b from pinned host "
+                              "memory, x read back; shard setup done once before timing"}
+        line["gpu_launches"] = launches
+        line["clocks"] = clk
+        print(json.dumps(line), flush=True)
+    del D, plan
+    destroy_all()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+# --------------------------------------------------------- reference arm
 def run_reference(args):
     """--impl reference: torch-sla's CPU pytorch-backend arithmetic (the
-    oracle port) on the host cores, same metric, bounded sample per step."""
+    oracle port; torch-sla is pure Python, nothing to compile) on the host
+    cores, same metric and config, a bounded number of PCG iterations per
+    step. Under torchrun only rank 0 works."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    if int(os.environ.get("RANK", "0")) != 0:
         return
     from oracle import krylov as K
     from torch_sla_b200 import problems as P
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    n = M ** 3
-    v, r, c, sh = P.poisson_3d_7pt(M)
-    # the reference sorts its COO on every solve (~40 s here); that setup is
-    # excluded, only iterations are timed
-    Acpu = K.csr(v, r, c, sh)
+    m = args.grid
+    n = m ** 3
+    v, r, c, sh = P.poisson_3d_7pt(m)
+    Acpu = K.csr(v, r, c, sh)  # one-time COO sort, outside the timed region
     del v, r, c
     b = P.rhs_normal(n, SEED)
     dinv = K.jacobi_inverse(K.csr_diagonal(Acpu), "eps")
@@ -283,149 +578,20 @@ def run_reference(args):
     for _ in range(args.warmup):
         K.pcg_iterations(Acpu, b, dinv, iterations=1)
     t0 = time.perf_counter()
-    its = 0
-    for _ in range(args.steps):
-        its += K.pcg_iterations(Acpu, b, dinv, iterations=per_step)
+    its = sum(K.pcg_iterations(Acpu, b, dinv, iterations=per_step) for _ in range(args.steps))
     dt = time.perf_counter() - t0
-    value = its / dt
-    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3),
-            "unit": "iterations/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [M, M, M], "n": n,
-                       "rtol": RTOL, "parallelism": "host CPU"},
-            "cpu_baseline": {"value": round(value, 3), "unit": "iterations/s", "cores": cores,
-                             "kind": "port",
-                             "sample": f"{per_step} PCG iterations per step on the 256^3 system"},
-            "e2e": {"value": round(value, 3), "unit": "iterations/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+    value = its / dt * world  # one 256^3 slab per GPU of the B200 run, processed in turn
+    line = base_line(args, METRIC, value, "iterations/s", dt * 1e3, world)
+    line["impl"] = "reference"
+    line["config"] = {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [m * world, m, m],
+                      "n_per_slab": n, "rtol": RTOL, "parallelism": "host CPU"}
+    sample = (f"{per_step} PCG iterations per step on one 256^3 slab; x{world} slabs" if world > 1
+              else f"{per_step} PCG iterations per step on the 256^3 system")
+    line["cpu_baseline"] = {"value": round(value, 3), "unit": "iterations/s", "cores": cores,
+                            "kind": "port", "sample": sample}
+    line["e2e"] = {"value": round(value, 3), "unit": "iterations/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}
     print(json.dumps(line), flush=True)
-
-
-def run_b200_sharded(args, world, rank, local):
-    """N GPUs: global grid (256 N) x 256 x 256, rank k owns z-slab k (the
-    'simple' row partition), built from its own rows only."""
-    import datetime
-
-    import torch.distributed as dist
-
-    from torch_sla_b200 import _lib as L
-    from torch_sla_b200 import problems as P
-    from torch_sla_b200.distributed import DSparseTensor, destroy_all
-
-    dev = torch.device("cuda", local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                            device_id=dev)
-    m = args.grid
-    dims = (m * world, m, m)
-    n_glob = dims[0] * dims[1] * dims[2]
-    n_loc = m ** 3
-    v, r, c = P.poisson_3d_7pt_rows(dims, rank * m, m, device=dev)
-    D = DSparseTensor.from_owned_rows(v, r, c, (n_glob, n_glob), rank=rank, world=world)
-    del v, r, c
-    b_full = P.rhs_normal(n_glob, SEED)
-    b_host = b_full[rank * n_loc:(rank + 1) * n_loc].clone().pin_memory()
-    del b_full
-    b = b_host.to(dev)
-    plan = D._shard_plan()
-    nnz = plan.csr.nnz
-
-    def solve_once(bb):
-        x = D.solve_distributed_shard(bb, method="cg", preconditioner="jacobi", atol=0.0,
-                                      rtol=RTOL, maxiter=100000)
-        return x, D._last_info["iterations"]
-
-    for _ in range(args.warmup):
-        solve_once(b)
-    torch.cuda.synchronize()
-    dist.barrier()
-    L.profile_enable(True, 8)
-    launches0 = L.launch_count()
-    iters = 0
-    with Clocks(local) as clk:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        dist.barrier()
-        t0.record()
-        for _ in range(args.steps):
-            _, it = solve_once(b)
-            iters += it
-        t1.record()
-        torch.cuda.synchronize()
-        dist.barrier()
-    ms_local = t0.elapsed_time(t1)
-    launches = L.launch_count() - launches0
-    ka_ms, ka_n = L.profile_read(0)
-    kb_ms, kb_n = L.profile_read(1)
-    L.profile_enable(False)
-    t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    value = iters * world / (ms / 1e3)
-
-    # end to end through D.solve with b in pinned host memory, x read back
-    e_steps = max(1, min(args.steps, 3))
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    e_iters = 0
-    for _ in range(e_steps):
-        x, it = solve_once(b_host.to(dev, non_blocking=True))
-        x.cpu()
-        e_iters += it
-    e1.record()
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e_ms = float(te.item())
-
-    ka_interior = plan.sell_int.n_slots
-    ka_bytes = matrix_bytes(nnz, n_loc) + 5 * 8 * n_loc
-    ka_bytes_int = int(ka_bytes * ka_interior / max(n_loc, 1))
-    ka_avg = ka_ms / max(ka_n, 1)
-    peak, peak_kind = peaks()
-    achieved = ka_bytes_int / (ka_avg / 1e3) / 1e9 if ka_n else None
-    iter_bytes = matrix_bytes(nnz, n_loc) + 13 * 8 * n_loc
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "iterations/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic",
-            "config": {"workload": "jacobi_pcg_poisson3d_7pt", "grid": list(dims), "n": n_glob,
-                       "n_per_gpu": n_loc, "nnz_per_gpu": nnz, "rtol": RTOL,
-                       "b": "N(0,1) seed 1 (global vector)",
-                       "iterations_per_solve": iters // args.steps,
-                       "partition": "z-slabs (partition_simple), halo one z-layer per neighbour",
-                       "halo_bytes_per_neighbour": m * m * 8, "check_every": 10,
-                       "format": "SELL-32 int32 (sigma=1)", "l2": "inputs larger than L2",
-                       "parallelism": f"row-sharded x{world} (NCCL)"},
-            "iteration_roofline": {"bytes_per_iter_per_gpu": iter_bytes,
-                                   "achieved_gbs_per_gpu": round(iter_bytes * value / world / 1e9, 1),
-                                   "frac": round(iter_bytes * value / world / 1e9 / peak, 4),
-                                   "peak_kind": peak_kind},
-            "roofline": {"kernel": "shard_cg_spmv (interior rows)", "bound": "hbm",
-                         "achieved": None if achieved is None else round(achieved, 1),
-                         "peak": peak, "unit": "GB/s",
-                         "frac": None if achieved is None else round(achieved / peak, 4),
-                         "traffic": read_traffic("shard_cg_spmv"),
-                         "algorithmic_bytes": ka_bytes_int, "avg_launch_ms": round(ka_avg, 5),
-                         "sampled_launches": ka_n, "peak_kind": peak_kind},
-            "e2e": {"value": round(e_iters * world / (e_ms / 1e3), 2), "unit": "iterations/s",
-                    "h2d_bytes_per_step": n_loc * 8 * world, "d2h_bytes_per_step": n_loc * 8 * world,
-                    "ms_per_step": round(e_ms / e_steps, 3), "steps": e_steps,
-                    "note": "matrix setup (partition maps, CSR) done once before timing"},
-            "gpu_launches": launches,
-            "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
-    del D, plan
-    destroy_all()
-    dist.barrier()
-    dist.destroy_process_group()
 
 
 def main():
@@ -434,15 +600,23 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--workload", default="pcg7",
+                    choices=["pcg7", "cg2d", "spmv", "batched", "bicgstab", "pcg27"])
     ap.add_argument("--grid", type=int, default=M, help="grid edge per GPU (default 256)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     if args.impl == "reference":
-        run_reference(args)
-    else:
-        run_b200(args)
+        return run_reference(args)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1 or args.workload == "pcg27":
+        return run_sharded(args, world, rank, local)
+    dev = torch.device("cuda", local)
+    print(json.dumps(WORKLOADS[args.workload](args, dev, local)), flush=True)
 
 
 if __name__ == "__main__":

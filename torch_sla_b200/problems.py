@@ -21,16 +21,18 @@ def _strides(dims):
     return s
 
 
-def grid_coo(dims: Sequence[int], diag, edges, dtype=torch.float64, device="cpu"):
-    """Stencil COO: diagonal entries first, then one block per
-    (axis, step, weight) coupling, only where the neighbour is in-bounds;
-    couplings to the same neighbour stay separate entries (summed on
-    coalesce). Returns (val, row, col)."""
+def grid_coo_rows(dims: Sequence[int], z0: int, nz_local: int, diag, edges,
+                  dtype=torch.float64, device="cpu"):
+    """Rows of the stencil COO whose axis-0 coordinate lies in
+    [z0, z0 + nz_local), with GLOBAL indices: diagonal entries first, then one
+    block per (axis, step, weight) coupling, only where the neighbour is
+    in-bounds; couplings to the same neighbour stay separate entries (summed
+    on coalesce). Returns (val, row, col)."""
     dims = tuple(int(d) for d in dims)
-    n = math.prod(dims)
     st = _strides(dims)
-    p = torch.arange(n, device=device)
-    rows, cols, vals = [p], [p], [torch.full((n,), float(diag), dtype=dtype, device=device)]
+    p = torch.arange(nz_local * st[0], device=device, dtype=torch.int64) + z0 * st[0]
+    rows, cols = [p], [p]
+    vals = [torch.full((p.numel(),), float(diag), dtype=dtype, device=device)]
     for axis, step, w in edges:
         coord = (p // st[axis]) % dims[axis]
         nb = coord + step
@@ -40,6 +42,12 @@ def grid_coo(dims: Sequence[int], diag, edges, dtype=torch.float64, device="cpu"
         cols.append(src + step * st[axis])
         vals.append(torch.full((src.numel(),), float(w), dtype=dtype, device=device))
     return torch.cat(vals), torch.cat(rows), torch.cat(cols)
+
+
+def grid_coo(dims: Sequence[int], diag, edges, dtype=torch.float64, device="cpu"):
+    """The whole stencil COO (all rows) in grid_coo_rows' entry order."""
+    dims = tuple(int(d) for d in dims)
+    return grid_coo_rows(dims, 0, dims[0], diag, edges, dtype, device)
 
 
 def axis_edges(ndim: int, w):
@@ -127,24 +135,19 @@ def diffusion_2d_batched(batch: int, m: int, seed: int = 2, dtype=torch.float64,
 
 
 def poisson_3d_7pt_rows(dims, z0: int, nz_local: int, dtype=torch.float64, device="cpu"):
-    """Rows of the global 7-point Laplacian on dims = (nz, ny, nx) whose z lies
-    in [z0, z0 + nz_local), as COO with GLOBAL indices (diagonal first, then
-    the six neighbour blocks). Coalesces to the same rows as poisson_3d_7pt."""
-    nz, ny, nx = dims
-    sz = ny * nx
-    st = (sz, nx, 1)
-    p = torch.arange(nz_local * sz, device=device, dtype=torch.int64) + z0 * sz
-    coords = (p // sz, (p // nx) % ny, p % nx)
-    rows, cols, vals = [p], [p], [torch.full((p.numel(),), 6.0, dtype=dtype, device=device)]
-    for axis in range(3):
-        for step in (1, -1):
-            nb = coords[axis] + step
-            keep = (nb >= 0) & (nb < dims[axis])
-            src = p[keep]
-            rows.append(src)
-            cols.append(src + step * st[axis])
-            vals.append(torch.full((src.numel(),), -1.0, dtype=dtype, device=device))
-    return torch.cat(vals), torch.cat(rows), torch.cat(cols)
+    """Rows [z0, z0 + nz_local) of poisson_3d_7pt on dims = (nz, ny, nx)."""
+    return grid_coo_rows(dims, z0, nz_local, 6.0, axis_edges(3, -1.0), dtype, device)
+
+
+def convdiff_3d_upwind_rows(m: int, z0: int, nz_local: int, velocity=(10.0, 5.0, 2.5),
+                            diffusion: float = 1.0, dtype=torch.float64, device="cpu", nz=None):
+    """Rows [z0, z0 + nz_local) of the upwind convection-diffusion operator on
+    a (nz or m) x m x m grid with h = 1/(m+1) (convdiff_3d_upwind's stencil)."""
+    h = 1.0 / (m + 1)
+    inv = diffusion / (h * h)
+    edges = axis_edges(3, -inv) + [(a, -1, -velocity[a] / h) for a in range(3)]
+    return grid_coo_rows((nz or m, m, m), z0, nz_local, 6.0 * inv + sum(velocity) / h, edges,
+                         dtype, device)
 
 
 # --------------------------------------------------------------- 27-point
