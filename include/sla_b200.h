@@ -198,6 +198,21 @@ int sla_batched_cg(int dtype, const int32_t *rowptr, const int32_t *colind,
                    int64_t maxiter, void *workspace, size_t workspace_bytes,
                    sla_solve_info_t *info, sla_stream_t stream);
 
+/* CG on K right-hand sides of one CSR matrix (batched_pcg_solve,
+ * pytorch_backend.py:2352-2504; pytorch_solve with a 2-D b). b and x are
+ * [n][K] row-major (x holds the guess when x_is_guess != 0); dinv [n] or
+ * NULL. Convergence is tested every `check_every` iterations (50 in
+ * torch-sla); iters_out / converged_out (host, K entries, may be NULL)
+ * receive the per-column iteration counts and flags. */
+int sla_multi_rhs_cg_workspace(int dtype, int64_t n, int64_t k, size_t *bytes);
+int sla_multi_rhs_cg(int dtype, const int32_t *rowptr, const int32_t *colind,
+                     const void *vals, int64_t n, int64_t k, const void *dinv,
+                     const void *b, void *x, int x_is_guess, double atol,
+                     double rtol, int64_t maxiter, int64_t check_every,
+                     int64_t *iters_out, int32_t *converged_out,
+                     void *workspace, size_t workspace_bytes,
+                     sla_solve_info_t *info, sla_stream_t stream);
+
 /* -------------------------------------------------- row-sharded (NCCL) */
 /* Opaque NCCL communicator management (one process per GPU). */
 int sla_comm_unique_id(unsigned char id[128]);

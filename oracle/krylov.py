@@ -226,6 +226,55 @@ def batched_cg_same_pattern(val_batch, row, col, shape, b_batch, *, atol=1e-10, 
     return X, it
 
 
+# ------------------------------------------------------ multi-RHS CG
+def batched_pcg(val, row, col, shape, B, *, X0=None, atol=1e-10, rtol=1e-6, maxiter=10000,
+                dinv=None, check_interval=50):
+    """batched_pcg_solve (pytorch_backend.py:2352-2504) with a column-wise
+    diagonal preconditioner `dinv` ([n]) or none. Returns
+    (X, num_iters [K], residuals [K], converged [K])."""
+    A = csr(val, row, col, shape)
+    n, K = B.shape
+    apply_m = (lambda R: R) if dinv is None else (lambda R: dinv.unsqueeze(1) * R)
+    if X0 is None:
+        X = torch.zeros(n, K, dtype=B.dtype)
+        R = B.clone()
+    else:
+        X = X0.clone()
+        R = B - torch.mm(A, X)
+    Z = apply_m(R)
+    P = Z.clone()
+    rz = (R * Z).sum(dim=0)
+    bn = torch.norm(B, dim=0)
+    bn = torch.where(bn == 0, torch.ones_like(bn), bn)
+    tols = torch.maximum(torch.full_like(bn, atol), rtol * bn)
+    tols_sq = tols ** 2
+    conv = torch.zeros(K, dtype=torch.bool)
+    iters = torch.zeros(K, dtype=torch.int32)
+    for i in range(maxiter):
+        if bool(conv.all()):
+            break
+        AP = torch.mm(A, P) if K > 1 else torch.mv(A, P.squeeze(1)).unsqueeze(1)
+        PAP = (P * AP).sum(dim=0)
+        PAP = torch.where(PAP > 0, PAP, torch.ones_like(PAP))
+        alpha = rz / PAP
+        X = X + alpha.unsqueeze(0) * P
+        R = R - alpha.unsqueeze(0) * AP
+        if (i + 1) % check_interval == 0:
+            new = ((R * R).sum(dim=0) < tols_sq) & ~conv
+            iters[new] = i + 1
+            conv = conv | new
+            if bool(conv.all()):
+                break
+        Z = apply_m(R)
+        rz_next = (R * Z).sum(dim=0)
+        P = Z + (rz_next / (rz + 1e-30)).unsqueeze(0) * P
+        rz = rz_next
+    res = torch.norm(R, dim=0)
+    iters[~conv] = maxiter
+    conv = conv | (res < tols)
+    return X, iters, res, conv
+
+
 # -------------------------------------------------------- adjoints
 def adjoint(val, row, col, shape, u, gradu, *, method="cg", atol=1e-10, rtol=1e-10,
             maxiter=10000, precond="jacobi"):

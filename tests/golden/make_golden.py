@@ -111,6 +111,21 @@ def single(ref_path):
     bicg_case("bicg_ad2d12_maxiter", spec, prob.val, prob.row, prob.col, prob.shape, b, atol=0.0,
               rtol=1e-12, maxiter=5, preconditioner="jacobi")
 
+    # multi-RHS CG: pytorch_solve with a 2-D b ('none' -- its 'jacobi' closure
+    # does not broadcast over columns) and batched_cg_solve's column Jacobi
+    v, r, c, sh = P.poisson_2d_5pt(24)
+    g = torch.Generator().manual_seed(12)
+    Bm = torch.randn(sh[0], 5, generator=g, dtype=torch.float64)
+    Xm = PB.pytorch_solve(v, r, c, sh, Bm, method="cg", atol=1e-12, rtol=1e-9,
+                          preconditioner="none")
+    Am = PB.CachedSparseMatrix(v, r, c, sh)
+    res_n = PB.batched_pcg_solve(Am, Bm, atol=1e-12, rtol=1e-9,
+                                 preconditioner=PB.get_preconditioner(Am, "none"))
+    res_j = PB.batched_cg_solve(v, r, c, sh, Bm, atol=1e-12, rtol=1e-9, preconditioner="jacobi")
+    out["mrhs_2d24"] = {**gen("poisson_2d_5pt", 24), "B": Bm, "X_none": Xm.clone(),
+                        "iters_none": res_n.num_iters.clone(), "X_jacobi": res_j.X.clone(),
+                        "iters_jacobi": res_j.num_iters.clone()}
+
     # batched same-pattern CG (forward at rtol 1e-8; autograd path at its 1e-6)
     vb, r, c, sh, bb = P.diffusion_2d_batched(3, 12, seed=2)
     X = PB.batched_cg_same_pattern(vb, r, c, sh, bb, atol=0.0, rtol=1e-8, maxiter=10000)

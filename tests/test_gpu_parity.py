@@ -261,3 +261,37 @@ def test_sparse_tensor_solve_auto(dev, golden):
     v, r, c, sh = case_inputs(case)
     x = T.SparseTensor(*cu(v, r, c, dev=dev), sh).solve(case["b"].to(dev))
     assert rel(x, case["x"]) < 1e-8
+
+
+# ------------------------------------------------------------ multi-RHS CG
+def test_multi_rhs_cg_matches_reference(dev, golden):
+    case = golden["mrhs_2d24"]
+    v, r, c, sh = case_inputs(case)
+    vd, rd, cd = cu(v, r, c, dev=dev)
+    B = case["B"].to(dev)
+    X = T.pytorch_solve(vd, rd, cd, sh, B, method="cg", atol=1e-12, rtol=1e-9,
+                        preconditioner="none")
+    assert X.shape == B.shape and rel(X, case["X_none"]) < 1e-9
+    A = PB.CachedSparseMatrix(vd, rd, cd, sh)
+    res = PB.batched_pcg_solve(A, B, atol=1e-12, rtol=1e-9,
+                               preconditioner=PB.get_preconditioner(A, "none"))
+    assert torch.equal(res.num_iters.cpu(), case["iters_none"]) and bool(res.converged.all())
+    Xj = T.pytorch_solve(vd, rd, cd, sh, B, method="cg", atol=1e-12, rtol=1e-9,
+                         preconditioner="jacobi")
+    assert rel(Xj, case["X_jacobi"]) < 1e-9
+
+
+def test_multi_rhs_cg_guess_and_single_column(dev):
+    v, r, c, sh = P.poisson_3d_7pt(12)
+    g = torch.Generator().manual_seed(3)
+    B = torch.randn(sh[0], 3, generator=g, dtype=torch.float64)
+    X0 = torch.randn(sh[0], 3, generator=g, dtype=torch.float64)
+    d = 1.0 / K.diagonal(v, r, c, sh[0])
+    Xo, ito, _, _ = K.batched_pcg(v, r, c, sh, B, X0=X0, atol=0.0, rtol=1e-10, dinv=d)
+    A = PB.CachedSparseMatrix(*cu(v, r, c, dev=dev), sh)
+    res = PB.batched_pcg_solve(A, B.to(dev), X0=X0.to(dev), atol=0.0, rtol=1e-10,
+                               preconditioner=PB.get_preconditioner(A, "jacobi"))
+    assert torch.equal(res.num_iters.cpu(), ito) and rel(res.X, Xo) < 1e-9
+    x1 = T.pytorch_solve(*cu(v, r, c, dev=dev), sh, B[:, :1].to(dev), method="cg", atol=0.0,
+                         rtol=1e-10, preconditioner="jacobi")
+    assert x1.shape == (sh[0], 1) and rel(x1[:, 0], Xo[:, 0]) < 1e-8

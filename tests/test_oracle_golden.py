@@ -116,3 +116,14 @@ def test_oracle_shard_solvers_match_reference(golden_shard, name):
     assert it == case["iters"]
     # the reference sums each dot product per rank before the allreduce
     torch.testing.assert_close(x, case["x"], rtol=1e-9, atol=1e-12)
+
+
+def test_oracle_multi_rhs_matches_reference(golden):
+    case = golden["mrhs_2d24"]
+    v, r, c, sh = case_inputs(case)
+    X, it, _, conv = K.batched_pcg(v, r, c, sh, case["B"], atol=1e-12, rtol=1e-9)
+    assert torch.equal(X, case["X_none"]) and torch.equal(it, case["iters_none"]) and conv.all()
+    d = 1.0 / K.diagonal(v, r, c, sh[0])
+    d = torch.where(torch.isinf(d), torch.ones_like(d), d)
+    Xj, itj, _, _ = K.batched_pcg(v, r, c, sh, case["B"], atol=1e-12, rtol=1e-9, dinv=d)
+    assert torch.equal(Xj, case["X_jacobi"]) and torch.equal(itj, case["iters_jacobi"])

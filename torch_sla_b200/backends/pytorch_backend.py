@@ -220,8 +220,10 @@ def pytorch_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int],
     L.require_cuda(val, b)
     if method == "cg":
         if b.dim() == 2:
-            raise NotImplementedError("torch_sla_b200: multi-RHS CG (b of shape [n, K]) is "
-                                      "not implemented yet; solve the columns one by one")
+            A_mat = CachedSparseMatrix(val, row, col, shape)
+            M = get_preconditioner(A_mat, preconditioner)
+            return batched_pcg_solve(A_mat, b, X0=x0, atol=atol, rtol=rtol, maxiter=maxiter,
+                                     preconditioner=M).X
         if mixed_precision and val.dtype == torch.float32:
             raise NotImplementedError("torch_sla_b200: mixed-precision PCG is not part of the "
                                       "B200 path")
@@ -239,6 +241,73 @@ def pytorch_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int],
         raise NotImplementedError(f"torch_sla_b200: method {method!r} is outside the B200 "
                                   "hot path (cg, bicgstab)")
     raise ValueError(f"Unknown method: {method}. Available: cg, bicgstab, gmres, minres, lsqr, lsmr")
+
+
+# ----------------------------------------------------------- multi-RHS CG
+class BatchSolveResult(NamedTuple):
+    """Result of the multi-RHS solve (pytorch_backend.py:2344-2349)."""
+    X: Tensor
+    num_iters: Tensor
+    residuals: Tensor
+    converged: Tensor
+
+
+def batched_pcg_solve(A: CachedSparseMatrix, B: Tensor, X0: Optional[Tensor] = None,
+                      atol: float = 1e-10, rtol: float = 1e-6, maxiter: int = 10000,
+                      preconditioner=None, check_interval: int = 50) -> BatchSolveResult:
+    """CG on the K columns of B (n, K) together (pytorch_backend.py:2352-2504).
+
+    Jacobi is applied column by column. (torch-sla's own pytorch_solve hands
+    its 1-D Jacobi closure a 2-D residual, which fails to broadcast unless
+    n == K; the column-wise form here is what its batched_cg_solve wrapper
+    and preconditioner=None do.)
+    """
+    L.require_cuda(B, X0)
+    if B.dim() == 1:
+        B = B.unsqueeze(1)
+    n, K = int(B.shape[0]), int(B.shape[1])
+    if n != A.n:
+        raise ValueError(f"torch_sla_b200: B must have {A.n} rows")
+    if preconditioner is None:
+        d = 1.0 / A.diagonal
+        dinv = torch.where(torch.isinf(d), torch.ones_like(d), d).contiguous()
+    else:
+        dinv = _as_dinv(preconditioner, A)
+    Bc = B.to(A.dtype).contiguous()
+    lib = L.lib()
+    X = torch.empty_like(Bc)
+    guess = X0 is not None
+    if guess:
+        X.copy_(X0 if X0.dim() == 2 else X0.unsqueeze(1))
+    iters = torch.zeros(K, dtype=torch.int64)
+    conv = torch.zeros(K, dtype=torch.int32)
+    info = L.SolveInfo()
+    for k0 in range(0, K, _MAX_BATCH):
+        k1 = min(K, k0 + _MAX_BATCH)
+        kk = k1 - k0
+        Bk = Bc if kk == K else Bc[:, k0:k1].contiguous()
+        Xk = X if kk == K else X[:, k0:k1].contiguous()
+        need = ctypes.c_size_t(0)
+        L.check("sla_multi_rhs_cg_workspace",
+                lib.sla_multi_rhs_cg_workspace(A.csr.code, n, kk, ctypes.byref(need)))
+        ws = L.workspace(need.value, A.device)
+        st = lib.sla_multi_rhs_cg(A.csr.code, L.ptr(A.csr.rowptr), L.ptr(A.csr.colind),
+                                  L.ptr(A.csr.vals), n, kk, L.ptr(dinv), L.ptr(Bk), L.ptr(Xk),
+                                  int(guess), float(atol), float(rtol), int(maxiter),
+                                  int(check_interval), iters[k0:k1].data_ptr(),
+                                  conv[k0:k1].data_ptr(), L.ptr(ws), ws.numel(),
+                                  ctypes.byref(info), L.stream_handle(A.device))
+        L.check("sla_multi_rhs_cg", st)
+        if kk != K:
+            X[:, k0:k1].copy_(Xk)
+    _record("multi_rhs_cg", info)
+    R = Bc - torch.stack([A.matvec(X[:, j].contiguous()) for j in range(K)], dim=1)
+    residuals = torch.linalg.vector_norm(R, dim=0)
+    converged = conv.to(torch.bool).to(A.device)
+    if not bool(converged.all()):
+        n_failed = int((~converged).sum().item())
+        warnings.warn(f"Batched PCG: {n_failed}/{K} RHS did not converge in {maxiter} iterations")
+    return BatchSolveResult(X, iters.to(torch.int32).to(A.device), residuals, converged)
 
 
 # ----------------------------------------------------------------- batched

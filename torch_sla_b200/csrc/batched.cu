@@ -8,7 +8,7 @@
 // fixed order (rows of the block, then blocks), so results are
 // deterministic. Stops when every ||R_b|| <= max(atol, rtol*||b_b||), with
 // all members iterating until then, as the reference does.
-#include "solver.cuh"
+#include "batch.cuh"
 
 namespace sla {
 
@@ -25,53 +25,6 @@ struct BatchState {
 struct BatchScalars {
   double *rz, *alpha, *beta, *tol, *rr;
 };
-
-inline int batch_block(int64_t B) {
-  if (B <= 256) return (int)(B * (256 / B));
-  return (int)B;
-}
-
-// Per-member totals over all rows: thread tid<B ends with member tid's sum.
-// acc is this thread's partial for member (threadIdx.x % B).
-template <int NV>
-__device__ bool batch_last_block(double (&acc)[NV], int B, double *smem, double *partials,
-                                 unsigned *counter) {
-  __shared__ unsigned s_last;
-  const int TB = blockDim.x;
-  const int rpb = TB / B;
-  const unsigned G = gridDim.x;
-#pragma unroll
-  for (int k = 0; k < NV; ++k) smem[k * TB + threadIdx.x] = acc[k];
-  __syncthreads();
-  if (threadIdx.x < B) {
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      double t = 0.0;
-      for (int q = 0; q < rpb; ++q) t += smem[k * TB + q * B + threadIdx.x];
-      partials[((size_t)k * B + threadIdx.x) * G + blockIdx.x] = t;
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned t = atomicAdd(counter, 1u);
-    s_last = (t == G - 1) ? 1u : 0u;
-  }
-  __syncthreads();
-  if (!s_last) return false;
-  __threadfence();
-  if (threadIdx.x < B) {
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-      double t = 0.0;
-      const double *pp = partials + ((size_t)k * B + threadIdx.x) * G;
-      for (unsigned g = 0; g < G; ++g) t += ld_l2(pp + g);
-      acc[k] = t;
-    }
-  }
-  if (threadIdx.x == 0) *counter = 0u;
-  return true;
-}
 
 template <typename T>
 __global__ void __launch_bounds__(1024)
@@ -200,14 +153,6 @@ __global__ void batch_unpack_kernel(int64_t n, int B, const T *__restrict__ xi, 
     int64_t b = t / n, row = t - b * n;
     xo[t] = xi[row * B + b];
   }
-}
-
-static int batch_grid(int64_t n, int B) {
-  int tb = batch_block(B);
-  int rpb = tb / B;
-  int64_t want = (n + rpb - 1) / rpb;
-  int64_t cap = (int64_t)device_info().sm_count * (2048 / tb > 0 ? 2048 / tb : 1);
-  return (int)(want < cap ? (want < 1 ? 1 : want) : cap);
 }
 
 static size_t batch_ws_bytes(size_t elem, int64_t n, int64_t B, int G) {

@@ -104,15 +104,15 @@ bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T 
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[1] = {0.0};
-  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
-    T sum = sell_row(A, s, lane, g);
+  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at(A, sbase, swidth, lane, g);
     int64_t row = s * 32 + lane;
     if (row < A.n_slots) {
       p_new[row] = g.pval((int32_t)row);
       v_new[row] = sum;
       acc[0] += (double)rhat[row] * (double)sum;
     }
-  }
+  });
   if (last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem) && threadIdx.x == 0)
     st->alpha = st->rho_new / acc[0];
 }
@@ -128,8 +128,8 @@ bicg_k2(Sell<T> A, const T *__restrict__ r, const T *__restrict__ v, const T *__
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[3] = {0.0, 0.0, 0.0};
-  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
-    T sum = sell_row(A, s, lane, g);
+  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at(A, sbase, swidth, lane, g);
     int64_t row = s * 32 + lane;
     if (row < A.n_slots) {
       T si = g.sval((int32_t)row);
@@ -138,7 +138,7 @@ bicg_k2(Sell<T> A, const T *__restrict__ r, const T *__restrict__ v, const T *__
       acc[1] += (double)sum * (double)sum;
       acc[2] += (double)sum * (double)si;
     }
-  }
+  });
   if (last_block_sum<3, kBlock>(acc, partials, &st->counter[2], smem) && threadIdx.x == 0) {
     st->ss = acc[0];
     st->tt = acc[1];

@@ -100,8 +100,8 @@ cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   CgPGather<T, PREC, false> g{r, dinv, p_old, (T)st->beta};
   double acc[1] = {0.0};
-  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
-    T sum = sell_row(A, s, lane, g);
+  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at(A, sbase, swidth, lane, g);
     int64_t row = s * 32 + lane;
     if (row < A.n_slots) {
       T pn = g((int32_t)row);
@@ -109,7 +109,7 @@ cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
       Ap[row] = sum;
       acc[0] += (double)pn * (double)sum;
     }
-  }
+  });
   if (last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem) && threadIdx.x == 0) {
     st->pAp = acc[0];
     st->alpha = st->rz / acc[0];
@@ -206,8 +206,8 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
     // phase A: p_new = p_old*beta + M^{-1} r (fused into the gather), Ap = A p_new
     CgPGather<T, PREC, true> g{r, dinv, p_old, (T)beta};
     double a1[1] = {0.0};
-    for (int64_t s = warp; s < A.n_slices; s += nwarps) {
-      T sum = sell_row(A, s, lane, g);
+    for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+      T sum = sell_row_at(A, sbase, swidth, lane, g);
       int64_t row = s * 32 + lane;
       if (row < n) {
         T pn = g((int32_t)row);
@@ -215,7 +215,7 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
         Ap[row] = sum;
         a1[0] += (double)pn * (double)sum;
       }
-    }
+    });
     block_sum<1, kBlock>(a1, smem);
     if (threadIdx.x == 0) partA[blockIdx.x] = a1[0];
     if (!grid_sync(&st->bar)) { done = kTimeout; break; }

@@ -46,11 +46,11 @@ inline bool sell_ok(const sla_sell_t *A) {
 // load -> gather round trip (7-point rows fit one batch, 27-point rows four).
 constexpr int kRowBatch = 8;
 
-// sum_j val[j] * g(col[j]) over the entries of this lane's slot.
+// sum_j val[j] * g(col[j]) over the entries of this lane's slot of the slice
+// starting at entry `base` with `width` entries per slot.
 template <typename T, typename G>
-__device__ __forceinline__ T sell_row(const Sell<T> &A, int64_t slice, int lane, const G &g) {
-  const int32_t base = A.slice_ptr[slice];
-  const int width = (A.slice_ptr[slice + 1] - base) >> 5;
+__device__ __forceinline__ T sell_row_at(const Sell<T> &A, int32_t base, int width, int lane,
+                                         const G &g) {
   const int32_t *__restrict__ cp = A.col + base + lane;
   const T *__restrict__ vp = A.val + base + lane;
   T sum = T(0);
@@ -73,6 +73,37 @@ __device__ __forceinline__ T sell_row(const Sell<T> &A, int64_t slice, int lane,
     for (int u = 0; u < kRowBatch; ++u) sum = fma(v[u], x[u], sum);
   }
   return sum;
+}
+
+template <typename T, typename G>
+__device__ __forceinline__ T sell_row(const Sell<T> &A, int64_t slice, int lane, const G &g) {
+  const int32_t base = A.slice_ptr[slice];
+  return sell_row_at(A, base, (A.slice_ptr[slice + 1] - base) >> 5, lane, g);
+}
+
+// Grid-stride walk over the slices owned by this warp (slices warp,
+// warp + nwarps, ...). The slice pointers of the next 32 slices are fetched
+// by the 32 lanes at once and broadcast by shuffles, so a slice's column and
+// value loads never wait on a dependent slice_ptr load.
+// body(slice, base, width) is called with warp-uniform arguments.
+template <typename T, typename Body>
+__device__ __forceinline__ void for_each_slice(const Sell<T> &A, int64_t warp, int64_t nwarps,
+                                               int lane, Body body) {
+  for (int64_t s0 = warp; s0 < A.n_slices; s0 += 32 * nwarps) {
+    const int64_t mine = s0 + (int64_t)lane * nwarps;
+    int32_t b0 = 0, b1 = 0;
+    if (mine < A.n_slices) {
+      b0 = __ldg(A.slice_ptr + mine);
+      b1 = __ldg(A.slice_ptr + mine + 1);
+    }
+    const int64_t left = (A.n_slices - s0 + nwarps - 1) / nwarps;
+    const int count = left < 32 ? (int)left : 32;
+    for (int q = 0; q < count; ++q) {
+      const int32_t base = __shfl_sync(kFull, b0, q);
+      const int32_t end = __shfl_sync(kFull, b1, q);
+      body(s0 + (int64_t)q * nwarps, base, (end - base) >> 5);
+    }
+  }
 }
 
 // Blocks per SM the SpMV-bearing kernels are compiled for (register cap):

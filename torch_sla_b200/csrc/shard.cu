@@ -151,11 +151,11 @@ shard_spmv_rows_kernel(Sell<T> A, G g, T *__restrict__ y) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
-    T sum = sell_row(A, s, lane, g);
+  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at(A, sbase, swidth, lane, g);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) y[A.row_ids ? A.row_ids[slot] : slot] = sum;
-  }
+  });
 }
 
 // ================================================================ shard CG
@@ -260,8 +260,8 @@ shard_cg_spmv(Sell<T> A, int32_t n_own, const T *__restrict__ r, const T *__rest
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[1] = {0.0};
-  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
-    T sum = HALO ? sell_row(A, s, lane, g) : sell_row(A, s, lane, inner);
+  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = HALO ? sell_row_at(A, sbase, swidth, lane, g) : sell_row_at(A, sbase, swidth, lane, inner);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
       int32_t row = A.row_ids[slot];
@@ -270,7 +270,7 @@ shard_cg_spmv(Sell<T> A, int32_t n_own, const T *__restrict__ r, const T *__rest
       Ap[row] = sum;
       acc[0] += (double)pn * (double)sum;
     }
-  }
+  });
   if (last_block_sum<1, kBlock>(acc, partials, &st->counter[HALO ? 2 : 1], smem) &&
       threadIdx.x == 0) {
     if (!HALO) st->pap_int = acc[0];
@@ -425,8 +425,8 @@ shard_bi_k1(Sell<T> A, int32_t n_own, BiP<T, PREC> g0, const T *__restrict__ pha
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[1] = {0.0};
-  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
-    T sum = HALO ? sell_row(A, s, lane, g) : sell_row(A, s, lane, inner);
+  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = HALO ? sell_row_at(A, sbase, swidth, lane, g) : sell_row_at(A, sbase, swidth, lane, inner);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
       int32_t row = A.row_ids[slot];
@@ -434,7 +434,7 @@ shard_bi_k1(Sell<T> A, int32_t n_own, BiP<T, PREC> g0, const T *__restrict__ pha
       v[row] = sum;
       acc[0] += (double)rhat[row] * (double)sum;
     }
-  }
+  });
   if (last_block_sum<1, kBlock>(acc, partials, &st->counter[HALO ? 2 : 1], smem) &&
       threadIdx.x == 0) {
     if (!HALO) st->pap_int = acc[0];
@@ -466,8 +466,8 @@ shard_bi_k2(Sell<T> A, int32_t n_own, BiS<T, PREC> g0, const T *__restrict__ sha
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[3] = {0.0, 0.0, 0.0};
-  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
-    T sum = HALO ? sell_row(A, s, lane, g) : sell_row(A, s, lane, inner);
+  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = HALO ? sell_row_at(A, sbase, swidth, lane, g) : sell_row_at(A, sbase, swidth, lane, inner);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
       int32_t row = A.row_ids[slot];
@@ -477,7 +477,7 @@ shard_bi_k2(Sell<T> A, int32_t n_own, BiS<T, PREC> g0, const T *__restrict__ sha
       acc[1] += (double)sum * (double)sum;
       acc[2] += (double)sum * (double)si;
     }
-  }
+  });
   if (last_block_sum<3, kBlock>(acc, partials, &st->counter[HALO ? 4 : 3], smem) &&
       threadIdx.x == 0) {
     if (!HALO) {

@@ -11,14 +11,14 @@ __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks) spmv_kernel(Sell<T> A,
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   PlainGather<T> g{x};
-  for (int64_t s = warp; s < A.n_slices; s += nwarps) {
-    T sum = sell_row(A, s, lane, g);
+  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at(A, sbase, swidth, lane, g);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
       int64_t row = A.row_ids ? A.row_ids[slot] : slot;
       y[row] = sum;
     }
-  }
+  });
 }
 
 template <typename T>
