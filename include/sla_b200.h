@@ -73,6 +73,9 @@ typedef struct {
   const void *val;           /* device, same length, dtype T                 */
   const int32_t *row_ids;    /* device [n_slots] row of each slot, or NULL
                                 when slot i is row i                          */
+  int32_t max_width;         /* widest slice (entries per slot)              */
+  int32_t uniform_width;     /* W when every slice has width W (then
+                                slice_ptr[s] == 32*W*s), else 0               */
 } sla_sell_t;
 
 typedef struct {
@@ -108,10 +111,13 @@ int sla_csr_build(int dtype, const int64_t *row, const int64_t *col,
 
 /* ------------------------------------------------------------- SELL-32 */
 /* Layout of a SELL-32 view over the CSR rows listed in row_ids (or rows
- * 0..n_slots-1). Writes slice_ptr and returns the padded entry count. */
+ * 0..n_slots-1), every slice padded to at least min_width entries per slot
+ * (min_width = the widest row gives a uniform-width layout). Writes
+ * slice_ptr and returns the padded entry count and the widest slice. */
 int sla_sell_layout_workspace(int64_t n_slots, size_t *bytes);
 int sla_sell_layout(const int32_t *rowptr, const int32_t *row_ids,
-                    int64_t n_slots, int32_t *slice_ptr, int64_t *padded_out,
+                    int64_t n_slots, int32_t min_width, int32_t *slice_ptr,
+                    int64_t *padded_out, int32_t *max_width_out,
                     void *workspace, size_t workspace_bytes,
                     sla_stream_t stream);
 int sla_sell_fill(int dtype, const int32_t *rowptr, const int32_t *colind,

@@ -15,14 +15,20 @@ from . import _lib as L
 
 
 class Sell:
-    """SELL-32 view (slice pointers, padded columns/values) of some CSR rows."""
+    """SELL-32 view (slice pointers, padded columns/values) of some CSR rows.
 
-    def __init__(self, slice_ptr, col, val, n_slots, row_ids=None):
+    uniform_width > 0 marks a layout whose slices all have that width, which
+    the kernels address arithmetically."""
+
+    def __init__(self, slice_ptr, col, val, n_slots, row_ids=None, max_width=0,
+                 uniform_width=0):
         self.slice_ptr, self.col, self.val, self.row_ids = slice_ptr, col, val, row_ids
         self.n_slots = int(n_slots)
         self.n_slices = (self.n_slots + 31) // 32
+        self.max_width = int(max_width)
+        self.uniform_width = int(uniform_width)
         self.view = L.SellView(self.n_slots, self.n_slices, L.ptr(slice_ptr), L.ptr(col),
-                               L.ptr(val), L.ptr(row_ids))
+                               L.ptr(val), L.ptr(row_ids), self.max_width, self.uniform_width)
 
     def ref(self):
         return ctypes.byref(self.view)
@@ -96,16 +102,29 @@ class DeviceCSR:
         L.check("sla_sell_layout_workspace", lib.sla_sell_layout_workspace(n_slots, ctypes.byref(need)))
         ws = L.workspace(need.value, dev)
         padded = ctypes.c_int64(0)
+        widest = ctypes.c_int32(0)
         stream = L.stream_handle(dev)
-        L.check("sla_sell_layout", lib.sla_sell_layout(
-            L.ptr(self.rowptr), L.ptr(row_ids), n_slots, L.ptr(slice_ptr), ctypes.byref(padded),
-            L.ptr(ws), ws.numel(), stream))
+
+        def layout(min_width):
+            L.check("sla_sell_layout", lib.sla_sell_layout(
+                L.ptr(self.rowptr), L.ptr(row_ids), n_slots, int(min_width), L.ptr(slice_ptr),
+                ctypes.byref(padded), ctypes.byref(widest), L.ptr(ws), ws.numel(), stream))
+
+        layout(0)
+        uniform = 0
+        w = int(widest.value)
+        # pad every slice to the widest one when that costs <= 3 % more
+        # entries: the kernels then address slices arithmetically
+        if 0 < w <= 32 and n_slices * 32 * w <= 1.03 * padded.value:
+            layout(w)
+            uniform = w
         scol = torch.empty(max(padded.value, 1), dtype=torch.int32, device=dev)
         sval = torch.empty(max(padded.value, 1), dtype=self.dtype, device=dev)
         L.check("sla_sell_fill", lib.sla_sell_fill(
             self.code, L.ptr(self.rowptr), L.ptr(self.colind), L.ptr(vals), L.ptr(row_ids), n_slots,
             L.ptr(slice_ptr), L.ptr(scol), L.ptr(sval), stream))
-        s = Sell(slice_ptr, scol, sval, n_slots, row_ids)
+        s = Sell(slice_ptr, scol, sval, n_slots, row_ids, max_width=widest.value,
+                 uniform_width=uniform)
         if row_ids is None and values is None:
             self._sell = s
         return s

@@ -29,7 +29,8 @@ c_i32, c_i64, c_dbl, c_ptr, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_dou
 
 class SellView(ctypes.Structure):
     _fields_ = [("n_slots", c_i64), ("n_slices", c_i64), ("slice_ptr", c_ptr),
-                ("col", c_ptr), ("val", c_ptr), ("row_ids", c_ptr)]
+                ("col", c_ptr), ("val", c_ptr), ("row_ids", c_ptr), ("max_width", c_i32),
+                ("uniform_width", c_i32)]
 
 
 class SolveInfo(ctypes.Structure):
@@ -55,8 +56,8 @@ _SIGNATURES = {
                                      c_ptr, c_ptr, c_ptr, c_ptr, c_ptr, _P(c_i64), c_ptr, c_sz,
                                      c_ptr]),
     "sla_sell_layout_workspace": (ctypes.c_int, [c_i64, _P(c_sz)]),
-    "sla_sell_layout": (ctypes.c_int, [c_ptr, c_ptr, c_i64, c_ptr, _P(c_i64), c_ptr, c_sz,
-                                       c_ptr]),
+    "sla_sell_layout": (ctypes.c_int, [c_ptr, c_ptr, c_i64, c_i32, c_ptr, _P(c_i64), _P(c_i32),
+                                       c_ptr, c_sz, c_ptr]),
     "sla_sell_fill": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr,
                                      c_ptr, c_ptr, c_ptr]),
     "sla_jacobi_inverse": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_i64,

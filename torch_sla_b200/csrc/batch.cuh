@@ -6,6 +6,34 @@
 
 namespace sla {
 
+// sum_k val(k) * g(colind[k]) over the CSR entries [k0, k1), in load batches
+// of kRowBatch (all column/value loads of a batch, then all its gathers), in
+// ascending k order.
+template <typename T, typename V, typename G>
+__device__ __forceinline__ T csr_row_batched(const int32_t *__restrict__ colind, int32_t k0,
+                                             int32_t k1, const V &val, const G &g) {
+  T sum = T(0);
+  for (int32_t kb = k0; kb < k1; kb += kRowBatch) {
+    int32_t c[kRowBatch];
+    T v[kRowBatch], x[kRowBatch];
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) {
+      if (kb + u < k1) {
+        c[u] = __ldg(colind + kb + u);
+        v[u] = val(kb + u);
+      } else {
+        c[u] = -1;
+        v[u] = T(0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) x[u] = c[u] >= 0 ? g(c[u]) : T(0);
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) sum = fma(v[u], x[u], sum);
+  }
+  return sum;
+}
+
 inline int batch_block(int64_t B) {
   if (B <= 256) return (int)(B * (256 / B));
   return (int)B;

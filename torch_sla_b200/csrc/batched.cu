@@ -80,13 +80,13 @@ batch_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict_
   if (rl < rpb) {
     const T beta = (T)sc.beta[bi];
     for (int64_t row = (int64_t)blockIdx.x * rpb + rl; row < n; row += (int64_t)gridDim.x * rpb) {
-      T sum = T(0);
-      const int32_t k0 = rowptr[row], k1 = rowptr[row + 1];
-      for (int32_t k = k0; k < k1; ++k) {
-        const int64_t c = (int64_t)__ldg(colind + k) * B + bi;
-        T pc = add_rn(mul_rn(__ldg(p_old + c), beta), mul_rn(__ldg(dinv + c), __ldg(r + c)));
-        sum = fma(ld_stream(vals + (int64_t)k * B + bi), pc, sum);
-      }
+      const T sum = csr_row_batched<T>(
+          colind, rowptr[row], rowptr[row + 1],
+          [&](int32_t k) { return ld_stream(vals + (int64_t)k * B + bi); },
+          [&](int32_t ci) {
+            const int64_t c = (int64_t)ci * B + bi;
+            return add_rn(mul_rn(__ldg(p_old + c), beta), mul_rn(__ldg(dinv + c), __ldg(r + c)));
+          });
       const int64_t o = row * B + bi;
       T pn = add_rn(mul_rn(p_old[o], beta), mul_rn(dinv[o], r[o]));
       p_new[o] = pn;

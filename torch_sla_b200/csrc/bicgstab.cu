@@ -91,7 +91,7 @@ bicg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T 
   }
 }
 
-template <typename T, bool PREC>
+template <typename T, bool PREC, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T *__restrict__ p_old,
         const T *__restrict__ v_old, const T *__restrict__ dinv, T *__restrict__ p_new,
@@ -104,8 +104,8 @@ bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T 
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[1] = {0.0};
-  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at(A, sbase, swidth, lane, g);
+  for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
     int64_t row = s * 32 + lane;
     if (row < A.n_slots) {
       p_new[row] = g.pval((int32_t)row);
@@ -117,7 +117,7 @@ bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T 
     st->alpha = st->rho_new / acc[0];
 }
 
-template <typename T, bool PREC>
+template <typename T, bool PREC, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 bicg_k2(Sell<T> A, const T *__restrict__ r, const T *__restrict__ v, const T *__restrict__ dinv,
         T *__restrict__ t, BicgState *st, double *partials) {
@@ -128,8 +128,8 @@ bicg_k2(Sell<T> A, const T *__restrict__ r, const T *__restrict__ v, const T *__
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[3] = {0.0, 0.0, 0.0};
-  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at(A, sbase, swidth, lane, g);
+  for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
     int64_t row = s * 32 + lane;
     if (row < A.n_slots) {
       T si = g.sval((int32_t)row);
@@ -203,7 +203,7 @@ static size_t bicg_ws_bytes(size_t elem, int64_t n) {
          align_up(sizeof(BicgState));
 }
 
-template <typename T, bool PREC>
+template <typename T, bool PREC, int WS>
 static int bicg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool guess,
                      double atol, double rtol, int64_t maxiter, void *ws, size_t ws_bytes,
                      sla_solve_info_t *info, cudaStream_t s) {
@@ -223,19 +223,19 @@ static int bicg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool
   if (guess) SLA_TRY(spmv_launch<T>(Ad, x, t, s));
   SLA_LAUNCH(bicg_init_kernel<T>, grid_for(n), kBlock, 0, s, n, b, x, guess ? t : nullptr, r, rhat,
              pA, vA, st, part[0], atol, rtol);
-  const int g1 = occupancy_grid((const void *)bicg_k1<T, PREC>);
-  const int g2 = occupancy_grid((const void *)bicg_k2<T, PREC>);
+  const int g1 = occupancy_grid((const void *)bicg_k1<T, PREC, WS>);
+  const int g2 = occupancy_grid((const void *)bicg_k2<T, PREC, WS>);
   const int g3 = occupancy_grid((const void *)bicg_k3<T, PREC>);
   SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
     T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
     T *v_old = (it & 1) ? vB : vA, *v_new = (it & 1) ? vA : vB;
     cudaEvent_t ev;
     profiler().begin(0, it, s, &ev);
-    SLA_LAUNCH((bicg_k1<T, PREC>), g1, kBlock, 0, s, A, r, rhat, p_old, v_old, dinv, p_new, v_new,
+    SLA_LAUNCH((bicg_k1<T, PREC, WS>), g1, kBlock, 0, s, A, r, rhat, p_old, v_old, dinv, p_new, v_new,
                st, part[1]);
     profiler().end(0, s, ev);
     profiler().begin(1, it, s, &ev);
-    SLA_LAUNCH((bicg_k2<T, PREC>), g2, kBlock, 0, s, A, r, v_new, dinv, t, st, part[2]);
+    SLA_LAUNCH((bicg_k2<T, PREC, WS>), g2, kBlock, 0, s, A, r, v_new, dinv, t, st, part[2]);
     profiler().end(1, s, ev);
     profiler().begin(2, it, s, &ev);
     SLA_LAUNCH((bicg_k3<T, PREC>), g3, kBlock, 0, s, n, x, r, rhat, p_new, v_new, t, dinv, st,
@@ -278,19 +278,20 @@ int sla_bicgstab(int dtype, const sla_sell_t *A, const void *dinv, const void *b
   if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
   cudaStream_t s = (cudaStream_t)stream;
   bool g = x_is_guess != 0;
+  const int wspec = width_spec(A);
   if (dtype == SLA_F64) {
     if (dinv)
-      return bicg_impl<double, true>(A, (const double *)dinv, (const double *)b, (double *)x, g,
-                                     atol, rtol, maxiter, workspace, workspace_bytes, info, s);
-    return bicg_impl<double, false>(A, nullptr, (const double *)b, (double *)x, g, atol, rtol,
-                                    maxiter, workspace, workspace_bytes, info, s);
+      SLA_WS_DISPATCH(wspec, return bicg_impl<double, true, WS>(A, (const double *)dinv, (const double *)b, (double *)x, g,
+                                     atol, rtol, maxiter, workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return bicg_impl<double, false, WS>(A, nullptr, (const double *)b, (double *)x, g, atol, rtol,
+                                    maxiter, workspace, workspace_bytes, info, s));
   }
   if (dtype == SLA_F32) {
     if (dinv)
-      return bicg_impl<float, true>(A, (const float *)dinv, (const float *)b, (float *)x, g, atol,
-                                    rtol, maxiter, workspace, workspace_bytes, info, s);
-    return bicg_impl<float, false>(A, nullptr, (const float *)b, (float *)x, g, atol, rtol, maxiter,
-                                   workspace, workspace_bytes, info, s);
+      SLA_WS_DISPATCH(wspec, return bicg_impl<float, true, WS>(A, (const float *)dinv, (const float *)b, (float *)x, g, atol,
+                                    rtol, maxiter, workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return bicg_impl<float, false, WS>(A, nullptr, (const float *)b, (float *)x, g, atol, rtol, maxiter,
+                                   workspace, workspace_bytes, info, s));
   }
   return SLA_ERR_INVALID;
 }

@@ -88,7 +88,7 @@ cg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *_
   }
 }
 
-template <typename T, bool PREC>
+template <typename T, bool PREC, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
                const T *__restrict__ p_old, T *__restrict__ p_new, T *__restrict__ Ap, CgState *st,
@@ -100,8 +100,8 @@ cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   CgPGather<T, PREC, false> g{r, dinv, p_old, (T)st->beta};
   double acc[1] = {0.0};
-  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at(A, sbase, swidth, lane, g);
+  for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
     int64_t row = s * 32 + lane;
     if (row < A.n_slots) {
       T pn = g((int32_t)row);
@@ -183,7 +183,7 @@ cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__res
   }
 }
 
-template <typename T, bool PREC>
+template <typename T, bool PREC, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
                      const T *__restrict__ dinv, T *pA, T *pB, T *__restrict__ Ap, CgState *st,
@@ -206,8 +206,8 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
     // phase A: p_new = p_old*beta + M^{-1} r (fused into the gather), Ap = A p_new
     CgPGather<T, PREC, true> g{r, dinv, p_old, (T)beta};
     double a1[1] = {0.0};
-    for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-      T sum = sell_row_at(A, sbase, swidth, lane, g);
+    for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+      T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
       int64_t row = s * 32 + lane;
       if (row < n) {
         T pn = g((int32_t)row);
@@ -260,7 +260,7 @@ static size_t cg_ws_bytes(size_t elem, int64_t n) {
 template <typename T>
 int spmv_launch(const sla_sell_t *A, const void *x, void *y, cudaStream_t s);
 
-template <typename T, bool PREC>
+template <typename T, bool PREC, int WS>
 static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool guess,
                     double atol, double rtol, int64_t maxiter, int flags, void *ws,
                     size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
@@ -285,7 +285,7 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
   if (flags != SLA_PCG_STREAMED && dev.coop) {
     int per_sm = 0;
     SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, cg_persistent_kernel<T, PREC>, kBlock, 0));
+        &per_sm, cg_persistent_kernel<T, PREC, WS>, kBlock, 0));
     int want = (int)((n + kBlock - 1) / kBlock);
     int cap = per_sm * dev.sm_count;
     coop_grid = want < cap ? want : cap;
@@ -300,12 +300,12 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
     void *args[] = {&A, &nn, &x, &r, (void *)&dinv, &pA, &pB, &Ap, &st, &part0, &part1};
     cudaEvent_t ev;
     profiler().begin(0, 0, s, &ev);
-    SLA_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)cg_persistent_kernel<T, PREC>,
+    SLA_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)cg_persistent_kernel<T, PREC, WS>,
                                              dim3(coop_grid), dim3(kBlock), args, 0, s));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     profiler().end(0, s, ev);
   } else {
-    const int grid_a = occupancy_grid((const void *)cg_spmv_kernel<T, PREC>);
+    const int grid_a = occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS>);
     const bool vec = aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv));
     const int grid_b = vec ? occupancy_grid((const void *)cg_update_kernel<T, PREC, true>)
                            : occupancy_grid((const void *)cg_update_kernel<T, PREC, false>);
@@ -314,7 +314,7 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
       T *p_new = (it & 1) ? pA : pB;
       cudaEvent_t ev;
       profiler().begin(0, it, s, &ev);
-      SLA_LAUNCH((cg_spmv_kernel<T, PREC>), grid_a, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap,
+      SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS>), grid_a, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap,
                  st, part0);
       profiler().end(0, s, ev);
       profiler().begin(1, it, s, &ev);
@@ -373,7 +373,7 @@ static int noalloc_scratch(void **out) {
 
 // Same kernels and launch shapes as pcg_impl; the convergence flag is polled
 // with a plain stream-ordered copy (no pinned buffer, no events).
-template <typename T, bool PREC>
+template <typename T, bool PREC, int WS>
 static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool guess,
                             double atol, double rtol, int64_t maxiter, int flags, void *ws,
                             size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
@@ -397,7 +397,7 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
   if (flags != SLA_PCG_STREAMED && dev.coop) {
     int per_sm = 0;
     SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, cg_persistent_kernel<T, PREC>, kBlock, 0));
+        &per_sm, cg_persistent_kernel<T, PREC, WS>, kBlock, 0));
     int want = (int)((n + kBlock - 1) / kBlock);
     int cap = per_sm * dev.sm_count;
     coop_grid = want < cap ? want : cap;
@@ -408,7 +408,7 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
   if (persistent) {
     int64_t nn = n;
     void *args[] = {&A, &nn, &x, &r, (void *)&dinv, &pA, &pB, &Ap, &st, &part0, &part1};
-    SLA_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)cg_persistent_kernel<T, PREC>,
+    SLA_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)cg_persistent_kernel<T, PREC, WS>,
                                              dim3(coop_grid), dim3(kBlock), args, 0, s));
     g_launches.fetch_add(1, std::memory_order_relaxed);
   } else {
@@ -417,7 +417,7 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
       for (int64_t j = 0; j < chunk; ++j, ++it) {
         T *p_old = (it & 1) ? pB : pA;
         T *p_new = (it & 1) ? pA : pB;
-        SLA_LAUNCH((cg_spmv_kernel<T, PREC>), occupancy_grid((const void *)cg_spmv_kernel<T, PREC>),
+        SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS>), occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS>),
                    kBlock, 0, s, A, r, dinv, p_old, p_new, Ap, st, part0);
         if (aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv)))
           SLA_LAUNCH((cg_update_kernel<T, PREC, true>),
@@ -469,19 +469,20 @@ int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b, voi
   if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
   cudaStream_t s = (cudaStream_t)stream;
   bool g = x_is_guess != 0;
+  const int wspec = width_spec(A);
   if (dtype == SLA_F64) {
     if (dinv)
-      return pcg_impl<double, true>(A, (const double *)dinv, (const double *)b, (double *)x, g, atol,
-                                    rtol, maxiter, flags, workspace, workspace_bytes, info, s);
-    return pcg_impl<double, false>(A, nullptr, (const double *)b, (double *)x, g, atol, rtol,
-                                   maxiter, flags, workspace, workspace_bytes, info, s);
+      SLA_WS_DISPATCH(wspec, return pcg_impl<double, true, WS>(A, (const double *)dinv, (const double *)b, (double *)x, g, atol,
+                                    rtol, maxiter, flags, workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return pcg_impl<double, false, WS>(A, nullptr, (const double *)b, (double *)x, g, atol, rtol,
+                                   maxiter, flags, workspace, workspace_bytes, info, s));
   }
   if (dtype == SLA_F32) {
     if (dinv)
-      return pcg_impl<float, true>(A, (const float *)dinv, (const float *)b, (float *)x, g, atol,
-                                   rtol, maxiter, flags, workspace, workspace_bytes, info, s);
-    return pcg_impl<float, false>(A, nullptr, (const float *)b, (float *)x, g, atol, rtol, maxiter,
-                                  flags, workspace, workspace_bytes, info, s);
+      SLA_WS_DISPATCH(wspec, return pcg_impl<float, true, WS>(A, (const float *)dinv, (const float *)b, (float *)x, g, atol,
+                                   rtol, maxiter, flags, workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return pcg_impl<float, false, WS>(A, nullptr, (const float *)b, (float *)x, g, atol, rtol, maxiter,
+                                  flags, workspace, workspace_bytes, info, s));
   }
   return SLA_ERR_INVALID;
 }
@@ -507,19 +508,20 @@ int sla_pcg_noalloc(int dtype, const sla_sell_t *A, const void *dinv, const void
   const size_t cap = SLA_PCG_NOALLOC_SCRATCH_BYTES;
   cudaStream_t s = (cudaStream_t)stream;
   bool g = x_is_guess != 0;
+  const int wspec = width_spec(A);
   if (dtype == SLA_F64) {
     if (dinv)
-      return pcg_noalloc_impl<double, true>(A, (const double *)dinv, (const double *)b,
+      SLA_WS_DISPATCH(wspec, return pcg_noalloc_impl<double, true, WS>(A, (const double *)dinv, (const double *)b,
                                             (double *)x, g, atol, rtol, maxiter, flags, ws, cap,
-                                            info, s);
-    return pcg_noalloc_impl<double, false>(A, nullptr, (const double *)b, (double *)x, g, atol,
-                                           rtol, maxiter, flags, ws, cap, info, s);
+                                            info, s));
+    SLA_WS_DISPATCH(wspec, return pcg_noalloc_impl<double, false, WS>(A, nullptr, (const double *)b, (double *)x, g, atol,
+                                           rtol, maxiter, flags, ws, cap, info, s));
   }
   if (dinv)
-    return pcg_noalloc_impl<float, true>(A, (const float *)dinv, (const float *)b, (float *)x, g,
-                                         atol, rtol, maxiter, flags, ws, cap, info, s);
-  return pcg_noalloc_impl<float, false>(A, nullptr, (const float *)b, (float *)x, g, atol, rtol,
-                                        maxiter, flags, ws, cap, info, s);
+    SLA_WS_DISPATCH(wspec, return pcg_noalloc_impl<float, true, WS>(A, (const float *)dinv, (const float *)b, (float *)x, g,
+                                         atol, rtol, maxiter, flags, ws, cap, info, s));
+  SLA_WS_DISPATCH(wspec, return pcg_noalloc_impl<float, false, WS>(A, nullptr, (const float *)b, (float *)x, g, atol, rtol,
+                                        maxiter, flags, ws, cap, info, s));
 }
 
 }  // extern "C"

@@ -320,7 +320,8 @@ static int csr_build_impl(const int64_t *row, const int64_t *col, const T *val, 
 
 // --------------------------------------------------------------- SELL-32
 __global__ void sell_width_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ row_ids,
-                                  int64_t n_slots, int64_t n_slices, int64_t *__restrict__ slice_len) {
+                                  int64_t n_slots, int64_t n_slices, int32_t min_width,
+                                  int64_t *__restrict__ slice_len, int32_t *__restrict__ max_width) {
   const int lane = threadIdx.x & 31;
   int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -333,7 +334,10 @@ __global__ void sell_width_kernel(const int32_t *__restrict__ rowptr, const int3
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) len = max(len, __shfl_xor_sync(kFull, len, o));
-    if (lane == 0) slice_len[sl] = (int64_t)len * 32;
+    if (lane == 0) {
+      atomicMax(max_width, len);
+      slice_len[sl] = (int64_t)max(len, (int)min_width) * 32;
+    }
   }
 }
 
@@ -424,15 +428,17 @@ int sla_csr_build(int dtype, const int64_t *row, const int64_t *col, const void 
 int sla_sell_layout_workspace(int64_t n_slots, size_t *bytes) {
   if (!bytes || n_slots < 0) return SLA_ERR_INVALID;
   int64_t n_slices = (n_slots + 31) / 32;
-  *bytes = 2 * align_up((n_slices + 1) * sizeof(int64_t)) + scan_workspace(n_slices + 1);
+  *bytes = 2 * align_up((n_slices + 1) * sizeof(int64_t)) + align_up(sizeof(int32_t)) +
+           scan_workspace(n_slices + 1);
   return SLA_OK;
 }
 
 int sla_sell_layout(const int32_t *rowptr, const int32_t *row_ids, int64_t n_slots,
-                    int32_t *slice_ptr, int64_t *padded_out, void *workspace,
-                    size_t workspace_bytes, sla_stream_t stream) {
+                    int32_t min_width, int32_t *slice_ptr, int64_t *padded_out,
+                    int32_t *max_width_out, void *workspace, size_t workspace_bytes,
+                    sla_stream_t stream) {
   cudaStream_t s = (cudaStream_t)stream;
-  if (!rowptr || !slice_ptr || !padded_out || n_slots < 0) return SLA_ERR_INVALID;
+  if (!rowptr || !slice_ptr || !padded_out || n_slots < 0 || min_width < 0) return SLA_ERR_INVALID;
   size_t need = 0;
   sla_sell_layout_workspace(n_slots, &need);
   if (workspace_bytes < need) return SLA_ERR_WORKSPACE;
@@ -440,19 +446,24 @@ int sla_sell_layout(const int32_t *rowptr, const int32_t *row_ids, int64_t n_slo
   Carver c(workspace, workspace_bytes);
   int64_t *len = c.take<int64_t>(n_slices + 1);
   int64_t *ptr64 = c.take<int64_t>(n_slices + 1);
+  int32_t *wmax = c.take<int32_t>(1);
   char *scan = c.base + c.off;
   SLA_CUDA_TRY(cudaMemsetAsync(len, 0, sizeof(int64_t) * (n_slices + 1), s));
+  SLA_CUDA_TRY(cudaMemsetAsync(wmax, 0, sizeof(int32_t), s));
   if (n_slices > 0)
     SLA_LAUNCH(sell_width_kernel, grid_for(n_slices * 32), kBlock, 0, s, rowptr, row_ids, n_slots,
-               n_slices, len);
+               n_slices, min_width, len, wmax);
   SLA_TRY(exclusive_scan<int64_t>(len, ptr64, n_slices + 1, scan, s));
   int64_t total = 0;
+  int32_t widest = 0;
   SLA_CUDA_TRY(cudaMemcpyAsync(&total, ptr64 + n_slices, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaMemcpyAsync(&widest, wmax, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
   SLA_CUDA_TRY(cudaStreamSynchronize(s));
   if (total >= INT32_MAX) return SLA_ERR_UNSUPPORTED;
   SLA_LAUNCH(rowptr_narrow_kernel, grid_for(n_slices + 1), kBlock, 0, s, ptr64, n_slices + 1,
              slice_ptr);
   *padded_out = total;
+  if (max_width_out) *max_width_out = widest;
   return SLA_OK;
 }
 

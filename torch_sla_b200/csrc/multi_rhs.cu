@@ -96,16 +96,14 @@ mrhs_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__
   if (rl < rpb) {
     const T beta = (T)cs.beta[bi];
     for (int64_t row = (int64_t)blockIdx.x * rpb + rl; row < n; row += (int64_t)gridDim.x * rpb) {
-      T sum = T(0);
-      const int32_t k0 = rowptr[row], k1 = rowptr[row + 1];
-      for (int32_t k = k0; k < k1; ++k) {
-        const int32_t cidx = __ldg(colind + k);
-        const int64_t c = (int64_t)cidx * K + bi;
-        T z = PREC ? mul_rn(__ldg(dinv + cidx), __ldg(r + c)) : __ldg(r + c);
-        // P = Z + beta P (pytorch_backend.py:2487)
-        T pc = add_rn(z, mul_rn(beta, __ldg(p_old + c)));
-        sum = fma(__ldg(vals + k), pc, sum);
-      }
+      // P = Z + beta P (pytorch_backend.py:2487), formed inside the gather
+      const T sum = csr_row_batched<T>(
+          colind, rowptr[row], rowptr[row + 1], [&](int32_t k) { return __ldg(vals + k); },
+          [&](int32_t cidx) {
+            const int64_t c = (int64_t)cidx * K + bi;
+            T z = PREC ? mul_rn(__ldg(dinv + cidx), __ldg(r + c)) : __ldg(r + c);
+            return add_rn(z, mul_rn(beta, __ldg(p_old + c)));
+          });
       const int64_t o = row * K + bi;
       T z = PREC ? mul_rn(dinv[row], r[o]) : r[o];
       T pn = add_rn(z, mul_rn(beta, p_old[o]));

@@ -6,6 +6,13 @@
 // The gathered vector is produced by a functor so a solver can fuse the
 // vector update that precedes the SpMV (p = z + beta p, p_hat = M^{-1} p,
 // s_hat = M^{-1}(r - alpha v)) into the gather instead of a separate pass.
+//
+// Width specialisation (template parameter WS): the row loop is cheapest
+// when its trip count is known at compile time, so kernels are instantiated
+//   WS > 0   uniform layout, every slice WS entries wide (slice base is
+//            32*WS*s, no slice_ptr load): the 7- and 27-point stencils;
+//   WS < 0   at most -WS batches of kRowBatch entries (static batch loop);
+//   WS == 0  any width (runtime loop).
 #pragma once
 
 #include "common.cuh"
@@ -20,6 +27,8 @@ struct Sell {
   const int32_t *__restrict__ col;
   const T *__restrict__ val;
   const int32_t *__restrict__ row_ids;
+  int32_t max_width;
+  int32_t uniform_width;
 };
 
 template <typename T>
@@ -31,6 +40,8 @@ inline Sell<T> make_sell(const sla_sell_t *A) {
   s.col = A ? A->col : nullptr;
   s.val = A ? (const T *)A->val : nullptr;
   s.row_ids = A ? A->row_ids : nullptr;
+  s.max_width = A ? A->max_width : 0;
+  s.uniform_width = A ? A->uniform_width : 0;
   return s;
 }
 
@@ -38,6 +49,8 @@ inline bool sell_ok(const sla_sell_t *A) {
   if (!A) return false;
   if (A->n_slots < 0 || A->n_slices != (A->n_slots + 31) / 32) return false;
   if (A->n_slices > 0 && (!A->slice_ptr || !A->col || !A->val)) return false;
+  if (A->max_width < 0 || A->uniform_width < 0) return false;
+  if (A->uniform_width > 0 && A->uniform_width != A->max_width) return false;
   return true;
 }
 
@@ -46,69 +59,102 @@ inline bool sell_ok(const sla_sell_t *A) {
 // load -> gather round trip (7-point rows fit one batch, 27-point rows four).
 constexpr int kRowBatch = 8;
 
-// sum_j val[j] * g(col[j]) over the entries of this lane's slot of the slice
-// starting at entry `base` with `width` entries per slot.
+// Blocks per SM the SpMV-bearing kernels are compiled for (register cap):
+// enough warps to keep ~8 batched loads each in flight.
+constexpr int kSpmvMinBlocks = 4;
+
+// Width spec of a view: the template value its kernels are launched with.
+inline int width_spec(const sla_sell_t *A) {
+  if (!A) return 0;
+  if (A->uniform_width == 7 || A->uniform_width == 27) return A->uniform_width;
+  const int w = A->max_width;
+  if (w <= kRowBatch) return -1;
+  if (w <= 2 * kRowBatch) return -2;
+  if (w <= 4 * kRowBatch) return -4;
+  return 0;
+}
+
+// Host dispatch: runs the statement(s) with WS bound to the view's spec.
+#define SLA_WS_DISPATCH(ws, ...)                          \
+  switch (ws) {                                           \
+    case 7: { constexpr int WS = 7; __VA_ARGS__; } break;   \
+    case 27: { constexpr int WS = 27; __VA_ARGS__; } break; \
+    case -1: { constexpr int WS = -1; __VA_ARGS__; } break; \
+    case -2: { constexpr int WS = -2; __VA_ARGS__; } break; \
+    case -4: { constexpr int WS = -4; __VA_ARGS__; } break; \
+    default: { constexpr int WS = 0; __VA_ARGS__; } break;  \
+  }
+
 template <typename T, typename G>
+__device__ __forceinline__ void row_batch(const int32_t *__restrict__ cp, const T *__restrict__ vp,
+                                          int j, int lim, const G &g, T &sum) {
+  int32_t c[kRowBatch];
+  T v[kRowBatch], x[kRowBatch];
+#pragma unroll
+  for (int u = 0; u < kRowBatch; ++u) {
+    if (j + u < lim) {
+      c[u] = ld_stream(cp + 32 * (j + u));
+      v[u] = ld_stream(vp + 32 * (j + u));
+    } else {
+      c[u] = -1;
+      v[u] = T(0);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kRowBatch; ++u) x[u] = c[u] >= 0 ? g(c[u]) : T(0);
+#pragma unroll
+  for (int u = 0; u < kRowBatch; ++u) sum = fma(v[u], x[u], sum);
+}
+
+// sum_j val[j] * g(col[j]) over the entries of this lane's slot of the slice
+// starting at entry `base` with `width` entries per slot (ascending j).
+template <int WS, typename T, typename G>
 __device__ __forceinline__ T sell_row_at(const Sell<T> &A, int32_t base, int width, int lane,
                                          const G &g) {
   const int32_t *__restrict__ cp = A.col + base + lane;
   const T *__restrict__ vp = A.val + base + lane;
   T sum = T(0);
-  for (int j = 0; j < width; j += kRowBatch) {
-    int32_t c[kRowBatch];
-    T v[kRowBatch], x[kRowBatch];
+  if constexpr (WS > 0) {
 #pragma unroll
-    for (int u = 0; u < kRowBatch; ++u) {
-      if (j + u < width) {
-        c[u] = ld_stream(cp + 32 * (j + u));
-        v[u] = ld_stream(vp + 32 * (j + u));
-      } else {
-        c[u] = -1;
-        v[u] = T(0);
-      }
-    }
+    for (int j = 0; j < WS; j += kRowBatch) row_batch(cp, vp, j, WS, g, sum);
+  } else if constexpr (WS < 0) {
 #pragma unroll
-    for (int u = 0; u < kRowBatch; ++u) x[u] = c[u] >= 0 ? g(c[u]) : T(0);
-#pragma unroll
-    for (int u = 0; u < kRowBatch; ++u) sum = fma(v[u], x[u], sum);
+    for (int jb = 0; jb < -WS; ++jb) row_batch(cp, vp, jb * kRowBatch, width, g, sum);
+  } else {
+    for (int j = 0; j < width; j += kRowBatch) row_batch(cp, vp, j, width, g, sum);
   }
   return sum;
 }
 
-template <typename T, typename G>
-__device__ __forceinline__ T sell_row(const Sell<T> &A, int64_t slice, int lane, const G &g) {
-  const int32_t base = A.slice_ptr[slice];
-  return sell_row_at(A, base, (A.slice_ptr[slice + 1] - base) >> 5, lane, g);
-}
-
 // Grid-stride walk over the slices owned by this warp (slices warp,
-// warp + nwarps, ...). The slice pointers of the next 32 slices are fetched
-// by the 32 lanes at once and broadcast by shuffles, so a slice's column and
-// value loads never wait on a dependent slice_ptr load.
-// body(slice, base, width) is called with warp-uniform arguments.
-template <typename T, typename Body>
+// warp + nwarps, ...). Uniform layouts compute each slice's base; otherwise
+// the slice pointers of the next 32 slices are fetched by the 32 lanes at once
+// and broadcast by shuffles, so a slice's column and value loads never wait on
+// a dependent slice_ptr load. body(slice, base, width) gets warp-uniform
+// arguments.
+template <int WS, typename T, typename Body>
 __device__ __forceinline__ void for_each_slice(const Sell<T> &A, int64_t warp, int64_t nwarps,
                                                int lane, Body body) {
-  for (int64_t s0 = warp; s0 < A.n_slices; s0 += 32 * nwarps) {
-    const int64_t mine = s0 + (int64_t)lane * nwarps;
-    int32_t b0 = 0, b1 = 0;
-    if (mine < A.n_slices) {
-      b0 = __ldg(A.slice_ptr + mine);
-      b1 = __ldg(A.slice_ptr + mine + 1);
-    }
-    const int64_t left = (A.n_slices - s0 + nwarps - 1) / nwarps;
-    const int count = left < 32 ? (int)left : 32;
-    for (int q = 0; q < count; ++q) {
-      const int32_t base = __shfl_sync(kFull, b0, q);
-      const int32_t end = __shfl_sync(kFull, b1, q);
-      body(s0 + (int64_t)q * nwarps, base, (end - base) >> 5);
+  if constexpr (WS > 0) {
+    for (int64_t s = warp; s < A.n_slices; s += nwarps) body(s, (int32_t)(s * 32 * WS), WS);
+  } else {
+    for (int64_t s0 = warp; s0 < A.n_slices; s0 += 32 * nwarps) {
+      const int64_t mine = s0 + (int64_t)lane * nwarps;
+      int32_t b0 = 0, b1 = 0;
+      if (mine < A.n_slices) {
+        b0 = __ldg(A.slice_ptr + mine);
+        b1 = __ldg(A.slice_ptr + mine + 1);
+      }
+      const int64_t left = (A.n_slices - s0 + nwarps - 1) / nwarps;
+      const int count = left < 32 ? (int)left : 32;
+      for (int q = 0; q < count; ++q) {
+        const int32_t base = __shfl_sync(kFull, b0, q);
+        const int32_t end = __shfl_sync(kFull, b1, q);
+        body(s0 + (int64_t)q * nwarps, base, (end - base) >> 5);
+      }
     }
   }
 }
-
-// Blocks per SM the SpMV-bearing kernels are compiled for (register cap):
-// enough warps to keep ~8 batched loads each in flight.
-constexpr int kSpmvMinBlocks = 4;
 
 template <typename T>
 struct PlainGather {

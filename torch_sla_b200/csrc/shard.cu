@@ -80,6 +80,20 @@ static bool plan_ok(const sla_halo_plan_t *p) {
   return true;
 }
 
+// One spec for the interior and boundary views of a shard (a uniform width
+// only when both views have it).
+static int width_spec2(const sla_sell_t *a, const sla_sell_t *b) {
+  if (a->n_slots == 0) return width_spec(b);
+  if (b->n_slots == 0) return width_spec(a);
+  int wa = width_spec(a), wb = width_spec(b);
+  if (wa == wb) return wa;
+  auto batches = [](int w) { return w > 0 ? -((w + kRowBatch - 1) / kRowBatch) : w; };
+  int ba = batches(wa), bb = batches(wb);
+  if (ba == 0 || bb == 0) return 0;
+  int m = ba < bb ? ba : bb;
+  return m == -3 ? -4 : m;
+}
+
 static int64_t n_send(const sla_halo_plan_t *p) {
   return p->n_neighbors > 0 ? p->send_offset[p->n_neighbors] : 0;
 }
@@ -145,14 +159,14 @@ struct HaloGather {
   }
 };
 
-template <typename T, typename G>
-__global__ void __launch_bounds__(kBlock)
+template <typename T, typename G, int WS>
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 shard_spmv_rows_kernel(Sell<T> A, G g, T *__restrict__ y) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at(A, sbase, swidth, lane, g);
+  for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) y[A.row_ids ? A.row_ids[slot] : slot] = sum;
   });
@@ -247,7 +261,7 @@ __global__ void shard_cg_pack(const int32_t *__restrict__ idx, int64_t n, const 
   for (; i < n; i += stride) out[i] = p(idx[i]);
 }
 
-template <typename T, bool PREC, bool HALO>
+template <typename T, bool PREC, bool HALO, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 shard_cg_spmv(Sell<T> A, int32_t n_own, const T *__restrict__ r, const T *__restrict__ dinv,
               const T *__restrict__ p_old, const T *__restrict__ phalo, T *__restrict__ p_new,
@@ -260,8 +274,8 @@ shard_cg_spmv(Sell<T> A, int32_t n_own, const T *__restrict__ r, const T *__rest
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[1] = {0.0};
-  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = HALO ? sell_row_at(A, sbase, swidth, lane, g) : sell_row_at(A, sbase, swidth, lane, inner);
+  for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = HALO ? sell_row_at<WS>(A, sbase, swidth, lane, g) : sell_row_at<WS>(A, sbase, swidth, lane, inner);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
       int32_t row = A.row_ids[slot];
@@ -410,7 +424,7 @@ __global__ void shard_bi_pack1(const int32_t *__restrict__ idx, int64_t n, BiP<T
   for (; i < n; i += stride) out[i] = g(idx[i]);
 }
 
-template <typename T, bool PREC, bool HALO>
+template <typename T, bool PREC, bool HALO, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 shard_bi_k1(Sell<T> A, int32_t n_own, BiP<T, PREC> g0, const T *__restrict__ phalo,
             const T *__restrict__ rhat, T *__restrict__ p_new, T *__restrict__ v, ShardState *st,
@@ -425,8 +439,8 @@ shard_bi_k1(Sell<T> A, int32_t n_own, BiP<T, PREC> g0, const T *__restrict__ pha
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[1] = {0.0};
-  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = HALO ? sell_row_at(A, sbase, swidth, lane, g) : sell_row_at(A, sbase, swidth, lane, inner);
+  for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = HALO ? sell_row_at<WS>(A, sbase, swidth, lane, g) : sell_row_at<WS>(A, sbase, swidth, lane, inner);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
       int32_t row = A.row_ids[slot];
@@ -453,7 +467,7 @@ __global__ void shard_bi_pack2(const int32_t *__restrict__ idx, int64_t n, BiS<T
   for (; i < n; i += stride) out[i] = g(idx[i]);
 }
 
-template <typename T, bool PREC, bool HALO>
+template <typename T, bool PREC, bool HALO, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
 shard_bi_k2(Sell<T> A, int32_t n_own, BiS<T, PREC> g0, const T *__restrict__ shalo,
             T *__restrict__ t, ShardState *st, BiRed *R, double *partials, long long k) {
@@ -466,8 +480,8 @@ shard_bi_k2(Sell<T> A, int32_t n_own, BiS<T, PREC> g0, const T *__restrict__ sha
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[3] = {0.0, 0.0, 0.0};
-  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = HALO ? sell_row_at(A, sbase, swidth, lane, g) : sell_row_at(A, sbase, swidth, lane, inner);
+  for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = HALO ? sell_row_at<WS>(A, sbase, swidth, lane, g) : sell_row_at<WS>(A, sbase, swidth, lane, inner);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
       int32_t row = A.row_ids[slot];
@@ -568,7 +582,7 @@ static int shard_loop(Comm *c, int64_t maxiter, int64_t chunk, const int *d_stop
   return SLA_OK;
 }
 
-template <typename T, bool PREC>
+template <typename T, bool PREC, int WS>
 static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const sla_sell_t *Ai,
                          const sla_sell_t *Ab, const T *dinv, const T *b, T *x, double atol,
                          double rtol, int64_t maxiter, int64_t every, void *ws, size_t ws_bytes,
@@ -592,8 +606,8 @@ static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
              part[0]);
   SLA_NCCL_TRY(ncclAllReduce(R->init, R->init, 2, ncclFloat64, ncclSum, cr->nccl, s));
   const T *hsrc = plan->halo_src ? halo : recvbuf;
-  const int gi = occupancy_grid((const void *)shard_cg_spmv<T, PREC, false>);
-  const int gb = occupancy_grid((const void *)shard_cg_spmv<T, PREC, true>);
+  const int gi = occupancy_grid((const void *)shard_cg_spmv<T, PREC, false, WS>);
+  const int gb = occupancy_grid((const void *)shard_cg_spmv<T, PREC, true, WS>);
   const int gu = occupancy_grid((const void *)shard_cg_update<T, PREC>);
   SLA_TRY(shard_loop(cr, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
     T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
@@ -606,14 +620,14 @@ static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
     SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
     cudaEvent_t ev;
     profiler().begin(0, k, s, &ev);
-    SLA_LAUNCH((shard_cg_spmv<T, PREC, false>), gi, kBlock, 0, s, AI, (int32_t)no, r, dinv, p_old,
+    SLA_LAUNCH((shard_cg_spmv<T, PREC, false, WS>), gi, kBlock, 0, s, AI, (int32_t)no, r, dinv, p_old,
                hsrc, p_new, Ap, st, R, part[1], (long long)k);
     profiler().end(0, s, ev);
     SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
     if (plan->halo_src && nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
                  halo, &st->stopped);
-    SLA_LAUNCH((shard_cg_spmv<T, PREC, true>), gb, kBlock, 0, s, AB, (int32_t)no, r, dinv, p_old,
+    SLA_LAUNCH((shard_cg_spmv<T, PREC, true, WS>), gb, kBlock, 0, s, AB, (int32_t)no, r, dinv, p_old,
                hsrc, p_new, Ap, st, R, part[2], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->pap, R->pap, 1, ncclFloat64, ncclSum, cr->nccl, s));
     profiler().begin(1, k, s, &ev);
@@ -642,7 +656,7 @@ static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
   return info->status;
 }
 
-template <typename T, bool PREC>
+template <typename T, bool PREC, int WS>
 static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const sla_sell_t *Ai,
                          const sla_sell_t *Ab, const T *dinv, const T *b, T *x, double atol,
                          double rtol, int64_t maxiter, int64_t every, void *ws, size_t ws_bytes,
@@ -667,10 +681,10 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
   SLA_NCCL_TRY(ncclAllReduce(R->init, R->init, 2, ncclFloat64, ncclSum, cr->nccl, s));
   const T *hsrc = plan->halo_src ? halo : recvbuf;
   const unsigned pack_grid = ns > 0 ? (unsigned)grid_for(ns) : 1u;
-  const int g1i = occupancy_grid((const void *)shard_bi_k1<T, PREC, false>);
-  const int g1b = occupancy_grid((const void *)shard_bi_k1<T, PREC, true>);
-  const int g2i = occupancy_grid((const void *)shard_bi_k2<T, PREC, false>);
-  const int g2b = occupancy_grid((const void *)shard_bi_k2<T, PREC, true>);
+  const int g1i = occupancy_grid((const void *)shard_bi_k1<T, PREC, false, WS>);
+  const int g1b = occupancy_grid((const void *)shard_bi_k1<T, PREC, true, WS>);
+  const int g2i = occupancy_grid((const void *)shard_bi_k2<T, PREC, false, WS>);
+  const int g2b = occupancy_grid((const void *)shard_bi_k2<T, PREC, true, WS>);
   const int g3 = occupancy_grid((const void *)shard_bi_k3<T, PREC>);
   SLA_TRY(shard_loop(cr, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
     T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
@@ -682,27 +696,27 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
     SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
     cudaEvent_t ev;
     profiler().begin(0, k, s, &ev);
-    SLA_LAUNCH((shard_bi_k1<T, PREC, false>), g1i, kBlock, 0, s, AI, (int32_t)no, gp, hsrc, rhat,
+    SLA_LAUNCH((shard_bi_k1<T, PREC, false, WS>), g1i, kBlock, 0, s, AI, (int32_t)no, gp, hsrc, rhat,
                p_new, v, st, R, part[1], (long long)k);
     profiler().end(0, s, ev);
     SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
     if (plan->halo_src && nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
                  halo, &st->stopped);
-    SLA_LAUNCH((shard_bi_k1<T, PREC, true>), g1b, kBlock, 0, s, AB, (int32_t)no, gp, hsrc, rhat,
+    SLA_LAUNCH((shard_bi_k1<T, PREC, true, WS>), g1b, kBlock, 0, s, AB, (int32_t)no, gp, hsrc, rhat,
                p_new, v, st, R, part[2], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->rv, R->rv, 1, ncclFloat64, ncclSum, cr->nccl, s));
     // s_hat halo, then t = A s_hat
     SLA_LAUNCH((shard_bi_pack2<T, PREC>), pack_grid, kBlock, 0, s, plan->send_index, ns, gs,
                sendbuf, st, R, (long long)k);
     SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
-    SLA_LAUNCH((shard_bi_k2<T, PREC, false>), g2i, kBlock, 0, s, AI, (int32_t)no, gs, hsrc, t, st, R,
+    SLA_LAUNCH((shard_bi_k2<T, PREC, false, WS>), g2i, kBlock, 0, s, AI, (int32_t)no, gs, hsrc, t, st, R,
                part[3], (long long)k);
     SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
     if (plan->halo_src && nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
                  halo, &st->stopped);
-    SLA_LAUNCH((shard_bi_k2<T, PREC, true>), g2b, kBlock, 0, s, AB, (int32_t)no, gs, hsrc, t, st, R,
+    SLA_LAUNCH((shard_bi_k2<T, PREC, true, WS>), g2b, kBlock, 0, s, AB, (int32_t)no, gs, hsrc, t, st, R,
                part[4], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->stt, R->stt, 3, ncclFloat64, ncclSum, cr->nccl, s));
     SLA_LAUNCH((shard_bi_k3<T, PREC>), g3, kBlock, 0, s, no, x, r, rhat, p_new, v, t, dinv, st, R,
@@ -825,16 +839,19 @@ int sla_shard_spmv(void *comm, const sla_halo_plan_t *plan, int dtype, const sla
       SLA_LAUNCH((halo_pack_kernel<T, LoadVal<T>>), grid_for(ns), kBlock, 0, s, plan->send_index,
                  ns, LoadVal<T>{x}, (T *)sendbuf, (const int *)nullptr);
     SLA_TRY(halo_enqueue<T>(c, plan, (const T *)sendbuf, (T *)recvbuf, s));
+    const int wspec = width_spec2(A_interior, A_boundary);
     if (AI.n_slices > 0)
-      SLA_LAUNCH((shard_spmv_rows_kernel<T, PlainGather<T>>), grid_for(AI.n_slices * 32), kBlock,
-                 0, s, AI, PlainGather<T>{x}, (T *)y_owned);
+      SLA_WS_DISPATCH(wspec, SLA_LAUNCH((shard_spmv_rows_kernel<T, PlainGather<T>, WS>),
+                                        grid_for(AI.n_slices * 32, kBlock, 4), kBlock, 0, s, AI,
+                                        PlainGather<T>{x}, (T *)y_owned));
     SLA_CUDA_TRY(cudaStreamWaitEvent(s, c->ev_halo, 0));
     if (nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, (const T *)recvbuf,
                  plan->halo_src, nh, x + no, (const int *)nullptr);
     if (AB.n_slices > 0)
-      SLA_LAUNCH((shard_spmv_rows_kernel<T, PlainGather<T>>), grid_for(AB.n_slices * 32), kBlock,
-                 0, s, AB, PlainGather<T>{x}, (T *)y_owned);
+      SLA_WS_DISPATCH(wspec, SLA_LAUNCH((shard_spmv_rows_kernel<T, PlainGather<T>, WS>),
+                                        grid_for(AB.n_slices * 32, kBlock, 4), kBlock, 0, s, AB,
+                                        PlainGather<T>{x}, (T *)y_owned));
     return SLA_OK;
   };
   if (dtype == SLA_F64) return run(double(0));
@@ -875,23 +892,24 @@ int sla_shard_cg(void *comm_halo, void *comm_reduce, const sla_halo_plan_t *plan
   if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
   Comm *ch = (Comm *)comm_halo, *cr = (Comm *)comm_reduce;
   cudaStream_t s = (cudaStream_t)stream;
+  const int wspec = width_spec2(A_interior, A_boundary);
   if (dtype == SLA_F64) {
     if (dinv)
-      return shard_cg_impl<double, true>(ch, cr, plan, A_interior, A_boundary, (const double *)dinv,
+      SLA_WS_DISPATCH(wspec, return shard_cg_impl<double, true, WS>(ch, cr, plan, A_interior, A_boundary, (const double *)dinv,
                                          (const double *)b, (double *)x, atol, rtol, maxiter,
-                                         check_every, workspace, workspace_bytes, info, s);
-    return shard_cg_impl<double, false>(ch, cr, plan, A_interior, A_boundary, nullptr,
+                                         check_every, workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return shard_cg_impl<double, false, WS>(ch, cr, plan, A_interior, A_boundary, nullptr,
                                         (const double *)b, (double *)x, atol, rtol, maxiter,
-                                        check_every, workspace, workspace_bytes, info, s);
+                                        check_every, workspace, workspace_bytes, info, s));
   }
   if (dtype == SLA_F32) {
     if (dinv)
-      return shard_cg_impl<float, true>(ch, cr, plan, A_interior, A_boundary, (const float *)dinv,
+      SLA_WS_DISPATCH(wspec, return shard_cg_impl<float, true, WS>(ch, cr, plan, A_interior, A_boundary, (const float *)dinv,
                                         (const float *)b, (float *)x, atol, rtol, maxiter,
-                                        check_every, workspace, workspace_bytes, info, s);
-    return shard_cg_impl<float, false>(ch, cr, plan, A_interior, A_boundary, nullptr,
+                                        check_every, workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return shard_cg_impl<float, false, WS>(ch, cr, plan, A_interior, A_boundary, nullptr,
                                        (const float *)b, (float *)x, atol, rtol, maxiter,
-                                       check_every, workspace, workspace_bytes, info, s);
+                                       check_every, workspace, workspace_bytes, info, s));
   }
   return SLA_ERR_INVALID;
 }
@@ -909,23 +927,24 @@ int sla_shard_bicgstab(void *comm_halo, void *comm_reduce, const sla_halo_plan_t
   if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
   Comm *ch = (Comm *)comm_halo, *cr = (Comm *)comm_reduce;
   cudaStream_t s = (cudaStream_t)stream;
+  const int wspec = width_spec2(A_interior, A_boundary);
   if (dtype == SLA_F64) {
     if (dinv)
-      return shard_bi_impl<double, true>(ch, cr, plan, A_interior, A_boundary, (const double *)dinv,
+      SLA_WS_DISPATCH(wspec, return shard_bi_impl<double, true, WS>(ch, cr, plan, A_interior, A_boundary, (const double *)dinv,
                                          (const double *)b, (double *)x, atol, rtol, maxiter,
-                                         check_every, workspace, workspace_bytes, info, s);
-    return shard_bi_impl<double, false>(ch, cr, plan, A_interior, A_boundary, nullptr,
+                                         check_every, workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return shard_bi_impl<double, false, WS>(ch, cr, plan, A_interior, A_boundary, nullptr,
                                         (const double *)b, (double *)x, atol, rtol, maxiter,
-                                        check_every, workspace, workspace_bytes, info, s);
+                                        check_every, workspace, workspace_bytes, info, s));
   }
   if (dtype == SLA_F32) {
     if (dinv)
-      return shard_bi_impl<float, true>(ch, cr, plan, A_interior, A_boundary, (const float *)dinv,
+      SLA_WS_DISPATCH(wspec, return shard_bi_impl<float, true, WS>(ch, cr, plan, A_interior, A_boundary, (const float *)dinv,
                                         (const float *)b, (float *)x, atol, rtol, maxiter,
-                                        check_every, workspace, workspace_bytes, info, s);
-    return shard_bi_impl<float, false>(ch, cr, plan, A_interior, A_boundary, nullptr,
+                                        check_every, workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return shard_bi_impl<float, false, WS>(ch, cr, plan, A_interior, A_boundary, nullptr,
                                        (const float *)b, (float *)x, atol, rtol, maxiter,
-                                       check_every, workspace, workspace_bytes, info, s);
+                                       check_every, workspace, workspace_bytes, info, s));
   }
   return SLA_ERR_INVALID;
 }

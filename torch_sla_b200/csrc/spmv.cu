@@ -4,15 +4,15 @@
 
 namespace sla {
 
-template <typename T>
+template <typename T, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks) spmv_kernel(Sell<T> A, const T *__restrict__ x,
                                                       T *__restrict__ y) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   PlainGather<T> g{x};
-  for_each_slice(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at(A, sbase, swidth, lane, g);
+  for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
       int64_t row = A.row_ids ? A.row_ids[slot] : slot;
@@ -25,7 +25,9 @@ template <typename T>
 int spmv_launch(const sla_sell_t *A, const void *x, void *y, cudaStream_t s) {
   Sell<T> a = make_sell<T>(A);
   if (a.n_slices == 0) return SLA_OK;
-  SLA_LAUNCH(spmv_kernel<T>, grid_for(a.n_slices * 32, kBlock, 4), kBlock, 0, s, a, (const T *)x, (T *)y);
+  SLA_WS_DISPATCH(width_spec(A),
+                  SLA_LAUNCH((spmv_kernel<T, WS>), grid_for(a.n_slices * 32, kBlock, 4), kBlock, 0,
+                             s, a, (const T *)x, (T *)y));
   return SLA_OK;
 }
 template int spmv_launch<float>(const sla_sell_t *, const void *, void *, cudaStream_t);
