@@ -251,6 +251,20 @@ int sla_shard_spmv(void *comm, const sla_halo_plan_t *plan, int dtype,
                    const sla_sell_t *A_interior, const sla_sell_t *A_boundary,
                    void *x_local, void *y_owned, void *sendbuf, void *recvbuf,
                    sla_stream_t stream);
+/* reverse_halo_exchange (distributed/matvec.py:96-170): the halo slots of
+ * w_local are sent to their owners, which add them onto the owned slots they
+ * sent in the forward exchange, neighbour by neighbour in ascending order.
+ * sendbuf holds n_halo values, recvbuf the plan's total send count. */
+int sla_reverse_halo_exchange(void *comm, const sla_halo_plan_t *plan,
+                              int dtype, void *w_local, void *sendbuf,
+                              void *recvbuf, sla_stream_t stream);
+/* shard_rmatvec (distributed/matvec.py:306-348): w_local = A_local^T y over
+ * AT, the SELL view of the local transpose (rows: the n_owned + n_halo local
+ * ids; columns: owned), then the reverse halo exchange. The owned part of
+ * w_local is the owned slice of A^T y. */
+int sla_shard_rmatvec(void *comm, const sla_halo_plan_t *plan, int dtype,
+                      const sla_sell_t *AT, const void *y_owned, void *w_local,
+                      void *sendbuf, void *recvbuf, sla_stream_t stream);
 /* cg_shard / bicgstab_shard (distributed/solve.py:279-436): stopping test
  * every `check_every` iterations, one fused allreduce per reduction point. */
 int sla_shard_krylov_workspace(int dtype, int64_t n_owned, int64_t n_halo,

@@ -63,8 +63,15 @@ def _worker(rank, world, port, out_dir):
             xl[: plan.n_owned] = case["b"].to(dev)[part.owned_nodes.to(dev)]
             halo_exchange(D, xl)
             halo_ok = torch.equal(xl[plan.n_owned:].cpu(), case["b"][part.halo_nodes])
+            # A^T y through the local transpose + reverse halo exchange
+            yo = case["b"].to(dev)[part.owned_nodes.to(dev)]
+            wt = torch.zeros(sh[0], dtype=torch.float64, device=dev)
+            wt[part.owned_nodes.to(dev)] = D._shard_rmatvec(yo)
+            if world > 1:
+                dist.all_reduce(wt)
+            wt_ref = K.spmv(v, c, r, sh, case["b"])
             res[name] = {"x": x, "iters": D._last_info["iterations"], "spmv_rel": _rel(y, y_ref),
-                         "halo_ok": halo_ok}
+                         "halo_ok": halo_ok, "rmatvec_rel": _rel(wt.cpu(), wt_ref)}
         # owned-rows construction on a slab-partitioned 7-point grid
         m = 12
         dims = (m * world, m, m)
@@ -108,6 +115,7 @@ def _check(results, golden_shard):
         for name, case in golden_shard.items():
             got = res[name]
             assert got["spmv_rel"] < 1e-13, (name, got["spmv_rel"])
+            assert got["rmatvec_rel"] < 1e-13, (name, got["rmatvec_rel"])
             assert got["halo_ok"], name
             # stop tests run every 10 iterations: counts agree to that stride
             slack = 10 if case["method"] == "bicgstab" else max(1, math.ceil(0.03 * case["iters"]))

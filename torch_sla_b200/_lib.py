@@ -93,6 +93,10 @@ _SIGNATURES = {
                                          c_ptr, c_ptr]),
     "sla_shard_spmv": (ctypes.c_int, [c_ptr, _P(HaloPlan), ctypes.c_int, _P(SellView),
                                       _P(SellView), c_ptr, c_ptr, c_ptr, c_ptr, c_ptr]),
+    "sla_reverse_halo_exchange": (ctypes.c_int, [c_ptr, _P(HaloPlan), ctypes.c_int, c_ptr, c_ptr,
+                                                 c_ptr, c_ptr]),
+    "sla_shard_rmatvec": (ctypes.c_int, [c_ptr, _P(HaloPlan), ctypes.c_int, _P(SellView), c_ptr,
+                                         c_ptr, c_ptr, c_ptr, c_ptr]),
     "sla_shard_krylov_workspace": (ctypes.c_int, [ctypes.c_int, c_i64, c_i64, c_i64, _P(c_sz)]),
     "sla_shard_cg": (ctypes.c_int, [c_ptr, c_ptr, _P(HaloPlan), ctypes.c_int, _P(SellView),
                                     _P(SellView), c_ptr, c_ptr, c_ptr, c_dbl, c_dbl, c_i64, c_i64,

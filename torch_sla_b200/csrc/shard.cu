@@ -172,6 +172,67 @@ shard_spmv_rows_kernel(Sell<T> A, G g, T *__restrict__ y) {
   });
 }
 
+// Reverse exchange helpers: halo slot h goes to recv-order position
+// halo_src[h] (identity when NULL); received contributions are added onto
+// the owned rows a neighbour was sent in the forward direction.
+template <typename T>
+__global__ void rev_pack_kernel(const T *__restrict__ w_halo, const int32_t *__restrict__ src,
+                                int64_t n_halo, T *__restrict__ out) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n_halo; i += stride) out[src ? src[i] : i] = w_halo[i];
+}
+
+template <typename T>
+__global__ void rev_add_kernel(const T *__restrict__ recv, const int32_t *__restrict__ idx,
+                               int64_t n, T *__restrict__ w) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) w[idx[i]] = add_rn(w[idx[i]], recv[i]);
+}
+
+// Reverse direction of halo_enqueue: send recv-order halo contributions,
+// receive owned-row contributions.
+template <typename T>
+static int rev_halo_enqueue(Comm *c, const sla_halo_plan_t *p, const T *sendbuf, T *recvbuf,
+                            cudaStream_t s) {
+  SLA_CUDA_TRY(cudaEventRecord(c->ev_ready, s));
+  SLA_CUDA_TRY(cudaStreamWaitEvent(c->side, c->ev_ready, 0));
+  if (p->n_neighbors > 0) {
+    SLA_NCCL_TRY(ncclGroupStart());
+    for (int i = 0; i < p->n_neighbors; ++i) {
+      const int64_t ro = p->recv_offset[i], rc = p->recv_offset[i + 1] - ro;
+      const int64_t so = p->send_offset[i], sc = p->send_offset[i + 1] - so;
+      if (rc > 0)
+        SLA_NCCL_TRY(ncclSend(sendbuf + ro, (size_t)rc, nccl_type<T>(), p->neighbor_rank[i],
+                              c->nccl, c->side));
+      if (sc > 0)
+        SLA_NCCL_TRY(ncclRecv(recvbuf + so, (size_t)sc, nccl_type<T>(), p->neighbor_rank[i],
+                              c->nccl, c->side));
+    }
+    SLA_NCCL_TRY(ncclGroupEnd());
+  }
+  SLA_CUDA_TRY(cudaEventRecord(c->ev_halo, c->side));
+  SLA_CUDA_TRY(cudaStreamWaitEvent(s, c->ev_halo, 0));
+  return SLA_OK;
+}
+
+template <typename T>
+static int reverse_exchange(Comm *c, const sla_halo_plan_t *p, T *w, T *sendbuf, T *recvbuf,
+                            cudaStream_t s) {
+  const int64_t nh = p->n_halo, no = p->n_owned;
+  if (nh > 0)
+    SLA_LAUNCH(rev_pack_kernel<T>, grid_for(nh), kBlock, 0, s, w + no, p->halo_src, nh, sendbuf);
+  SLA_TRY(rev_halo_enqueue<T>(c, p, sendbuf, recvbuf, s));
+  for (int i = 0; i < p->n_neighbors; ++i) {  // ascending neighbours, one add pass each
+    const int64_t so = p->send_offset[i], sc = p->send_offset[i + 1] - so;
+    if (sc > 0)
+      SLA_LAUNCH(rev_add_kernel<T>, grid_for(sc), kBlock, 0, s, recvbuf + so, p->send_index + so,
+                 sc, w);
+  }
+  return SLA_OK;
+}
+
 // ================================================================ shard CG
 struct ShardState {
   int stopped;
@@ -856,6 +917,44 @@ int sla_shard_spmv(void *comm, const sla_halo_plan_t *plan, int dtype, const sla
   };
   if (dtype == SLA_F64) return run(double(0));
   if (dtype == SLA_F32) return run(float(0));
+  return SLA_ERR_INVALID;
+}
+
+int sla_reverse_halo_exchange(void *comm, const sla_halo_plan_t *plan, int dtype, void *w_local,
+                              void *sendbuf, void *recvbuf, sla_stream_t stream) {
+  Comm *c = (Comm *)comm;
+  if (!c || !c->nccl || !plan_ok(plan) || !w_local) return SLA_ERR_INVALID;
+  if ((plan->n_halo > 0 && !sendbuf) || (n_send(plan) > 0 && !recvbuf)) return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SLA_F64)
+    return reverse_exchange<double>(c, plan, (double *)w_local, (double *)sendbuf,
+                                    (double *)recvbuf, s);
+  if (dtype == SLA_F32)
+    return reverse_exchange<float>(c, plan, (float *)w_local, (float *)sendbuf, (float *)recvbuf,
+                                   s);
+  return SLA_ERR_INVALID;
+}
+
+int sla_shard_rmatvec(void *comm, const sla_halo_plan_t *plan, int dtype, const sla_sell_t *AT,
+                      const void *y_owned, void *w_local, void *sendbuf, void *recvbuf,
+                      sla_stream_t stream) {
+  Comm *c = (Comm *)comm;
+  if (!c || !c->nccl || !plan_ok(plan) || !sell_ok(AT) || !w_local) return SLA_ERR_INVALID;
+  if (AT->n_slots != plan->n_owned + plan->n_halo || AT->row_ids) return SLA_ERR_INVALID;
+  if ((plan->n_owned > 0 && !y_owned) || (plan->n_halo > 0 && !sendbuf) ||
+      (n_send(plan) > 0 && !recvbuf))
+    return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SLA_F64) {
+    SLA_TRY(spmv_launch<double>(AT, y_owned, w_local, s));
+    return reverse_exchange<double>(c, plan, (double *)w_local, (double *)sendbuf,
+                                    (double *)recvbuf, s);
+  }
+  if (dtype == SLA_F32) {
+    SLA_TRY(spmv_launch<float>(AT, y_owned, w_local, s));
+    return reverse_exchange<float>(c, plan, (float *)w_local, (float *)sendbuf, (float *)recvbuf,
+                                   s);
+  }
   return SLA_ERR_INVALID;
 }
 

@@ -5,11 +5,12 @@ from ..partition import (Partition, build_partition, build_partition_from_rows, 
 from .collectives import gather_owned_to_global
 from .comm import communicators, destroy_all
 from .core import DSparseSpec, DSparseTensor, OwnedShard, VertexShard
-from .matvec import halo_exchange, matmul_row_shard, shard_matvec
+from .matvec import (halo_exchange, matmul_row_shard, reverse_halo_exchange, shard_matvec,
+                     shard_rmatvec)
 from .solve import bicgstab_shard, cg_shard, make_preconditioner
 
 __all__ = ["DSparseTensor", "DSparseSpec", "VertexShard", "OwnedShard", "Partition",
            "partition_simple", "build_partition", "build_partition_from_rows", "find_halo_nodes",
            "resolve_partition_ids", "gather_owned_to_global", "halo_exchange", "shard_matvec",
-           "matmul_row_shard", "cg_shard", "bicgstab_shard", "make_preconditioner",
+           "matmul_row_shard", "reverse_halo_exchange", "shard_rmatvec", "cg_shard", "bicgstab_shard", "make_preconditioner",
            "communicators", "destroy_all"]

@@ -329,6 +329,11 @@ class DSparseTensor:
         from .matvec import shard_matvec
         return shard_matvec(self, x_owned)
 
+    def _shard_rmatvec(self, y_owned: torch.Tensor) -> torch.Tensor:
+        """Owned slice of A^T y (core.py:2017-2023)."""
+        from .matvec import shard_rmatvec
+        return shard_rmatvec(self, y_owned)
+
     def _shard_dot(self, u: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         d = torch.dot(u, v)
         if dist.is_initialized():

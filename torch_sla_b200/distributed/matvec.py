@@ -51,3 +51,47 @@ def matmul_row_shard(D, x):
     x_local = x.to_local() if _is_wrapped(x) else x
     y = shard_matvec(D, x_local)
     return D._wrap(y) if _is_wrapped(x) else y
+
+
+def _transpose_view(D):
+    plan = D._shard_plan()
+    if getattr(plan, "sell_t", None) is None:
+        from .._csr import DeviceCSR
+        st = D._local_tensor
+        nl = plan.n_owned + plan.n_halo
+        plan.csr_t = DeviceCSR(st.values, st.col_indices, st.row_indices, (nl, plan.n_owned))
+        plan.sell_t = plan.csr_t.sell()
+        plan.rev_send = torch.empty(max(plan.n_halo, 1), dtype=plan.dtype, device=plan.device)
+        plan.rev_recv = torch.empty(max(plan.n_send, 1), dtype=plan.dtype, device=plan.device)
+    return plan
+
+
+def reverse_halo_exchange(D, w: torch.Tensor, partition=None) -> torch.Tensor:
+    """Send the halo slots of w to their owners and add the incoming
+    contributions onto the owned slots, in place (matvec.py:96-170)."""
+    plan = _transpose_view(D)
+    L.require_cuda(w)
+    if w.numel() != plan.n_owned + plan.n_halo or not w.is_contiguous():
+        raise ValueError("reverse_halo_exchange expects a contiguous [num_owned + num_halo] vector")
+    comms = communicators(D._group)
+    L.check("sla_reverse_halo_exchange", L.lib().sla_reverse_halo_exchange(
+        comms.halo, plan.plan, L.dtype_code(w.dtype), L.ptr(w), L.ptr(plan.rev_send),
+        L.ptr(plan.rev_recv), L.stream_handle(w.device)))
+    return w
+
+
+def shard_rmatvec(D, y_owned: torch.Tensor) -> torch.Tensor:
+    """Owned slice of A^T y (matvec.py:306-348): local transpose SpMV, then the
+    reverse halo exchange."""
+    plan = _transpose_view(D)
+    L.require_cuda(y_owned)
+    if y_owned.shape[0] != plan.n_owned:
+        raise ValueError(f"y shape[0]={y_owned.shape[0]}, expected num_owned={plan.n_owned}")
+    y = y_owned.to(plan.dtype).contiguous()
+    nl = plan.n_owned + plan.n_halo
+    w = torch.empty(max(nl, 1), dtype=plan.dtype, device=plan.device)[:nl]
+    comms = communicators(D._group)
+    L.check("sla_shard_rmatvec", L.lib().sla_shard_rmatvec(
+        comms.halo, plan.plan, plan.code, plan.sell_t.ref(), L.ptr(y), L.ptr(w),
+        L.ptr(plan.rev_send), L.ptr(plan.rev_recv), L.stream_handle(plan.device)))
+    return w[: plan.n_owned].contiguous()
