@@ -108,14 +108,15 @@ def matrix_bytes(nnz: int, n: int, V: int = 8) -> int:
     return nnz * (V + 4) + 4 * (n + 1)
 
 
-def read_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` at the full workload from the ncu
-    summary profiles/traffic.txt ('<kernel> <bytes>' lines)."""
+def read_traffic(key: str):
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum)
+    of a kernel on one workload, from the ncu summary profiles/traffic.txt
+    ('<kernel>@<workload>:<size> <bytes>' lines); None when not captured."""
     try:
         with open(os.path.join(HERE, "profiles", "traffic.txt")) as f:
             for line in f:
                 parts = line.split()
-                if len(parts) >= 2 and parts[0] == kernel:
+                if len(parts) >= 2 and parts[0] == key:
                     return int(float(parts[1]))
     except OSError:
         pass
@@ -145,13 +146,14 @@ def base_line(args, metric, value, unit, ms, n_gpus, dtype="f64", hib=True):
             "data": "synthetic"}
 
 
-def roofline(kernel, alg_bytes, ms_total, launches, traffic_key=None):
+def roofline(kernel, alg_bytes, ms_total, launches, traffic_key):
     peak, kind = peaks()
     avg = ms_total / max(launches, 1)
     ach = alg_bytes / (avg / 1e3) / 1e9 if launches else None
     return {"kernel": kernel, "bound": "hbm", "achieved": None if ach is None else round(ach, 1),
             "peak": peak, "unit": "GB/s", "frac": None if ach is None else round(ach / peak, 4),
-            "traffic": read_traffic(traffic_key or kernel), "algorithmic_bytes": int(alg_bytes),
+            "traffic": read_traffic(traffic_key), "traffic_key": traffic_key,
+            "algorithmic_bytes": int(alg_bytes),
             "avg_launch_ms": round(avg, 5), "sampled_launches": launches,
             "peak_kind": "measured (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else kind}
 
@@ -194,7 +196,8 @@ def wl_pcg7(args, dev, local):
                       "format": "SELL-32 int32 (sigma=1)",
                       "l2": "inputs larger than L2 (1.4 GB matrix); no flush",
                       "parallelism": "single GPU"}
-    line["roofline"] = roofline("cg_spmv_kernel", matrix_bytes(nnz, n) + 5 * 8 * n, ka_ms, ka_n)
+    line["roofline"] = roofline("cg_spmv_kernel", matrix_bytes(nnz, n) + 5 * 8 * n, ka_ms, ka_n,
+                                f"cg_spmv_kernel@pcg7:{m}")
     line["roofline"]["update_kernel"] = {
         "kernel": "cg_update_kernel", "avg_launch_ms": round(kb_ms / max(kb_n, 1), 5),
         "achieved": round(7 * 8 * n / (kb_ms / max(kb_n, 1) / 1e3) / 1e9, 1) if kb_n else None}
@@ -285,6 +288,14 @@ def wl_cg2d(args, dev, local):
                       "kernel": "cg_persistent_kernel (one cooperative launch per solve)",
                       "iterations_per_s": round(sum(its) / (ms / 1e3), 1)}
     line["gpu_launches"] = L.launch_count() - l0
+    # unpreconditioned CG: matrix + 11 vector passes per iteration; the
+    # 9.9 MB working set stays in L2, so this is reported against HBM only
+    # for comparison (the kernel is bound by its two grid barriers per
+    # iteration, not by bandwidth)
+    per_iter = matrix_bytes(A.csr.nnz, sh[0]) + 11 * 8 * sh[0]
+    line["roofline"] = roofline("cg_persistent_kernel", per_iter * its[0], ms, args.steps,
+                                "cg_persistent_kernel@cg2d:256")
+    line["roofline"]["note"] = "L2-resident; one launch per solve"
     line["clocks"] = clk
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
@@ -376,7 +387,8 @@ def wl_batched(args, dev, local):
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
                                   "frac": round(iter_bytes * value / 1e9 / peak, 4)}
     line["roofline"] = roofline("batch_spmv_kernel",
-                                B * nnz * 8 + 4 * nnz + 4 * (n + 1) + 5 * B * 8 * n, ka_ms, ka_n)
+                                B * nnz * 8 + 4 * nnz + 4 * (n + 1) + 5 * B * 8 * n, ka_ms, ka_n,
+                                f"batch_spmv_kernel@batched:{B}x{m}")
     line["clocks"] = clk
     return line
 
@@ -414,7 +426,8 @@ def wl_bicgstab(args, dev, local):
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
                                   "frac": round(iter_bytes * value / 1e9 / peak, 4),
                                   "bytes_formula": "2 (12 nnz + 4 (N+1)) + 25 * 8 N"}
-    line["roofline"] = roofline("bicg_k1", matrix_bytes(nnz, n) + 6 * 8 * n, k1_ms, k1_n)
+    line["roofline"] = roofline("bicg_k1", matrix_bytes(nnz, n) + 6 * 8 * n, k1_ms, k1_n,
+                                f"bicg_k1@bicgstab:{m}")
     line["clocks"] = clk
     return line
 
@@ -538,7 +551,8 @@ def run_sharded(args, world, rank, local):
                                       "achieved_gbs_per_gpu":
                                           round(iter_bytes * value / world / 1e9, 1),
                                       "frac": round(iter_bytes * value / world / 1e9 / peak, 4)}
-        line["roofline"] = roofline(f"{kname} (interior rows)", ka_bytes, ka_ms, ka_n, kname)
+        line["roofline"] = roofline(f"{kname} (interior rows)", ka_bytes, ka_ms, ka_n,
+                                    f"{kname}@{wl}-shard:{m}")
         line["e2e"] = {"value": round(sum(e_its) * world / (e_ms / 1e3), 3),
                        "unit": "iterations/s", "h2d_bytes_per_step": n_loc * V * world,
                        "d2h_bytes_per_step": n_loc * V * world,

@@ -70,8 +70,14 @@ def _worker(rank, world, port, out_dir):
             if world > 1:
                 dist.all_reduce(wt)
             wt_ref = K.spmv(v, c, r, sh, case["b"])
+            # autograd of D @ x: the gradient is A^T w on the owned rows
+            xg = yo.clone().requires_grad_(True)
+            w = torch.linspace(-1.0, 2.0, sh[0], dtype=torch.float64)
+            ((D @ xg) * w.to(dev)[part.owned_nodes.to(dev)]).sum().backward()
+            g_ref = K.spmv(v, c, r, sh, w)[part.owned_nodes]
             res[name] = {"x": x, "iters": D._last_info["iterations"], "spmv_rel": _rel(y, y_ref),
-                         "halo_ok": halo_ok, "rmatvec_rel": _rel(wt.cpu(), wt_ref)}
+                         "halo_ok": halo_ok, "rmatvec_rel": _rel(wt.cpu(), wt_ref),
+                         "grad_rel": _rel(xg.grad.cpu(), g_ref)}
         # owned-rows construction on a slab-partitioned 7-point grid
         m = 12
         dims = (m * world, m, m)
@@ -116,6 +122,7 @@ def _check(results, golden_shard):
             got = res[name]
             assert got["spmv_rel"] < 1e-13, (name, got["spmv_rel"])
             assert got["rmatvec_rel"] < 1e-13, (name, got["rmatvec_rel"])
+            assert got["grad_rel"] < 1e-13, (name, got["grad_rel"])
             assert got["halo_ok"], name
             # stop tests run every 10 iterations: counts agree to that stride
             slack = 10 if case["method"] == "bicgstab" else max(1, math.ceil(0.03 * case["iters"]))
@@ -131,3 +138,8 @@ def test_shard_solvers_one_gpu(tmp_path, golden_shard):
 
 def test_shard_solvers_two_gpus(tmp_path, golden_shard):
     _check(_run(2, tmp_path), golden_shard)
+
+
+def test_shard_solvers_four_gpus(tmp_path, golden_shard):
+    """Middle ranks have two neighbours (one halo per side)."""
+    _check(_run(4, tmp_path), golden_shard)

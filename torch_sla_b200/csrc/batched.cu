@@ -32,109 +32,141 @@ batch_init_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict_
                   const T *__restrict__ vals, int64_t n, int B, const T *__restrict__ b_in,
                   T *__restrict__ x, T *__restrict__ r, T *__restrict__ p_old, T *__restrict__ dinv,
                   BatchState *st, BatchScalars sc, double *partials, double atol, double rtol) {
-  __shared__ double smem[2 * 1024];
-  const int rpb = blockDim.x / B;
-  const int bi = threadIdx.x % B, rl = threadIdx.x / B;
-  double acc[2] = {0.0, 0.0};
-  if (rl < rpb) {
-    for (int64_t row = (int64_t)blockIdx.x * rpb + rl; row < n; row += (int64_t)gridDim.x * rpb) {
-      T d = T(0);
-      for (int32_t k = rowptr[row]; k < rowptr[row + 1]; ++k)
-        if (colind[k] == (int32_t)row) d = vals[(int64_t)k * B + bi];
-      T di = (fabs(d) > T(0)) ? T(1) / d : T(1);
-      T bv = b_in[(int64_t)bi * n + row];
-      int64_t o = row * B + bi;
-      dinv[o] = di;
-      r[o] = bv;
-      x[o] = T(0);
-      p_old[o] = T(0);
-      T z = mul_rn(di, bv);
-      acc[0] += (double)bv * (double)z;
-      acc[1] += (double)bv * (double)bv;
-    }
+  extern __shared__ double smem[];
+  const BatchLane ln(B, 1);
+  const int bi = ln.m0;
+  double acc[2][1] = {{0.0}, {0.0}};
+  for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
+       row += (int64_t)gridDim.x * ln.rpb) {
+    T d = T(0);
+    for (int32_t k = rowptr[row]; k < rowptr[row + 1]; ++k)
+      if (colind[k] == (int32_t)row) d = vals[(int64_t)k * B + bi];
+    T di = (fabs(d) > T(0)) ? T(1) / d : T(1);
+    T bv = b_in[(int64_t)bi * n + row];
+    int64_t o = row * B + bi;
+    dinv[o] = di;
+    r[o] = bv;
+    x[o] = T(0);
+    p_old[o] = T(0);
+    T z = mul_rn(di, bv);
+    acc[0][0] += (double)bv * (double)z;
+    acc[1][0] += (double)bv * (double)bv;
   }
-  if (batch_last_block<2>(acc, B, smem, partials, &st->counter[0]) && threadIdx.x < B) {
-    sc.rz[threadIdx.x] = acc[0];
-    double bn = fmax(sqrt(acc[1]), 1e-30);
-    sc.tol[threadIdx.x] = fmax(rtol * bn, atol);
-    sc.beta[threadIdx.x] = 0.0;
-    if (threadIdx.x == 0) {
-      st->iter = 0;
-      st->done = st->maxiter <= 0 ? 2 : 0;
-      st->iters_out = 0;
-    }
+  if (!batch_reduce<2, 1>(acc, B, smem, partials, &st->counter[0])) return;
+  for (int m = threadIdx.x; m < B; m += blockDim.x) {
+    sc.rz[m] = smem[m];
+    double bn = fmax(sqrt(smem[B + m]), 1e-30);
+    sc.tol[m] = fmax(rtol * bn, atol);
+    sc.beta[m] = 0.0;
+  }
+  if (threadIdx.x == 0) {
+    st->iter = 0;
+    st->done = st->maxiter <= 0 ? 2 : 0;
+    st->iters_out = 0;
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(1024)
+// K_A: p = p_old * beta + D^-1 r formed inside the gather, Ap = A p, writes
+// p and Ap, per-member (p, Ap); the last block forms alpha.
+template <typename T, int VEC, int RB>
+__global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
 batch_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
                   const T *__restrict__ vals, int64_t n, int B, const T *__restrict__ r,
                   const T *__restrict__ dinv, const T *__restrict__ p_old, T *__restrict__ p_new,
                   T *__restrict__ Ap, BatchState *st, BatchScalars sc, double *partials) {
-  __shared__ double smem[1024];
+  extern __shared__ double smem[];
   if (*(volatile int *)&st->done) return;
-  const int rpb = blockDim.x / B;
-  const int bi = threadIdx.x % B, rl = threadIdx.x / B;
-  double acc[1] = {0.0};
-  if (rl < rpb) {
-    const T beta = (T)sc.beta[bi];
-    for (int64_t row = (int64_t)blockIdx.x * rpb + rl; row < n; row += (int64_t)gridDim.x * rpb) {
-      const T sum = csr_row_batched<T>(
-          colind, rowptr[row], rowptr[row + 1],
-          [&](int32_t k) { return ld_stream(vals + (int64_t)k * B + bi); },
-          [&](int32_t ci) {
-            const int64_t c = (int64_t)ci * B + bi;
-            return add_rn(mul_rn(__ldg(p_old + c), beta), mul_rn(__ldg(dinv + c), __ldg(r + c)));
-          });
-      const int64_t o = row * B + bi;
-      T pn = add_rn(mul_rn(p_old[o], beta), mul_rn(dinv[o], r[o]));
-      p_new[o] = pn;
-      Ap[o] = sum;
-      acc[0] += (double)pn * (double)sum;
+  const BatchLane ln(B, VEC);
+  T beta[VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) beta[u] = (T)sc.beta[ln.m0 + u];
+  double acc[1][VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) acc[0][u] = 0.0;
+  for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
+       row += (int64_t)gridDim.x * ln.rpb) {
+    T sum[VEC];
+    csr_row_vec<T, VEC, RB>(
+        colind, __ldg(rowptr + row), __ldg(rowptr + row + 1),
+        [&](int32_t k) { return vload<T, VEC, kLoadStream>(vals + (int64_t)k * B + ln.m0); },
+        [&](int32_t ci) {
+          const int64_t c = (int64_t)ci * B + ln.m0;
+          const Pack<T, VEC> po = vload<T, VEC, kLoadRO>(p_old + c);
+          const Pack<T, VEC> d = vload<T, VEC, kLoadRO>(dinv + c);
+          const Pack<T, VEC> rv = vload<T, VEC, kLoadRO>(r + c);
+          Pack<T, VEC> out;
+#pragma unroll
+          for (int u = 0; u < VEC; ++u)
+            out.v[u] = add_rn(mul_rn(po.v[u], beta[u]), mul_rn(d.v[u], rv.v[u]));
+          return out;
+        },
+        sum);
+    const int64_t o = row * B + ln.m0;
+    const Pack<T, VEC> po = vload<T, VEC, kLoadRO>(p_old + o);
+    const Pack<T, VEC> d = vload<T, VEC, kLoadRO>(dinv + o);
+    const Pack<T, VEC> rv = vload<T, VEC, kLoadRO>(r + o);
+    Pack<T, VEC> pn, ap;
+#pragma unroll
+    for (int u = 0; u < VEC; ++u) {
+      pn.v[u] = add_rn(mul_rn(po.v[u], beta[u]), mul_rn(d.v[u], rv.v[u]));
+      ap.v[u] = sum[u];
+      acc[0][u] += (double)pn.v[u] * (double)sum[u];
     }
+    vstore(p_new + o, pn);
+    vstore(Ap + o, ap);
   }
-  if (batch_last_block<1>(acc, B, smem, partials, &st->counter[1]) && threadIdx.x < B) {
-    double pap = acc[0];
-    sc.alpha[threadIdx.x] = sc.rz[threadIdx.x] / (fabs(pap) > 0.0 ? pap : 1e-30);
+  if (!batch_reduce<1, VEC>(acc, B, smem, partials, &st->counter[1])) return;
+  for (int m = threadIdx.x; m < B; m += blockDim.x) {
+    const double pap = smem[m];
+    sc.alpha[m] = sc.rz[m] / (fabs(pap) > 0.0 ? pap : 1e-30);
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(1024)
+// K_B: x += alpha p, r -= alpha Ap, per-member (r, r) and (r, D^-1 r); the
+// last block forms beta and the all-members stop test.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
 batch_update_kernel(int64_t n, int B, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
                     const T *__restrict__ Ap, const T *__restrict__ dinv, BatchState *st,
                     BatchScalars sc, double *partials) {
-  __shared__ double smem[2 * 1024];
+  extern __shared__ double smem[];
   __shared__ int s_all;
   if (*(volatile int *)&st->done) return;
-  const int rpb = blockDim.x / B;
-  const int bi = threadIdx.x % B, rl = threadIdx.x / B;
-  double acc[2] = {0.0, 0.0};
-  if (rl < rpb) {
-    const T alpha = (T)sc.alpha[bi];
-    for (int64_t row = (int64_t)blockIdx.x * rpb + rl; row < n; row += (int64_t)gridDim.x * rpb) {
-      const int64_t o = row * B + bi;
-      T xi = add_rn(x[o], mul_rn(alpha, p[o]));
-      T ri = sub_rn(r[o], mul_rn(alpha, Ap[o]));
-      x[o] = xi;
-      r[o] = ri;
-      T zi = mul_rn(dinv[o], ri);
-      acc[0] += (double)ri * (double)ri;
-      acc[1] += (double)ri * (double)zi;
+  const BatchLane ln(B, VEC);
+  T alpha[VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) alpha[u] = (T)sc.alpha[ln.m0 + u];
+  double acc[2][VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) acc[0][u] = acc[1][u] = 0.0;
+  for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
+       row += (int64_t)gridDim.x * ln.rpb) {
+    const int64_t o = row * B + ln.m0;
+    Pack<T, VEC> xv = vload<T, VEC>(x + o), rv = vload<T, VEC>(r + o);
+    const Pack<T, VEC> pv = vload<T, VEC, kLoadStream>(p + o);
+    const Pack<T, VEC> av = vload<T, VEC, kLoadStream>(Ap + o);
+    const Pack<T, VEC> dv = vload<T, VEC, kLoadRO>(dinv + o);
+#pragma unroll
+    for (int u = 0; u < VEC; ++u) {
+      xv.v[u] = add_rn(xv.v[u], mul_rn(alpha[u], pv.v[u]));
+      rv.v[u] = sub_rn(rv.v[u], mul_rn(alpha[u], av.v[u]));
+      const T zi = mul_rn(dv.v[u], rv.v[u]);
+      acc[0][u] += (double)rv.v[u] * (double)rv.v[u];
+      acc[1][u] += (double)rv.v[u] * (double)zi;
     }
+    vstore(x + o, xv);
+    vstore(r + o, rv);
   }
-  bool last = batch_last_block<2>(acc, B, smem, partials, &st->counter[2]);
-  if (!last) return;
+  if (!batch_reduce<2, VEC>(acc, B, smem, partials, &st->counter[2])) return;
   if (threadIdx.x == 0) s_all = 1;
   __syncthreads();
-  if (threadIdx.x < B) {
-    const int b = threadIdx.x;
-    sc.rr[b] = acc[0];
-    if (!(sqrt(acc[0]) <= sc.tol[b])) atomicAnd(&s_all, 0);
-    double rz_old = sc.rz[b];
-    sc.beta[b] = acc[1] / (fabs(rz_old) > 0.0 ? rz_old : 1e-30);
-    sc.rz[b] = acc[1];
+  for (int m = threadIdx.x; m < B; m += blockDim.x) {
+    const double rr = smem[m], rz = smem[B + m];
+    sc.rr[m] = rr;
+    if (!(sqrt(rr) <= sc.tol[m])) atomicAnd(&s_all, 0);
+    const double rz_old = sc.rz[m];
+    sc.beta[m] = rz / (fabs(rz_old) > 0.0 ? rz_old : 1e-30);
+    sc.rz[m] = rz;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -155,23 +187,49 @@ __global__ void batch_unpack_kernel(int64_t n, int B, const T *__restrict__ xi, 
   }
 }
 
-static size_t batch_ws_bytes(size_t elem, int64_t n, int64_t B, int G) {
-  return 6 * align_up(elem * (size_t)(n * B)) + 3 * align_up(2 * (size_t)B * G * sizeof(double)) +
+static size_t batch_ws_bytes(size_t elem, int64_t n, int64_t B) {
+  return 6 * align_up(elem * (size_t)(n * B)) +
+         3 * align_up(2 * (size_t)B * batch_max_grid() * sizeof(double)) +
          5 * align_up((size_t)B * sizeof(double)) + align_up(sizeof(BatchState));
+}
+
+// Row load batch of the vectorised SpMV: one dependent round trip covers a
+// row of up to RB entries (5- and 7-point stencils).
+
+template <typename T, int VEC>
+static int batched_loop(const int32_t *rowptr, const int32_t *colind, const T *vals, int64_t n,
+                        int B, T *xi, T *r, T *pA, T *pB, T *Ap, T *dinv, BatchState *st,
+                        BatchScalars sc, double *const part[3], int64_t maxiter, cudaStream_t s) {
+  auto spmv = batch_spmv_kernel<T, VEC, kBatchRB>;
+  auto upd = batch_update_kernel<T, VEC>;
+  const int TB = batch_block(B, VEC);
+  const size_t sm1 = batch_smem(1, TB, VEC), sm2 = batch_smem(2, TB, VEC);
+  const int G1 = occupancy_grid((const void *)spmv, TB, sm1);
+  const int G2 = occupancy_grid((const void *)upd, TB, sm2);
+  return run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
+    T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
+    cudaEvent_t ev;
+    profiler().begin(0, it, s, &ev);
+    SLA_LAUNCH(spmv, G1, TB, sm1, s, rowptr, colind, vals, n, B, r, dinv, p_old, p_new, Ap, st,
+               sc, part[1]);
+    profiler().end(0, s, ev);
+    profiler().begin(1, it, s, &ev);
+    SLA_LAUNCH(upd, G2, TB, sm2, s, n, B, xi, r, p_new, Ap, dinv, st, sc, part[2]);
+    profiler().end(1, s, ev);
+    return SLA_OK;
+  });
 }
 
 template <typename T>
 static int batched_impl(const int32_t *rowptr, const int32_t *colind, const T *vals, int64_t n,
                         int B, const T *b, T *x, double atol, double rtol, int64_t maxiter,
                         void *ws, size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
-  const int G = batch_grid(n, B);
-  const int TB = batch_block(B);
   Carver c(ws, ws_bytes);
   const size_t nb = (size_t)(n * B);
   T *r = c.take<T>(nb), *xi = c.take<T>(nb), *pA = c.take<T>(nb), *pB = c.take<T>(nb);
   T *Ap = c.take<T>(nb), *dinv = c.take<T>(nb);
   double *part[3];
-  for (int k = 0; k < 3; ++k) part[k] = c.take<double>(2 * (size_t)B * G);
+  for (int k = 0; k < 3; ++k) part[k] = c.take<double>(2 * (size_t)B * batch_max_grid());
   BatchScalars sc;
   sc.rz = c.take<double>(B); sc.alpha = c.take<double>(B); sc.beta = c.take<double>(B);
   sc.tol = c.take<double>(B); sc.rr = c.take<double>(B);
@@ -180,20 +238,24 @@ static int batched_impl(const int32_t *rowptr, const int32_t *colind, const T *v
   BatchState init{};
   init.maxiter = maxiter;
   SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(BatchState), cudaMemcpyHostToDevice, s));
-  SLA_LAUNCH(batch_init_kernel<T>, G, TB, 0, s, rowptr, colind, vals, n, B, b, xi, r, pA, dinv, st,
-             sc, part[0], atol, rtol);
-  SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
-    T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
-    cudaEvent_t ev;
-    profiler().begin(0, it, s, &ev);
-    SLA_LAUNCH(batch_spmv_kernel<T>, G, TB, 0, s, rowptr, colind, vals, n, B, r, dinv, p_old, p_new,
-               Ap, st, sc, part[1]);
-    profiler().end(0, s, ev);
-    profiler().begin(1, it, s, &ev);
-    SLA_LAUNCH(batch_update_kernel<T>, G, TB, 0, s, n, B, xi, r, p_new, Ap, dinv, st, sc, part[2]);
-    profiler().end(1, s, ev);
-    return SLA_OK;
-  }));
+  {
+    const int TB0 = batch_block(B, 1);
+    const size_t sm0 = batch_smem(2, TB0, 1);
+    const int G0 = occupancy_grid((const void *)batch_init_kernel<T>, TB0, sm0);
+    SLA_LAUNCH(batch_init_kernel<T>, G0, TB0, sm0, s, rowptr, colind, vals, n, B, b, xi, r, pA,
+               dinv, st, sc, part[0], atol, rtol);
+  }
+  // 16-byte vector groups of members where B allows it (the interleaved
+  // buffers are all 256-byte aligned)
+  constexpr int kVec = 16 / sizeof(T);
+  int rc;
+  if (B % kVec == 0 && aligned16(vals))
+    rc = batched_loop<T, kVec>(rowptr, colind, vals, n, B, xi, r, pA, pB, Ap, dinv, st, sc, part,
+                               maxiter, s);
+  else
+    rc = batched_loop<T, 1>(rowptr, colind, vals, n, B, xi, r, pA, pB, Ap, dinv, st, sc, part,
+                            maxiter, s);
+  SLA_TRY(rc);
   SLA_LAUNCH(batch_unpack_kernel<T>, grid_for(n * B), kBlock, 0, s, n, B, xi, x);
   BatchState out;
   SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(BatchState), cudaMemcpyDeviceToHost, s));
@@ -219,7 +281,7 @@ extern "C" {
 int sla_batched_cg_workspace(int dtype, int64_t n, int64_t batch, size_t *bytes) {
   if (!bytes || n < 0 || batch < 1 || batch > kMaxBatch) return SLA_ERR_INVALID;
   if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
-  *bytes = batch_ws_bytes(dtype == SLA_F64 ? 8 : 4, n, batch, batch_grid(n, (int)batch));
+  *bytes = batch_ws_bytes(dtype == SLA_F64 ? 8 : 4, n, batch);
   return SLA_OK;
 }
 

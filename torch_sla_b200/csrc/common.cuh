@@ -91,7 +91,7 @@ inline int solver_grid() { return device_info().sm_count * 8; }
 // One wave of resident blocks of `fn` on the current device (cached per
 // kernel): grid-stride kernels get no tail wave, and the grid (hence the
 // reduction order) is the same in every launch.
-int occupancy_grid(const void *fn, int block = kBlock);
+int occupancy_grid(const void *fn, int block = kBlock, size_t smem = 0);
 
 // True when every pointer is 16-byte aligned (vectorised streaming paths).
 inline bool aligned16() { return true; }

@@ -34,42 +34,41 @@ mrhs_init_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__
                  T *__restrict__ x, int guess, const T *__restrict__ dinv, T *__restrict__ r,
                  T *__restrict__ p_old, MrhsState *st, MrhsCols cs, double *partials,
                  double atol, double rtol) {
-  __shared__ double smem[2 * 1024];
-  const int rpb = blockDim.x / K;
-  const int bi = threadIdx.x % K, rl = threadIdx.x / K;
-  double acc[2] = {0.0, 0.0};
-  if (rl < rpb) {
-    for (int64_t row = (int64_t)blockIdx.x * rpb + rl; row < n; row += (int64_t)gridDim.x * rpb) {
-      const int64_t o = row * K + bi;
-      T bv = b[o];
-      T rv = bv;
-      if (guess) {  // R = B - A X0
-        T ax = T(0);
-        for (int32_t k = rowptr[row]; k < rowptr[row + 1]; ++k)
-          ax = fma(vals[k], x[(int64_t)colind[k] * K + bi], ax);
-        rv = sub_rn(bv, ax);
-      }
-      r[o] = rv;
-      p_old[o] = T(0);
-      T z = PREC ? mul_rn(dinv[row], rv) : rv;
-      acc[0] += (double)rv * (double)z;
-      acc[1] += (double)bv * (double)bv;
+  extern __shared__ double smem[];
+  const BatchLane ln(K, 1);
+  const int bi = ln.m0;
+  double acc[2][1] = {{0.0}, {0.0}};
+  for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
+       row += (int64_t)gridDim.x * ln.rpb) {
+    const int64_t o = row * K + bi;
+    T bv = b[o];
+    T rv = bv;
+    if (guess) {  // R = B - A X0
+      T ax = T(0);
+      for (int32_t k = rowptr[row]; k < rowptr[row + 1]; ++k)
+        ax = fma(vals[k], x[(int64_t)colind[k] * K + bi], ax);
+      rv = sub_rn(bv, ax);
     }
+    r[o] = rv;
+    p_old[o] = T(0);
+    T z = PREC ? mul_rn(dinv[row], rv) : rv;
+    acc[0][0] += (double)rv * (double)z;
+    acc[1][0] += (double)bv * (double)bv;
   }
-  if (batch_last_block<2>(acc, K, smem, partials, &st->counter[0]) && threadIdx.x < K) {
-    const int c = threadIdx.x;
-    cs.rz[c] = acc[0];
-    double bn = sqrt(acc[1]);
+  if (!batch_reduce<2, 1>(acc, K, smem, partials, &st->counter[0])) return;
+  for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    cs.rz[c] = smem[c];
+    double bn = sqrt(smem[K + c]);
     if (bn == 0.0) bn = 1.0;
     double tol = fmax(atol, rtol * bn);
     cs.tol_sq[c] = tol * tol;
     cs.beta[c] = 0.0;
     cs.iters[c] = 0;
     cs.conv[c] = 0;
-    if (c == 0) {
-      st->iter = 0;
-      st->done = st->maxiter <= 0 ? 2 : 0;
-    }
+  }
+  if (threadIdx.x == 0) {
+    st->iter = 0;
+    st->done = st->maxiter <= 0 ? 2 : 0;
   }
 }
 
@@ -82,82 +81,114 @@ __global__ void zero_kernel(T *__restrict__ x, int64_t n) {
   for (; i < n; i += stride) x[i] = T(0);
 }
 
-template <typename T, bool PREC>
-__global__ void __launch_bounds__(1024)
+// P = Z + beta P (pytorch_backend.py:2487) formed inside the gather, AP = A P,
+// per-column (P, AP); the last block forms alpha with (P, AP) <= 0 -> 1.
+template <typename T, bool PREC, int VEC, int RB>
+__global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
 mrhs_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
                  const T *__restrict__ vals, int64_t n, int K, const T *__restrict__ r,
                  const T *__restrict__ dinv, const T *__restrict__ p_old, T *__restrict__ p_new,
                  T *__restrict__ Ap, MrhsState *st, MrhsCols cs, double *partials) {
-  __shared__ double smem[1024];
+  extern __shared__ double smem[];
   if (*(volatile int *)&st->done) return;
-  const int rpb = blockDim.x / K;
-  const int bi = threadIdx.x % K, rl = threadIdx.x / K;
-  double acc[1] = {0.0};
-  if (rl < rpb) {
-    const T beta = (T)cs.beta[bi];
-    for (int64_t row = (int64_t)blockIdx.x * rpb + rl; row < n; row += (int64_t)gridDim.x * rpb) {
-      // P = Z + beta P (pytorch_backend.py:2487), formed inside the gather
-      const T sum = csr_row_batched<T>(
-          colind, rowptr[row], rowptr[row + 1], [&](int32_t k) { return __ldg(vals + k); },
-          [&](int32_t cidx) {
-            const int64_t c = (int64_t)cidx * K + bi;
-            T z = PREC ? mul_rn(__ldg(dinv + cidx), __ldg(r + c)) : __ldg(r + c);
-            return add_rn(z, mul_rn(beta, __ldg(p_old + c)));
-          });
-      const int64_t o = row * K + bi;
-      T z = PREC ? mul_rn(dinv[row], r[o]) : r[o];
-      T pn = add_rn(z, mul_rn(beta, p_old[o]));
-      p_new[o] = pn;
-      Ap[o] = sum;
-      acc[0] += (double)pn * (double)sum;
+  const BatchLane ln(K, VEC);
+  T beta[VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) beta[u] = (T)cs.beta[ln.m0 + u];
+  double acc[1][VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) acc[0][u] = 0.0;
+  for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
+       row += (int64_t)gridDim.x * ln.rpb) {
+    T sum[VEC];
+    csr_row_vec<T, VEC, RB>(
+        colind, __ldg(rowptr + row), __ldg(rowptr + row + 1),
+        [&](int32_t k) { return splat<T, VEC>(__ldg(vals + k)); },
+        [&](int32_t ci) {
+          const int64_t c = (int64_t)ci * K + ln.m0;
+          const Pack<T, VEC> rv = vload<T, VEC, kLoadRO>(r + c);
+          const Pack<T, VEC> po = vload<T, VEC, kLoadRO>(p_old + c);
+          const T d = PREC ? __ldg(dinv + ci) : T(1);
+          Pack<T, VEC> out;
+#pragma unroll
+          for (int u = 0; u < VEC; ++u) {
+            const T z = PREC ? mul_rn(d, rv.v[u]) : rv.v[u];
+            out.v[u] = add_rn(z, mul_rn(beta[u], po.v[u]));
+          }
+          return out;
+        },
+        sum);
+    const int64_t o = row * K + ln.m0;
+    const Pack<T, VEC> rv = vload<T, VEC, kLoadRO>(r + o);
+    const Pack<T, VEC> po = vload<T, VEC, kLoadRO>(p_old + o);
+    const T d = PREC ? __ldg(dinv + row) : T(1);
+    Pack<T, VEC> pn, ap;
+#pragma unroll
+    for (int u = 0; u < VEC; ++u) {
+      const T z = PREC ? mul_rn(d, rv.v[u]) : rv.v[u];
+      pn.v[u] = add_rn(z, mul_rn(beta[u], po.v[u]));
+      ap.v[u] = sum[u];
+      acc[0][u] += (double)pn.v[u] * (double)sum[u];
     }
+    vstore(p_new + o, pn);
+    vstore(Ap + o, ap);
   }
-  if (batch_last_block<1>(acc, K, smem, partials, &st->counter[1]) && threadIdx.x < K) {
-    double pap = acc[0];
-    cs.alpha[threadIdx.x] = cs.rz[threadIdx.x] / (pap > 0.0 ? pap : 1.0);
+  if (!batch_reduce<1, VEC>(acc, K, smem, partials, &st->counter[1])) return;
+  for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    const double pap = smem[c];
+    cs.alpha[c] = cs.rz[c] / (pap > 0.0 ? pap : 1.0);
   }
 }
 
-template <typename T, bool PREC>
-__global__ void __launch_bounds__(1024)
+template <typename T, bool PREC, int VEC>
+__global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
 mrhs_update_kernel(int64_t n, int K, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
                    const T *__restrict__ Ap, const T *__restrict__ dinv, MrhsState *st,
                    MrhsCols cs, double *partials) {
-  __shared__ double smem[2 * 1024];
+  extern __shared__ double smem[];
   __shared__ int s_all;
   if (*(volatile int *)&st->done) return;
-  const int rpb = blockDim.x / K;
-  const int bi = threadIdx.x % K, rl = threadIdx.x / K;
-  double acc[2] = {0.0, 0.0};
-  if (rl < rpb) {
-    const T alpha = (T)cs.alpha[bi];
-    for (int64_t row = (int64_t)blockIdx.x * rpb + rl; row < n; row += (int64_t)gridDim.x * rpb) {
-      const int64_t o = row * K + bi;
-      T xi = add_rn(x[o], mul_rn(alpha, p[o]));
-      T ri = sub_rn(r[o], mul_rn(alpha, Ap[o]));
-      x[o] = xi;
-      r[o] = ri;
-      T zi = PREC ? mul_rn(dinv[row], ri) : ri;
-      acc[0] += (double)ri * (double)ri;
-      acc[1] += (double)ri * (double)zi;
+  const BatchLane ln(K, VEC);
+  T alpha[VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) alpha[u] = (T)cs.alpha[ln.m0 + u];
+  double acc[2][VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) acc[0][u] = acc[1][u] = 0.0;
+  for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
+       row += (int64_t)gridDim.x * ln.rpb) {
+    const int64_t o = row * K + ln.m0;
+    Pack<T, VEC> xv = vload<T, VEC>(x + o), rv = vload<T, VEC>(r + o);
+    const Pack<T, VEC> pv = vload<T, VEC, kLoadStream>(p + o);
+    const Pack<T, VEC> av = vload<T, VEC, kLoadStream>(Ap + o);
+    const T d = PREC ? __ldg(dinv + row) : T(1);
+#pragma unroll
+    for (int u = 0; u < VEC; ++u) {
+      xv.v[u] = add_rn(xv.v[u], mul_rn(alpha[u], pv.v[u]));
+      rv.v[u] = sub_rn(rv.v[u], mul_rn(alpha[u], av.v[u]));
+      const T zi = PREC ? mul_rn(d, rv.v[u]) : rv.v[u];
+      acc[0][u] += (double)rv.v[u] * (double)rv.v[u];
+      acc[1][u] += (double)rv.v[u] * (double)zi;
     }
+    vstore(x + o, xv);
+    vstore(r + o, rv);
   }
-  if (!batch_last_block<2>(acc, K, smem, partials, &st->counter[2])) return;
+  if (!batch_reduce<2, VEC>(acc, K, smem, partials, &st->counter[2])) return;
   const long long it = st->iter + 1;
   const bool check = (it % st->check_every) == 0;
   if (threadIdx.x == 0) s_all = 1;
   __syncthreads();
-  if (threadIdx.x < K) {
-    const int c = threadIdx.x;
-    cs.rr[c] = acc[0];
-    if (check && !cs.conv[c] && acc[0] < cs.tol_sq[c]) {
+  for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    const double rr = smem[c], rz = smem[K + c];
+    cs.rr[c] = rr;
+    if (check && !cs.conv[c] && rr < cs.tol_sq[c]) {
       cs.conv[c] = 1;
       cs.iters[c] = it;
     }
     if (!cs.conv[c]) atomicAnd(&s_all, 0);
-    double rz_old = cs.rz[c];
-    cs.beta[c] = acc[1] / (rz_old + 1e-30);
-    cs.rz[c] = acc[1];
+    const double rz_old = cs.rz[c];
+    cs.beta[c] = rz / (rz_old + 1e-30);
+    cs.rz[c] = rz;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -167,10 +198,34 @@ mrhs_update_kernel(int64_t n, int K, T *__restrict__ x, T *__restrict__ r, const
   }
 }
 
-static size_t mrhs_ws_bytes(size_t elem, int64_t n, int64_t K, int G) {
-  return 5 * align_up(elem * (size_t)(n * K)) + 3 * align_up(2 * (size_t)K * G * sizeof(double)) +
+static size_t mrhs_ws_bytes(size_t elem, int64_t n, int64_t K) {
+  return 4 * align_up(elem * (size_t)(n * K)) +
+         3 * align_up(2 * (size_t)K * batch_max_grid() * sizeof(double)) +
          5 * align_up((size_t)K * sizeof(double)) + align_up((size_t)K * sizeof(long long)) +
          align_up((size_t)K * sizeof(int)) + align_up(sizeof(MrhsState));
+}
+
+
+template <typename T, bool PREC, int VEC>
+static int mrhs_loop(const int32_t *rowptr, const int32_t *colind, const T *vals, int64_t n, int K,
+                     const T *dinv, T *x, T *r, T *pA, T *pB, T *Ap, MrhsState *st, MrhsCols cs,
+                     double *const part[3], int64_t maxiter, cudaStream_t s) {
+  auto spmv = mrhs_spmv_kernel<T, PREC, VEC, kBatchRB>;
+  auto upd = mrhs_update_kernel<T, PREC, VEC>;
+  const int TB = batch_block(K, VEC);
+  const size_t sm1 = batch_smem(1, TB, VEC), sm2 = batch_smem(2, TB, VEC);
+  const int G1 = occupancy_grid((const void *)spmv, TB, sm1);
+  const int G2 = occupancy_grid((const void *)upd, TB, sm2);
+  return run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
+    T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
+    cudaEvent_t ev;
+    profiler().begin(0, it, s, &ev);
+    SLA_LAUNCH(spmv, G1, TB, sm1, s, rowptr, colind, vals, n, K, r, dinv, p_old, p_new, Ap, st,
+               cs, part[1]);
+    profiler().end(0, s, ev);
+    SLA_LAUNCH(upd, G2, TB, sm2, s, n, K, x, r, p_new, Ap, dinv, st, cs, part[2]);
+    return SLA_OK;
+  });
 }
 
 template <typename T, bool PREC>
@@ -178,14 +233,11 @@ static int mrhs_impl(const int32_t *rowptr, const int32_t *colind, const T *vals
                      const T *dinv, const T *b, T *x, bool guess, double atol, double rtol,
                      int64_t maxiter, int64_t every, int64_t *iters_out, int32_t *conv_out,
                      void *ws, size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
-  const int G = batch_grid(n, K);
-  const int TB = batch_block(K);
   Carver c(ws, ws_bytes);
   const size_t nk = (size_t)(n * K);
   T *r = c.take<T>(nk), *pA = c.take<T>(nk), *pB = c.take<T>(nk), *Ap = c.take<T>(nk);
-  c.take<T>(nk);
   double *part[3];
-  for (int q = 0; q < 3; ++q) part[q] = c.take<double>(2 * (size_t)K * G);
+  for (int q = 0; q < 3; ++q) part[q] = c.take<double>(2 * (size_t)K * batch_max_grid());
   MrhsCols cs;
   cs.rz = c.take<double>(K); cs.alpha = c.take<double>(K); cs.beta = c.take<double>(K);
   cs.tol_sq = c.take<double>(K); cs.rr = c.take<double>(K);
@@ -197,20 +249,25 @@ static int mrhs_impl(const int32_t *rowptr, const int32_t *colind, const T *vals
   init.maxiter = maxiter;
   init.check_every = every;
   SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(init), cudaMemcpyHostToDevice, s));
-  SLA_LAUNCH((mrhs_init_kernel<T, PREC>), G, TB, 0, s, rowptr, colind, vals, n, K, b, x,
-             guess ? 1 : 0, dinv, r, pA, st, cs, part[0], atol, rtol);
+  {
+    auto init_fn = mrhs_init_kernel<T, PREC>;
+    const int TB0 = batch_block(K, 1);
+    const size_t sm0 = batch_smem(2, TB0, 1);
+    const int G0 = occupancy_grid((const void *)init_fn, TB0, sm0);
+    SLA_LAUNCH(init_fn, G0, TB0, sm0, s, rowptr, colind, vals, n, K, b, x, guess ? 1 : 0, dinv, r,
+               pA, st, cs, part[0], atol, rtol);
+  }
   if (!guess) SLA_LAUNCH(zero_kernel<T>, grid_for((int64_t)nk), kBlock, 0, s, x, (int64_t)nk);
-  SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
-    T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
-    cudaEvent_t ev;
-    profiler().begin(0, it, s, &ev);
-    SLA_LAUNCH((mrhs_spmv_kernel<T, PREC>), G, TB, 0, s, rowptr, colind, vals, n, K, r, dinv,
-               p_old, p_new, Ap, st, cs, part[1]);
-    profiler().end(0, s, ev);
-    SLA_LAUNCH((mrhs_update_kernel<T, PREC>), G, TB, 0, s, n, K, x, r, p_new, Ap, dinv, st, cs,
-               part[2]);
-    return SLA_OK;
-  }));
+  // 16-byte vector groups of columns where K and the caller's x allow it
+  constexpr int kVec = 16 / sizeof(T);
+  int rc;
+  if (K % kVec == 0 && aligned16(x))
+    rc = mrhs_loop<T, PREC, kVec>(rowptr, colind, vals, n, K, dinv, x, r, pA, pB, Ap, st, cs, part,
+                                  maxiter, s);
+  else
+    rc = mrhs_loop<T, PREC, 1>(rowptr, colind, vals, n, K, dinv, x, r, pA, pB, Ap, st, cs, part,
+                               maxiter, s);
+  SLA_TRY(rc);
   MrhsState out;
   std::vector<double> rr(K), tol_sq(K);
   std::vector<long long> its(K);
@@ -250,7 +307,7 @@ extern "C" {
 int sla_multi_rhs_cg_workspace(int dtype, int64_t n, int64_t k, size_t *bytes) {
   if (!bytes || n < 0 || k < 1 || k > 1024) return SLA_ERR_INVALID;
   if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
-  *bytes = mrhs_ws_bytes(dtype == SLA_F64 ? 8 : 4, n, k, batch_grid(n, (int)k));
+  *bytes = mrhs_ws_bytes(dtype == SLA_F64 ? 8 : 4, n, k);
   return SLA_OK;
 }
 

@@ -30,17 +30,17 @@ const DeviceInfo &device_info() {
   return cache.emplace(dev, info).first->second;
 }
 
-int occupancy_grid(const void *fn, int block) {
+int occupancy_grid(const void *fn, int block, size_t smem) {
   static std::mutex mu;
-  static std::map<std::tuple<int, const void *, int>, int> cache;
+  static std::map<std::tuple<int, const void *, int, size_t>, int> cache;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
-  auto key = std::make_tuple(dev, fn, block);
+  auto key = std::make_tuple(dev, fn, block, smem);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, block, 0) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, block, smem) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
   const int sms = device_info().sm_count;

@@ -45,11 +45,31 @@ def shard_matvec(D, x_owned: torch.Tensor) -> torch.Tensor:
     return y
 
 
+class _RowShardMatvec(torch.autograd.Function):
+    """y = A x on the owned rows; the backward pass is the distributed
+    adjoint A^T g (local transpose SpMV + reverse halo exchange), so every
+    rank takes part in it."""
+
+    @staticmethod
+    def forward(ctx, x_owned, D):
+        ctx.D = D
+        return shard_matvec(D, x_owned)
+
+    @staticmethod
+    def backward(ctx, g):
+        return shard_rmatvec(ctx.D, g.contiguous()), None
+
+
 def matmul_row_shard(D, x):
-    """D @ x for the row-storage layout (matvec.py:173-203)."""
+    """D @ x for the row-storage layout (matvec.py:173-203); differentiable
+    in an owned-size x."""
     from .core import _is_wrapped
     x_local = x.to_local() if _is_wrapped(x) else x
-    y = shard_matvec(D, x_local)
+    if (torch.is_grad_enabled() and x_local.requires_grad
+            and x_local.shape[0] == D._shard_plan().n_owned):
+        y = _RowShardMatvec.apply(x_local, D)
+    else:
+        y = shard_matvec(D, x_local)
     return D._wrap(y) if _is_wrapped(x) else y
 
 

@@ -6,7 +6,7 @@ implementation (that CPU path is torch-sla's, not a fallback of this
 package). The names rebound are torch-sla's patch points: `pytorch_solve` is
 bound by name in `linear_solve.py:60`, the batched CG and the shard
 functions are imported lazily at call time (`batch_solve.py:72,135`,
-`distributed/core.py:1693, 2013-2014`), so rebinding the module attributes
+`distributed/core.py:1693, 2013-2023`), so rebinding the module attributes
 is enough.
 """
 from __future__ import annotations
@@ -79,6 +79,9 @@ def install(torch_sla=None):
     for name in ("cg_shard", "bicgstab_shard"):
         setattr(ref_dsolve, name, _cuda_first(getattr(our_shard, name), getattr(ref_dsolve, name)))
         done.append(f"torch_sla.distributed.solve.{name}")
-    ref_dmv.shard_matvec = _cuda_first(our_matvec.shard_matvec, ref_dmv.shard_matvec)
-    done.append("torch_sla.distributed.matvec.shard_matvec")
+    # shard_matvec / shard_rmatvec are imported lazily by DSparseTensor
+    # (core.py:2013-2023); the halo exchanges are module globals of matvec.py
+    for name in ("shard_matvec", "shard_rmatvec", "halo_exchange", "reverse_halo_exchange"):
+        setattr(ref_dmv, name, _cuda_first(getattr(our_matvec, name), getattr(ref_dmv, name)))
+        done.append(f"torch_sla.distributed.matvec.{name}")
     return done
