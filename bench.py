@@ -146,16 +146,35 @@ def base_line(args, metric, value, unit, ms, n_gpus, dtype="f64", hib=True):
             "data": "synthetic"}
 
 
-def roofline(kernel, alg_bytes, ms_total, launches, traffic_key):
+def sell_format(sell, V=8):
+    """Layout of a SELL view and the matrix bytes that layout itself moves
+    per sweep (padding included): a diagonal-offset view reads values only,
+    the explicit layout values and int32 columns."""
+    if sell.diagonal_offsets:
+        return {"format": f"SELL-32 diagonal-offset ({sell.uniform_width} diagonals, "
+                          "no column array)", "matrix_bytes": sell.padded_nnz * V}
+    return {"format": "SELL-32 int32 (sigma=1)", "matrix_bytes": sell.padded_nnz * (V + 4)}
+
+
+def roofline(kernel, alg_bytes, ms_total, launches, traffic_key, format_bytes=None):
+    """achieved = algorithmic bytes (int32 CSR definition) / mean launch time;
+    format_* = the same time against the bytes the layout in use must move
+    (below the CSR figure for a diagonal-offset view, hence frac > format_frac
+    there)."""
     peak, kind = peaks()
     avg = ms_total / max(launches, 1)
     ach = alg_bytes / (avg / 1e3) / 1e9 if launches else None
-    return {"kernel": kernel, "bound": "hbm", "achieved": None if ach is None else round(ach, 1),
-            "peak": peak, "unit": "GB/s", "frac": None if ach is None else round(ach / peak, 4),
-            "traffic": read_traffic(traffic_key), "traffic_key": traffic_key,
-            "algorithmic_bytes": int(alg_bytes),
-            "avg_launch_ms": round(avg, 5), "sampled_launches": launches,
-            "peak_kind": "measured (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else kind}
+    out = {"kernel": kernel, "bound": "hbm", "achieved": None if ach is None else round(ach, 1),
+           "peak": peak, "unit": "GB/s", "frac": None if ach is None else round(ach / peak, 4),
+           "traffic": read_traffic(traffic_key), "traffic_key": traffic_key,
+           "algorithmic_bytes": int(alg_bytes),
+           "avg_launch_ms": round(avg, 5), "sampled_launches": launches,
+           "peak_kind": "measured (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else kind}
+    if format_bytes is not None and launches:
+        fa = format_bytes / (avg / 1e3) / 1e9
+        out.update({"format_bytes": int(format_bytes), "format_achieved": round(fa, 1),
+                    "format_frac": round(fa / peak, 4)})
+    return out
 
 
 # ----------------------------------------------------- single-GPU workloads
@@ -189,15 +208,16 @@ def wl_pcg7(args, dev, local):
     value = iters / (ms / 1e3)
     peak, kind = peaks()
     iter_bytes = matrix_bytes(nnz, n) + 13 * 8 * n
+    fm = sell_format(A.sell())
     line = base_line(args, METRIC, value, "iterations/s", ms, 1)
     line["config"] = {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [m, m, m], "n": n,
                       "nnz": nnz, "rtol": RTOL, "b": "N(0,1) seed 1",
                       "iterations_per_solve": iters // args.steps,
-                      "format": "SELL-32 int32 (sigma=1)",
-                      "l2": "inputs larger than L2 (1.4 GB matrix); no flush",
+                      "format": fm["format"],
+                      "l2": "inputs larger than L2 (0.9-1.4 GB matrix); no flush",
                       "parallelism": "single GPU"}
     line["roofline"] = roofline("cg_spmv_kernel", matrix_bytes(nnz, n) + 5 * 8 * n, ka_ms, ka_n,
-                                f"cg_spmv_kernel@pcg7:{m}")
+                                f"cg_spmv_kernel@pcg7:{m}", fm["matrix_bytes"] + 5 * 8 * n)
     line["roofline"]["update_kernel"] = {
         "kernel": "cg_update_kernel", "avg_launch_ms": round(kb_ms / max(kb_n, 1), 5),
         "achieved": round(7 * 8 * n / (kb_ms / max(kb_n, 1) / 1e3) / 1e9, 1) if kb_n else None}
@@ -205,7 +225,10 @@ def wl_pcg7(args, dev, local):
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
                                   "frac": round(iter_bytes * value / 1e9 / peak, 4),
                                   "frac_of_8tbs": round(iter_bytes * value / 8e12, 4),
-                                  "bytes_formula": "12 nnz + 4 (N+1) + 13 * 8 N"}
+                                  "bytes_formula": "12 nnz + 4 (N+1) + 13 * 8 N",
+                                  "format_bytes_per_iter": fm["matrix_bytes"] + 12 * 8 * n,
+                                  "format_frac": round((fm["matrix_bytes"] + 12 * 8 * n) * value
+                                                       / 1e9 / peak, 4)}
     if not args.no_e2e:
         line["e2e"] = e2e_pcg7(args, v, r, c, b_host, sh, dev)
     line["gpu_launches"] = launches
@@ -223,6 +246,7 @@ def e2e_pcg7(args, v, r, c, b_host, sh, dev):
     from torch_sla_b200.backends import pytorch_backend as PB
     vh, rh, ch = v.cpu().pin_memory(), r.cpu().pin_memory(), c.cpu().pin_memory()
     bh = b_host.pin_memory()
+    xh = torch.empty_like(bh).pin_memory()
     h2d = (vh.numel() + rh.numel() + ch.numel() + bh.numel()) * 8
     steps = max(1, min(args.steps, 3))
 
@@ -230,7 +254,7 @@ def e2e_pcg7(args, v, r, c, b_host, sh, dev):
         vd, rd, cd, bd = (t.to(dev, non_blocking=True) for t in (vh, rh, ch, bh))
         x = T.pytorch_solve(vd, rd, cd, sh, bd, method="cg", atol=0.0, rtol=RTOL,
                             preconditioner="jacobi")
-        x.cpu()
+        xh.copy_(x)  # device -> pinned host read of the solution
         return PB.last_solve_info()["iterations"]
 
     ms, its, _ = timed(once, steps, dev, dev.index)
@@ -328,12 +352,17 @@ def wl_spmv(args, dev, local):
             spmv(sell, x, n, y)
         ms, _, clk = timed(lambda: spmv(sell, x, n, y), reps, dev, local)
         alg = matrix_bytes(csr.nnz, n, V) + 2 * V * n
+        fm = sell_format(sell, V)
+        fb = fm["matrix_bytes"] + 2 * V * n
         sec = ms / reps / 1e3
         res["f64" if V == 8 else "f32"] = {"us_per_spmv": round(sec * 1e6, 2),
                                           "achieved_gbs": round(alg / sec / 1e9, 1),
                                           "frac": round(alg / sec / 1e9 / peak, 4),
                                           "frac_of_8tbs": round(alg / sec / 8e12, 4),
-                                          "algorithmic_bytes": alg, "clocks": clk}
+                                          "algorithmic_bytes": alg, "format": fm["format"],
+                                          "format_bytes": fb,
+                                          "format_frac": round(fb / sec / 1e9 / peak, 4),
+                                          "clocks": clk}
         del csr, sell, x, y
     line = base_line(args, "SpMV HBM GB/s (256^3 7-point, fp64)", res["f64"]["achieved_gbs"],
                      "GB/s", res["f64"]["us_per_spmv"] / 1e3 * args.steps, 1)
@@ -426,8 +455,10 @@ def wl_bicgstab(args, dev, local):
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
                                   "frac": round(iter_bytes * value / 1e9 / peak, 4),
                                   "bytes_formula": "2 (12 nnz + 4 (N+1)) + 25 * 8 N"}
+    fm = sell_format(A.sell())
+    line["config"]["format"] = fm["format"]
     line["roofline"] = roofline("bicg_k1", matrix_bytes(nnz, n) + 6 * 8 * n, k1_ms, k1_n,
-                                f"bicg_k1@bicgstab:{m}")
+                                f"bicg_k1@bicgstab:{m}", fm["matrix_bytes"] + 6 * 8 * n)
     line["clocks"] = clk
     return line
 
@@ -511,9 +542,11 @@ def run_sharded(args, world, rank, local):
     e_steps = max(1, min(args.steps, 3))
     dist.barrier()
 
+    x_host = torch.empty_like(b_host).pin_memory()
+
     def e2e_once():
         x, it = once(b_host.to(dev, non_blocking=True))
-        x.cpu()
+        x_host.copy_(x.to_local() if hasattr(x, "to_local") else x)  # pinned read-back
         return it
     e_ms_local, e_its, _ = timed(e2e_once, e_steps, dev, local)
     te = torch.tensor([e_ms_local], dtype=torch.float64, device=dev)
@@ -522,16 +555,23 @@ def run_sharded(args, world, rank, local):
 
     V = 8
     interior_frac = plan.sell_int.n_slots / max(n_loc, 1)
+    fm_int = sell_format(plan.sell_int, V)
+    exchange = ("halo values and dot products stored into peer GPUs' memory by the solver "
+                "kernels (CUDA IPC over NVLink), 2 launches per iteration"
+                if method == "cg" and plan.p2p is not None else
+                "NCCL grouped send/recv halo + allreduce per reduction point")
     mat = matrix_bytes(nnz, n_loc)
     if method == "cg":
         metric = (METRIC if wl == "pcg7" else
                   "fp64 Jacobi-PCG iterations/s (3-D 27-point, 256^3 unknowns per GPU)")
         ka_bytes = (mat + 5 * V * n_loc) * interior_frac
+        ka_fmt = fm_int["matrix_bytes"] + 5 * V * plan.sell_int.n_slots
         iter_bytes = mat + 13 * V * n_loc
         kname = "shard_cg_spmv"
     else:
         metric = "fp64 Jacobi-BiCGStab iterations/s (convection-diffusion, 192^3 per GPU)"
         ka_bytes = (mat + 6 * V * n_loc) * interior_frac
+        ka_fmt = fm_int["matrix_bytes"] + 6 * V * plan.sell_int.n_slots
         iter_bytes = 2 * mat + 25 * V * n_loc
         kname = "shard_bi_k1"
     peak, _ = peaks()
@@ -545,14 +585,15 @@ def run_sharded(args, world, rank, local):
                           "iterations_per_solve": iters // args.steps,
                           "partition": "z-slabs (partition_simple), one-layer halos",
                           "halo_bytes_per_neighbour": m * m * V, "check_every": 10,
-                          "format": "SELL-32 int32 (sigma=1)", "l2": "inputs larger than L2",
-                          "parallelism": f"row-sharded x{world} (NCCL send/recv + allreduce)"}
+                          "format": fm_int["format"] + " interior rows; explicit boundary rows",
+                          "l2": "inputs larger than L2",
+                          "parallelism": f"row-sharded x{world} ({exchange})"}
         line["iteration_roofline"] = {"bytes_per_iter_per_gpu": iter_bytes,
                                       "achieved_gbs_per_gpu":
                                           round(iter_bytes * value / world / 1e9, 1),
                                       "frac": round(iter_bytes * value / world / 1e9 / peak, 4)}
         line["roofline"] = roofline(f"{kname} (interior rows)", ka_bytes, ka_ms, ka_n,
-                                    f"{kname}@{wl}-shard:{m}")
+                                    f"{kname}@{wl}-shard:{m}", ka_fmt)
         line["e2e"] = {"value": round(sum(e_its) * world / (e_ms / 1e3), 3),
                        "unit": "iterations/s", "h2d_bytes_per_step": n_loc * V * world,
                        "d2h_bytes_per_step": n_loc * V * world,

@@ -64,7 +64,16 @@ enum {
 
 /* SELL-32 (SELL-C-sigma with C = 32, sigma = 1) matrix view. Slice s holds
  * 32 consecutive row slots; entry j of slot l sits at
- * slice_ptr[s] + 32*j + l. Padding entries have col == -1. */
+ * slice_ptr[s] + 32*j + l. Padding entries have col == -1.
+ *
+ * Diagonal-offset views (n_diags > 0): every row's columns lie on the
+ * n_diags diagonals diag_offsets[0] < ... < diag_offsets[n_diags-1]; the
+ * layout is uniform (width n_diags), entry j of a slot belongs to column
+ * row + diag_offsets[j] and `col` is not stored (NULL). Entries whose
+ * diagonal the row does not use, or whose column falls outside
+ * [0, n_cols), hold value 0 and are skipped. The summation order of a row
+ * (ascending column) is the same as in the explicit layout. */
+#define SLA_MAX_DIAGS 32
 typedef struct {
   int64_t n_slots;           /* row slots covered by this view               */
   int64_t n_slices;          /* ceil(n_slots / 32)                           */
@@ -76,6 +85,10 @@ typedef struct {
   int32_t max_width;         /* widest slice (entries per slot)              */
   int32_t uniform_width;     /* W when every slice has width W (then
                                 slice_ptr[s] == 32*W*s), else 0               */
+  int64_t n_cols;            /* columns of the matrix (diagonal-offset views) */
+  int64_t row_base;          /* row_ids == NULL: slot i is row row_base + i   */
+  int32_t n_diags;           /* > 0: diagonal-offset view, 5, 7 or 27          */
+  int32_t diag_offsets[SLA_MAX_DIAGS]; /* ascending, first n_diags used     */
 } sla_sell_t;
 
 typedef struct {
@@ -124,6 +137,28 @@ int sla_sell_fill(int dtype, const int32_t *rowptr, const int32_t *colind,
                   const void *vals, const int32_t *row_ids, int64_t n_slots,
                   const int32_t *slice_ptr, int32_t *sell_col, void *sell_val,
                   sla_stream_t stream);
+
+/* Distinct diagonal offsets (col - row) of the CSR rows listed in row_ids
+ * (or rows 0..n_slots-1). Writes up to SLA_MAX_DIAGS ascending offsets to
+ * the host array offsets_out and their count to *count_out; *count_out = -1
+ * when the rows use more than SLA_MAX_DIAGS diagonals. Synchronises the
+ * stream. */
+int sla_sell_diag_probe_workspace(size_t *bytes);
+int sla_sell_diag_probe(const int32_t *rowptr, const int32_t *colind,
+                        const int32_t *row_ids, int64_t n_slots,
+                        int32_t *offsets_out, int32_t *count_out,
+                        void *workspace, size_t workspace_bytes,
+                        sla_stream_t stream);
+/* Values of a diagonal-offset view (see sla_sell_t): sell_val holds
+ * ceil(n_slots/32)*32*n_diags entries and is fully written (0 where a row
+ * has no entry on a diagonal). Every CSR entry of the listed rows must lie
+ * on one of the n_diags ascending host-side offsets (SLA_ERR_INVALID
+ * otherwise). Workspace as for the probe. Synchronises the stream. */
+int sla_sell_diag_fill(int dtype, const int32_t *rowptr, const int32_t *colind,
+                       const void *vals, const int32_t *row_ids, int64_t n_slots,
+                       const int32_t *offsets, int32_t n_diags, void *sell_val,
+                       void *workspace, size_t workspace_bytes,
+                       sla_stream_t stream);
 
 /* Inverse diagonal for Jacobi (pytorch_backend.py:167-174, 221-235;
  * distributed/solve.py:95-115). Rows without a stored diagonal use d = 0. */
@@ -284,6 +319,29 @@ int sla_shard_bicgstab(void *comm_halo, void *comm_reduce,
                        int64_t maxiter, int64_t check_every, void *workspace,
                        size_t workspace_bytes, sla_solve_info_t *info,
                        sla_stream_t stream);
+
+/* Peer-memory shard CG (single node, 2..8 ranks; the same algorithm and
+ * stopping rule as sla_shard_cg, distributed/solve.py:279-350). Halo values
+ * and dot products are stored by the solver kernels directly into the other
+ * GPUs' memory through CUDA IPC mappings, so an iteration is two kernel
+ * launches and no NCCL call.
+ * sla_p2p_create is collective over `comm` (NCCL is used once to trade the
+ * IPC handles and agree): it maps every rank's exchange buffer and returns
+ * *p2p_out = NULL with SLA_OK on every rank when any rank cannot (more than
+ * 8 ranks, peer mapping refused, a halo permutation in the plan). The handle
+ * owns its device buffer; sla_p2p_destroy is collective (it waits until
+ * every rank is past its last remote store). Every cross-GPU wait inside the
+ * kernels is bounded; a peer that stops answering ends the solve with
+ * SLA_ERR_TIMEOUT. The ranks must call the solver the same number of times
+ * with the same arguments, as with sla_shard_cg. */
+int sla_p2p_create(void *comm, const sla_halo_plan_t *plan, int dtype, void **p2p_out);
+int sla_p2p_destroy(void *p2p);
+int sla_shard_cg_p2p(void *p2p, const sla_halo_plan_t *plan, int dtype,
+                     const sla_sell_t *A_interior, const sla_sell_t *A_boundary,
+                     const void *dinv, const void *b, void *x, double atol,
+                     double rtol, int64_t maxiter, int64_t check_every,
+                     void *workspace, size_t workspace_bytes,
+                     sla_solve_info_t *info, sla_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -91,7 +91,17 @@ def _worker(rank, world, port, out_dir):
         xo, ito = K.cg_shard(vg, rg, cg_, sh, b, atol=0.0, rtol=1e-8, maxiter=5000,
                              precond="jacobi")
         res["owned_rows"] = {"rel": _rel(x2.full_tensor().cpu(), xo),
-                             "iters": D2._last_info["iterations"], "oracle_iters": ito}
+                             "iters": D2._last_info["iterations"], "oracle_iters": ito,
+                             "p2p": D2._shard_plan().p2p is not None}
+        # the same solve on the NCCL path (peer-memory exchange disabled)
+        os.environ["TORCH_SLA_B200_P2P"] = "0"
+        D3 = DSparseTensor.from_owned_rows(vr, rr_, cr, (n, n), mesh=mesh)
+        x3 = D3.solve(D3.scatter(b.to(dev)), method="cg", preconditioner="jacobi", atol=0.0,
+                      rtol=1e-8, maxiter=5000)
+        del os.environ["TORCH_SLA_B200_P2P"]
+        res["owned_rows"].update(nccl_rel=_rel(x3.full_tensor().cpu(), xo),
+                                 nccl_iters=D3._last_info["iterations"],
+                                 nccl_p2p=D3._shard_plan().p2p is not None)
         destroy_all()
     finally:
         torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
@@ -130,6 +140,8 @@ def _check(results, golden_shard):
             assert _rel(got["x"], case["x"]) < 1e-6, name
         o = res["owned_rows"]
         assert o["iters"] == o["oracle_iters"] and o["rel"] < 1e-8, o
+        assert o["nccl_iters"] == o["oracle_iters"] and o["nccl_rel"] < 1e-8, o
+        assert not o["nccl_p2p"]
 
 
 def test_shard_solvers_one_gpu(tmp_path, golden_shard):
@@ -137,7 +149,9 @@ def test_shard_solvers_one_gpu(tmp_path, golden_shard):
 
 
 def test_shard_solvers_two_gpus(tmp_path, golden_shard):
-    _check(_run(2, tmp_path), golden_shard)
+    res = _run(2, tmp_path)
+    _check(res, golden_shard)
+    assert all(r["owned_rows"]["p2p"] for r in res)  # peer-memory path on one node
 
 
 def test_shard_solvers_four_gpus(tmp_path, golden_shard):

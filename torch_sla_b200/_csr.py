@@ -18,24 +18,44 @@ class Sell:
     """SELL-32 view (slice pointers, padded columns/values) of some CSR rows.
 
     uniform_width > 0 marks a layout whose slices all have that width, which
-    the kernels address arithmetically."""
+    the kernels address arithmetically. A diagonal-offset view (`offsets`
+    given, `col` None) stores no columns: entry j of a row belongs to column
+    row + offsets[j]."""
 
     def __init__(self, slice_ptr, col, val, n_slots, row_ids=None, max_width=0,
-                 uniform_width=0):
-        self.slice_ptr, self.col, self.val, self.row_ids = slice_ptr, col, val, row_ids
+                 uniform_width=0, n_cols=0, offsets=None):
+        self.slice_ptr, self.col, self.val = slice_ptr, col, val
+        self.row_base = 0
+        # a contiguous run of rows is addressed as row_base + slot (no row
+        # id loads in the kernels)
+        if row_ids is not None and row_ids.numel() > 0:
+            r0 = int(row_ids[0])
+            if int(row_ids[-1]) - r0 + 1 == row_ids.numel() and bool(
+                    (row_ids[1:] - row_ids[:-1] == 1).all()):
+                row_ids, self.row_base = None, r0
+        self.row_ids = row_ids
         self.n_slots = int(n_slots)
         self.n_slices = (self.n_slots + 31) // 32
         self.max_width = int(max_width)
         self.uniform_width = int(uniform_width)
+        self.n_cols = int(n_cols)
+        self.offsets = list(offsets) if offsets else []
+        arr = (L.c_i32 * L.MAX_DIAGS)(*self.offsets)
         self.view = L.SellView(self.n_slots, self.n_slices, L.ptr(slice_ptr), L.ptr(col),
-                               L.ptr(val), L.ptr(row_ids), self.max_width, self.uniform_width)
+                               L.ptr(val), L.ptr(self.row_ids), self.max_width,
+                               self.uniform_width, self.n_cols, self.row_base,
+                               len(self.offsets), arr)
 
     def ref(self):
         return ctypes.byref(self.view)
 
     @property
+    def diagonal_offsets(self) -> bool:
+        return bool(self.offsets)
+
+    @property
     def padded_nnz(self) -> int:
-        return int(self.col.numel())
+        return int(self.val.numel())
 
 
 class DeviceCSR:
@@ -84,9 +104,23 @@ class DeviceCSR:
         self._sell = None
 
     # ------------------------------------------------------------------ SELL
-    def sell(self, row_ids: torch.Tensor | None = None, values: torch.Tensor | None = None) -> Sell:
-        """SELL-32 view of all rows (row_ids=None) or of the listed rows."""
-        if row_ids is None and values is None and self._sell is not None:
+    # widths the kernels have diagonal-offset instantiations for
+    DIAG_WIDTHS = (5, 7, 27)
+    # largest padding (zero entries / stored entries) a diagonal-offset view
+    # may add over the rows' own entries
+    DIAG_MAX_PAD = 0.10
+
+    def sell(self, row_ids: torch.Tensor | None = None, values: torch.Tensor | None = None,
+             n_cols: int | None = None, diagonal: bool = True) -> Sell:
+        """SELL-32 view of all rows (row_ids=None) or of the listed rows.
+
+        When the rows' columns lie on 5, 7 or 27 diagonals (stencil
+        matrices) the view stores no column indices (diagonal-offset
+        layout); `n_cols` bounds the columns the kernels may touch (default:
+        the matrix's column count) and must exceed every stored column of
+        the rows. diagonal=False forces the explicit layout."""
+        cacheable = row_ids is None and values is None and n_cols is None and diagonal
+        if cacheable and self._sell is not None:
             return self._sell
         vals = self.vals if values is None else values
         if vals is None:
@@ -96,6 +130,53 @@ class DeviceCSR:
         n_slots = self.shape[0] if row_ids is None else int(row_ids.numel())
         if row_ids is not None:
             row_ids = row_ids.to(device=dev, dtype=torch.int32).contiguous()
+        n_cols = self.shape[1] if n_cols is None else int(n_cols)
+        n_slices = (n_slots + 31) // 32
+        stream = L.stream_handle(dev)
+        s = self._diagonal_view(row_ids, n_slots, n_cols, vals, stream) if diagonal else None
+        if s is None:
+            s = self._explicit_view(row_ids, n_slots, n_cols, vals, stream)
+        if cacheable:
+            self._sell = s
+        return s
+
+    def _diagonal_view(self, row_ids, n_slots, n_cols, vals, stream):
+        if n_slots == 0 or self.nnz == 0:
+            return None
+        lib = L.lib()
+        dev = self.device
+        need = ctypes.c_size_t(0)
+        L.check("sla_sell_diag_probe_workspace", lib.sla_sell_diag_probe_workspace(ctypes.byref(need)))
+        ws = L.workspace(need.value, dev)
+        offs = (L.c_i32 * L.MAX_DIAGS)()
+        count = L.c_i32(0)
+        L.check("sla_sell_diag_probe", lib.sla_sell_diag_probe(
+            L.ptr(self.rowptr), L.ptr(self.colind), L.ptr(row_ids), n_slots, offs,
+            ctypes.byref(count), L.ptr(ws), ws.numel(), stream))
+        w = int(count.value)
+        if w not in self.DIAG_WIDTHS:
+            return None
+        if row_ids is None:
+            nnz_view = self.nnz
+        else:
+            rl = row_ids.to(torch.int64)
+            nnz_view = int((self.rowptr[rl + 1] - self.rowptr[rl]).sum())
+        n_slices = (n_slots + 31) // 32
+        padded = n_slices * 32 * w
+        if padded > (1.0 + self.DIAG_MAX_PAD) * max(nnz_view, 1):
+            return None
+        sval = torch.empty(padded, dtype=self.dtype, device=dev)
+        L.check("sla_sell_diag_fill", lib.sla_sell_diag_fill(
+            self.code, L.ptr(self.rowptr), L.ptr(self.colind), L.ptr(vals), L.ptr(row_ids),
+            n_slots, offs, w, L.ptr(sval), L.ptr(ws), ws.numel(), stream))
+        slice_ptr = (torch.arange(n_slices + 1, device=dev, dtype=torch.int64) * (32 * w)).to(
+            torch.int32)
+        return Sell(slice_ptr, None, sval, n_slots, row_ids, max_width=w, uniform_width=w,
+                    n_cols=n_cols, offsets=list(offs)[:w])
+
+    def _explicit_view(self, row_ids, n_slots, n_cols, vals, stream):
+        lib = L.lib()
+        dev = self.device
         n_slices = (n_slots + 31) // 32
         slice_ptr = torch.empty(n_slices + 1, dtype=torch.int32, device=dev)
         need = ctypes.c_size_t(0)
@@ -103,7 +184,6 @@ class DeviceCSR:
         ws = L.workspace(need.value, dev)
         padded = ctypes.c_int64(0)
         widest = ctypes.c_int32(0)
-        stream = L.stream_handle(dev)
 
         def layout(min_width):
             L.check("sla_sell_layout", lib.sla_sell_layout(
@@ -123,11 +203,8 @@ class DeviceCSR:
         L.check("sla_sell_fill", lib.sla_sell_fill(
             self.code, L.ptr(self.rowptr), L.ptr(self.colind), L.ptr(vals), L.ptr(row_ids), n_slots,
             L.ptr(slice_ptr), L.ptr(scol), L.ptr(sval), stream))
-        s = Sell(slice_ptr, scol, sval, n_slots, row_ids, max_width=widest.value,
-                 uniform_width=uniform)
-        if row_ids is None and values is None:
-            self._sell = s
-        return s
+        return Sell(slice_ptr, scol, sval, n_slots, row_ids, max_width=widest.value,
+                    uniform_width=uniform, n_cols=n_cols)
 
     # --------------------------------------------------------------- helpers
     def jacobi_inverse(self, rule: int, n_rows: int | None = None) -> torch.Tensor:

@@ -27,10 +27,15 @@ c_i32, c_i64, c_dbl, c_ptr, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_dou
                                     ctypes.c_void_p, ctypes.c_size_t)
 
 
+MAX_DIAGS = 32  # SLA_MAX_DIAGS
+
+
 class SellView(ctypes.Structure):
     _fields_ = [("n_slots", c_i64), ("n_slices", c_i64), ("slice_ptr", c_ptr),
                 ("col", c_ptr), ("val", c_ptr), ("row_ids", c_ptr), ("max_width", c_i32),
-                ("uniform_width", c_i32)]
+                ("uniform_width", c_i32), ("n_cols", c_i64), ("row_base", c_i64),
+                ("n_diags", c_i32),
+                ("diag_offsets", c_i32 * MAX_DIAGS)]
 
 
 class SolveInfo(ctypes.Structure):
@@ -60,6 +65,11 @@ _SIGNATURES = {
                                        c_ptr, c_sz, c_ptr]),
     "sla_sell_fill": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr,
                                      c_ptr, c_ptr, c_ptr]),
+    "sla_sell_diag_probe_workspace": (ctypes.c_int, [_P(c_sz)]),
+    "sla_sell_diag_probe": (ctypes.c_int, [c_ptr, c_ptr, c_ptr, c_i64, _P(c_i32), _P(c_i32),
+                                           c_ptr, c_sz, c_ptr]),
+    "sla_sell_diag_fill": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_i64,
+                                          _P(c_i32), c_i32, c_ptr, c_ptr, c_sz, c_ptr]),
     "sla_jacobi_inverse": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_i64,
                                           ctypes.c_int, c_ptr, c_ptr]),
     "sla_spmv": (ctypes.c_int, [ctypes.c_int, _P(SellView), c_ptr, c_ptr, c_ptr]),
@@ -105,6 +115,11 @@ _SIGNATURES = {
                                           _P(SellView), _P(SellView), c_ptr, c_ptr, c_ptr, c_dbl,
                                           c_dbl, c_i64, c_i64, c_ptr, c_sz, _P(SolveInfo),
                                           c_ptr]),
+    "sla_p2p_create": (ctypes.c_int, [c_ptr, _P(HaloPlan), ctypes.c_int, _P(c_ptr)]),
+    "sla_p2p_destroy": (ctypes.c_int, [c_ptr]),
+    "sla_shard_cg_p2p": (ctypes.c_int, [c_ptr, _P(HaloPlan), ctypes.c_int, _P(SellView),
+                                        _P(SellView), c_ptr, c_ptr, c_ptr, c_dbl, c_dbl, c_i64,
+                                        c_i64, c_ptr, c_sz, _P(SolveInfo), c_ptr]),
 }
 
 _lib = None

@@ -105,7 +105,7 @@ bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T 
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[1] = {0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
+    T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
     int64_t row = s * 32 + lane;
     if (row < A.n_slots) {
       p_new[row] = g.pval((int32_t)row);
@@ -129,7 +129,7 @@ bicg_k2(Sell<T> A, const T *__restrict__ r, const T *__restrict__ v, const T *__
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[3] = {0.0, 0.0, 0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
+    T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
     int64_t row = s * 32 + lane;
     if (row < A.n_slots) {
       T si = g.sval((int32_t)row);
@@ -270,7 +270,8 @@ int sla_bicgstab_workspace(int dtype, int64_t n, size_t *bytes) {
 int sla_bicgstab(int dtype, const sla_sell_t *A, const void *dinv, const void *b, void *x,
                  int x_is_guess, double atol, double rtol, int64_t maxiter, void *workspace,
                  size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
-  if (!sell_ok(A) || !b || !x || !info || A->row_ids) return SLA_ERR_INVALID;
+  if (!sell_ok(A) || !b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
   info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
   size_t need = 0;

@@ -101,7 +101,7 @@ cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
   CgPGather<T, PREC, false> g{r, dinv, p_old, (T)st->beta};
   double acc[1] = {0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
+    T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
     int64_t row = s * 32 + lane;
     if (row < A.n_slots) {
       T pn = g((int32_t)row);
@@ -207,7 +207,7 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
     CgPGather<T, PREC, true> g{r, dinv, p_old, (T)beta};
     double a1[1] = {0.0};
     for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-      T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
+      T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
       int64_t row = s * 32 + lane;
       if (row < n) {
         T pn = g((int32_t)row);
@@ -460,7 +460,8 @@ int sla_pcg_workspace(int dtype, int64_t n, size_t *bytes) {
 int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b, void *x,
             int x_is_guess, double atol, double rtol, int64_t maxiter, int flags, void *workspace,
             size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
-  if (!sell_ok(A) || !b || !x || !info || A->row_ids) return SLA_ERR_INVALID;
+  if (!sell_ok(A) || !b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
   if (flags < 0 || flags > 2) return SLA_ERR_INVALID;
   info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
@@ -490,7 +491,8 @@ int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b, voi
 int sla_pcg_noalloc(int dtype, const sla_sell_t *A, const void *dinv, const void *b, void *x,
                     int x_is_guess, double atol, double rtol, int64_t maxiter, int flags,
                     sla_solve_info_t *info, sla_stream_t stream) {
-  if (!sell_ok(A) || !b || !x || !info || A->row_ids) return SLA_ERR_INVALID;
+  if (!sell_ok(A) || !b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
   if (flags < 0 || flags > 2) return SLA_ERR_INVALID;
   if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;

@@ -8,6 +8,8 @@
 // int32 CSR. Rows of <= 32 entries sort in registers of one thread, rows of
 // <= 2048 entries in shared memory of one block, longer rows with an
 // in-place bitonic network in global memory.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace sla {
@@ -397,6 +399,91 @@ __global__ void jacobi_kernel(const int32_t *__restrict__ rowptr, const int32_t 
   }
 }
 
+
+// ------------------------------------------------ diagonal-offset SELL views
+// Distinct col - row values of the listed rows: each block collects them in
+// a 64-slot shared table (insert only after a miss), then merges its table
+// into the global one. More than 32 distinct values sets the overflow flag.
+constexpr int kDiagTable = 64;
+constexpr int32_t kDiagEmpty = INT32_MIN;
+
+__device__ __forceinline__ bool diag_insert(int32_t *tab, int32_t d) {
+  unsigned h = ((unsigned)d * 2654435761u) >> 26;  // 6 bits
+  for (int probe = 0; probe < kDiagTable; ++probe, h = (h + 1) & (kDiagTable - 1)) {
+    int32_t cur = ((volatile int32_t *)tab)[h];
+    if (cur == d) return true;
+    if (cur == kDiagEmpty) {
+      cur = atomicCAS(tab + h, kDiagEmpty, d);
+      if (cur == kDiagEmpty || cur == d) return true;
+    }
+  }
+  return false;  // table full
+}
+
+__global__ void __launch_bounds__(kBlock)
+diag_probe_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
+                  const int32_t *__restrict__ row_ids, int64_t n_slots, int32_t *gtab,
+                  int *overflow) {
+  __shared__ int32_t tab[kDiagTable];
+  __shared__ int full;
+  for (int i = threadIdx.x; i < kDiagTable; i += blockDim.x) tab[i] = kDiagEmpty;
+  if (threadIdx.x == 0) full = 0;
+  __syncthreads();
+  int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; t < n_slots; t += stride) {
+    if (*(volatile int *)&full) break;
+    const int64_t r = row_ids ? row_ids[t] : t;
+    for (int32_t k = rowptr[r]; k < rowptr[r + 1]; ++k) {
+      const int32_t d = (int32_t)((int64_t)colind[k] - r);
+      if (!diag_insert(tab, d)) { full = 1; break; }
+    }
+  }
+  __syncthreads();
+  if (full) {
+    if (threadIdx.x == 0) atomicExch(overflow, 1);
+    return;
+  }
+  for (int i = threadIdx.x; i < kDiagTable; i += blockDim.x)
+    if (tab[i] != kDiagEmpty && !diag_insert(gtab, tab[i])) atomicExch(overflow, 1);
+}
+
+__global__ void diag_table_init_kernel(int32_t *gtab, int *overflow) {
+  if (threadIdx.x < kDiagTable) gtab[threadIdx.x] = kDiagEmpty;
+  if (threadIdx.x == 0) *overflow = 0;
+}
+
+struct DiagOffsets {
+  int32_t n;
+  int32_t off[SLA_MAX_DIAGS];
+};
+
+// Scatter the CSR entries of each slot onto its diagonal position; the value
+// array is zeroed beforehand. An entry on no listed diagonal sets *bad.
+template <typename T>
+__global__ void __launch_bounds__(kBlock)
+diag_fill_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
+                 const T *__restrict__ vals, const int32_t *__restrict__ row_ids, int64_t n_slots,
+                 DiagOffsets D, T *__restrict__ sval, int *bad) {
+  int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; t < n_slots; t += stride) {
+    const int64_t r = row_ids ? row_ids[t] : t;
+    const int64_t base = (t >> 5) * 32 * D.n + (t & 31);
+    for (int32_t k = rowptr[r]; k < rowptr[r + 1]; ++k) {
+      const int64_t d = (int64_t)colind[k] - r;
+      int lo = 0, hi = D.n - 1, j = -1;
+      while (lo <= hi) {
+        const int mid = (lo + hi) >> 1;
+        if (D.off[mid] == d) { j = mid; break; }
+        if (D.off[mid] < d) lo = mid + 1; else hi = mid - 1;
+      }
+      if (j < 0) { atomicExch(bad, 1); continue; }
+      sval[base + 32 * j] = vals[k];
+    }
+  }
+}
+
 }  // namespace sla
 
 using namespace sla;
@@ -501,6 +588,82 @@ int sla_jacobi_inverse(int dtype, const int32_t *rowptr, const int32_t *colind, 
   else
     return SLA_ERR_INVALID;
   return SLA_OK;
+}
+
+int sla_sell_diag_probe_workspace(size_t *bytes) {
+  if (!bytes) return SLA_ERR_INVALID;
+  *bytes = align_up(kDiagTable * sizeof(int32_t)) + align_up(sizeof(int));
+  return SLA_OK;
+}
+
+int sla_sell_diag_probe(const int32_t *rowptr, const int32_t *colind, const int32_t *row_ids,
+                        int64_t n_slots, int32_t *offsets_out, int32_t *count_out,
+                        void *workspace, size_t workspace_bytes, sla_stream_t stream) {
+  if (!rowptr || !offsets_out || !count_out || n_slots < 0) return SLA_ERR_INVALID;
+  size_t need = 0;
+  sla_sell_diag_probe_workspace(&need);
+  if (!workspace || workspace_bytes < need) return SLA_ERR_WORKSPACE;
+  cudaStream_t s = (cudaStream_t)stream;
+  Carver c(workspace, workspace_bytes);
+  int32_t *gtab = c.take<int32_t>(kDiagTable);
+  int *overflow = c.take<int>(1);
+  SLA_LAUNCH(diag_table_init_kernel, 1, kDiagTable, 0, s, gtab, overflow);
+  if (n_slots > 0) {
+    if (!colind) return SLA_ERR_INVALID;
+    SLA_LAUNCH(diag_probe_kernel, grid_for(n_slots), kBlock, 0, s, rowptr, colind, row_ids,
+               n_slots, gtab, overflow);
+  }
+  int32_t tab[kDiagTable];
+  int of = 0;
+  SLA_CUDA_TRY(cudaMemcpyAsync(tab, gtab, sizeof(tab), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaMemcpyAsync(&of, overflow, sizeof(int), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaStreamSynchronize(s));
+  std::vector<int32_t> got;
+  for (int i = 0; i < kDiagTable; ++i)
+    if (tab[i] != kDiagEmpty) got.push_back(tab[i]);
+  if (of || (int)got.size() > SLA_MAX_DIAGS) {
+    *count_out = -1;
+    return SLA_OK;
+  }
+  std::sort(got.begin(), got.end());
+  for (size_t i = 0; i < got.size(); ++i) offsets_out[i] = got[i];
+  *count_out = (int32_t)got.size();
+  return SLA_OK;
+}
+
+int sla_sell_diag_fill(int dtype, const int32_t *rowptr, const int32_t *colind, const void *vals,
+                       const int32_t *row_ids, int64_t n_slots, const int32_t *offsets,
+                       int32_t n_diags, void *sell_val, void *workspace, size_t workspace_bytes,
+                       sla_stream_t stream) {
+  if (!rowptr || !offsets || n_slots < 0 || n_diags < 1 || n_diags > SLA_MAX_DIAGS)
+    return SLA_ERR_INVALID;
+  size_t need = 0;
+  sla_sell_diag_probe_workspace(&need);
+  if (!workspace || workspace_bytes < need) return SLA_ERR_WORKSPACE;
+  if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
+  DiagOffsets D;
+  D.n = n_diags;
+  for (int i = 0; i < SLA_MAX_DIAGS; ++i) D.off[i] = i < n_diags ? offsets[i] : INT32_MAX;
+  for (int i = 1; i < n_diags; ++i)
+    if (D.off[i] <= D.off[i - 1]) return SLA_ERR_INVALID;
+  if (n_slots == 0) return SLA_OK;
+  if (!colind || !vals || !sell_val) return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t elem = dtype == SLA_F64 ? 8 : 4;
+  const int64_t padded = (n_slots + 31) / 32 * 32 * n_diags;
+  SLA_CUDA_TRY(cudaMemsetAsync(sell_val, 0, elem * padded, s));
+  int *bad = (int *)workspace;
+  SLA_CUDA_TRY(cudaMemsetAsync(bad, 0, sizeof(int), s));
+  if (dtype == SLA_F64)
+    SLA_LAUNCH(diag_fill_kernel<double>, grid_for(n_slots), kBlock, 0, s, rowptr, colind,
+               (const double *)vals, row_ids, n_slots, D, (double *)sell_val, bad);
+  else
+    SLA_LAUNCH(diag_fill_kernel<float>, grid_for(n_slots), kBlock, 0, s, rowptr, colind,
+               (const float *)vals, row_ids, n_slots, D, (float *)sell_val, bad);
+  int hb = 0;
+  SLA_CUDA_TRY(cudaMemcpyAsync(&hb, bad, sizeof(int), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaStreamSynchronize(s));
+  return hb ? SLA_ERR_INVALID : SLA_OK;
 }
 
 }  // extern "C"

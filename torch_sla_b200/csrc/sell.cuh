@@ -9,10 +9,12 @@
 //
 // Width specialisation (template parameter WS): the row loop is cheapest
 // when its trip count is known at compile time, so kernels are instantiated
-//   WS > 0   uniform layout, every slice WS entries wide (slice base is
-//            32*WS*s, no slice_ptr load): the 7- and 27-point stencils;
-//   WS < 0   at most -WS batches of kRowBatch entries (static batch loop);
-//   WS == 0  any width (runtime loop).
+//   WS > 1000  diagonal-offset view of width WS - 1000 (5, 7, 27): columns
+//              are row + off[j], no column array is read at all;
+//   WS > 0     uniform layout, every slice WS entries wide (slice base is
+//              32*WS*s, no slice_ptr load): the 7- and 27-point stencils;
+//   WS < 0     at most -WS batches of kRowBatch entries (static batch loop);
+//   WS == 0    any width (runtime loop).
 #pragma once
 
 #include "common.cuh"
@@ -29,7 +31,20 @@ struct Sell {
   const int32_t *__restrict__ row_ids;
   int32_t max_width;
   int32_t uniform_width;
+  int64_t n_cols;
+  int64_t row_base;
+  int32_t n_diags;
+  int32_t off[SLA_MAX_DIAGS];
 };
+
+// Matrix row of a slot: the row id list, or row_base + slot.
+template <typename T>
+__device__ __forceinline__ int64_t slot_row(const Sell<T> &A, int64_t slot) {
+  return A.row_ids ? (int64_t)__ldg(A.row_ids + slot) : A.row_base + slot;
+}
+
+constexpr int kDiagSpec = 1000;  // WS = kDiagSpec + width: diagonal-offset view
+constexpr int ws_width(int ws) { return ws > kDiagSpec ? ws - kDiagSpec : ws; }
 
 template <typename T>
 inline Sell<T> make_sell(const sla_sell_t *A) {
@@ -42,15 +57,32 @@ inline Sell<T> make_sell(const sla_sell_t *A) {
   s.row_ids = A ? A->row_ids : nullptr;
   s.max_width = A ? A->max_width : 0;
   s.uniform_width = A ? A->uniform_width : 0;
+  s.n_cols = A ? A->n_cols : 0;
+  s.row_base = A ? A->row_base : 0;
+  s.n_diags = A ? A->n_diags : 0;
+  for (int i = 0; i < SLA_MAX_DIAGS; ++i) s.off[i] = A ? A->diag_offsets[i] : 0;
   return s;
 }
+
+inline bool diag_width_supported(int w) { return w == 5 || w == 7 || w == 27; }
 
 inline bool sell_ok(const sla_sell_t *A) {
   if (!A) return false;
   if (A->n_slots < 0 || A->n_slices != (A->n_slots + 31) / 32) return false;
-  if (A->n_slices > 0 && (!A->slice_ptr || !A->col || !A->val)) return false;
   if (A->max_width < 0 || A->uniform_width < 0) return false;
   if (A->uniform_width > 0 && A->uniform_width != A->max_width) return false;
+  if (A->row_base < 0 || (A->row_ids && A->row_base != 0)) return false;
+  if (A->row_base + A->n_slots > INT32_MAX) return false;
+  if (A->n_diags > 0) {
+    if (!diag_width_supported(A->n_diags) || A->uniform_width != A->n_diags) return false;
+    if (A->n_slices > 0 && !A->val) return false;
+    if (A->n_cols <= 0 || A->n_cols > INT32_MAX) return false;
+    for (int i = 1; i < A->n_diags; ++i)
+      if (A->diag_offsets[i] <= A->diag_offsets[i - 1]) return false;
+    return true;
+  }
+  if (A->n_diags < 0) return false;
+  if (A->n_slices > 0 && (!A->slice_ptr || !A->col || !A->val)) return false;
   return true;
 }
 
@@ -66,6 +98,7 @@ constexpr int kSpmvMinBlocks = 4;
 // Width spec of a view: the template value its kernels are launched with.
 inline int width_spec(const sla_sell_t *A) {
   if (!A) return 0;
+  if (A->n_diags > 0) return kDiagSpec + A->n_diags;
   if (A->uniform_width == 7 || A->uniform_width == 27) return A->uniform_width;
   const int w = A->max_width;
   if (w <= kRowBatch) return -1;
@@ -77,6 +110,9 @@ inline int width_spec(const sla_sell_t *A) {
 // Host dispatch: runs the statement(s) with WS bound to the view's spec.
 #define SLA_WS_DISPATCH(ws, ...)                          \
   switch (ws) {                                           \
+    case kDiagSpec + 5: { constexpr int WS = kDiagSpec + 5; __VA_ARGS__; } break; \
+    case kDiagSpec + 7: { constexpr int WS = kDiagSpec + 7; __VA_ARGS__; } break; \
+    case kDiagSpec + 27: { constexpr int WS = kDiagSpec + 27; __VA_ARGS__; } break; \
     case 7: { constexpr int WS = 7; __VA_ARGS__; } break;   \
     case 27: { constexpr int WS = 27; __VA_ARGS__; } break; \
     case -1: { constexpr int WS = -1; __VA_ARGS__; } break; \
@@ -106,21 +142,54 @@ __device__ __forceinline__ void row_batch(const int32_t *__restrict__ cp, const 
   for (int u = 0; u < kRowBatch; ++u) sum = fma(v[u], x[u], sum);
 }
 
-// sum_j val[j] * g(col[j]) over the entries of this lane's slot of the slice
+// Diagonal-offset twin of row_batch: entry j of the slot is column
+// row + off[j]; columns outside [0, n_cols) are skipped like padding, and
+// entries the row does not use hold 0.
+template <int W, typename T, typename G>
+__device__ __forceinline__ void row_batch_diag(const Sell<T> &A, const T *__restrict__ vp,
+                                               int64_t row, int j, const G &g, T &sum) {
+  int32_t c[kRowBatch];
+  T v[kRowBatch], x[kRowBatch];
+#pragma unroll
+  for (int u = 0; u < kRowBatch; ++u) {
+    if (j + u < W) {
+      const int64_t cc = row + A.off[j + u];
+      c[u] = (cc >= 0 && cc < A.n_cols) ? (int32_t)cc : -1;
+      v[u] = ld_stream(vp + 32 * (j + u));
+    } else {
+      c[u] = -1;
+      v[u] = T(0);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kRowBatch; ++u) x[u] = c[u] >= 0 ? g(c[u]) : T(0);
+#pragma unroll
+  for (int u = 0; u < kRowBatch; ++u) sum = fma(v[u], x[u], sum);
+}
+
+// sum_j val[j] * g(col[j]) over the entries of this lane's slot of slice s
 // starting at entry `base` with `width` entries per slot (ascending j).
 template <int WS, typename T, typename G>
-__device__ __forceinline__ T sell_row_at(const Sell<T> &A, int32_t base, int width, int lane,
-                                         const G &g) {
-  const int32_t *__restrict__ cp = A.col + base + lane;
+__device__ __forceinline__ T sell_row_at(const Sell<T> &A, int64_t s, int32_t base, int width,
+                                         int lane, const G &g) {
   const T *__restrict__ vp = A.val + base + lane;
   T sum = T(0);
-  if constexpr (WS > 0) {
+  if constexpr (WS > kDiagSpec) {
+    constexpr int W = WS - kDiagSpec;
+    const int64_t slot = s * 32 + lane;
+    const int64_t row = slot < A.n_slots ? slot_row(A, slot) : -((int64_t)1 << 40);
+#pragma unroll
+    for (int j = 0; j < W; j += kRowBatch) row_batch_diag<W>(A, vp, row, j, g, sum);
+  } else if constexpr (WS > 0) {
+    const int32_t *__restrict__ cp = A.col + base + lane;
 #pragma unroll
     for (int j = 0; j < WS; j += kRowBatch) row_batch(cp, vp, j, WS, g, sum);
   } else if constexpr (WS < 0) {
+    const int32_t *__restrict__ cp = A.col + base + lane;
 #pragma unroll
     for (int jb = 0; jb < -WS; ++jb) row_batch(cp, vp, jb * kRowBatch, width, g, sum);
   } else {
+    const int32_t *__restrict__ cp = A.col + base + lane;
     for (int j = 0; j < width; j += kRowBatch) row_batch(cp, vp, j, width, g, sum);
   }
   return sum;
@@ -136,7 +205,8 @@ template <int WS, typename T, typename Body>
 __device__ __forceinline__ void for_each_slice(const Sell<T> &A, int64_t warp, int64_t nwarps,
                                                int lane, Body body) {
   if constexpr (WS > 0) {
-    for (int64_t s = warp; s < A.n_slices; s += nwarps) body(s, (int32_t)(s * 32 * WS), WS);
+    constexpr int W = ws_width(WS);
+    for (int64_t s = warp; s < A.n_slices; s += nwarps) body(s, (int32_t)(s * 32 * W), W);
   } else {
     for (int64_t s0 = warp; s0 < A.n_slices; s0 += 32 * nwarps) {
       const int64_t mine = s0 + (int64_t)lane * nwarps;

@@ -13,6 +13,8 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <cstddef>
+#include <vector>
 #include <cstring>
 #include <thread>
 
@@ -81,9 +83,12 @@ static bool plan_ok(const sla_halo_plan_t *p) {
 }
 
 // One spec for the interior and boundary views of a shard (a uniform width
-// only when both views have it).
+// only when both views have it). A diagonal-offset interior view keeps its
+// own spec; the boundary launches then use the runtime-width walk
+// (boundary_spec), boundary views are always explicit.
 static int width_spec2(const sla_sell_t *a, const sla_sell_t *b) {
   if (a->n_slots == 0) return width_spec(b);
+  if (width_spec(a) > kDiagSpec) return width_spec(a);
   if (b->n_slots == 0) return width_spec(a);
   int wa = width_spec(a), wb = width_spec(b);
   if (wa == wb) return wa;
@@ -93,6 +98,8 @@ static int width_spec2(const sla_sell_t *a, const sla_sell_t *b) {
   int m = ba < bb ? ba : bb;
   return m == -3 ? -4 : m;
 }
+
+constexpr int boundary_spec(int ws) { return ws > kDiagSpec ? 0 : ws; }
 
 static int64_t n_send(const sla_halo_plan_t *p) {
   return p->n_neighbors > 0 ? p->send_offset[p->n_neighbors] : 0;
@@ -166,9 +173,9 @@ shard_spmv_rows_kernel(Sell<T> A, G g, T *__restrict__ y) {
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
+    T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
     int64_t slot = s * 32 + lane;
-    if (slot < A.n_slots) y[A.row_ids ? A.row_ids[slot] : slot] = sum;
+    if (slot < A.n_slots) y[slot_row(A, slot)] = sum;
   });
 }
 
@@ -336,10 +343,10 @@ shard_cg_spmv(Sell<T> A, int32_t n_own, const T *__restrict__ r, const T *__rest
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[1] = {0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = HALO ? sell_row_at<WS>(A, sbase, swidth, lane, g) : sell_row_at<WS>(A, sbase, swidth, lane, inner);
+    T sum = HALO ? sell_row_at<WS>(A, s, sbase, swidth, lane, g) : sell_row_at<WS>(A, s, sbase, swidth, lane, inner);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
-      int32_t row = A.row_ids[slot];
+      int32_t row = (int32_t)slot_row(A, slot);
       T pn = inner(row);
       p_new[row] = pn;
       Ap[row] = sum;
@@ -501,10 +508,10 @@ shard_bi_k1(Sell<T> A, int32_t n_own, BiP<T, PREC> g0, const T *__restrict__ pha
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[1] = {0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = HALO ? sell_row_at<WS>(A, sbase, swidth, lane, g) : sell_row_at<WS>(A, sbase, swidth, lane, inner);
+    T sum = HALO ? sell_row_at<WS>(A, s, sbase, swidth, lane, g) : sell_row_at<WS>(A, s, sbase, swidth, lane, inner);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
-      int32_t row = A.row_ids[slot];
+      int32_t row = (int32_t)slot_row(A, slot);
       p_new[row] = inner.pval(row);
       v[row] = sum;
       acc[0] += (double)rhat[row] * (double)sum;
@@ -542,10 +549,10 @@ shard_bi_k2(Sell<T> A, int32_t n_own, BiS<T, PREC> g0, const T *__restrict__ sha
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   double acc[3] = {0.0, 0.0, 0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = HALO ? sell_row_at<WS>(A, sbase, swidth, lane, g) : sell_row_at<WS>(A, sbase, swidth, lane, inner);
+    T sum = HALO ? sell_row_at<WS>(A, s, sbase, swidth, lane, g) : sell_row_at<WS>(A, s, sbase, swidth, lane, inner);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
-      int32_t row = A.row_ids[slot];
+      int32_t row = (int32_t)slot_row(A, slot);
       T si = inner.sval(row);
       t[row] = sum;
       acc[0] += (double)si * (double)si;
@@ -668,7 +675,7 @@ static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
   SLA_NCCL_TRY(ncclAllReduce(R->init, R->init, 2, ncclFloat64, ncclSum, cr->nccl, s));
   const T *hsrc = plan->halo_src ? halo : recvbuf;
   const int gi = occupancy_grid((const void *)shard_cg_spmv<T, PREC, false, WS>);
-  const int gb = occupancy_grid((const void *)shard_cg_spmv<T, PREC, true, WS>);
+  const int gb = occupancy_grid((const void *)shard_cg_spmv<T, PREC, true, boundary_spec(WS)>);
   const int gu = occupancy_grid((const void *)shard_cg_update<T, PREC>);
   SLA_TRY(shard_loop(cr, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
     T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
@@ -688,7 +695,7 @@ static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
     if (plan->halo_src && nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
                  halo, &st->stopped);
-    SLA_LAUNCH((shard_cg_spmv<T, PREC, true, WS>), gb, kBlock, 0, s, AB, (int32_t)no, r, dinv, p_old,
+    SLA_LAUNCH((shard_cg_spmv<T, PREC, true, boundary_spec(WS)>), gb, kBlock, 0, s, AB, (int32_t)no, r, dinv, p_old,
                hsrc, p_new, Ap, st, R, part[2], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->pap, R->pap, 1, ncclFloat64, ncclSum, cr->nccl, s));
     profiler().begin(1, k, s, &ev);
@@ -743,9 +750,9 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
   const T *hsrc = plan->halo_src ? halo : recvbuf;
   const unsigned pack_grid = ns > 0 ? (unsigned)grid_for(ns) : 1u;
   const int g1i = occupancy_grid((const void *)shard_bi_k1<T, PREC, false, WS>);
-  const int g1b = occupancy_grid((const void *)shard_bi_k1<T, PREC, true, WS>);
+  const int g1b = occupancy_grid((const void *)shard_bi_k1<T, PREC, true, boundary_spec(WS)>);
   const int g2i = occupancy_grid((const void *)shard_bi_k2<T, PREC, false, WS>);
-  const int g2b = occupancy_grid((const void *)shard_bi_k2<T, PREC, true, WS>);
+  const int g2b = occupancy_grid((const void *)shard_bi_k2<T, PREC, true, boundary_spec(WS)>);
   const int g3 = occupancy_grid((const void *)shard_bi_k3<T, PREC>);
   SLA_TRY(shard_loop(cr, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
     T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
@@ -764,7 +771,7 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
     if (plan->halo_src && nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
                  halo, &st->stopped);
-    SLA_LAUNCH((shard_bi_k1<T, PREC, true, WS>), g1b, kBlock, 0, s, AB, (int32_t)no, gp, hsrc, rhat,
+    SLA_LAUNCH((shard_bi_k1<T, PREC, true, boundary_spec(WS)>), g1b, kBlock, 0, s, AB, (int32_t)no, gp, hsrc, rhat,
                p_new, v, st, R, part[2], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->rv, R->rv, 1, ncclFloat64, ncclSum, cr->nccl, s));
     // s_hat halo, then t = A s_hat
@@ -777,7 +784,7 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
     if (plan->halo_src && nh > 0)
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
                  halo, &st->stopped);
-    SLA_LAUNCH((shard_bi_k2<T, PREC, true, WS>), g2b, kBlock, 0, s, AB, (int32_t)no, gs, hsrc, t, st, R,
+    SLA_LAUNCH((shard_bi_k2<T, PREC, true, boundary_spec(WS)>), g2b, kBlock, 0, s, AB, (int32_t)no, gs, hsrc, t, st, R,
                part[4], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->stt, R->stt, 3, ncclFloat64, ncclSum, cr->nccl, s));
     SLA_LAUNCH((shard_bi_k3<T, PREC>), g3, kBlock, 0, s, no, x, r, rhat, p_new, v, t, dinv, st, R,
@@ -801,6 +808,351 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
   info->residual = last >= 0 ? sqrt(red.rr[last & 1][0]) : sqrt(red.init[0]);
   info->status = out.stopped ? SLA_OK : SLA_NOT_CONVERGED;
   info->reason = out.stopped;
+  return info->status;
+}
+
+
+// ============================================================ peer-memory path
+// Single-node path of the shard CG: halo values and dot products travel as
+// stores into the other GPUs' memory (CUDA IPC mappings over NVLink /
+// NVSwitch) from inside the solver kernels. An iteration is two launches:
+//   K_A  stop test; send this rank's share of the neighbours' halo (the
+//        search direction computed on the fly) straight into their halo
+//        buffers, the last block raising an arrival sequence number;
+//        interior rows; wait for the neighbours' arrivals; boundary rows;
+//        (p, Ap) summed over the grid and then over the ranks in rank order
+//   K_B  x / r update, (r, r) and (r, z) summed the same way.
+// K_A is a cooperative launch (all blocks co-resident), so no block can
+// wait on a block that has not started; every wait is bounded (kSpinLimit)
+// and a timeout stops the solve with SLA_ERR_TIMEOUT on the host. Sequence
+// numbers are (solve epoch << 32) + iteration + 1, so flags left from an
+// earlier solve never satisfy a wait.
+constexpr int kP2PMaxRanks = 8;
+constexpr int kRedPoints = 3;  // 0 init, 1 (p,Ap), 2 (r,r)/(r,z)
+constexpr int kStopTimeout = 3;
+
+struct P2PHeader {
+  long long recv_off[kP2PMaxRanks];  // where rank q's values start in my halo; -1 none
+  unsigned long long arrive[kP2PMaxRanks];
+  unsigned long long red_flag[2][kRedPoints][kP2PMaxRanks];
+  double red_val[2][kRedPoints][kP2PMaxRanks][2];
+  unsigned send_count;
+  unsigned pad[63];
+};
+
+template <typename T>
+struct P2PDev {
+  int world, me, n_nb, pad;
+  P2PHeader *local;
+  P2PHeader *hdr[kP2PMaxRanks];  // every rank's header (hdr[me] == local)
+  T *dst[kP2PMaxRanks];          // per neighbour: its halo buffer + my offset there
+  int nb_rank[kP2PMaxRanks];
+  long long send_off[kP2PMaxRanks + 1];
+  const T *halo;                 // my halo buffer (written by the neighbours)
+  unsigned long long seq;        // epoch << 32
+};
+
+struct P2PPlan {
+  Comm *comm = nullptr;
+  int world = 1, me = 0, n_nb = 0;
+  int64_t n_halo = 0, n_owned = 0;
+  size_t elem = 8;
+  char *local = nullptr;
+  char *peer[kP2PMaxRanks] = {};
+  int nb_rank[kP2PMaxRanks] = {};
+  long long dst_off[kP2PMaxRanks] = {};
+  long long send_off[kP2PMaxRanks + 1] = {};
+  unsigned long long epoch = 0;
+};
+
+inline size_t p2p_halo_offset() { return align_up(sizeof(P2PHeader)); }
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until *p >= want (sequence numbers only grow).
+__device__ __forceinline__ bool wait_seq(const unsigned long long *p, unsigned long long want) {
+  for (unsigned long long spins = 0; ld_acquire_sys(p) < want; ++spins) {
+    if (spins > kSpinLimit) return false;
+    if (spins > 32) __nanosleep(32);
+  }
+  return true;
+}
+
+// This block's share of the halo values of all neighbours, then the arrival
+// signal from the last block to finish (all threads of the block call it).
+template <typename T, typename PV>
+__device__ __forceinline__ void p2p_send_halo(const P2PDev<T> &P, const int32_t *__restrict__ idx,
+                                              const PV &pval, unsigned long long seq) {
+  const long long ns = P.send_off[P.n_nb];
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < ns;
+       i += (long long)gridDim.x * blockDim.x) {
+    int nb = 0;
+    while (i >= P.send_off[nb + 1]) ++nb;
+    P.dst[nb][i - P.send_off[nb]] = pval(idx[i]);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned t = atomicAdd(&P.local->send_count, 1u);
+    if (t == gridDim.x - 1) {
+      P.local->send_count = 0u;
+      __threadfence_system();
+      for (int nb = 0; nb < P.n_nb; ++nb) st_release_sys(&P.hdr[P.nb_rank[nb]]->arrive[P.me], seq);
+    }
+  }
+}
+
+// Wait until every neighbour's halo values of this iteration have landed.
+template <typename T>
+__device__ __forceinline__ bool p2p_wait_halo(const P2PDev<T> &P, unsigned long long seq) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (threadIdx.x < P.n_nb && !wait_seq(&P.local->arrive[P.nb_rank[threadIdx.x]], seq)) s_ok = 0;
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// Sum of NV rank totals over all ranks in rank order (identical on every
+// rank). Called by all threads of one block; v holds this rank's totals.
+template <int NV, typename T>
+__device__ __forceinline__ bool p2p_allreduce(const P2PDev<T> &P, int point, int par,
+                                              unsigned long long seq, double (&v)[NV]) {
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (threadIdx.x < P.world) {
+    P2PHeader *h = P.hdr[threadIdx.x];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) h->red_val[par][point][P.me][i] = v[i];
+    __threadfence_system();
+    st_release_sys(&h->red_flag[par][point][P.me], seq);
+    if (!wait_seq(&P.local->red_flag[par][point][threadIdx.x], seq)) s_ok = 0;
+  }
+  __syncthreads();
+  if (!s_ok) return false;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    double t = 0.0;
+    for (int q = 0; q < P.world; ++q) t += ld_l2(&P.local->red_val[par][point][q][i]);
+    v[i] = t;
+  }
+  return true;
+}
+
+template <typename T, typename Inner>
+struct HaloGatherL2 {  // halo written by other GPUs during this launch: L2 loads
+  Inner inner;
+  const T *halo;
+  int32_t n_own;
+  __device__ __forceinline__ T operator()(int32_t c) const {
+    return c < n_own ? inner(c) : ld_l2(halo + (c - n_own));
+  }
+};
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+shard_cg_p2p_init(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *__restrict__ dinv,
+                  T *__restrict__ r, T *__restrict__ p_old, ShardState *st, CgRed *R,
+                  double *partials, P2PDev<T> P) {
+  __shared__ double smem[2 * kWarps];
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T bi = b[i];
+    x[i] = T(0);
+    r[i] = bi;
+    p_old[i] = T(0);
+    T zi = PREC ? mul_rn(dinv[i], bi) : bi;
+    acc[0] += (double)bi * (double)zi;
+    acc[1] += (double)bi * (double)bi;
+  }
+  if (!last_block_sum<2, kBlock>(acc, partials, &st->counter[0], smem)) return;
+  if (!p2p_allreduce<2>(P, 0, 0, P.seq, acc)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  if (threadIdx.x == 0) {
+    R->init[0] = acc[0];
+    R->init[1] = acc[1];
+  }
+}
+
+template <typename T, bool PREC, int WS>
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
+shard_cg_p2p_spmv(Sell<T> AI, Sell<T> AB, int32_t n_own, const int32_t *__restrict__ send_index,
+                  const T *__restrict__ r, const T *__restrict__ dinv, const T *__restrict__ p_old,
+                  T *__restrict__ p_new, T *__restrict__ Ap, ShardState *st, CgRed *R,
+                  double *partials, long long k, long long every, double atol, double rtol,
+                  P2PDev<T> P) {
+  constexpr int WSB = boundary_spec(WS);
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  if (cg_stop(R, k, every, cg_tol(R, atol, rtol))) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) { st->stopped = 1; st->iters = k; }
+    return;
+  }
+  const unsigned long long seq = P.seq + (unsigned long long)(k + 1);
+  ShardP<T, PREC> inner{r, dinv, p_old, (T)cg_beta(R, k)};
+  p2p_send_halo(P, send_index, inner, seq);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[1] = {0.0};
+  auto emit = [&](const Sell<T> &A, int64_t s, T sum) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int32_t row = (int32_t)slot_row(A, slot);
+      const T pn = inner(row);
+      p_new[row] = pn;
+      Ap[row] = sum;
+      acc[0] += (double)pn * (double)sum;
+    }
+  };
+  for_each_slice<WS>(AI, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    emit(AI, s, sell_row_at<WS>(AI, s, sbase, swidth, lane, inner));
+  });
+  if (!p2p_wait_halo(P, seq)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  HaloGatherL2<T, ShardP<T, PREC>> g{inner, P.halo, n_own};
+  for_each_slice<WSB>(AB, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    emit(AB, s, sell_row_at<WSB>(AB, s, sbase, swidth, lane, g));
+  });
+  if (!last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem)) return;
+  if (!p2p_allreduce<1>(P, 1, (int)(k & 1), seq, acc)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  if (threadIdx.x == 0) R->pap[0] = acc[0];
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+shard_cg_p2p_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
+                    const T *__restrict__ Ap, const T *__restrict__ dinv, ShardState *st,
+                    CgRed *R, double *partials, long long k, P2PDev<T> P) {
+  __shared__ double smem[2 * kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  const T alpha = (T)(cg_rz(R, k) / R->pap[0]);
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T xi = add_rn(x[i], mul_rn(alpha, p[i]));
+    T ri = sub_rn(r[i], mul_rn(alpha, Ap[i]));
+    x[i] = xi;
+    r[i] = ri;
+    T zi = PREC ? mul_rn(dinv[i], ri) : ri;
+    acc[0] += (double)ri * (double)ri;
+    acc[1] += (double)ri * (double)zi;
+  }
+  if (!last_block_sum<2, kBlock>(acc, partials, &st->counter[3], smem)) return;
+  if (!p2p_allreduce<2>(P, 2, (int)(k & 1), P.seq + (unsigned long long)(k + 1), acc)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  if (threadIdx.x == 0) {
+    R->loc[k & 1][0] = acc[0];
+    R->loc[k & 1][1] = acc[1];
+  }
+}
+
+template <typename T>
+static P2PDev<T> p2p_dev(const P2PPlan *pp) {
+  P2PDev<T> d{};
+  d.world = pp->world;
+  d.me = pp->me;
+  d.n_nb = pp->n_nb;
+  d.local = (P2PHeader *)pp->local;
+  for (int q = 0; q < pp->world; ++q) d.hdr[q] = (P2PHeader *)pp->peer[q];
+  for (int i = 0; i < pp->n_nb; ++i) {
+    d.nb_rank[i] = pp->nb_rank[i];
+    d.dst[i] = (T *)(pp->peer[pp->nb_rank[i]] + p2p_halo_offset()) + pp->dst_off[i];
+  }
+  for (int i = 0; i <= pp->n_nb; ++i) d.send_off[i] = pp->send_off[i];
+  d.halo = (const T *)(pp->local + p2p_halo_offset());
+  d.seq = pp->epoch << 32;
+  return d;
+}
+
+template <typename T, bool PREC, int WS>
+static int shard_cg_p2p_impl(P2PPlan *pp, const sla_halo_plan_t *plan, const sla_sell_t *Ai,
+                             const sla_sell_t *Ab, const T *dinv, const T *b, T *x, double atol,
+                             double rtol, int64_t maxiter, int64_t every, void *ws,
+                             size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
+  Sell<T> AI = make_sell<T>(Ai), AB = make_sell<T>(Ab);
+  const int64_t no = plan->n_owned;
+  Carver c(ws, ws_bytes);
+  T *r = c.take<T>(no + 1), *pA = c.take<T>(no + 1), *pB = c.take<T>(no + 1);
+  T *Ap = c.take<T>(no + 1);
+  const int G = solver_grid();
+  double *part[4];
+  for (int q = 0; q < 4; ++q) part[q] = c.take<double>(4 * (size_t)G);
+  ShardState *st = c.take<ShardState>(1);
+  CgRed *R = c.take<CgRed>(1);
+  if (!c.ok) return SLA_ERR_WORKSPACE;
+  ++pp->epoch;
+  P2PDev<T> P = p2p_dev<T>(pp);
+  ShardState init{};
+  SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(init), cudaMemcpyHostToDevice, s));
+  SLA_CUDA_TRY(cudaMemsetAsync(R, 0, sizeof(CgRed), s));
+  SLA_LAUNCH((shard_cg_p2p_init<T, PREC>), grid_for(no), kBlock, 0, s, no, b, x, dinv, r, pA, st,
+             R, part[0], P);
+  // co-resident grid for the kernel whose blocks wait on other GPUs
+  const void *ka = (const void *)shard_cg_p2p_spmv<T, PREC, WS>;
+  int per_sm = 0;
+  SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ka, kBlock, 0));
+  if (per_sm < 1) return SLA_ERR_UNSUPPORTED;
+  int ga = per_sm * device_info().sm_count;
+  if (ga > G) ga = G;
+  const int gu = occupancy_grid((const void *)shard_cg_p2p_update<T, PREC>);
+  const int32_t n_own = (int32_t)no;
+  SLA_TRY(shard_loop(pp->comm, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
+    T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
+    long long kk = (long long)k, ev_ = (long long)every;
+    void *args[] = {&AI, &AB, (void *)&n_own, (void *)&plan->send_index, (void *)&r,
+                    (void *)&dinv, (void *)&p_old, (void *)&p_new, (void *)&Ap, (void *)&st,
+                    (void *)&R, (void *)&part[1], &kk, &ev_, (void *)&atol, (void *)&rtol, &P};
+    cudaEvent_t e;
+    profiler().begin(0, k, s, &e);
+    SLA_CUDA_TRY(cudaLaunchCooperativeKernel(ka, dim3(ga), dim3(kBlock), args, 0, s));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    profiler().end(0, s, e);
+    profiler().begin(1, k, s, &e);
+    SLA_LAUNCH((shard_cg_p2p_update<T, PREC>), gu, kBlock, 0, s, no, x, r, p_new, Ap, dinv, st, R,
+               part[3], kk, P);
+    profiler().end(1, s, e);
+    return SLA_OK;
+  }));
+  ShardState out;
+  CgRed red;
+  SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(out), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaMemcpyAsync(&red, R, sizeof(red), cudaMemcpyDeviceToHost, s));
+  cudaEvent_t done;
+  SLA_CUDA_TRY(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+  SLA_CUDA_TRY(cudaEventRecord(done, s));
+  int wrc = wait_bounded(done, pp->comm);
+  cudaEventDestroy(done);
+  SLA_TRY(wrc);
+  profiler().resolve();
+  if (out.stopped == kStopTimeout) {
+    fprintf(stderr, "[sla_b200] shard CG: a peer did not answer within the bounded wait\n");
+    return SLA_ERR_TIMEOUT;
+  }
+  const long long iters = out.stopped == 1 ? out.iters : maxiter;
+  info->iterations = iters;
+  info->residual = iters > 0 ? sqrt(red.loc[(iters - 1) & 1][0]) : sqrt(red.init[0]);
+  info->reason = out.stopped;
+  info->status = out.stopped == 1 ? SLA_OK : SLA_NOT_CONVERGED;
   return info->status;
 }
 
@@ -886,9 +1238,13 @@ int sla_shard_spmv(void *comm, const sla_halo_plan_t *plan, int dtype, const sla
   Comm *c = (Comm *)comm;
   if (!c || !c->nccl || !plan_ok(plan) || !x_local || !y_owned) return SLA_ERR_INVALID;
   if (!sell_ok(A_interior) || !sell_ok(A_boundary)) return SLA_ERR_INVALID;
-  if ((A_interior->n_slots > 0 && !A_interior->row_ids) ||
-      (A_boundary->n_slots > 0 && !A_boundary->row_ids))
+  if (A_boundary->n_diags > 0) return SLA_ERR_UNSUPPORTED;
+  if (A_interior->n_diags > 0 && A_interior->n_cols > plan->n_owned + plan->n_halo)
     return SLA_ERR_INVALID;
+  if ((!A_interior->row_ids && A_interior->row_base + A_interior->n_slots > plan->n_owned) ||
+      (!A_boundary->row_ids && A_boundary->row_base + A_boundary->n_slots > plan->n_owned))
+    return SLA_ERR_INVALID;
+
   cudaStream_t s = (cudaStream_t)stream;
   const int64_t ns = n_send(plan), nh = plan->n_halo, no = plan->n_owned;
   if ((ns > 0 && !sendbuf) || (nh > 0 && !recvbuf)) return SLA_ERR_INVALID;
@@ -910,9 +1266,10 @@ int sla_shard_spmv(void *comm, const sla_halo_plan_t *plan, int dtype, const sla
       SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, (const T *)recvbuf,
                  plan->halo_src, nh, x + no, (const int *)nullptr);
     if (AB.n_slices > 0)
-      SLA_WS_DISPATCH(wspec, SLA_LAUNCH((shard_spmv_rows_kernel<T, PlainGather<T>, WS>),
-                                        grid_for(AB.n_slices * 32, kBlock, 4), kBlock, 0, s, AB,
-                                        PlainGather<T>{x}, (T *)y_owned));
+      SLA_WS_DISPATCH(boundary_spec(wspec),
+                      SLA_LAUNCH((shard_spmv_rows_kernel<T, PlainGather<T>, WS>),
+                                 grid_for(AB.n_slices * 32, kBlock, 4), kBlock, 0, s, AB,
+                                 PlainGather<T>{x}, (T *)y_owned));
     return SLA_OK;
   };
   if (dtype == SLA_F64) return run(double(0));
@@ -940,7 +1297,9 @@ int sla_shard_rmatvec(void *comm, const sla_halo_plan_t *plan, int dtype, const 
                       sla_stream_t stream) {
   Comm *c = (Comm *)comm;
   if (!c || !c->nccl || !plan_ok(plan) || !sell_ok(AT) || !w_local) return SLA_ERR_INVALID;
-  if (AT->n_slots != plan->n_owned + plan->n_halo || AT->row_ids) return SLA_ERR_INVALID;
+  if (AT->n_slots != plan->n_owned + plan->n_halo || AT->row_ids || AT->row_base)
+    return SLA_ERR_INVALID;
+  if (AT->n_diags > 0 && AT->n_cols > plan->n_owned) return SLA_ERR_INVALID;
   if ((plan->n_owned > 0 && !y_owned) || (plan->n_halo > 0 && !sendbuf) ||
       (n_send(plan) > 0 && !recvbuf))
     return SLA_ERR_INVALID;
@@ -971,9 +1330,14 @@ static int shard_args_ok(void *ch, void *cr, const sla_halo_plan_t *plan, const 
                          int64_t every) {
   if (!ch || !cr || !((Comm *)ch)->nccl || !((Comm *)cr)->nccl) return SLA_ERR_INVALID;
   if (!plan_ok(plan) || !sell_ok(Ai) || !sell_ok(Ab) || !info || every < 1) return SLA_ERR_INVALID;
+  if (Ab->n_diags > 0) return SLA_ERR_UNSUPPORTED;
+  // interior gathers read owned vectors only
+  if (Ai->n_diags > 0 && Ai->n_cols > plan->n_owned) return SLA_ERR_INVALID;
   if (plan->n_owned > 0 && (!b || !x)) return SLA_ERR_INVALID;
-  if ((Ai->n_slots > 0 && !Ai->row_ids) || (Ab->n_slots > 0 && !Ab->row_ids)) return SLA_ERR_INVALID;
   if (Ai->n_slots + Ab->n_slots != plan->n_owned) return SLA_ERR_INVALID;
+  if ((!Ai->row_ids && Ai->row_base + Ai->n_slots > plan->n_owned) ||
+      (!Ab->row_ids && Ab->row_base + Ab->n_slots > plan->n_owned))
+    return SLA_ERR_INVALID;
   if (plan->n_owned + plan->n_halo >= INT32_MAX) return SLA_ERR_UNSUPPORTED;
   return SLA_OK;
 }
@@ -1044,6 +1408,167 @@ int sla_shard_bicgstab(void *comm_halo, void *comm_reduce, const sla_halo_plan_t
     SLA_WS_DISPATCH(wspec, return shard_bi_impl<float, false, WS>(ch, cr, plan, A_interior, A_boundary, nullptr,
                                        (const float *)b, (float *)x, atol, rtol, maxiter,
                                        check_every, workspace, workspace_bytes, info, s));
+  }
+  return SLA_ERR_INVALID;
+}
+
+// ----------------------------------------------------------- peer-memory path
+int sla_p2p_create(void *comm, const sla_halo_plan_t *plan, int dtype, void **p2p_out) {
+  if (!p2p_out) return SLA_ERR_INVALID;
+  *p2p_out = nullptr;
+  Comm *c = (Comm *)comm;
+  if (!c || !c->nccl || !plan_ok(plan)) return SLA_ERR_INVALID;
+  if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
+  const int world = c->nranks, me = c->rank;
+  if (world < 2 || world > kP2PMaxRanks) return SLA_OK;  // same answer on every rank
+  P2PPlan *pp = new P2PPlan();
+  pp->comm = c;
+  pp->world = world;
+  pp->me = me;
+  pp->n_nb = plan->n_neighbors;
+  pp->n_halo = plan->n_halo;
+  pp->n_owned = plan->n_owned;
+  pp->elem = dtype == SLA_F64 ? 8 : 4;
+  int ok = plan->halo_src == nullptr && plan->n_neighbors < kP2PMaxRanks ? 1 : 0;
+  const size_t bytes = p2p_halo_offset() + align_up(pp->elem * (size_t)(plan->n_halo + 1));
+  cudaStream_t s = c->side;
+  unsigned char *dbuf = nullptr;  // handles of all ranks + agreement flag
+  cudaIpcMemHandle_t mine{};
+  if (ok && cudaMalloc((void **)&pp->local, bytes) != cudaSuccess) ok = 0;
+  if (ok) {
+    P2PHeader h{};
+    for (int q = 0; q < kP2PMaxRanks; ++q) h.recv_off[q] = -1;
+    for (int i = 0; i < plan->n_neighbors; ++i) {
+      h.recv_off[plan->neighbor_rank[i]] = plan->recv_offset[i];
+      pp->nb_rank[i] = plan->neighbor_rank[i];
+      pp->send_off[i] = plan->send_offset[i];
+    }
+    pp->send_off[plan->n_neighbors] = plan->n_neighbors > 0 ? plan->send_offset[plan->n_neighbors] : 0;
+    if (cudaMemset(pp->local, 0, bytes) != cudaSuccess ||
+        cudaMemcpy(pp->local, &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaIpcGetMemHandle(&mine, pp->local) != cudaSuccess)
+      ok = 0;
+  }
+  cudaGetLastError();
+  const size_t hs = sizeof(cudaIpcMemHandle_t);
+  SLA_CUDA_TRY(cudaMalloc((void **)&dbuf, hs * world + 16));
+  int *flag = (int *)(dbuf + hs * world);
+  SLA_CUDA_TRY(cudaMemcpy(dbuf + hs * me, &mine, hs, cudaMemcpyHostToDevice));
+  SLA_NCCL_TRY(ncclAllGather(dbuf + hs * me, dbuf, hs, ncclUint8, c->nccl, s));
+  std::vector<cudaIpcMemHandle_t> all(world);
+  cudaEvent_t ev;
+  SLA_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  SLA_CUDA_TRY(cudaEventRecord(ev, s));
+  int w = wait_bounded(ev, c);
+  if (w != SLA_OK) { cudaEventDestroy(ev); return w; }
+  SLA_CUDA_TRY(cudaMemcpy(all.data(), dbuf, hs * world, cudaMemcpyDeviceToHost));
+  pp->peer[me] = pp->local;
+  for (int q = 0; q < world && ok; ++q) {
+    if (q == me) continue;
+    void *ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      ok = 0;
+      cudaGetLastError();
+    } else {
+      pp->peer[q] = (char *)ptr;
+    }
+  }
+  // where my values go in each neighbour's halo
+  for (int i = 0; i < pp->n_nb && ok; ++i) {
+    long long off = -1;
+    const int q = pp->nb_rank[i];
+    if (cudaMemcpy(&off, pp->peer[q] + offsetof(P2PHeader, recv_off) + sizeof(long long) * me,
+                   sizeof(off), cudaMemcpyDeviceToHost) != cudaSuccess || off < 0)
+      ok = 0;
+    pp->dst_off[i] = off;
+  }
+  cudaGetLastError();
+  SLA_CUDA_TRY(cudaMemcpy(flag, &ok, sizeof(int), cudaMemcpyHostToDevice));
+  SLA_NCCL_TRY(ncclAllReduce(flag, flag, 1, ncclInt32, ncclMin, c->nccl, s));
+  SLA_CUDA_TRY(cudaEventRecord(ev, s));
+  w = wait_bounded(ev, c);
+  cudaEventDestroy(ev);
+  if (w != SLA_OK) return w;
+  int all_ok = 0;
+  SLA_CUDA_TRY(cudaMemcpy(&all_ok, flag, sizeof(int), cudaMemcpyDeviceToHost));
+  cudaFree(dbuf);
+  if (!all_ok) {
+    for (int q = 0; q < world; ++q)
+      if (q != me && pp->peer[q]) cudaIpcCloseMemHandle(pp->peer[q]);
+    if (pp->local) cudaFree(pp->local);
+    delete pp;
+    return SLA_OK;  // *p2p_out stays NULL: the NCCL path serves
+  }
+  *p2p_out = pp;
+  return SLA_OK;
+}
+
+int sla_p2p_destroy(void *p2p) {
+  P2PPlan *pp = (P2PPlan *)p2p;
+  if (!pp) return SLA_OK;
+  // every rank is past its last remote store before any mapping goes away
+  int rc = SLA_OK;
+  Comm *c = pp->comm;
+  if (c && c->nccl) {
+    cudaStream_t s = c->side;
+    int *d = nullptr;
+    if (cudaMalloc((void **)&d, sizeof(int)) == cudaSuccess) {
+      if (ncclAllReduce(d, d, 1, ncclInt32, ncclSum, c->nccl, s) != ncclSuccess) rc = SLA_ERR_NCCL;
+      cudaEvent_t ev;
+      if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) == cudaSuccess) {
+        cudaEventRecord(ev, s);
+        int w = wait_bounded(ev, c);
+        if (w != SLA_OK) rc = w;
+        cudaEventDestroy(ev);
+      }
+      cudaFree(d);
+    }
+  }
+  cudaDeviceSynchronize();
+  for (int q = 0; q < pp->world; ++q)
+    if (q != pp->me && pp->peer[q]) cudaIpcCloseMemHandle(pp->peer[q]);
+  if (pp->local) cudaFree(pp->local);
+  delete pp;
+  return rc;
+}
+
+int sla_shard_cg_p2p(void *p2p, const sla_halo_plan_t *plan, int dtype,
+                     const sla_sell_t *A_interior, const sla_sell_t *A_boundary, const void *dinv,
+                     const void *b, void *x, double atol, double rtol, int64_t maxiter,
+                     int64_t check_every, void *workspace, size_t workspace_bytes,
+                     sla_solve_info_t *info, sla_stream_t stream) {
+  P2PPlan *pp = (P2PPlan *)p2p;
+  if (!pp || !pp->comm) return SLA_ERR_INVALID;
+  SLA_TRY(shard_args_ok(pp->comm, pp->comm, plan, A_interior, A_boundary, b, x, info,
+                        check_every));
+  if (plan->n_owned != pp->n_owned || plan->n_halo != pp->n_halo ||
+      plan->n_neighbors != pp->n_nb || plan->halo_src)
+    return SLA_ERR_INVALID;
+  if ((dtype == SLA_F64 ? 8u : 4u) != pp->elem) return SLA_ERR_INVALID;
+  if (!device_info().coop) return SLA_ERR_UNSUPPORTED;
+  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
+  size_t need = 0;
+  SLA_TRY(sla_shard_krylov_workspace(dtype, plan->n_owned, plan->n_halo, n_send(plan), &need));
+  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int wspec = width_spec2(A_interior, A_boundary);
+  if (dtype == SLA_F64) {
+    if (dinv)
+      SLA_WS_DISPATCH(wspec, return shard_cg_p2p_impl<double, true, WS>(pp, plan, A_interior, A_boundary, (const double *)dinv,
+                                                                 (const double *)b, (double *)x, atol, rtol, maxiter, check_every,
+                                                                 workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return shard_cg_p2p_impl<double, false, WS>(pp, plan, A_interior, A_boundary, nullptr,
+                                                                (const double *)b, (double *)x, atol, rtol, maxiter, check_every,
+                                                                workspace, workspace_bytes, info, s));
+  }
+  if (dtype == SLA_F32) {
+    if (dinv)
+      SLA_WS_DISPATCH(wspec, return shard_cg_p2p_impl<float, true, WS>(pp, plan, A_interior, A_boundary, (const float *)dinv,
+                                                                (const float *)b, (float *)x, atol, rtol, maxiter, check_every,
+                                                                workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return shard_cg_p2p_impl<float, false, WS>(pp, plan, A_interior, A_boundary, nullptr,
+                                                               (const float *)b, (float *)x, atol, rtol, maxiter, check_every,
+                                                               workspace, workspace_bytes, info, s));
   }
   return SLA_ERR_INVALID;
 }

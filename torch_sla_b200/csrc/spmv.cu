@@ -12,10 +12,10 @@ __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks) spmv_kernel(Sell<T> A,
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   PlainGather<T> g{x};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at<WS>(A, sbase, swidth, lane, g);
+    T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
     int64_t slot = s * 32 + lane;
     if (slot < A.n_slots) {
-      int64_t row = A.row_ids ? A.row_ids[slot] : slot;
+      int64_t row = slot_row(A, slot);
       y[row] = sum;
     }
   });

@@ -4,7 +4,9 @@ The kernels drive NCCL themselves (grouped send/recv for the halo on a side
 stream, small allreduces on the compute stream), so each process group gets
 two communicators of its own -- one per stream, so their operations never
 interleave differently on different ranks. The unique ids travel through
-the caller's torch.distributed group.
+the caller's torch.distributed group. On one node the shard CG runs instead
+on peer-memory exchange buffers (sla_p2p_create), which use NCCL only to
+trade their IPC handles.
 """
 from __future__ import annotations
 
@@ -16,6 +18,7 @@ import torch.distributed as dist
 from .. import _lib as L
 
 _COMMS: dict = {}
+_P2P: list = []  # peer-memory handles, released (collectively) by destroy_all
 
 
 class Communicators:
@@ -58,8 +61,17 @@ def communicators(group=None) -> Communicators:
     return c
 
 
+def register_p2p(handle) -> None:
+    _P2P.append(handle)
+
+
 def destroy_all() -> None:
-    """Release the communicators (call before destroy_process_group)."""
+    """Release the peer-memory exchange buffers and the communicators, on
+    every rank together (call before destroy_process_group)."""
+    for h in _P2P:
+        if h:
+            L.lib().sla_p2p_destroy(h)
+    _P2P.clear()
     for c in list(_COMMS.values()):
         c.destroy()
     _COMMS.clear()

@@ -11,6 +11,7 @@ _OwnedShardDTensor does) or plain owned-slice tensors; any object with
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 from typing import Any, Optional, Tuple
 
@@ -141,8 +142,11 @@ class _ShardPlan:
         bmask[hit[hit < no]] = True
         self.boundary = bmask.nonzero().squeeze(-1).to(torch.int32)
         self.interior = (~bmask).nonzero().squeeze(-1).to(torch.int32)
-        self.sell_int = self.csr.sell(row_ids=self.interior)
-        self.sell_bnd = self.csr.sell(row_ids=self.boundary)
+        # interior rows read owned columns only (diagonal-offset layout when
+        # the local stencil allows it); boundary rows keep explicit columns,
+        # their halo columns do not sit on fixed diagonals
+        self.sell_int = self.csr.sell(row_ids=self.interior, n_cols=no)
+        self.sell_bnd = self.csr.sell(row_ids=self.boundary, diagonal=False)
         nbrs = sorted(int(q) for q in part.neighbor_partitions)
         self.neighbors = nbrs
         send = [part.send_indices[q].to(torch.int64) for q in nbrs]
@@ -176,6 +180,24 @@ class _ShardPlan:
         self.sendbuf = torch.empty(max(self.n_send, 1), dtype=self.dtype, device=self.device)
         self.recvbuf = torch.empty(max(self.n_halo, 1), dtype=self.dtype, device=self.device)
         self._dinv = {}
+        self.p2p = None
+        self._group = D._group
+
+    def enable_p2p(self) -> None:
+        """Map the peer-memory exchange buffers of the shard CG (collective;
+        stays None when any rank cannot, or TORCH_SLA_B200_P2P=0)."""
+        if self.p2p is not None or os.environ.get("TORCH_SLA_B200_P2P", "1") == "0":
+            return
+        if not dist.is_initialized() or dist.get_world_size(self._group) < 2:
+            return
+        from .comm import communicators, register_p2p
+        h = ctypes.c_void_p()
+        L.check("sla_p2p_create", L.lib().sla_p2p_create(
+            communicators(self._group).halo, ctypes.byref(self.plan), self.code,
+            ctypes.byref(h)))
+        if h.value:
+            self.p2p = h
+            register_p2p(h)
 
     def dinv(self, kind: str):
         if kind not in self._dinv:
@@ -305,6 +327,7 @@ class DSparseTensor:
         if self._plan is None:
             self._plan = _ShardPlan(self)
             check_halo_symmetry(self._plan, self._group)
+            self._plan.enable_p2p()
         return self._plan
 
     # --------------------------------------------------------------- vectors

@@ -5,8 +5,10 @@ Each solve runs entirely inside libsla_b200: per iteration the search
 direction is computed inside the SpMV gather, its halo values travel by
 grouped NCCL send/recv while the interior rows compute, and the dot products
 of each reduction point are combined by one small ncclAllReduce (CG: 2 per
-iteration; BiCGStab: 3). The stopping test runs every 10 iterations on the
-allreduced norms, as in the reference.
+iteration; BiCGStab: 3). On a single node the CG instead stores halo values
+and dot products straight into the other GPUs' memory from inside its two
+kernels (sla_shard_cg_p2p). The stopping test runs every 10 iterations on
+the allreduced norms, as in the reference.
 """
 from __future__ import annotations
 
@@ -67,13 +69,16 @@ def _run(fn_name, D, b_owned, M_apply, atol, rtol, maxiter, verbose):
     L.check("sla_shard_krylov_workspace", lib.sla_shard_krylov_workspace(
         plan.code, no, plan.n_halo, plan.n_send, ctypes.byref(need)))
     ws = L.workspace(need.value, plan.device)
-    comms = communicators(D._group)
     info = L.SolveInfo()
-    fn = getattr(lib, fn_name)
-    st = fn(comms.halo, comms.reduce, ctypes.byref(plan.plan), plan.code, plan.sell_int.ref(),
-            plan.sell_bnd.ref(), L.ptr(M_apply.dinv), L.ptr(b), L.ptr(x), float(atol),
-            float(rtol), int(maxiter), CHECK_EVERY, L.ptr(ws), ws.numel(), ctypes.byref(info),
-            L.stream_handle(plan.device))
+    args = (ctypes.byref(plan.plan), plan.code, plan.sell_int.ref(), plan.sell_bnd.ref(),
+            L.ptr(M_apply.dinv), L.ptr(b), L.ptr(x), float(atol), float(rtol), int(maxiter),
+            CHECK_EVERY, L.ptr(ws), ws.numel(), ctypes.byref(info), L.stream_handle(plan.device))
+    if fn_name == "sla_shard_cg" and getattr(plan, "p2p", None) is not None:
+        fn_name = "sla_shard_cg_p2p"  # same algorithm on the peer-memory exchange buffers
+        st = lib.sla_shard_cg_p2p(plan.p2p, *args)
+    else:
+        comms = communicators(D._group)
+        st = getattr(lib, fn_name)(comms.halo, comms.reduce, *args)
     L.check(fn_name, st)
     D._last_info = dict(iterations=int(info.iterations), residual=float(info.residual),
                         status=int(info.status))

@@ -60,6 +60,7 @@ def install(torch_sla=None):
         if plan is None:
             plan = _ShardPlan(self)
             check_halo_symmetry(plan, getattr(self, "_group", None))
+            plan.enable_p2p()
             self._plan_b200 = plan
         return plan
 
