@@ -157,3 +157,87 @@ def test_shard_solvers_two_gpus(tmp_path, golden_shard):
 def test_shard_solvers_four_gpus(tmp_path, golden_shard):
     """Middle ranks have two neighbours (one halo per side)."""
     _check(_run(4, tmp_path), golden_shard)
+
+
+def test_shard_solvers_eight_gpus(tmp_path, golden_shard):
+    """A full node: six middle ranks, allreduces over eight ranks."""
+    res = _run(8, tmp_path)
+    _check(res, golden_shard)
+    assert all(r["owned_rows"]["p2p"] for r in res)
+
+
+# ------------------------------------------------------- failure detection
+def _worker_peer_stops(rank, world, port, out_dir):
+    """Rank 1 ends its solve early (maxiter 5) while rank 0 keeps
+    iterating: rank 0's kernels find no arrival from rank 1 within the
+    bounded wait and the solve returns SLA_ERR_TIMEOUT. Both ranks then run
+    the same solve again on the same plan, which must succeed."""
+    import sys
+    import warnings
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    sys.path.insert(0, os.path.dirname(here))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["TORCH_SLA_B200_P2P_WAIT_S"] = "0.5"
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    res = {}
+    try:
+        from oracle import krylov as K
+        from torch_sla_b200 import _lib as L
+        from torch_sla_b200 import problems as P
+        from torch_sla_b200.distributed import DSparseTensor, destroy_all
+        from torch.distributed.device_mesh import init_device_mesh
+        mesh = init_device_mesh("cuda", (world,))
+        m = 12
+        dims = (m * world, m, m)
+        n = dims[0] * m * m
+        vr, rr_, cr = P.poisson_3d_7pt_rows(dims, rank * m, m, device=dev)
+        D = DSparseTensor.from_owned_rows(vr, rr_, cr, (n, n), mesh=mesh)
+        res["p2p"] = D._shard_plan().p2p is not None
+        b = P.rhs_normal(n, 1)
+        bd = D.scatter(b.to(dev))
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            try:
+                D.solve(bd, method="cg", preconditioner="jacobi", atol=0.0, rtol=1e-12,
+                        maxiter=2000 if rank == 0 else 5)
+                res["first"] = "ok"
+            except L.SlaError as e:
+                res["first"] = e.status
+        x = D.solve(bd, method="cg", preconditioner="jacobi", atol=0.0, rtol=1e-8, maxiter=5000)
+        vg, rg, cg_, sh = P.poisson_3d_7pt(dims)
+        xo, ito = K.cg_shard(vg, rg, cg_, sh, b, atol=0.0, rtol=1e-8, maxiter=5000,
+                             precond="jacobi")
+        res["second_rel"] = _rel(x.full_tensor().cpu(), xo)
+        res["second_iters"] = (D._last_info["iterations"], ito)
+        destroy_all()
+    finally:
+        torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
+        dist.destroy_process_group()
+
+
+def test_peer_stops_gives_timeout_then_recovers(tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_peer_stops, args=(rk, 2, port, str(tmp_path)))
+             for rk in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.terminate()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    r0, r1 = (torch.load(tmp_path / f"r{rk}.pt") for rk in range(2))
+    assert r0["p2p"] and r1["p2p"]
+    assert r0["first"] == -4 and r1["first"] == "ok"  # SLA_ERR_TIMEOUT on the waiting rank
+    for r in (r0, r1):
+        assert r["second_iters"][0] == r["second_iters"][1] and r["second_rel"] < 1e-8

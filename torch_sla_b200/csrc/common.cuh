@@ -17,9 +17,10 @@ namespace sla {
 constexpr int kBlock = 256;           // threads per block of the streaming kernels
 constexpr int kWarps = kBlock / 32;   // warps per block
 constexpr unsigned kFull = 0xffffffffu;
-// Bounded spin of the grid barrier: ~1-2 s with the back-off below, after
-// which the kernel records SLA_ERR_TIMEOUT and returns.
-constexpr unsigned long long kSpinLimit = 1ull << 25;
+// Bound of every device-side wait (grid barrier, flags written by other
+// GPUs), measured on the GPU's nanosecond global timer: after it the kernel
+// records a timeout status and returns.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 // ----------------------------------------------------------------- host side
 extern std::atomic<int64_t> g_launches;
@@ -126,6 +127,11 @@ struct Sizer {
 };
 
 // ---------------------------------------------------------------- device side
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 template <typename T> __device__ __forceinline__ T mul_rn(T a, T b);
 template <> __device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
 template <> __device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
@@ -224,10 +230,10 @@ __device__ __forceinline__ bool grid_sync(GridBarrier *gb) {
       __threadfence();
       atomicAdd(&gb->gen, 1u);
     } else {
-      unsigned long long spins = 0;
+      const unsigned long long t0 = global_ns();
       while (*vgen == g) {
         if (*verr) break;
-        if (++spins > kSpinLimit) { atomicExch(&gb->err, 1); break; }
+        if (global_ns() - t0 > kWaitLimitNs) { atomicExch(&gb->err, 1); break; }
         __nanosleep(40);
       }
     }

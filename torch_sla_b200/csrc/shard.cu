@@ -823,7 +823,8 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
 //        (p, Ap) summed over the grid and then over the ranks in rank order
 //   K_B  x / r update, (r, r) and (r, z) summed the same way.
 // K_A is a cooperative launch (all blocks co-resident), so no block can
-// wait on a block that has not started; every wait is bounded (kSpinLimit)
+// wait on a block that has not started; every wait is bounded (wait_ns of
+// the descriptor, default kWaitLimitNs on the GPU's global timer)
 // and a timeout stops the solve with SLA_ERR_TIMEOUT on the host. Sequence
 // numbers are (solve epoch << 32) + iteration + 1, so flags left from an
 // earlier solve never satisfy a wait.
@@ -850,6 +851,7 @@ struct P2PDev {
   long long send_off[kP2PMaxRanks + 1];
   const T *halo;                 // my halo buffer (written by the neighbours)
   unsigned long long seq;        // epoch << 32
+  unsigned long long wait_ns;    // bound of every wait on another GPU
 };
 
 struct P2PPlan {
@@ -858,11 +860,13 @@ struct P2PPlan {
   int64_t n_halo = 0, n_owned = 0;
   size_t elem = 8;
   char *local = nullptr;
+  int *barrier = nullptr;  // device int inside `local` for the solve-start barrier
   char *peer[kP2PMaxRanks] = {};
   int nb_rank[kP2PMaxRanks] = {};
   long long dst_off[kP2PMaxRanks] = {};
   long long send_off[kP2PMaxRanks + 1] = {};
   unsigned long long epoch = 0;
+  unsigned long long wait_ns = kWaitLimitNs;
 };
 
 inline size_t p2p_halo_offset() { return align_up(sizeof(P2PHeader)); }
@@ -876,10 +880,13 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 // Bounded wait until *p >= want (sequence numbers only grow).
-__device__ __forceinline__ bool wait_seq(const unsigned long long *p, unsigned long long want) {
-  for (unsigned long long spins = 0; ld_acquire_sys(p) < want; ++spins) {
-    if (spins > kSpinLimit) return false;
-    if (spins > 32) __nanosleep(32);
+__device__ __forceinline__ bool wait_seq(const unsigned long long *p, unsigned long long want,
+                                         unsigned long long limit_ns) {
+  if (ld_acquire_sys(p) >= want) return true;
+  const unsigned long long t0 = global_ns();
+  while (ld_acquire_sys(p) < want) {
+    if (global_ns() - t0 > limit_ns) return false;
+    __nanosleep(32);
   }
   return true;
 }
@@ -914,7 +921,9 @@ __device__ __forceinline__ bool p2p_wait_halo(const P2PDev<T> &P, unsigned long 
   __shared__ int s_ok;
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
-  if (threadIdx.x < P.n_nb && !wait_seq(&P.local->arrive[P.nb_rank[threadIdx.x]], seq)) s_ok = 0;
+  if (threadIdx.x < P.n_nb &&
+      !wait_seq(&P.local->arrive[P.nb_rank[threadIdx.x]], seq, P.wait_ns))
+    s_ok = 0;
   __syncthreads();
   return s_ok != 0;
 }
@@ -933,7 +942,7 @@ __device__ __forceinline__ bool p2p_allreduce(const P2PDev<T> &P, int point, int
     for (int i = 0; i < NV; ++i) h->red_val[par][point][P.me][i] = v[i];
     __threadfence_system();
     st_release_sys(&h->red_flag[par][point][P.me], seq);
-    if (!wait_seq(&P.local->red_flag[par][point][threadIdx.x], seq)) s_ok = 0;
+    if (!wait_seq(&P.local->red_flag[par][point][threadIdx.x], seq, P.wait_ns)) s_ok = 0;
   }
   __syncthreads();
   if (!s_ok) return false;
@@ -1081,6 +1090,7 @@ static P2PDev<T> p2p_dev(const P2PPlan *pp) {
   for (int i = 0; i <= pp->n_nb; ++i) d.send_off[i] = pp->send_off[i];
   d.halo = (const T *)(pp->local + p2p_halo_offset());
   d.seq = pp->epoch << 32;
+  d.wait_ns = pp->wait_ns;
   return d;
 }
 
@@ -1102,6 +1112,9 @@ static int shard_cg_p2p_impl(P2PPlan *pp, const sla_halo_plan_t *plan, const sla
   if (!c.ok) return SLA_ERR_WORKSPACE;
   ++pp->epoch;
   P2PDev<T> P = p2p_dev<T>(pp);
+  // the ranks enter the solve together (one NCCL barrier per solve), so the
+  // bounded waits inside the kernels only ever cover in-step skew
+  SLA_NCCL_TRY(ncclAllReduce(pp->barrier, pp->barrier, 1, ncclInt32, ncclSum, pp->comm->nccl, s));
   ShardState init{};
   SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(init), cudaMemcpyHostToDevice, s));
   SLA_CUDA_TRY(cudaMemsetAsync(R, 0, sizeof(CgRed), s));
@@ -1498,6 +1511,11 @@ int sla_p2p_create(void *comm, const sla_halo_plan_t *plan, int dtype, void **p2
     if (pp->local) cudaFree(pp->local);
     delete pp;
     return SLA_OK;  // *p2p_out stays NULL: the NCCL path serves
+  }
+  pp->barrier = (int *)(pp->local + offsetof(P2PHeader, pad));
+  if (const char *w = getenv("TORCH_SLA_B200_P2P_WAIT_S")) {
+    const double sec = atof(w);
+    if (sec > 0.0) pp->wait_ns = (unsigned long long)(sec * 1e9);
   }
   *p2p_out = pp;
   return SLA_OK;
