@@ -17,7 +17,6 @@
 // Persistent path (small systems, vectors L2-resident): the same two phases
 // in one cooperative launch separated by a bounded grid barrier.
 #include <mutex>
-#include <type_traits>
 
 #include "solver.cuh"
 
@@ -55,23 +54,11 @@ struct CgPGather {
   }
 };
 
-// Gather of the streamed path when K_B has stored z = M^{-1} r: two vectors
-// per neighbour instead of three (same rounding: z is the same product).
-template <typename T>
-struct CgZGather {
-  const T *z;
-  const T *p_old;
-  T beta;
-  __device__ __forceinline__ T operator()(int32_t c) const {
-    return add_rn(mul_rn(__ldg(p_old + c), beta), __ldg(z + c));
-  }
-};
-
 template <typename T, bool PREC>
 __global__ void __launch_bounds__(kBlock)
 cg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *__restrict__ Ax,
                const T *__restrict__ dinv, T *__restrict__ r, T *__restrict__ p_old, CgState *st,
-               double *partials, double atol, double rtol, T *__restrict__ z) {
+               double *partials, double atol, double rtol) {
   __shared__ double smem[3 * kWarps];
   double acc[3] = {0.0, 0.0, 0.0};
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -83,7 +70,6 @@ cg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *_
     r[i] = ri;
     p_old[i] = T(0);
     T zi = PREC ? mul_rn(dinv[i], ri) : ri;
-    if (z) z[i] = zi;
     acc[0] += (double)ri * (double)ri;
     acc[1] += (double)ri * (double)zi;
     acc[2] += (double)bi * (double)bi;
@@ -102,10 +88,9 @@ cg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *_
   }
 }
 
-// ZV: `rz` holds z = M^{-1} r (stored by the previous K_B) instead of r.
-template <typename T, bool PREC, int WS, bool ZV>
+template <typename T, bool PREC, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
-cg_spmv_kernel(Sell<T> A, const T *__restrict__ rz, const T *__restrict__ dinv,
+cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
                const T *__restrict__ p_old, T *__restrict__ p_new, T *__restrict__ Ap, CgState *st,
                double *partials) {
   __shared__ double smem[kWarps];
@@ -113,10 +98,7 @@ cg_spmv_kernel(Sell<T> A, const T *__restrict__ rz, const T *__restrict__ dinv,
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  using Gather = typename std::conditional<ZV, CgZGather<T>, CgPGather<T, PREC, false>>::type;
-  Gather g;
-  if constexpr (ZV) g = Gather{rz, p_old, (T)st->beta};
-  else g = Gather{rz, dinv, p_old, (T)st->beta};
+  CgPGather<T, PREC, false> g{r, dinv, p_old, (T)st->beta};
   double acc[1] = {0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
@@ -138,16 +120,14 @@ template <typename T> struct Pair;
 template <> struct Pair<double> { using type = double2; };
 template <> struct Pair<float> { using type = float2; };
 
-// x += alpha p ; r -= alpha Ap (torch addcmul_ rounding) and the two dots;
-// returns z = M^{-1} r.
+// x += alpha p ; r -= alpha Ap (torch addcmul_ rounding) and the two dots.
 template <typename T, bool PREC>
-__device__ __forceinline__ T cg_axpy(T &xi, T &ri, T pi, T api, T di, T alpha, double (&acc)[2]) {
+__device__ __forceinline__ void cg_axpy(T &xi, T &ri, T pi, T api, T di, T alpha, double (&acc)[2]) {
   xi = add_rn(xi, mul_rn(alpha, pi));
   ri = sub_rn(ri, mul_rn(alpha, api));
   T zi = PREC ? mul_rn(di, ri) : ri;
   acc[0] += (double)ri * (double)ri;
   acc[1] += (double)ri * (double)zi;
-  return zi;
 }
 
 // VEC: 2 elements per 16-byte (fp64) / 8-byte (fp32) access; only launched
@@ -156,7 +136,7 @@ template <typename T, bool PREC, bool VEC>
 __global__ void __launch_bounds__(kBlock)
 cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
                  const T *__restrict__ Ap, const T *__restrict__ dinv, CgState *st,
-                 double *partials, T *__restrict__ z) {
+                 double *partials) {
   __shared__ double smem[2 * kWarps];
   if (*(volatile int *)&st->done) return;
   const T alpha = (T)st->alpha;
@@ -171,28 +151,24 @@ cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__res
       const V pv = __ldcs((const V *)p + i), av = __ldcs((const V *)Ap + i);
       V dv = pv;
       if (PREC) dv = __ldg((const V *)dinv + i);
-      V zv;
-      zv.x = cg_axpy<T, PREC>(xv.x, rv.x, pv.x, av.x, dv.x, alpha, acc);
-      zv.y = cg_axpy<T, PREC>(xv.y, rv.y, pv.y, av.y, dv.y, alpha, acc);
+      cg_axpy<T, PREC>(xv.x, rv.x, pv.x, av.x, dv.x, alpha, acc);
+      cg_axpy<T, PREC>(xv.y, rv.y, pv.y, av.y, dv.y, alpha, acc);
       ((V *)x)[i] = xv;
       ((V *)r)[i] = rv;
-      if (z) ((V *)z)[i] = zv;
     }
     if ((n & 1) && tid == 0) {
       const int64_t i = n - 1;
       T xi = x[i], ri = r[i];
-      const T zi = cg_axpy<T, PREC>(xi, ri, p[i], Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
+      cg_axpy<T, PREC>(xi, ri, p[i], Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
       x[i] = xi;
       r[i] = ri;
-      if (z) z[i] = zi;
     }
   } else {
     for (int64_t i = tid; i < n; i += stride) {
       T xi = x[i], ri = r[i];
-      const T zi = cg_axpy<T, PREC>(xi, ri, p[i], Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
+      cg_axpy<T, PREC>(xi, ri, p[i], Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
       x[i] = xi;
       r[i] = ri;
-      if (z) z[i] = zi;
     }
   }
   if (last_block_sum<2, kBlock>(acc, partials, &st->counter[2], smem) && threadIdx.x == 0) {
@@ -275,11 +251,9 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
   }
 }
 
-// nvec = 5: r, p (x2), Ap, z of the streamed path; the allocation-free
-// variant keeps 4 (no stored z).
-static size_t cg_ws_bytes(size_t elem, int64_t n, int nvec = 5) {
+static size_t cg_ws_bytes(size_t elem, int64_t n) {
   size_t G = (size_t)solver_grid();
-  return nvec * align_up(elem * (size_t)n) + 2 * align_up(4 * G * sizeof(double)) +
+  return 4 * align_up(elem * (size_t)n) + 2 * align_up(4 * G * sizeof(double)) +
          align_up(sizeof(CgState));
 }
 
@@ -294,8 +268,6 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
   const int64_t n = A.n_slots;
   Carver c(ws, ws_bytes);
   T *r = c.take<T>(n), *pA = c.take<T>(n), *pB = c.take<T>(n), *Ap = c.take<T>(n);
-  // z = M^{-1} r, stored by the update so the SpMV gathers two vectors
-  T *z = PREC ? c.take<T>(n) : nullptr;
   const int G = solver_grid();
   double *part0 = c.take<double>(4 * (size_t)G), *part1 = c.take<double>(4 * (size_t)G);
   CgState *st = c.take<CgState>(1);
@@ -305,7 +277,7 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
   SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
   if (guess) SLA_TRY(spmv_launch<T>(Ad, x, Ap, s));
   SLA_LAUNCH((cg_init_kernel<T, PREC>), grid_for(n), kBlock, 0, s, n, b, x, guess ? Ap : nullptr,
-             dinv, r, pA, st, part0, atol, rtol, z);
+             dinv, r, pA, st, part0, atol, rtol);
 
   const DeviceInfo &dev = device_info();
   bool persistent = false;
@@ -333,9 +305,8 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
     g_launches.fetch_add(1, std::memory_order_relaxed);
     profiler().end(0, s, ev);
   } else {
-    const int grid_a = occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS, PREC>);
-    const bool vec = aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv, z));
-    const T *rz = PREC ? z : r;
+    const int grid_a = occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS>);
+    const bool vec = aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv));
     const int grid_b = vec ? occupancy_grid((const void *)cg_update_kernel<T, PREC, true>)
                            : occupancy_grid((const void *)cg_update_kernel<T, PREC, false>);
     SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
@@ -343,16 +314,16 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
       T *p_new = (it & 1) ? pA : pB;
       cudaEvent_t ev;
       profiler().begin(0, it, s, &ev);
-      SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS, PREC>), grid_a, kBlock, 0, s, A, rz, dinv, p_old,
-                 p_new, Ap, st, part0);
+      SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS>), grid_a, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap,
+                 st, part0);
       profiler().end(0, s, ev);
       profiler().begin(1, it, s, &ev);
       if (vec)
         SLA_LAUNCH((cg_update_kernel<T, PREC, true>), grid_b, kBlock, 0, s, n, x, r, p_new, Ap,
-                   dinv, st, part1, z);
+                   dinv, st, part1);
       else
         SLA_LAUNCH((cg_update_kernel<T, PREC, false>), grid_b, kBlock, 0, s, n, x, r, p_new, Ap,
-                   dinv, st, part1, z);
+                   dinv, st, part1);
       profiler().end(1, s, ev);
       return SLA_OK;
     }));
@@ -419,7 +390,7 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
   SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(CgState), cudaMemcpyHostToDevice, s));
   if (guess) SLA_TRY(spmv_launch<T>(Ad, x, Ap, s));
   SLA_LAUNCH((cg_init_kernel<T, PREC>), grid_for(n), kBlock, 0, s, n, b, x, guess ? Ap : nullptr,
-             dinv, r, pA, st, part0, atol, rtol, (T *)nullptr);
+             dinv, r, pA, st, part0, atol, rtol);
   const DeviceInfo &dev = device_info();
   bool persistent = false;
   int coop_grid = 0;
@@ -446,17 +417,16 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
       for (int64_t j = 0; j < chunk; ++j, ++it) {
         T *p_old = (it & 1) ? pB : pA;
         T *p_new = (it & 1) ? pA : pB;
-        SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS, false>),
-                   occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS, false>), kBlock, 0, s,
-                   A, r, dinv, p_old, p_new, Ap, st, part0);
+        SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS>), occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS>),
+                   kBlock, 0, s, A, r, dinv, p_old, p_new, Ap, st, part0);
         if (aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv)))
           SLA_LAUNCH((cg_update_kernel<T, PREC, true>),
                      occupancy_grid((const void *)cg_update_kernel<T, PREC, true>), kBlock, 0, s,
-                     n, x, r, p_new, Ap, dinv, st, part1, (T *)nullptr);
+                     n, x, r, p_new, Ap, dinv, st, part1);
         else
           SLA_LAUNCH((cg_update_kernel<T, PREC, false>),
                      occupancy_grid((const void *)cg_update_kernel<T, PREC, false>), kBlock, 0, s,
-                     n, x, r, p_new, Ap, dinv, st, part1, (T *)nullptr);
+                     n, x, r, p_new, Ap, dinv, st, part1);
       }
       int done = 0;
       SLA_CUDA_TRY(cudaMemcpyAsync(&done, &st->done, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -527,7 +497,7 @@ int sla_pcg_noalloc(int dtype, const sla_sell_t *A, const void *dinv, const void
   if (flags < 0 || flags > 2) return SLA_ERR_INVALID;
   if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
   info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
-  size_t need = cg_ws_bytes(dtype == SLA_F64 ? 8 : 4, A->n_slots, 4);
+  size_t need = cg_ws_bytes(dtype == SLA_F64 ? 8 : 4, A->n_slots);
   if (need > (size_t)SLA_PCG_NOALLOC_SCRATCH_BYTES) {
     fprintf(stderr,
             "[sla_b200] sla_pcg_noalloc: n=%lld needs %zu scratch bytes, above the fixed "
