@@ -556,24 +556,31 @@ def run_sharded(args, world, rank, local):
     V = 8
     interior_frac = plan.sell_int.n_slots / max(n_loc, 1)
     fm_int = sell_format(plan.sell_int, V)
-    exchange = ("halo values and dot products stored into peer GPUs' memory by the solver "
-                "kernels (CUDA IPC over NVLink), 2 launches per iteration"
-                if method == "cg" and plan.p2p is not None else
+    exchange = (("halo values and dot products stored into peer GPUs' memory by the solver "
+                 f"kernels (CUDA IPC over NVLink), {2 if method == 'cg' else 3} launches per "
+                 "iteration") if plan.p2p is not None else
                 "NCCL grouped send/recv halo + allreduce per reduction point")
     mat = matrix_bytes(nnz, n_loc)
     if method == "cg":
         metric = (METRIC if wl == "pcg7" else
                   "fp64 Jacobi-PCG iterations/s (3-D 27-point, 256^3 unknowns per GPU)")
-        ka_bytes = (mat + 5 * V * n_loc) * interior_frac
-        ka_fmt = fm_int["matrix_bytes"] + 5 * V * plan.sell_int.n_slots
         iter_bytes = mat + 13 * V * n_loc
-        kname = "shard_cg_spmv"
+        if plan.p2p is not None:
+            # one kernel covers every owned row (halo send, interior, boundary)
+            ka_bytes = mat + 5 * V * n_loc
+            ka_fmt = (fm_int["matrix_bytes"] + sell_format(plan.sell_bnd, V)["matrix_bytes"]
+                      + 5 * V * n_loc)
+            kname, rows = "shard_cg_p2p_spmv", "all rows, halo send and cross-rank sum fused"
+        else:
+            ka_bytes = (mat + 5 * V * n_loc) * interior_frac
+            ka_fmt = fm_int["matrix_bytes"] + 5 * V * plan.sell_int.n_slots
+            kname, rows = "shard_cg_spmv", "interior rows"
     else:
         metric = "fp64 Jacobi-BiCGStab iterations/s (convection-diffusion, 192^3 per GPU)"
         ka_bytes = (mat + 6 * V * n_loc) * interior_frac
         ka_fmt = fm_int["matrix_bytes"] + 6 * V * plan.sell_int.n_slots
         iter_bytes = 2 * mat + 25 * V * n_loc
-        kname = "shard_bi_k1"
+        kname, rows = "shard_bi_k1", "interior rows"
     peak, _ = peaks()
     if rank == 0:
         line = base_line(args, metric, value, "iterations/s", ms, world)
@@ -592,7 +599,7 @@ def run_sharded(args, world, rank, local):
                                       "achieved_gbs_per_gpu":
                                           round(iter_bytes * value / world / 1e9, 1),
                                       "frac": round(iter_bytes * value / world / 1e9 / peak, 4)}
-        line["roofline"] = roofline(f"{kname} (interior rows)", ka_bytes, ka_ms, ka_n,
+        line["roofline"] = roofline(f"{kname} ({rows})", ka_bytes, ka_ms, ka_n,
                                     f"{kname}@{wl}-shard:{m}", ka_fmt)
         line["e2e"] = {"value": round(sum(e_its) * world / (e_ms / 1e3), 3),
                        "unit": "iterations/s", "h2d_bytes_per_step": n_loc * V * world,

@@ -342,6 +342,16 @@ int sla_shard_cg_p2p(void *p2p, const sla_halo_plan_t *plan, int dtype,
                      double rtol, int64_t maxiter, int64_t check_every,
                      void *workspace, size_t workspace_bytes,
                      sla_solve_info_t *info, sla_stream_t stream);
+/* Peer-memory twin of sla_shard_bicgstab (distributed/solve.py:356-436,
+ * including the reference's reuse of the SpMV output buffer): three kernel
+ * launches and three cross-rank sums per iteration, no NCCL call. */
+int sla_shard_bicgstab_p2p(void *p2p, const sla_halo_plan_t *plan, int dtype,
+                           const sla_sell_t *A_interior,
+                           const sla_sell_t *A_boundary, const void *dinv,
+                           const void *b, void *x, double atol, double rtol,
+                           int64_t maxiter, int64_t check_every, void *workspace,
+                           size_t workspace_bytes, sla_solve_info_t *info,
+                           sla_stream_t stream);
 
 #ifdef __cplusplus
 }

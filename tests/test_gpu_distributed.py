@@ -93,6 +93,16 @@ def _worker(rank, world, port, out_dir):
         res["owned_rows"] = {"rel": _rel(x2.full_tensor().cpu(), xo),
                              "iters": D2._last_info["iterations"], "oracle_iters": ito,
                              "p2p": D2._shard_plan().p2p is not None}
+        # gradient through the distributed solve: d/db sum(w * A^{-1} b) = A^{-1} w
+        owned = D2.partition_info.owned_nodes
+        bl = b.to(dev)[owned.to(dev)].clone().requires_grad_(True)
+        w = torch.linspace(-1.0, 1.0, n, dtype=torch.float64)
+        xg = D2.solve(bl, method="cg", preconditioner="jacobi", atol=0.0, rtol=1e-10,
+                      maxiter=5000)
+        (xg * w.to(dev)[owned.to(dev)]).sum().backward()
+        yo, _ = K.cg_shard(vg, rg, cg_, sh, w, atol=0.0, rtol=1e-12, maxiter=5000,
+                           precond="jacobi")
+        res["owned_rows"]["grad_rel"] = _rel(bl.grad.cpu(), yo[owned.cpu()])
         # the same solve on the NCCL path (peer-memory exchange disabled)
         os.environ["TORCH_SLA_B200_P2P"] = "0"
         D3 = DSparseTensor.from_owned_rows(vr, rr_, cr, (n, n), mesh=mesh)
@@ -141,6 +151,7 @@ def _check(results, golden_shard):
         o = res["owned_rows"]
         assert o["iters"] == o["oracle_iters"] and o["rel"] < 1e-8, o
         assert o["nccl_iters"] == o["oracle_iters"] and o["nccl_rel"] < 1e-8, o
+        assert o["grad_rel"] < 1e-7, o
         assert not o["nccl_p2p"]
 
 

@@ -120,6 +120,9 @@ _SIGNATURES = {
     "sla_shard_cg_p2p": (ctypes.c_int, [c_ptr, _P(HaloPlan), ctypes.c_int, _P(SellView),
                                         _P(SellView), c_ptr, c_ptr, c_ptr, c_dbl, c_dbl, c_i64,
                                         c_i64, c_ptr, c_sz, _P(SolveInfo), c_ptr]),
+    "sla_shard_bicgstab_p2p": (ctypes.c_int, [c_ptr, _P(HaloPlan), ctypes.c_int, _P(SellView),
+                                              _P(SellView), c_ptr, c_ptr, c_ptr, c_dbl, c_dbl,
+                                              c_i64, c_i64, c_ptr, c_sz, _P(SolveInfo), c_ptr]),
 }
 
 _lib = None

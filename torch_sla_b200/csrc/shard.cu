@@ -829,14 +829,15 @@ static int shard_bi_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
 // numbers are (solve epoch << 32) + iteration + 1, so flags left from an
 // earlier solve never satisfy a wait.
 constexpr int kP2PMaxRanks = 8;
-constexpr int kRedPoints = 3;  // 0 init, 1 (p,Ap), 2 (r,r)/(r,z)
+constexpr int kRedPoints = 4;  // CG: 0 init, 1 (p,Ap), 2 (r,r)/(r,z); BiCGStab: 0..3
+constexpr int kRedValues = 4;
 constexpr int kStopTimeout = 3;
 
 struct P2PHeader {
   long long recv_off[kP2PMaxRanks];  // where rank q's values start in my halo; -1 none
   unsigned long long arrive[kP2PMaxRanks];
   unsigned long long red_flag[2][kRedPoints][kP2PMaxRanks];
-  double red_val[2][kRedPoints][kP2PMaxRanks][2];
+  double red_val[2][kRedPoints][kP2PMaxRanks][kRedValues];
   unsigned send_count;
   unsigned pad[63];
 };
@@ -1075,6 +1076,193 @@ shard_cg_p2p_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__
   }
 }
 
+// ------------------------------------------------ peer-memory shard BiCGStab
+// Same scheme as the CG: K1 (v = A p_hat) and K2 (t = A s_hat) each send
+// their halo share first (arrival sequence numbers 2k+1 and 2k+2), run the
+// interior rows, wait, run the boundary rows and sum their dots over the
+// ranks; K3 updates x and r and sums (r,r), (r_hat,r). The halo buffer is
+// reused by both SpMVs: a neighbour can only start the next send after the
+// cross-rank sum that needs this rank's completed SpMV.
+template <typename T>
+__global__ void __launch_bounds__(kBlock)
+shard_bi_p2p_init(int64_t n, const T *__restrict__ b, T *__restrict__ x, T *__restrict__ r,
+                  T *__restrict__ rhat, T *__restrict__ p, T *__restrict__ t, ShardState *st,
+                  BiRed *R, double *partials, P2PDev<T> P) {
+  __shared__ double smem[2 * kWarps];
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T bi = b[i];
+    x[i] = T(0);
+    r[i] = bi;
+    rhat[i] = bi;
+    p[i] = T(0);
+    t[i] = T(0);
+    acc[0] += (double)bi * (double)bi;
+    acc[1] += (double)bi * (double)bi;
+  }
+  if (!last_block_sum<2, kBlock>(acc, partials, &st->counter[0], smem)) return;
+  if (!p2p_allreduce<2>(P, 0, 0, P.seq, acc)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  if (threadIdx.x == 0) {
+    R->init[0] = acc[0];
+    R->init[1] = acc[1];
+    st->alpha_prev = 1.0;
+    st->omega_prev = 1.0;
+  }
+}
+
+template <typename T, bool PREC, int WS>
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
+shard_bi_p2p_k1(Sell<T> AI, Sell<T> AB, int32_t n_own, const int32_t *__restrict__ send_index,
+                BiP<T, PREC> g0, const T *__restrict__ rhat, T *__restrict__ p_new,
+                T *__restrict__ v, ShardState *st, BiRed *R, double *partials, long long k,
+                long long every, double atol, double rtol, P2PDev<T> P) {
+  constexpr int WSB = boundary_spec(WS);
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  if (bi_stop(R, k, every, bi_tol(R, atol, rtol))) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) { st->stopped = 1; st->iters = k; }
+    return;
+  }
+  BiP<T, PREC> inner = g0;
+  inner.beta = (T)bi_beta(R, st, k);
+  inner.omega = (T)st->omega_prev;
+  const unsigned long long seq = P.seq + (unsigned long long)(2 * k + 1);
+  p2p_send_halo(P, send_index, inner, seq);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[1] = {0.0};
+  auto emit = [&](const Sell<T> &A, int64_t s, T sum) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int32_t row = (int32_t)slot_row(A, slot);
+      p_new[row] = inner.pval(row);
+      v[row] = sum;
+      acc[0] += (double)rhat[row] * (double)sum;
+    }
+  };
+  for_each_slice<WS>(AI, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    emit(AI, s, sell_row_at<WS>(AI, s, sbase, swidth, lane, inner));
+  });
+  if (!p2p_wait_halo(P, seq)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  HaloGatherL2<T, BiP<T, PREC>> g{inner, P.halo, n_own};
+  for_each_slice<WSB>(AB, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    emit(AB, s, sell_row_at<WSB>(AB, s, sbase, swidth, lane, g));
+  });
+  if (!last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem)) return;
+  if (!p2p_allreduce<1>(P, 1, (int)(k & 1), P.seq + (unsigned long long)(k + 1), acc)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  if (threadIdx.x == 0) R->rv[0] = acc[0];
+}
+
+template <typename T, bool PREC, int WS>
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
+shard_bi_p2p_k2(Sell<T> AI, Sell<T> AB, int32_t n_own, const int32_t *__restrict__ send_index,
+                BiS<T, PREC> g0, T *__restrict__ t, ShardState *st, BiRed *R, double *partials,
+                long long k, P2PDev<T> P) {
+  constexpr int WSB = boundary_spec(WS);
+  __shared__ double smem[3 * kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  BiS<T, PREC> inner = g0;
+  inner.alpha = (T)(bi_rho(R, k) / R->rv[0]);
+  const unsigned long long seq = P.seq + (unsigned long long)(2 * k + 2);
+  p2p_send_halo(P, send_index, inner, seq);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[3] = {0.0, 0.0, 0.0};
+  auto emit = [&](const Sell<T> &A, int64_t s, T sum) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int32_t row = (int32_t)slot_row(A, slot);
+      const T si = inner.sval(row);
+      t[row] = sum;
+      acc[0] += (double)si * (double)si;
+      acc[1] += (double)sum * (double)sum;
+      acc[2] += (double)sum * (double)si;
+    }
+  };
+  for_each_slice<WS>(AI, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    emit(AI, s, sell_row_at<WS>(AI, s, sbase, swidth, lane, inner));
+  });
+  if (!p2p_wait_halo(P, seq)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  HaloGatherL2<T, BiS<T, PREC>> g{inner, P.halo, n_own};
+  for_each_slice<WSB>(AB, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    emit(AB, s, sell_row_at<WSB>(AB, s, sbase, swidth, lane, g));
+  });
+  if (!last_block_sum<3, kBlock>(acc, partials, &st->counter[3], smem)) return;
+  if (!p2p_allreduce<3>(P, 2, (int)(k & 1), P.seq + (unsigned long long)(k + 1), acc)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  if (threadIdx.x == 0) {
+    R->stt[0] = acc[0];
+    R->stt[1] = acc[1];
+    R->stt[2] = acc[2];
+  }
+}
+
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+shard_bi_p2p_k3(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ rhat,
+                const T *__restrict__ p, const T *__restrict__ v, const T *__restrict__ t,
+                const T *__restrict__ dinv, ShardState *st, BiRed *R, double *partials,
+                long long k, long long every, double atol, double rtol, P2PDev<T> P) {
+  __shared__ double smem[2 * kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  const double alpha_d = bi_rho(R, k) / R->rv[0];
+  const T alpha = (T)alpha_d;
+  // the same allreduced (s,s) on every rank: all ranks take the same branch
+  const bool half = (k % every) == 0 && sqrt(R->stt[0]) < bi_tol(R, atol, rtol);
+  const double omega_d = R->stt[2] / R->stt[1];
+  const T omega = (T)omega_d;
+  double acc[2] = {0.0, 0.0};
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    T ph = PREC ? mul_rn(dinv[i], p[i]) : p[i];
+    T xi = add_rn(x[i], mul_rn(alpha, ph));
+    if (!half) {
+      T si = sub_rn(r[i], mul_rn(alpha, v[i]));
+      T sh = PREC ? mul_rn(dinv[i], si) : si;
+      xi = add_rn(xi, mul_rn(omega, sh));
+      T ri = sub_rn(si, mul_rn(omega, t[i]));
+      r[i] = ri;
+      acc[0] += (double)ri * (double)ri;
+      acc[1] += (double)rhat[i] * (double)ri;
+    }
+    x[i] = xi;
+  }
+  if (!last_block_sum<2, kBlock>(acc, partials, &st->counter[5], smem)) return;
+  if (half) {
+    if (threadIdx.x == 0) { st->stopped = 1; st->iters = k + 1; }
+    return;
+  }
+  if (!p2p_allreduce<2>(P, 3, (int)(k & 1), P.seq + (unsigned long long)(k + 1), acc)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  if (threadIdx.x == 0) {
+    R->rr[k & 1][0] = acc[0];
+    R->rr[k & 1][1] = acc[1];
+    st->alpha_prev = alpha_d;
+    st->omega_prev = omega_d;
+  }
+}
+
 template <typename T>
 static P2PDev<T> p2p_dev(const P2PPlan *pp) {
   P2PDev<T> d{};
@@ -1169,6 +1357,84 @@ static int shard_cg_p2p_impl(P2PPlan *pp, const sla_halo_plan_t *plan, const sla
   return info->status;
 }
 
+
+template <typename T, bool PREC, int WS>
+static int shard_bi_p2p_impl(P2PPlan *pp, const sla_halo_plan_t *plan, const sla_sell_t *Ai,
+                             const sla_sell_t *Ab, const T *dinv, const T *b, T *x, double atol,
+                             double rtol, int64_t maxiter, int64_t every, void *ws,
+                             size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
+  Sell<T> AI = make_sell<T>(Ai), AB = make_sell<T>(Ab);
+  const int64_t no = plan->n_owned;
+  Carver c(ws, ws_bytes);
+  T *r = c.take<T>(no + 1), *rhat = c.take<T>(no + 1), *pA = c.take<T>(no + 1);
+  T *pB = c.take<T>(no + 1), *v = c.take<T>(no + 1), *t = c.take<T>(no + 1);
+  const int G = solver_grid();
+  double *part[6];
+  for (int q = 0; q < 6; ++q) part[q] = c.take<double>(4 * (size_t)G);
+  ShardState *st = c.take<ShardState>(1);
+  BiRed *R = c.take<BiRed>(1);
+  if (!c.ok) return SLA_ERR_WORKSPACE;
+  ++pp->epoch;
+  P2PDev<T> P = p2p_dev<T>(pp);
+  SLA_NCCL_TRY(ncclAllReduce(pp->barrier, pp->barrier, 1, ncclInt32, ncclSum, pp->comm->nccl, s));
+  ShardState init{};
+  SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(init), cudaMemcpyHostToDevice, s));
+  SLA_CUDA_TRY(cudaMemsetAsync(R, 0, sizeof(BiRed), s));
+  SLA_LAUNCH(shard_bi_p2p_init<T>, grid_for(no), kBlock, 0, s, no, b, x, r, rhat, pA, t, st, R,
+             part[0], P);
+  const void *k1 = (const void *)shard_bi_p2p_k1<T, PREC, WS>;
+  const void *k2 = (const void *)shard_bi_p2p_k2<T, PREC, WS>;
+  int per1 = 0, per2 = 0;
+  SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per1, k1, kBlock, 0));
+  SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per2, k2, kBlock, 0));
+  if (per1 < 1 || per2 < 1) return SLA_ERR_UNSUPPORTED;
+  const int sms = device_info().sm_count;
+  const int g1 = per1 * sms < G ? per1 * sms : G, g2 = per2 * sms < G ? per2 * sms : G;
+  const int g3 = occupancy_grid((const void *)shard_bi_p2p_k3<T, PREC>);
+  const int32_t n_own = (int32_t)no;
+  SLA_TRY(shard_loop(pp->comm, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
+    T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
+    BiP<T, PREC> gp{r, p_old, t, dinv, T(0), T(1)};
+    BiS<T, PREC> gs{r, v, dinv, T(0)};
+    long long kk = (long long)k, ev_ = (long long)every;
+    void *a1[] = {&AI, &AB, (void *)&n_own, (void *)&plan->send_index, &gp, (void *)&rhat,
+                  (void *)&p_new, (void *)&v, (void *)&st, (void *)&R, (void *)&part[1], &kk,
+                  &ev_, (void *)&atol, (void *)&rtol, &P};
+    cudaEvent_t e;
+    profiler().begin(0, k, s, &e);
+    SLA_CUDA_TRY(cudaLaunchCooperativeKernel(k1, dim3(g1), dim3(kBlock), a1, 0, s));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    profiler().end(0, s, e);
+    void *a2[] = {&AI, &AB, (void *)&n_own, (void *)&plan->send_index, &gs, (void *)&t,
+                  (void *)&st, (void *)&R, (void *)&part[3], &kk, &P};
+    SLA_CUDA_TRY(cudaLaunchCooperativeKernel(k2, dim3(g2), dim3(kBlock), a2, 0, s));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    SLA_LAUNCH((shard_bi_p2p_k3<T, PREC>), g3, kBlock, 0, s, no, x, r, rhat, p_new, v, t, dinv,
+               st, R, part[5], kk, ev_, atol, rtol, P);
+    return SLA_OK;
+  }));
+  ShardState out;
+  BiRed red;
+  SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(out), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaMemcpyAsync(&red, R, sizeof(red), cudaMemcpyDeviceToHost, s));
+  cudaEvent_t done;
+  SLA_CUDA_TRY(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+  SLA_CUDA_TRY(cudaEventRecord(done, s));
+  int wrc = wait_bounded(done, pp->comm);
+  cudaEventDestroy(done);
+  SLA_TRY(wrc);
+  profiler().resolve();
+  if (out.stopped == kStopTimeout) {
+    fprintf(stderr, "[sla_b200] shard BiCGStab: a peer did not answer within the bounded wait\n");
+    return SLA_ERR_TIMEOUT;
+  }
+  info->iterations = out.stopped == 1 ? out.iters : maxiter;
+  const long long last = info->iterations - 1;
+  info->residual = last >= 0 ? sqrt(red.rr[last & 1][0]) : sqrt(red.init[0]);
+  info->status = out.stopped == 1 ? SLA_OK : SLA_NOT_CONVERGED;
+  info->reason = out.stopped;
+  return info->status;
+}
 }  // namespace sla
 
 using namespace sla;
@@ -1550,24 +1816,32 @@ int sla_p2p_destroy(void *p2p) {
   return rc;
 }
 
+static int p2p_args_ok(P2PPlan *pp, const sla_halo_plan_t *plan, int dtype, const sla_sell_t *Ai,
+                       const sla_sell_t *Ab, const void *b, void *x, sla_solve_info_t *info,
+                       int64_t every, size_t workspace_bytes, void *workspace) {
+  if (!pp || !pp->comm) return SLA_ERR_INVALID;
+  SLA_TRY(shard_args_ok(pp->comm, pp->comm, plan, Ai, Ab, b, x, info, every));
+  if (plan->n_owned != pp->n_owned || plan->n_halo != pp->n_halo ||
+      plan->n_neighbors != pp->n_nb || plan->halo_src)
+    return SLA_ERR_INVALID;
+  if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
+  if ((dtype == SLA_F64 ? 8u : 4u) != pp->elem) return SLA_ERR_INVALID;
+  if (!device_info().coop) return SLA_ERR_UNSUPPORTED;
+  size_t need = 0;
+  SLA_TRY(sla_shard_krylov_workspace(dtype, plan->n_owned, plan->n_halo, n_send(plan), &need));
+  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  return SLA_OK;
+}
+
 int sla_shard_cg_p2p(void *p2p, const sla_halo_plan_t *plan, int dtype,
                      const sla_sell_t *A_interior, const sla_sell_t *A_boundary, const void *dinv,
                      const void *b, void *x, double atol, double rtol, int64_t maxiter,
                      int64_t check_every, void *workspace, size_t workspace_bytes,
                      sla_solve_info_t *info, sla_stream_t stream) {
   P2PPlan *pp = (P2PPlan *)p2p;
-  if (!pp || !pp->comm) return SLA_ERR_INVALID;
-  SLA_TRY(shard_args_ok(pp->comm, pp->comm, plan, A_interior, A_boundary, b, x, info,
-                        check_every));
-  if (plan->n_owned != pp->n_owned || plan->n_halo != pp->n_halo ||
-      plan->n_neighbors != pp->n_nb || plan->halo_src)
-    return SLA_ERR_INVALID;
-  if ((dtype == SLA_F64 ? 8u : 4u) != pp->elem) return SLA_ERR_INVALID;
-  if (!device_info().coop) return SLA_ERR_UNSUPPORTED;
+  SLA_TRY(p2p_args_ok(pp, plan, dtype, A_interior, A_boundary, b, x, info, check_every,
+                      workspace_bytes, workspace));
   info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
-  size_t need = 0;
-  SLA_TRY(sla_shard_krylov_workspace(dtype, plan->n_owned, plan->n_halo, n_send(plan), &need));
-  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
   cudaStream_t s = (cudaStream_t)stream;
   const int wspec = width_spec2(A_interior, A_boundary);
   if (dtype == SLA_F64) {
@@ -1579,15 +1853,43 @@ int sla_shard_cg_p2p(void *p2p, const sla_halo_plan_t *plan, int dtype,
                                                                 (const double *)b, (double *)x, atol, rtol, maxiter, check_every,
                                                                 workspace, workspace_bytes, info, s));
   }
-  if (dtype == SLA_F32) {
+  if (dinv)
+    SLA_WS_DISPATCH(wspec, return shard_cg_p2p_impl<float, true, WS>(pp, plan, A_interior, A_boundary, (const float *)dinv,
+                                                              (const float *)b, (float *)x, atol, rtol, maxiter, check_every,
+                                                              workspace, workspace_bytes, info, s));
+  SLA_WS_DISPATCH(wspec, return shard_cg_p2p_impl<float, false, WS>(pp, plan, A_interior, A_boundary, nullptr,
+                                                             (const float *)b, (float *)x, atol, rtol, maxiter, check_every,
+                                                             workspace, workspace_bytes, info, s));
+  return SLA_ERR_INVALID;
+}
+
+int sla_shard_bicgstab_p2p(void *p2p, const sla_halo_plan_t *plan, int dtype,
+                           const sla_sell_t *A_interior, const sla_sell_t *A_boundary,
+                           const void *dinv, const void *b, void *x, double atol, double rtol,
+                           int64_t maxiter, int64_t check_every, void *workspace,
+                           size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
+  P2PPlan *pp = (P2PPlan *)p2p;
+  SLA_TRY(p2p_args_ok(pp, plan, dtype, A_interior, A_boundary, b, x, info, check_every,
+                      workspace_bytes, workspace));
+  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int wspec = width_spec2(A_interior, A_boundary);
+  if (dtype == SLA_F64) {
     if (dinv)
-      SLA_WS_DISPATCH(wspec, return shard_cg_p2p_impl<float, true, WS>(pp, plan, A_interior, A_boundary, (const float *)dinv,
-                                                                (const float *)b, (float *)x, atol, rtol, maxiter, check_every,
+      SLA_WS_DISPATCH(wspec, return shard_bi_p2p_impl<double, true, WS>(pp, plan, A_interior, A_boundary, (const double *)dinv,
+                                                                 (const double *)b, (double *)x, atol, rtol, maxiter, check_every,
+                                                                 workspace, workspace_bytes, info, s));
+    SLA_WS_DISPATCH(wspec, return shard_bi_p2p_impl<double, false, WS>(pp, plan, A_interior, A_boundary, nullptr,
+                                                                (const double *)b, (double *)x, atol, rtol, maxiter, check_every,
                                                                 workspace, workspace_bytes, info, s));
-    SLA_WS_DISPATCH(wspec, return shard_cg_p2p_impl<float, false, WS>(pp, plan, A_interior, A_boundary, nullptr,
-                                                               (const float *)b, (float *)x, atol, rtol, maxiter, check_every,
-                                                               workspace, workspace_bytes, info, s));
   }
+  if (dinv)
+    SLA_WS_DISPATCH(wspec, return shard_bi_p2p_impl<float, true, WS>(pp, plan, A_interior, A_boundary, (const float *)dinv,
+                                                              (const float *)b, (float *)x, atol, rtol, maxiter, check_every,
+                                                              workspace, workspace_bytes, info, s));
+  SLA_WS_DISPATCH(wspec, return shard_bi_p2p_impl<float, false, WS>(pp, plan, A_interior, A_boundary, nullptr,
+                                                             (const float *)b, (float *)x, atol, rtol, maxiter, check_every,
+                                                             workspace, workspace_bytes, info, s));
   return SLA_ERR_INVALID;
 }
 

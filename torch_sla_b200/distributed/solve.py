@@ -5,9 +5,10 @@ Each solve runs entirely inside libsla_b200: per iteration the search
 direction is computed inside the SpMV gather, its halo values travel by
 grouped NCCL send/recv while the interior rows compute, and the dot products
 of each reduction point are combined by one small ncclAllReduce (CG: 2 per
-iteration; BiCGStab: 3). On a single node the CG instead stores halo values
-and dot products straight into the other GPUs' memory from inside its two
-kernels (sla_shard_cg_p2p). The stopping test runs every 10 iterations on
+iteration; BiCGStab: 3). On a single node both solvers instead store halo
+values and dot products straight into the other GPUs' memory from inside
+their kernels (sla_shard_cg_p2p: two launches per iteration,
+sla_shard_bicgstab_p2p: three). The stopping test runs every 10 iterations on
 the allreduced norms, as in the reference.
 """
 from __future__ import annotations
@@ -73,9 +74,9 @@ def _run(fn_name, D, b_owned, M_apply, atol, rtol, maxiter, verbose):
     args = (ctypes.byref(plan.plan), plan.code, plan.sell_int.ref(), plan.sell_bnd.ref(),
             L.ptr(M_apply.dinv), L.ptr(b), L.ptr(x), float(atol), float(rtol), int(maxiter),
             CHECK_EVERY, L.ptr(ws), ws.numel(), ctypes.byref(info), L.stream_handle(plan.device))
-    if fn_name == "sla_shard_cg" and getattr(plan, "p2p", None) is not None:
-        fn_name = "sla_shard_cg_p2p"  # same algorithm on the peer-memory exchange buffers
-        st = lib.sla_shard_cg_p2p(plan.p2p, *args)
+    if getattr(plan, "p2p", None) is not None:
+        fn_name += "_p2p"  # same algorithm on the peer-memory exchange buffers
+        st = getattr(lib, fn_name)(plan.p2p, *args)
     else:
         comms = communicators(D._group)
         st = getattr(lib, fn_name)(comms.halo, comms.reduce, *args)
@@ -88,9 +89,32 @@ def _run(fn_name, D, b_owned, M_apply, atol, rtol, maxiter, verbose):
     return x
 
 
+class _ShardCGSolve(torch.autograd.Function):
+    """x = A^{-1} b on the owned rows. CG needs A symmetric positive
+    definite, so the adjoint system is A itself: the backward pass is one
+    more distributed solve with the incoming gradient (the single-process
+    adjoint of linear_solve.py:283-324, in Shard(0) space); every rank takes
+    part in it."""
+
+    @staticmethod
+    def forward(ctx, b_owned, D, M_apply, atol, rtol, maxiter, verbose):
+        ctx.D = D
+        ctx.args = (M_apply, atol, rtol, maxiter, verbose)
+        return _run("sla_shard_cg", D, b_owned.detach(), M_apply, atol, rtol, maxiter, verbose)
+
+    @staticmethod
+    def backward(ctx, g):
+        M_apply, atol, rtol, maxiter, verbose = ctx.args
+        gb = _run("sla_shard_cg", ctx.D, g.contiguous(), M_apply, atol, rtol, maxiter, verbose)
+        return gb, None, None, None, None, None, None
+
+
 def cg_shard(D, b_owned: torch.Tensor, *, M_apply: Callable, atol: float, rtol: float,
              maxiter: int, verbose: bool) -> torch.Tensor:
-    """Preconditioned CG in Shard(0) space (distributed/solve.py:279-350)."""
+    """Preconditioned CG in Shard(0) space (distributed/solve.py:279-350);
+    differentiable in b (adjoint solve on the same shards)."""
+    if torch.is_grad_enabled() and b_owned.requires_grad:
+        return _ShardCGSolve.apply(b_owned, D, M_apply, atol, rtol, maxiter, verbose)
     return _run("sla_shard_cg", D, b_owned, M_apply, atol, rtol, maxiter, verbose)
 
 
