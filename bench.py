@@ -13,10 +13,10 @@ Other workloads (--workload): cg2d (2-D 256^2 plain CG, rtol 1e-10,
 persistent kernel), spmv (256^3 SpMV fp64 and fp32), batched (64 x 512^2
 same-pattern CG, rtol 1e-8, with backward), bicgstab (192^3 convection-
 diffusion, Jacobi BiCGStab), pcg27 (27-point variable-coefficient 256^3 per
-GPU).
+GPU), mrhs (128^3 7-point with 16 right-hand sides, multi-RHS CG).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                  [--workload pcg7|cg2d|spmv|batched|bicgstab|pcg27] [--grid M]
+                  [--workload pcg7|cg2d|spmv|batched|bicgstab|pcg27|mrhs] [--grid M]
 """
 from __future__ import annotations
 
@@ -179,7 +179,7 @@ def roofline(kernel, alg_bytes, ms_total, launches, traffic_key, format_bytes=No
 
 # ----------------------------------------------------- single-GPU workloads
 def wl_pcg7(args, dev, local):
-    """3-D 7-point Poisson 256^3, fp64 Jacobi PCG, rtol 1e-8."""
+    """3-D 7-point Poisson 256^3, fp64 Jacobi PCG, rtol 1e-8 (the headline workload)."""
     from torch_sla_b200 import _lib as L
     from torch_sla_b200 import problems as P
     from torch_sla_b200.backends import pytorch_backend as PB
@@ -288,7 +288,7 @@ def cpu_baseline_pcg(A, b_host, budget_s):
 
 
 def wl_cg2d(args, dev, local):
-    """configs[0]: 2-D 5-point 256^2, b ~ U(-1,1) seed 0, plain CG rtol 1e-10."""
+    """2-D 5-point 256^2, b ~ U(-1,1) seed 0, plain CG rtol 1e-10."""
     from oracle import krylov as K
     from torch_sla_b200 import _lib as L
     from torch_sla_b200 import problems as P
@@ -333,7 +333,7 @@ def wl_cg2d(args, dev, local):
 
 
 def wl_spmv(args, dev, local):
-    """configs[1] SpMV sweep: y = A x on the 256^3 7-point matrix, fp64 and fp32."""
+    """SpMV sweep: y = A x on the 256^3 7-point matrix, fp64 and fp32."""
     from torch_sla_b200 import problems as P
     from torch_sla_b200._csr import DeviceCSR, spmv
     res = {}
@@ -372,7 +372,7 @@ def wl_spmv(args, dev, local):
 
 
 def wl_batched(args, dev, local):
-    """configs[2]: 64 x 512^2 variable-coefficient diffusion, batched CG
+    """64 x 512^2 variable-coefficient diffusion, batched CG
     rtol 1e-8, forward + backward through spsolve_batch_same_layout."""
     import torch_sla_b200 as T
     from torch_sla_b200 import _lib as L
@@ -423,7 +423,7 @@ def wl_batched(args, dev, local):
 
 
 def wl_bicgstab(args, dev, local):
-    """configs[3]: 192^3 upwind convection-diffusion, Jacobi BiCGStab rtol 1e-8."""
+    """192^3 upwind convection-diffusion, Jacobi BiCGStab rtol 1e-8."""
     from torch_sla_b200 import _lib as L
     from torch_sla_b200 import problems as P
     from torch_sla_b200.backends import pytorch_backend as PB
@@ -463,8 +463,53 @@ def wl_bicgstab(args, dev, local):
     return line
 
 
+def wl_mrhs(args, dev, local):
+    """Multi-RHS CG (pytorch_solve with a 2-D b, batched_pcg_solve): 3-D
+    7-point 128^3 with 16 right-hand sides, Jacobi, rtol 1e-8."""
+    from torch_sla_b200 import _lib as L
+    from torch_sla_b200 import problems as P
+    from torch_sla_b200.backends import pytorch_backend as PB
+    m, K = 128, 16
+    v, r, c, sh = P.poisson_3d_7pt(m, device=dev)
+    n = sh[0]
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    M = PB.get_preconditioner(A, "jacobi")
+    g = torch.Generator().manual_seed(5)
+    B = torch.randn(n, K, generator=g, dtype=torch.float64).to(dev)
+    nnz = A.csr.nnz
+
+    def once():
+        PB.batched_pcg_solve(A, B, atol=0.0, rtol=RTOL, maxiter=10000, preconditioner=M)
+        return PB.last_solve_info()["iterations"]
+
+    for _ in range(args.warmup):
+        once()
+    L.profile_enable(True, 8)
+    ms, its, clk = timed(once, args.steps, dev, local)
+    ka_ms, ka_n = L.profile_read(0)
+    L.profile_enable(False)
+    iters = sum(its)
+    value = iters * K / (ms / 1e3)
+    iter_bytes = nnz * 12 + 4 * (n + 1) + 13 * K * 8 * n
+    peak, _ = peaks()
+    line = base_line(args, "fp64 multi-RHS Jacobi-PCG column-iterations/s (128^3 7-point, 16 RHS)",
+                     value, "column-iterations/s", ms, 1)
+    line["config"] = {"workload": "multi_rhs_cg_poisson3d_7pt", "grid": [m, m, m], "n": n,
+                      "rhs": K, "rtol": RTOL, "iterations_per_solve": iters // args.steps,
+                      "layout": "X, B and work vectors [n][16]; int32 CSR shared by the columns",
+                      "l2": "inputs larger than L2"}
+    line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
+                                  "achieved_gbs": round(iter_bytes * value / K / 1e9, 1),
+                                  "frac": round(iter_bytes * value / K / 1e9 / peak, 4),
+                                  "bytes_formula": "12 nnz + 4 (N+1) + 13 * 16 * 8 N"}
+    line["roofline"] = roofline("mrhs_spmv_kernel", nnz * 12 + 4 * (n + 1) + 5 * K * 8 * n + 8 * n,
+                                ka_ms, ka_n, "mrhs_spmv_kernel@mrhs:128x16")
+    line["clocks"] = clk
+    return line
+
+
 WORKLOADS = {"pcg7": wl_pcg7, "cg2d": wl_cg2d, "spmv": wl_spmv, "batched": wl_batched,
-             "bicgstab": wl_bicgstab}
+             "bicgstab": wl_bicgstab, "mrhs": wl_mrhs}
 
 
 # ------------------------------------------------------------ N GPUs
@@ -642,7 +687,10 @@ def run_reference(args):
     t0 = time.perf_counter()
     its = sum(K.pcg_iterations(Acpu, b, dinv, iterations=per_step) for _ in range(args.steps))
     dt = time.perf_counter() - t0
-    value = its / dt * world  # one 256^3 slab per GPU of the B200 run, processed in turn
+    # The host does every slab of the N-slab system in turn: one global
+    # iteration costs N slab-iterations, so iterations/s x N (the metric of
+    # the B200 arm) equals the one-slab rate measured here.
+    value = its / dt
     line = base_line(args, METRIC, value, "iterations/s", dt * 1e3, world)
     line["impl"] = "reference"
     line["config"] = {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [m * world, m, m],
@@ -663,7 +711,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="pcg7",
-                    choices=["pcg7", "cg2d", "spmv", "batched", "bicgstab", "pcg27"])
+                    choices=["pcg7", "cg2d", "spmv", "batched", "bicgstab", "pcg27", "mrhs"])
     ap.add_argument("--grid", type=int, default=M, help="grid edge per GPU (default 256)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

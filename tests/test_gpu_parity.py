@@ -295,3 +295,19 @@ def test_multi_rhs_cg_guess_and_single_column(dev):
     x1 = T.pytorch_solve(*cu(v, r, c, dev=dev), sh, B[:, :1].to(dev), method="cg", atol=0.0,
                          rtol=1e-10, preconditioner="jacobi")
     assert x1.shape == (sh[0], 1) and rel(x1[:, 0], Xo[:, 0]) < 1e-8
+
+
+# ------------------------------------------------------------------- fp32
+def test_pcg_fp32_matches_oracle(dev):
+    """fp32 Jacobi PCG (the fp32 variant of the 3-D 7-point config) against
+    the oracle run in fp32 with the same ops."""
+    v, r, c, sh = P.poisson_3d_7pt(20)
+    b = P.rhs_normal(sh[0], 1).float()
+    xo, ito, _, _ = K.pcg(v.float(), r, c, sh, b, atol=0.0, rtol=1e-5, precond="jacobi")
+    A = PB.CachedSparseMatrix(*cu(v.float(), r, c, dev=dev), sh)
+    assert A.sell().diagonal_offsets
+    res = PB.pcg_solve_optimized(A, b.to(dev), atol=0.0, rtol=1e-5,
+                                 preconditioner=PB.get_preconditioner(A, "jacobi"))
+    assert res.x.dtype == torch.float32 and res.converged
+    assert iters_close(res.num_iters, ito), (res.num_iters, ito)
+    assert rel(res.x, xo) < 1e-4

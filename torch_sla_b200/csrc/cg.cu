@@ -40,6 +40,28 @@ struct CgState {
 
 enum { kRunning = 0, kConverged = 1, kMaxiter = 2, kNonFinite = 3, kTimeout = 4 };
 
+// Threads per block of the persistent kernel: its two grid barriers per
+// iteration cost more with more blocks, so it runs fewer, larger blocks
+// than the streamed kernels.
+#ifndef SLA_PERSIST_BLOCK
+#define SLA_PERSIST_BLOCK 256
+#endif
+constexpr int kPBlock = SLA_PERSIST_BLOCK;
+constexpr int kPWarps = kPBlock / 32;
+
+template <int NV>
+__device__ __forceinline__ void reduce_partials_bs(double (&v)[NV], const double *parts,
+                                                   double *smem) {
+  const unsigned G = gridDim.x;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) v[k] = 0.0;
+  for (unsigned i = threadIdx.x; i < G; i += kPBlock) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) v[k] += ld_l2(parts + k * G + i);
+  }
+  block_sum<NV, kPBlock>(v, smem);
+}
+
 template <typename T, bool PREC, bool COH>
 struct CgPGather {
   const T *r;
@@ -184,11 +206,11 @@ cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__res
 }
 
 template <typename T, bool PREC, int WS>
-__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
+__global__ void __launch_bounds__(kPBlock, 1024 / kPBlock)
 cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
                      const T *__restrict__ dinv, T *pA, T *pB, T *__restrict__ Ap, CgState *st,
                      double *partA, double *partB) {
-  __shared__ double smem[2 * kWarps];
+  __shared__ double smem[2 * kPWarps];
   if (*(volatile int *)&st->done) return;
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -216,10 +238,10 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
         a1[0] += (double)pn * (double)sum;
       }
     });
-    block_sum<1, kBlock>(a1, smem);
+    block_sum<1, kPBlock>(a1, smem);
     if (threadIdx.x == 0) partA[blockIdx.x] = a1[0];
     if (!grid_sync(&st->bar)) { done = kTimeout; break; }
-    reduce_partials<1>(a1, partA, smem);
+    reduce_partials_bs<1>(a1, partA, smem);
     const T alpha = (T)(rz / a1[0]);
     // phase B: x, r update and the two residual dots
     double a2[2] = {0.0, 0.0};
@@ -232,10 +254,10 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
       a2[0] += (double)ri * (double)ri;
       a2[1] += (double)ri * (double)zi;
     }
-    block_sum<2, kBlock>(a2, smem);
+    block_sum<2, kPBlock>(a2, smem);
     if (threadIdx.x == 0) { partB[blockIdx.x] = a2[0]; partB[gridDim.x + blockIdx.x] = a2[1]; }
     if (!grid_sync(&st->bar)) { done = kTimeout; break; }
-    reduce_partials<2>(a2, partB, smem);
+    reduce_partials_bs<2>(a2, partB, smem);
     rr = a2[0];
     beta = a2[1] / rz;
     rz = a2[1];
@@ -285,8 +307,8 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
   if (flags != SLA_PCG_STREAMED && dev.coop) {
     int per_sm = 0;
     SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, cg_persistent_kernel<T, PREC, WS>, kBlock, 0));
-    int want = (int)((n + kBlock - 1) / kBlock);
+        &per_sm, cg_persistent_kernel<T, PREC, WS>, kPBlock, 0));
+    int want = (int)((n + kPBlock - 1) / kPBlock);
     int cap = per_sm * dev.sm_count;
     coop_grid = want < cap ? want : cap;
     if (coop_grid < 1) coop_grid = 1;
@@ -301,7 +323,7 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
     cudaEvent_t ev;
     profiler().begin(0, 0, s, &ev);
     SLA_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)cg_persistent_kernel<T, PREC, WS>,
-                                             dim3(coop_grid), dim3(kBlock), args, 0, s));
+                                             dim3(coop_grid), dim3(kPBlock), args, 0, s));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     profiler().end(0, s, ev);
   } else {
@@ -397,8 +419,8 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
   if (flags != SLA_PCG_STREAMED && dev.coop) {
     int per_sm = 0;
     SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, cg_persistent_kernel<T, PREC, WS>, kBlock, 0));
-    int want = (int)((n + kBlock - 1) / kBlock);
+        &per_sm, cg_persistent_kernel<T, PREC, WS>, kPBlock, 0));
+    int want = (int)((n + kPBlock - 1) / kPBlock);
     int cap = per_sm * dev.sm_count;
     coop_grid = want < cap ? want : cap;
     if (coop_grid < 1) coop_grid = 1;
@@ -409,7 +431,7 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
     int64_t nn = n;
     void *args[] = {&A, &nn, &x, &r, (void *)&dinv, &pA, &pB, &Ap, &st, &part0, &part1};
     SLA_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)cg_persistent_kernel<T, PREC, WS>,
-                                             dim3(coop_grid), dim3(kBlock), args, 0, s));
+                                             dim3(coop_grid), dim3(kPBlock), args, 0, s));
     g_launches.fetch_add(1, std::memory_order_relaxed);
   } else {
     for (int64_t it = 0; it < maxiter;) {
