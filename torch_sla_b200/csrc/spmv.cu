@@ -25,9 +25,14 @@ template <typename T>
 int spmv_launch(const sla_sell_t *A, const void *x, void *y, cudaStream_t s) {
   Sell<T> a = make_sell<T>(A);
   if (a.n_slices == 0) return SLA_OK;
-  SLA_WS_DISPATCH(width_spec(A),
-                  SLA_LAUNCH((spmv_kernel<T, WS>), grid_for(a.n_slices * 32, kBlock, 4), kBlock, 0,
-                             s, a, (const T *)x, (T *)y));
+  // one wave of resident blocks (fp32 views fit five 256-thread blocks per
+  // SM), never more blocks than warps have slices
+  SLA_WS_DISPATCH(width_spec(A), {
+    const int g = occupancy_grid((const void *)spmv_kernel<T, WS>);
+    const int64_t want = (a.n_slices + kWarps - 1) / kWarps;
+    SLA_LAUNCH((spmv_kernel<T, WS>), want < g ? (int)want : g, kBlock, 0, s, a, (const T *)x,
+               (T *)y);
+  });
   return SLA_OK;
 }
 template int spmv_launch<float>(const sla_sell_t *, const void *, void *, cudaStream_t);
