@@ -27,6 +27,7 @@ struct CgState {
   double rr;
   double pAp;
   double alpha;
+  double alpha_prev;  // alpha of the previous (even) iteration, whose x update is pending
   double beta;
   double tol_sq;
   long long iter;
@@ -142,60 +143,75 @@ template <typename T> struct Pair;
 template <> struct Pair<double> { using type = double2; };
 template <> struct Pair<float> { using type = float2; };
 
-// x += alpha p ; r -= alpha Ap (torch addcmul_ rounding) and the two dots.
+// r -= alpha Ap (torch addcmul_ rounding) and the two dots.
 template <typename T, bool PREC>
-__device__ __forceinline__ void cg_axpy(T &xi, T &ri, T pi, T api, T di, T alpha, double (&acc)[2]) {
-  xi = add_rn(xi, mul_rn(alpha, pi));
+__device__ __forceinline__ void cg_rupd(T &ri, T api, T di, T alpha, double (&acc)[2]) {
   ri = sub_rn(ri, mul_rn(alpha, api));
   T zi = PREC ? mul_rn(di, ri) : ri;
   acc[0] += (double)ri * (double)ri;
   acc[1] += (double)ri * (double)zi;
 }
 
-// VEC: 2 elements per 16-byte (fp64) / 8-byte (fp32) access; only launched
-// when every vector is 16-byte aligned.
-template <typename T, bool PREC, bool VEC>
+// x updates are applied two iterations at a time: at an even iteration the
+// kernel only updates r; at the following odd one it applies
+// x = (x + alpha_prev p_prev) + alpha p -- the same two roundings as two
+// separate x += alpha p steps, so x is bitwise unchanged -- while both
+// search directions still sit in the ping-pong buffers. That saves the x
+// read, the x write and the p read of every other iteration. A solve that
+// stops after an even iteration gets the pending step from cg_xflush_kernel.
+template <typename T, bool PREC, bool VEC, bool XU>
 __global__ void __launch_bounds__(kBlock)
 cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
-                 const T *__restrict__ Ap, const T *__restrict__ dinv, CgState *st,
-                 double *partials) {
+                 const T *__restrict__ p_prev, const T *__restrict__ Ap,
+                 const T *__restrict__ dinv, CgState *st, double *partials) {
   __shared__ double smem[2 * kWarps];
   if (*(volatile int *)&st->done) return;
   const T alpha = (T)st->alpha;
+  const T alpha_prev = (T)st->alpha_prev;
   double acc[2] = {0.0, 0.0};
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  auto xstep = [&](T xi, T pp, T pc) {
+    return add_rn(add_rn(xi, mul_rn(alpha_prev, pp)), mul_rn(alpha, pc));
+  };
   if (VEC) {
     using V = typename Pair<T>::type;
     const int64_t n2 = n >> 1;
     for (int64_t i = tid; i < n2; i += stride) {
-      V xv = ((V *)x)[i], rv = ((V *)r)[i];
-      const V pv = __ldcs((const V *)p + i), av = __ldcs((const V *)Ap + i);
-      V dv = pv;
+      V rv = ((V *)r)[i];
+      const V av = __ldcs((const V *)Ap + i);
+      V dv = av;
       if (PREC) dv = __ldg((const V *)dinv + i);
-      cg_axpy<T, PREC>(xv.x, rv.x, pv.x, av.x, dv.x, alpha, acc);
-      cg_axpy<T, PREC>(xv.y, rv.y, pv.y, av.y, dv.y, alpha, acc);
-      ((V *)x)[i] = xv;
+      if (XU) {
+        V xv = ((V *)x)[i];
+        const V pv = __ldcs((const V *)p + i), qv = __ldcs((const V *)p_prev + i);
+        xv.x = xstep(xv.x, qv.x, pv.x);
+        xv.y = xstep(xv.y, qv.y, pv.y);
+        ((V *)x)[i] = xv;
+      }
+      cg_rupd<T, PREC>(rv.x, av.x, dv.x, alpha, acc);
+      cg_rupd<T, PREC>(rv.y, av.y, dv.y, alpha, acc);
       ((V *)r)[i] = rv;
     }
     if ((n & 1) && tid == 0) {
       const int64_t i = n - 1;
-      T xi = x[i], ri = r[i];
-      cg_axpy<T, PREC>(xi, ri, p[i], Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
-      x[i] = xi;
+      if (XU) x[i] = xstep(x[i], p_prev[i], p[i]);
+      T ri = r[i];
+      cg_rupd<T, PREC>(ri, Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
       r[i] = ri;
     }
   } else {
     for (int64_t i = tid; i < n; i += stride) {
-      T xi = x[i], ri = r[i];
-      cg_axpy<T, PREC>(xi, ri, p[i], Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
-      x[i] = xi;
+      if (XU) x[i] = xstep(x[i], p_prev[i], p[i]);
+      T ri = r[i];
+      cg_rupd<T, PREC>(ri, Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
       r[i] = ri;
     }
   }
   if (last_block_sum<2, kBlock>(acc, partials, &st->counter[2], smem) && threadIdx.x == 0) {
     const long long it = st->iter + 1;
     st->iter = it;
+    st->alpha_prev = st->alpha;
     st->rr = acc[0];
     st->beta = acc[1] / st->rz;
     st->rz = acc[1];
@@ -203,6 +219,18 @@ cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__res
     else if (!isfinite(acc[0])) { st->done = kNonFinite; st->iters_out = st->maxiter; }
     else if (it >= st->maxiter) { st->done = kMaxiter; st->iters_out = st->maxiter; }
   }
+}
+
+// The x step of a last even iteration (st->iter odd), left pending by the
+// deferred update; p_last is that iteration's search direction.
+template <typename T>
+__global__ void __launch_bounds__(kBlock)
+cg_xflush_kernel(int64_t n, T *__restrict__ x, const T *__restrict__ p_last, const CgState *st) {
+  if ((st->iter & 1) == 0 || st->done == kTimeout) return;
+  const T alpha = (T)st->alpha_prev;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) x[i] = add_rn(x[i], mul_rn(alpha, p_last[i]));
 }
 
 template <typename T, bool PREC, int WS>
@@ -273,6 +301,22 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
   }
 }
 
+// K_B of iteration `it`: x is updated at odd iterations only (see
+// cg_update_kernel); p_new / p_old are that iteration's directions.
+template <typename T, bool PREC>
+static int update_launch(bool vec, int64_t it, int64_t n, T *x, T *r, const T *p_new,
+                         const T *p_old, const T *Ap, const T *dinv, CgState *st, double *part,
+                         cudaStream_t s) {
+  auto go = [&](auto fn) -> int {
+    SLA_LAUNCH(fn, occupancy_grid((const void *)fn), kBlock, 0, s, n, x, r, p_new, p_old, Ap, dinv,
+               st, part);
+    return SLA_OK;
+  };
+  const bool odd = (it & 1) != 0;
+  if (vec) return odd ? go(cg_update_kernel<T, PREC, true, true>) : go(cg_update_kernel<T, PREC, true, false>);
+  return odd ? go(cg_update_kernel<T, PREC, false, true>) : go(cg_update_kernel<T, PREC, false, false>);
+}
+
 static size_t cg_ws_bytes(size_t elem, int64_t n) {
   size_t G = (size_t)solver_grid();
   return 4 * align_up(elem * (size_t)n) + 2 * align_up(4 * G * sizeof(double)) +
@@ -329,8 +373,6 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
   } else {
     const int grid_a = occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS>);
     const bool vec = aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv));
-    const int grid_b = vec ? occupancy_grid((const void *)cg_update_kernel<T, PREC, true>)
-                           : occupancy_grid((const void *)cg_update_kernel<T, PREC, false>);
     SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
       T *p_old = (it & 1) ? pB : pA;
       T *p_new = (it & 1) ? pA : pB;
@@ -340,15 +382,12 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
                  st, part0);
       profiler().end(0, s, ev);
       profiler().begin(1, it, s, &ev);
-      if (vec)
-        SLA_LAUNCH((cg_update_kernel<T, PREC, true>), grid_b, kBlock, 0, s, n, x, r, p_new, Ap,
-                   dinv, st, part1);
-      else
-        SLA_LAUNCH((cg_update_kernel<T, PREC, false>), grid_b, kBlock, 0, s, n, x, r, p_new, Ap,
-                   dinv, st, part1);
+      SLA_TRY((update_launch<T, PREC>(vec, it, n, x, r, p_new, p_old, Ap, dinv, st, part1, s)));
       profiler().end(1, s, ev);
       return SLA_OK;
     }));
+    // pending x step of a last even iteration (its direction sits in pB)
+    SLA_LAUNCH(cg_xflush_kernel<T>, grid_for(n), kBlock, 0, s, n, x, pB, st);
   }
   CgState out;
   SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(CgState), cudaMemcpyDeviceToHost, s));
@@ -441,20 +480,15 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
         T *p_new = (it & 1) ? pA : pB;
         SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS>), occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS>),
                    kBlock, 0, s, A, r, dinv, p_old, p_new, Ap, st, part0);
-        if (aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv)))
-          SLA_LAUNCH((cg_update_kernel<T, PREC, true>),
-                     occupancy_grid((const void *)cg_update_kernel<T, PREC, true>), kBlock, 0, s,
-                     n, x, r, p_new, Ap, dinv, st, part1);
-        else
-          SLA_LAUNCH((cg_update_kernel<T, PREC, false>),
-                     occupancy_grid((const void *)cg_update_kernel<T, PREC, false>), kBlock, 0, s,
-                     n, x, r, p_new, Ap, dinv, st, part1);
+        const bool vec = aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv));
+        SLA_TRY((update_launch<T, PREC>(vec, it, n, x, r, p_new, p_old, Ap, dinv, st, part1, s)));
       }
       int done = 0;
       SLA_CUDA_TRY(cudaMemcpyAsync(&done, &st->done, sizeof(int), cudaMemcpyDeviceToHost, s));
       SLA_CUDA_TRY(cudaStreamSynchronize(s));
       if (done) break;
     }
+    SLA_LAUNCH(cg_xflush_kernel<T>, grid_for(n), kBlock, 0, s, n, x, pB, st);
   }
   CgState out;
   SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(CgState), cudaMemcpyDeviceToHost, s));

@@ -245,6 +245,7 @@ struct ShardState {
   int stopped;
   int pad;
   long long iters;
+  long long kb_done;     // CG updates executed (x is updated at odd ones, see shard_cg_update)
   double pap_int;        // interior-rows part of the local (p, Ap)
   double part3[3];       // interior-rows parts of the local (s,s),(t,t),(t,s)
   double alpha_prev, omega_prev;
@@ -360,22 +361,33 @@ shard_cg_spmv(Sell<T> A, int32_t n_own, const T *__restrict__ r, const T *__rest
   }
 }
 
+// x += alpha p is applied two iterations at a time (at odd k:
+// x = (x + alpha_prev p_prev) + alpha p, the same two roundings as two
+// steps) while both directions sit in the ping-pong buffers; a solve whose
+// last update was an even one gets the pending step from shard_cg_xflush.
+template <typename T>
+__device__ __forceinline__ T cg_x2(T xi, T ap, T pp, T a, T pc) {
+  return add_rn(add_rn(xi, mul_rn(ap, pp)), mul_rn(a, pc));
+}
+
 template <typename T, bool PREC>
 __global__ void __launch_bounds__(kBlock)
 shard_cg_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
-                const T *__restrict__ Ap, const T *__restrict__ dinv, ShardState *st, CgRed *R,
-                double *partials, long long k) {
+                const T *__restrict__ p_prev, const T *__restrict__ Ap,
+                const T *__restrict__ dinv, ShardState *st, CgRed *R, double *partials,
+                long long k) {
   __shared__ double smem[2 * kWarps];
   if (*(volatile int *)&st->stopped) return;
-  const T alpha = (T)(cg_rz(R, k) / R->pap[0]);
+  const double alpha_d = cg_rz(R, k) / R->pap[0];
+  const T alpha = (T)alpha_d, alpha_prev = (T)st->alpha_prev;
+  const bool xu = (k & 1) != 0;
   double acc[2] = {0.0, 0.0};
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (; i < n; i += stride) {
     // torch.addcmul(x, alpha, p, value=1) / (r, alpha, Ap, value=-1)
-    T xi = add_rn(x[i], mul_rn(alpha, p[i]));
+    if (xu) x[i] = cg_x2(x[i], alpha_prev, p_prev[i], alpha, p[i]);
     T ri = sub_rn(r[i], mul_rn(alpha, Ap[i]));
-    x[i] = xi;
     r[i] = ri;
     T zi = PREC ? mul_rn(dinv[i], ri) : ri;
     acc[0] += (double)ri * (double)ri;
@@ -384,7 +396,22 @@ shard_cg_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__rest
   if (last_block_sum<2, kBlock>(acc, partials, &st->counter[3], smem) && threadIdx.x == 0) {
     R->loc[k & 1][0] = acc[0];
     R->loc[k & 1][1] = acc[1];
+    st->alpha_prev = alpha_d;
+    st->kb_done = k + 1;
   }
+}
+
+// Pending x step after a last even update (kb_done odd); p_last is its
+// direction.
+template <typename T>
+__global__ void __launch_bounds__(kBlock)
+shard_cg_xflush(int64_t n, T *__restrict__ x, const T *__restrict__ p_last,
+                const ShardState *st) {
+  if ((st->kb_done & 1) == 0) return;
+  const T a = (T)st->alpha_prev;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) x[i] = add_rn(x[i], mul_rn(a, p_last[i]));
 }
 
 // ========================================================== shard BiCGStab
@@ -699,12 +726,13 @@ static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
                hsrc, p_new, Ap, st, R, part[2], (long long)k);
     SLA_NCCL_TRY(ncclAllReduce(R->pap, R->pap, 1, ncclFloat64, ncclSum, cr->nccl, s));
     profiler().begin(1, k, s, &ev);
-    SLA_LAUNCH((shard_cg_update<T, PREC>), gu, kBlock, 0, s, no, x, r, p_new, Ap, dinv, st, R,
-               part[3], (long long)k);
+    SLA_LAUNCH((shard_cg_update<T, PREC>), gu, kBlock, 0, s, no, x, r, p_new, p_old, Ap, dinv, st,
+               R, part[3], (long long)k);
     profiler().end(1, s, ev);
     SLA_NCCL_TRY(ncclAllReduce(R->loc[k & 1], R->loc[k & 1], 2, ncclFloat64, ncclSum, cr->nccl, s));
     return SLA_OK;
   }));
+  SLA_LAUNCH(shard_cg_xflush<T>, grid_for(no), kBlock, 0, s, no, x, pB, st);
   ShardState out;
   CgRed red;
   SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(out), cudaMemcpyDeviceToHost, s));
@@ -1048,18 +1076,20 @@ shard_cg_p2p_spmv(Sell<T> AI, Sell<T> AB, int32_t n_own, const int32_t *__restri
 template <typename T, bool PREC>
 __global__ void __launch_bounds__(kBlock)
 shard_cg_p2p_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
-                    const T *__restrict__ Ap, const T *__restrict__ dinv, ShardState *st,
-                    CgRed *R, double *partials, long long k, P2PDev<T> P) {
+                    const T *__restrict__ p_prev, const T *__restrict__ Ap,
+                    const T *__restrict__ dinv, ShardState *st, CgRed *R, double *partials,
+                    long long k, P2PDev<T> P) {
   __shared__ double smem[2 * kWarps];
   if (*(volatile int *)&st->stopped) return;
-  const T alpha = (T)(cg_rz(R, k) / R->pap[0]);
+  const double alpha_d = cg_rz(R, k) / R->pap[0];
+  const T alpha = (T)alpha_d, alpha_prev = (T)st->alpha_prev;
+  const bool xu = (k & 1) != 0;  // deferred x update, as in shard_cg_update
   double acc[2] = {0.0, 0.0};
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (; i < n; i += stride) {
-    T xi = add_rn(x[i], mul_rn(alpha, p[i]));
+    if (xu) x[i] = cg_x2(x[i], alpha_prev, p_prev[i], alpha, p[i]);
     T ri = sub_rn(r[i], mul_rn(alpha, Ap[i]));
-    x[i] = xi;
     r[i] = ri;
     T zi = PREC ? mul_rn(dinv[i], ri) : ri;
     acc[0] += (double)ri * (double)ri;
@@ -1073,6 +1103,8 @@ shard_cg_p2p_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__
   if (threadIdx.x == 0) {
     R->loc[k & 1][0] = acc[0];
     R->loc[k & 1][1] = acc[1];
+    st->alpha_prev = alpha_d;
+    st->kb_done = k + 1;
   }
 }
 
@@ -1329,11 +1361,12 @@ static int shard_cg_p2p_impl(P2PPlan *pp, const sla_halo_plan_t *plan, const sla
     g_launches.fetch_add(1, std::memory_order_relaxed);
     profiler().end(0, s, e);
     profiler().begin(1, k, s, &e);
-    SLA_LAUNCH((shard_cg_p2p_update<T, PREC>), gu, kBlock, 0, s, no, x, r, p_new, Ap, dinv, st, R,
-               part[3], kk, P);
+    SLA_LAUNCH((shard_cg_p2p_update<T, PREC>), gu, kBlock, 0, s, no, x, r, p_new, p_old, Ap, dinv,
+               st, R, part[3], kk, P);
     profiler().end(1, s, e);
     return SLA_OK;
   }));
+  SLA_LAUNCH(shard_cg_xflush<T>, grid_for(no), kBlock, 0, s, no, x, pB, st);
   ShardState out;
   CgRed red;
   SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(out), cudaMemcpyDeviceToHost, s));
@@ -1692,6 +1725,71 @@ int sla_shard_bicgstab(void *comm_halo, void *comm_reduce, const sla_halo_plan_t
 }
 
 // ----------------------------------------------------------- peer-memory path
+static void p2p_release(P2PPlan *pp) {
+  if (!pp) return;
+  for (int q = 0; q < pp->world; ++q)
+    if (q != pp->me && pp->peer[q]) cudaIpcCloseMemHandle(pp->peer[q]);
+  if (pp->local) cudaFree(pp->local);
+  delete pp;
+}
+
+// Trade the IPC handles over NCCL and agree on the outcome; fills pp->peer
+// and pp->dst_off. Returns a negative status only when the collective
+// itself failed; *all_ok says whether every rank mapped every buffer.
+static int p2p_exchange(P2PPlan *pp, Comm *c, int ok, const cudaIpcMemHandle_t &mine,
+                        int *all_ok) {
+  const int world = pp->world, me = pp->me;
+  const size_t hs = sizeof(cudaIpcMemHandle_t);
+  cudaStream_t s = c->side;
+  unsigned char *dbuf = nullptr;  // handles of all ranks + agreement flag
+  cudaEvent_t ev = nullptr;
+  int rc = SLA_OK;
+  std::vector<cudaIpcMemHandle_t> all(world);
+  auto done = [&](int r) {
+    if (ev) cudaEventDestroy(ev);
+    if (dbuf) cudaFree(dbuf);
+    return r;
+  };
+  if (cudaMalloc((void **)&dbuf, hs * world + 16) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess)
+    return done(SLA_ERR_CUDA);
+  int *flag = (int *)(dbuf + hs * world);
+  if (cudaMemcpy(dbuf + hs * me, &mine, hs, cudaMemcpyHostToDevice) != cudaSuccess)
+    return done(SLA_ERR_CUDA);
+  if (ncclAllGather(dbuf + hs * me, dbuf, hs, ncclUint8, c->nccl, s) != ncclSuccess)
+    return done(SLA_ERR_NCCL);
+  if (cudaEventRecord(ev, s) != cudaSuccess) return done(SLA_ERR_CUDA);
+  if ((rc = wait_bounded(ev, c)) != SLA_OK) return done(rc);
+  if (cudaMemcpy(all.data(), dbuf, hs * world, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return done(SLA_ERR_CUDA);
+  pp->peer[me] = pp->local;
+  for (int q = 0; q < world && ok; ++q) {
+    if (q == me) continue;
+    void *ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) ok = 0;
+    else pp->peer[q] = (char *)ptr;
+  }
+  // where this rank's values go in each neighbour's halo
+  for (int i = 0; i < pp->n_nb && ok; ++i) {
+    long long off = -1;
+    const int q = pp->nb_rank[i];
+    if (cudaMemcpy(&off, pp->peer[q] + offsetof(P2PHeader, recv_off) + sizeof(long long) * me,
+                   sizeof(off), cudaMemcpyDeviceToHost) != cudaSuccess || off < 0)
+      ok = 0;
+    pp->dst_off[i] = off;
+  }
+  cudaGetLastError();  // a refused mapping is an answer, not a sticky error
+  if (cudaMemcpy(flag, &ok, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+    return done(SLA_ERR_CUDA);
+  if (ncclAllReduce(flag, flag, 1, ncclInt32, ncclMin, c->nccl, s) != ncclSuccess)
+    return done(SLA_ERR_NCCL);
+  if (cudaEventRecord(ev, s) != cudaSuccess) return done(SLA_ERR_CUDA);
+  if ((rc = wait_bounded(ev, c)) != SLA_OK) return done(rc);
+  if (cudaMemcpy(all_ok, flag, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return done(SLA_ERR_CUDA);
+  return done(SLA_OK);
+}
+
 int sla_p2p_create(void *comm, const sla_halo_plan_t *plan, int dtype, void **p2p_out) {
   if (!p2p_out) return SLA_ERR_INVALID;
   *p2p_out = nullptr;
@@ -1710,8 +1808,6 @@ int sla_p2p_create(void *comm, const sla_halo_plan_t *plan, int dtype, void **p2
   pp->elem = dtype == SLA_F64 ? 8 : 4;
   int ok = plan->halo_src == nullptr && plan->n_neighbors < kP2PMaxRanks ? 1 : 0;
   const size_t bytes = p2p_halo_offset() + align_up(pp->elem * (size_t)(plan->n_halo + 1));
-  cudaStream_t s = c->side;
-  unsigned char *dbuf = nullptr;  // handles of all ranks + agreement flag
   cudaIpcMemHandle_t mine{};
   if (ok && cudaMalloc((void **)&pp->local, bytes) != cudaSuccess) ok = 0;
   if (ok) {
@@ -1722,61 +1818,19 @@ int sla_p2p_create(void *comm, const sla_halo_plan_t *plan, int dtype, void **p2
       pp->nb_rank[i] = plan->neighbor_rank[i];
       pp->send_off[i] = plan->send_offset[i];
     }
-    pp->send_off[plan->n_neighbors] = plan->n_neighbors > 0 ? plan->send_offset[plan->n_neighbors] : 0;
+    pp->send_off[plan->n_neighbors] =
+        plan->n_neighbors > 0 ? plan->send_offset[plan->n_neighbors] : 0;
     if (cudaMemset(pp->local, 0, bytes) != cudaSuccess ||
         cudaMemcpy(pp->local, &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaIpcGetMemHandle(&mine, pp->local) != cudaSuccess)
       ok = 0;
   }
   cudaGetLastError();
-  const size_t hs = sizeof(cudaIpcMemHandle_t);
-  SLA_CUDA_TRY(cudaMalloc((void **)&dbuf, hs * world + 16));
-  int *flag = (int *)(dbuf + hs * world);
-  SLA_CUDA_TRY(cudaMemcpy(dbuf + hs * me, &mine, hs, cudaMemcpyHostToDevice));
-  SLA_NCCL_TRY(ncclAllGather(dbuf + hs * me, dbuf, hs, ncclUint8, c->nccl, s));
-  std::vector<cudaIpcMemHandle_t> all(world);
-  cudaEvent_t ev;
-  SLA_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-  SLA_CUDA_TRY(cudaEventRecord(ev, s));
-  int w = wait_bounded(ev, c);
-  if (w != SLA_OK) { cudaEventDestroy(ev); return w; }
-  SLA_CUDA_TRY(cudaMemcpy(all.data(), dbuf, hs * world, cudaMemcpyDeviceToHost));
-  pp->peer[me] = pp->local;
-  for (int q = 0; q < world && ok; ++q) {
-    if (q == me) continue;
-    void *ptr = nullptr;
-    if (cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-      ok = 0;
-      cudaGetLastError();
-    } else {
-      pp->peer[q] = (char *)ptr;
-    }
-  }
-  // where my values go in each neighbour's halo
-  for (int i = 0; i < pp->n_nb && ok; ++i) {
-    long long off = -1;
-    const int q = pp->nb_rank[i];
-    if (cudaMemcpy(&off, pp->peer[q] + offsetof(P2PHeader, recv_off) + sizeof(long long) * me,
-                   sizeof(off), cudaMemcpyDeviceToHost) != cudaSuccess || off < 0)
-      ok = 0;
-    pp->dst_off[i] = off;
-  }
-  cudaGetLastError();
-  SLA_CUDA_TRY(cudaMemcpy(flag, &ok, sizeof(int), cudaMemcpyHostToDevice));
-  SLA_NCCL_TRY(ncclAllReduce(flag, flag, 1, ncclInt32, ncclMin, c->nccl, s));
-  SLA_CUDA_TRY(cudaEventRecord(ev, s));
-  w = wait_bounded(ev, c);
-  cudaEventDestroy(ev);
-  if (w != SLA_OK) return w;
   int all_ok = 0;
-  SLA_CUDA_TRY(cudaMemcpy(&all_ok, flag, sizeof(int), cudaMemcpyDeviceToHost));
-  cudaFree(dbuf);
-  if (!all_ok) {
-    for (int q = 0; q < world; ++q)
-      if (q != me && pp->peer[q]) cudaIpcCloseMemHandle(pp->peer[q]);
-    if (pp->local) cudaFree(pp->local);
-    delete pp;
-    return SLA_OK;  // *p2p_out stays NULL: the NCCL path serves
+  const int rc = p2p_exchange(pp, c, ok, mine, &all_ok);
+  if (rc != SLA_OK || !all_ok) {
+    p2p_release(pp);
+    return rc;  // SLA_OK with *p2p_out NULL: the NCCL path serves
   }
   pp->barrier = (int *)(pp->local + offsetof(P2PHeader, pad));
   if (const char *w = getenv("TORCH_SLA_B200_P2P_WAIT_S")) {
@@ -1809,10 +1863,7 @@ int sla_p2p_destroy(void *p2p) {
     }
   }
   cudaDeviceSynchronize();
-  for (int q = 0; q < pp->world; ++q)
-    if (q != pp->me && pp->peer[q]) cudaIpcCloseMemHandle(pp->peer[q]);
-  if (pp->local) cudaFree(pp->local);
-  delete pp;
+  p2p_release(pp);
   return rc;
 }
 
