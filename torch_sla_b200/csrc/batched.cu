@@ -23,7 +23,7 @@ struct BatchState {
 
 // Device arrays of per-member scalars live next to the state.
 struct BatchScalars {
-  double *rz, *alpha, *beta, *tol, *rr;
+  double *rz, *alpha, *beta, *tol, *rr, *alpha_prev;
 };
 
 template <typename T>
@@ -122,39 +122,53 @@ batch_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict_
   }
 }
 
-// K_B: x += alpha p, r -= alpha Ap, per-member (r, r) and (r, D^-1 r); the
-// last block forms beta and the all-members stop test.
+// K_B: r -= alpha Ap, per-member (r, r) and (r, D^-1 r); the last block
+// forms beta and the all-members stop test. x is updated at odd iterations
+// only, x = (x + alpha_prev p_prev) + alpha p (the same two roundings as two
+// single steps) while both directions sit in the ping-pong buffers;
+// batch_xflush_kernel applies a step left pending at the end.
 template <typename T, int VEC>
 __global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
 batch_update_kernel(int64_t n, int B, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
-                    const T *__restrict__ Ap, const T *__restrict__ dinv, BatchState *st,
-                    BatchScalars sc, double *partials) {
+                    const T *__restrict__ p_prev, const T *__restrict__ Ap,
+                    const T *__restrict__ dinv, BatchState *st, BatchScalars sc,
+                    double *partials, int xu) {
   extern __shared__ double smem[];
   __shared__ int s_all;
   if (*(volatile int *)&st->done) return;
   const BatchLane ln(B, VEC);
-  T alpha[VEC];
+  T alpha[VEC], alpha_prev[VEC];
 #pragma unroll
-  for (int u = 0; u < VEC; ++u) alpha[u] = (T)sc.alpha[ln.m0 + u];
+  for (int u = 0; u < VEC; ++u) {
+    alpha[u] = (T)sc.alpha[ln.m0 + u];
+    alpha_prev[u] = (T)sc.alpha_prev[ln.m0 + u];
+  }
   double acc[2][VEC];
 #pragma unroll
   for (int u = 0; u < VEC; ++u) acc[0][u] = acc[1][u] = 0.0;
   for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
        row += (int64_t)gridDim.x * ln.rpb) {
     const int64_t o = row * B + ln.m0;
-    Pack<T, VEC> xv = vload<T, VEC>(x + o), rv = vload<T, VEC>(r + o);
-    const Pack<T, VEC> pv = vload<T, VEC, kLoadStream>(p + o);
+    Pack<T, VEC> rv = vload<T, VEC>(r + o);
     const Pack<T, VEC> av = vload<T, VEC, kLoadStream>(Ap + o);
     const Pack<T, VEC> dv = vload<T, VEC, kLoadRO>(dinv + o);
+    if (xu) {
+      Pack<T, VEC> xv = vload<T, VEC>(x + o);
+      const Pack<T, VEC> pv = vload<T, VEC, kLoadStream>(p + o);
+      const Pack<T, VEC> qv = vload<T, VEC, kLoadStream>(p_prev + o);
+#pragma unroll
+      for (int u = 0; u < VEC; ++u)
+        xv.v[u] = add_rn(add_rn(xv.v[u], mul_rn(alpha_prev[u], qv.v[u])),
+                         mul_rn(alpha[u], pv.v[u]));
+      vstore(x + o, xv);
+    }
 #pragma unroll
     for (int u = 0; u < VEC; ++u) {
-      xv.v[u] = add_rn(xv.v[u], mul_rn(alpha[u], pv.v[u]));
       rv.v[u] = sub_rn(rv.v[u], mul_rn(alpha[u], av.v[u]));
       const T zi = mul_rn(dv.v[u], rv.v[u]);
       acc[0][u] += (double)rv.v[u] * (double)rv.v[u];
       acc[1][u] += (double)rv.v[u] * (double)zi;
     }
-    vstore(x + o, xv);
     vstore(r + o, rv);
   }
   if (!batch_reduce<2, VEC>(acc, B, smem, partials, &st->counter[2])) return;
@@ -167,6 +181,7 @@ batch_update_kernel(int64_t n, int B, T *__restrict__ x, T *__restrict__ r, cons
     const double rz_old = sc.rz[m];
     sc.beta[m] = rz / (fabs(rz_old) > 0.0 ? rz_old : 1e-30);
     sc.rz[m] = rz;
+    sc.alpha_prev[m] = sc.alpha[m];
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -175,6 +190,18 @@ batch_update_kernel(int64_t n, int B, T *__restrict__ x, T *__restrict__ r, cons
     if (s_all) { st->done = 1; st->iters_out = it; }
     else if (it >= st->maxiter) { st->done = 2; st->iters_out = st->maxiter; }
   }
+}
+
+// Pending x step after a last even iteration (st->iter odd).
+template <typename T>
+__global__ void batch_xflush_kernel(int64_t n, int B, T *__restrict__ x,
+                                    const T *__restrict__ p_last, const BatchState *st,
+                                    BatchScalars sc) {
+  if ((st->iter & 1) == 0) return;
+  int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; t < n * B; t += stride)
+    x[t] = add_rn(x[t], mul_rn((T)sc.alpha_prev[t % B], p_last[t]));
 }
 
 template <typename T>
@@ -190,7 +217,7 @@ __global__ void batch_unpack_kernel(int64_t n, int B, const T *__restrict__ xi, 
 static size_t batch_ws_bytes(size_t elem, int64_t n, int64_t B) {
   return 6 * align_up(elem * (size_t)(n * B)) +
          3 * align_up(2 * (size_t)B * batch_max_grid() * sizeof(double)) +
-         5 * align_up((size_t)B * sizeof(double)) + align_up(sizeof(BatchState));
+         6 * align_up((size_t)B * sizeof(double)) + align_up(sizeof(BatchState));
 }
 
 // Row load batch of the vectorised SpMV: one dependent round trip covers a
@@ -214,7 +241,8 @@ static int batched_loop(const int32_t *rowptr, const int32_t *colind, const T *v
                sc, part[1]);
     profiler().end(0, s, ev);
     profiler().begin(1, it, s, &ev);
-    SLA_LAUNCH(upd, G2, TB, sm2, s, n, B, xi, r, p_new, Ap, dinv, st, sc, part[2]);
+    SLA_LAUNCH(upd, G2, TB, sm2, s, n, B, xi, r, p_new, p_old, Ap, dinv, st, sc, part[2],
+               (int)(it & 1));
     profiler().end(1, s, ev);
     return SLA_OK;
   });
@@ -232,7 +260,7 @@ static int batched_impl(const int32_t *rowptr, const int32_t *colind, const T *v
   for (int k = 0; k < 3; ++k) part[k] = c.take<double>(2 * (size_t)B * batch_max_grid());
   BatchScalars sc;
   sc.rz = c.take<double>(B); sc.alpha = c.take<double>(B); sc.beta = c.take<double>(B);
-  sc.tol = c.take<double>(B); sc.rr = c.take<double>(B);
+  sc.tol = c.take<double>(B); sc.rr = c.take<double>(B); sc.alpha_prev = c.take<double>(B);
   BatchState *st = c.take<BatchState>(1);
   if (!c.ok) return SLA_ERR_WORKSPACE;
   BatchState init{};
@@ -256,6 +284,8 @@ static int batched_impl(const int32_t *rowptr, const int32_t *colind, const T *v
     rc = batched_loop<T, 1>(rowptr, colind, vals, n, B, xi, r, pA, pB, Ap, dinv, st, sc, part,
                             maxiter, s);
   SLA_TRY(rc);
+  // a last even iteration's direction sits in pB
+  SLA_LAUNCH(batch_xflush_kernel<T>, grid_for(n * B), kBlock, 0, s, n, B, xi, pB, st, sc);
   SLA_LAUNCH(batch_unpack_kernel<T>, grid_for(n * B), kBlock, 0, s, n, B, xi, x);
   BatchState out;
   SLA_CUDA_TRY(cudaMemcpyAsync(&out, st, sizeof(BatchState), cudaMemcpyDeviceToHost, s));

@@ -22,7 +22,7 @@ struct MrhsState {
 };
 
 struct MrhsCols {
-  double *rz, *alpha, *beta, *tol_sq, *rr;
+  double *rz, *alpha, *beta, *tol_sq, *rr, *alpha_prev;
   long long *iters;   // per column, 0 until converged
   int *conv;          // per column convergence flag
 };
@@ -140,37 +140,51 @@ mrhs_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__
   }
 }
 
+// X is updated at odd iterations only, X = (X + alpha_prev P_prev) + alpha P
+// (the same two roundings as two single steps), while both directions sit
+// in the ping-pong buffers; mrhs_xflush_kernel applies a step left pending.
 template <typename T, bool PREC, int VEC>
 __global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
 mrhs_update_kernel(int64_t n, int K, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
-                   const T *__restrict__ Ap, const T *__restrict__ dinv, MrhsState *st,
-                   MrhsCols cs, double *partials) {
+                   const T *__restrict__ p_prev, const T *__restrict__ Ap,
+                   const T *__restrict__ dinv, MrhsState *st, MrhsCols cs, double *partials,
+                   int xu) {
   extern __shared__ double smem[];
   __shared__ int s_all;
   if (*(volatile int *)&st->done) return;
   const BatchLane ln(K, VEC);
-  T alpha[VEC];
+  T alpha[VEC], alpha_prev[VEC];
 #pragma unroll
-  for (int u = 0; u < VEC; ++u) alpha[u] = (T)cs.alpha[ln.m0 + u];
+  for (int u = 0; u < VEC; ++u) {
+    alpha[u] = (T)cs.alpha[ln.m0 + u];
+    alpha_prev[u] = (T)cs.alpha_prev[ln.m0 + u];
+  }
   double acc[2][VEC];
 #pragma unroll
   for (int u = 0; u < VEC; ++u) acc[0][u] = acc[1][u] = 0.0;
   for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
        row += (int64_t)gridDim.x * ln.rpb) {
     const int64_t o = row * K + ln.m0;
-    Pack<T, VEC> xv = vload<T, VEC>(x + o), rv = vload<T, VEC>(r + o);
-    const Pack<T, VEC> pv = vload<T, VEC, kLoadStream>(p + o);
+    Pack<T, VEC> rv = vload<T, VEC>(r + o);
     const Pack<T, VEC> av = vload<T, VEC, kLoadStream>(Ap + o);
     const T d = PREC ? __ldg(dinv + row) : T(1);
+    if (xu) {
+      Pack<T, VEC> xv = vload<T, VEC>(x + o);
+      const Pack<T, VEC> pv = vload<T, VEC, kLoadStream>(p + o);
+      const Pack<T, VEC> qv = vload<T, VEC, kLoadStream>(p_prev + o);
+#pragma unroll
+      for (int u = 0; u < VEC; ++u)
+        xv.v[u] = add_rn(add_rn(xv.v[u], mul_rn(alpha_prev[u], qv.v[u])),
+                         mul_rn(alpha[u], pv.v[u]));
+      vstore(x + o, xv);
+    }
 #pragma unroll
     for (int u = 0; u < VEC; ++u) {
-      xv.v[u] = add_rn(xv.v[u], mul_rn(alpha[u], pv.v[u]));
       rv.v[u] = sub_rn(rv.v[u], mul_rn(alpha[u], av.v[u]));
       const T zi = PREC ? mul_rn(d, rv.v[u]) : rv.v[u];
       acc[0][u] += (double)rv.v[u] * (double)rv.v[u];
       acc[1][u] += (double)rv.v[u] * (double)zi;
     }
-    vstore(x + o, xv);
     vstore(r + o, rv);
   }
   if (!batch_reduce<2, VEC>(acc, K, smem, partials, &st->counter[2])) return;
@@ -189,6 +203,7 @@ mrhs_update_kernel(int64_t n, int K, T *__restrict__ x, T *__restrict__ r, const
     const double rz_old = cs.rz[c];
     cs.beta[c] = rz / (rz_old + 1e-30);
     cs.rz[c] = rz;
+    cs.alpha_prev[c] = cs.alpha[c];
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -198,10 +213,22 @@ mrhs_update_kernel(int64_t n, int K, T *__restrict__ x, T *__restrict__ r, const
   }
 }
 
+// Pending X step after a last even iteration (st->iter odd).
+template <typename T>
+__global__ void mrhs_xflush_kernel(int64_t n, int K, T *__restrict__ x,
+                                   const T *__restrict__ p_last, const MrhsState *st,
+                                   MrhsCols cs) {
+  if ((st->iter & 1) == 0) return;
+  int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; t < n * K; t += stride)
+    x[t] = add_rn(x[t], mul_rn((T)cs.alpha_prev[t % K], p_last[t]));
+}
+
 static size_t mrhs_ws_bytes(size_t elem, int64_t n, int64_t K) {
   return 4 * align_up(elem * (size_t)(n * K)) +
          3 * align_up(2 * (size_t)K * batch_max_grid() * sizeof(double)) +
-         5 * align_up((size_t)K * sizeof(double)) + align_up((size_t)K * sizeof(long long)) +
+         6 * align_up((size_t)K * sizeof(double)) + align_up((size_t)K * sizeof(long long)) +
          align_up((size_t)K * sizeof(int)) + align_up(sizeof(MrhsState));
 }
 
@@ -223,7 +250,8 @@ static int mrhs_loop(const int32_t *rowptr, const int32_t *colind, const T *vals
     SLA_LAUNCH(spmv, G1, TB, sm1, s, rowptr, colind, vals, n, K, r, dinv, p_old, p_new, Ap, st,
                cs, part[1]);
     profiler().end(0, s, ev);
-    SLA_LAUNCH(upd, G2, TB, sm2, s, n, K, x, r, p_new, Ap, dinv, st, cs, part[2]);
+    SLA_LAUNCH(upd, G2, TB, sm2, s, n, K, x, r, p_new, p_old, Ap, dinv, st, cs, part[2],
+               (int)(it & 1));
     return SLA_OK;
   });
 }
@@ -240,7 +268,7 @@ static int mrhs_impl(const int32_t *rowptr, const int32_t *colind, const T *vals
   for (int q = 0; q < 3; ++q) part[q] = c.take<double>(2 * (size_t)K * batch_max_grid());
   MrhsCols cs;
   cs.rz = c.take<double>(K); cs.alpha = c.take<double>(K); cs.beta = c.take<double>(K);
-  cs.tol_sq = c.take<double>(K); cs.rr = c.take<double>(K);
+  cs.tol_sq = c.take<double>(K); cs.rr = c.take<double>(K); cs.alpha_prev = c.take<double>(K);
   cs.iters = c.take<long long>(K);
   cs.conv = c.take<int>(K);
   MrhsState *st = c.take<MrhsState>(1);
@@ -268,6 +296,8 @@ static int mrhs_impl(const int32_t *rowptr, const int32_t *colind, const T *vals
     rc = mrhs_loop<T, PREC, 1>(rowptr, colind, vals, n, K, dinv, x, r, pA, pB, Ap, st, cs, part,
                                maxiter, s);
   SLA_TRY(rc);
+  // a last even iteration's direction sits in pB
+  SLA_LAUNCH(mrhs_xflush_kernel<T>, grid_for((int64_t)nk), kBlock, 0, s, n, K, x, pB, st, cs);
   MrhsState out;
   std::vector<double> rr(K), tol_sq(K);
   std::vector<long long> its(K);
