@@ -92,9 +92,10 @@ def find_halo_nodes(row: torch.Tensor, col: torch.Tensor, partition_ids: torch.T
 
 def _assemble(pid: int, owned: torch.Tensor, halo: torch.Tensor, send_map: Dict[int, torch.Tensor],
               num_nodes: int, owner_of) -> Partition:
+    dev = owned.device
     local = torch.cat([owned, halo])
-    g2l = torch.full((num_nodes,), -1, dtype=torch.int64)
-    g2l[local] = torch.arange(local.numel(), dtype=torch.int64)
+    g2l = torch.full((num_nodes,), -1, dtype=torch.int64, device=dev)
+    g2l[local] = torch.arange(local.numel(), dtype=torch.int64, device=dev)
     halo_owner = owner_of(halo)
     recv: Dict[int, torch.Tensor] = {}
     for q in send_map:
@@ -122,12 +123,14 @@ def build_partition_from_rows(row_g: torch.Tensor, col_g: torch.Tensor, lo: int,
     """build_partition for a 'simple' partition from the owned rows [lo, hi)
     only (their COO entries in global ids). Requires a structurally symmetric
     pattern, for which the entries with an owned column and an off-rank row
-    mirror the owned-row entries."""
+    mirror the owned-row entries. Runs on the device of the entries (the
+    O(nnz) masks and sorts of a large shard stay on the GPU); the maps come
+    back on that device."""
     per = (num_nodes + num_parts - 1) // num_parts
     owner = lambda g: torch.clamp(g // per, max=num_parts - 1)  # noqa: E731
-    row_g = row_g.to(torch.int64).cpu()
-    col_g = col_g.to(torch.int64).cpu()
-    owned = torch.arange(lo, hi, dtype=torch.int64)
+    row_g = row_g.to(torch.int64)
+    col_g = col_g.to(device=row_g.device, dtype=torch.int64)
+    owned = torch.arange(lo, hi, dtype=torch.int64, device=row_g.device)
     off = (col_g < lo) | (col_g >= hi)
     halo_pts = col_g[off]
     mine = row_g[off]
