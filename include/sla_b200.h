@@ -253,6 +253,17 @@ int sla_multi_rhs_cg(int dtype, const int32_t *rowptr, const int32_t *colind,
                      int64_t *iters_out, int32_t *converged_out,
                      void *workspace, size_t workspace_bytes,
                      sla_solve_info_t *info, sla_stream_t stream);
+/* The same solve with the matrix given as a diagonal-offset SELL view
+ * (n_diags 5, 7 or 27, square, no row ids): no column or row-pointer loads
+ * in the SpMV. Same results as sla_multi_rhs_cg on the same matrix up to
+ * the sign of zero sums. */
+int sla_multi_rhs_cg_diag(int dtype, const sla_sell_t *A, int64_t k,
+                          const void *dinv, const void *b, void *x,
+                          int x_is_guess, double atol, double rtol,
+                          int64_t maxiter, int64_t check_every,
+                          int64_t *iters_out, int32_t *converged_out,
+                          void *workspace, size_t workspace_bytes,
+                          sla_solve_info_t *info, sla_stream_t stream);
 
 /* -------------------------------------------------- row-sharded (NCCL) */
 /* Opaque NCCL communicator management (one process per GPU). */

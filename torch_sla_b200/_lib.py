@@ -96,6 +96,9 @@ _SIGNATURES = {
     "sla_multi_rhs_cg": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_ptr,
                                         c_ptr, c_ptr, ctypes.c_int, c_dbl, c_dbl, c_i64, c_i64,
                                         c_ptr, c_ptr, c_ptr, c_sz, _P(SolveInfo), c_ptr]),
+    "sla_multi_rhs_cg_diag": (ctypes.c_int, [ctypes.c_int, _P(SellView), c_i64, c_ptr, c_ptr,
+                                             c_ptr, ctypes.c_int, c_dbl, c_dbl, c_i64, c_i64,
+                                             c_ptr, c_ptr, c_ptr, c_sz, _P(SolveInfo), c_ptr]),
     "sla_comm_unique_id": (ctypes.c_int, [c_ptr]),
     "sla_comm_init": (ctypes.c_int, [_P(c_ptr), ctypes.c_int, c_ptr, ctypes.c_int]),
     "sla_comm_destroy": (ctypes.c_int, [c_ptr]),

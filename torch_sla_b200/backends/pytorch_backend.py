@@ -291,13 +291,19 @@ def batched_pcg_solve(A: CachedSparseMatrix, B: Tensor, X0: Optional[Tensor] = N
         L.check("sla_multi_rhs_cg_workspace",
                 lib.sla_multi_rhs_cg_workspace(A.csr.code, n, kk, ctypes.byref(need)))
         ws = L.workspace(need.value, A.device)
-        st = lib.sla_multi_rhs_cg(A.csr.code, L.ptr(A.csr.rowptr), L.ptr(A.csr.colind),
-                                  L.ptr(A.csr.vals), n, kk, L.ptr(dinv), L.ptr(Bk), L.ptr(Xk),
-                                  int(guess), float(atol), float(rtol), int(maxiter),
-                                  int(check_interval), iters[k0:k1].data_ptr(),
-                                  conv[k0:k1].data_ptr(), L.ptr(ws), ws.numel(),
-                                  ctypes.byref(info), L.stream_handle(A.device))
-        L.check("sla_multi_rhs_cg", st)
+        tail = (L.ptr(dinv), L.ptr(Bk), L.ptr(Xk), int(guess), float(atol), float(rtol),
+                int(maxiter), int(check_interval), iters[k0:k1].data_ptr(),
+                conv[k0:k1].data_ptr(), L.ptr(ws), ws.numel(), ctypes.byref(info),
+                L.stream_handle(A.device))
+        sell = A.sell()
+        if sell.diagonal_offsets and sell.row_ids is None and sell.row_base == 0:
+            fn = "sla_multi_rhs_cg_diag"  # stencil matrix: columns computed, not loaded
+            st = lib.sla_multi_rhs_cg_diag(A.csr.code, sell.ref(), kk, *tail)
+        else:
+            fn = "sla_multi_rhs_cg"
+            st = lib.sla_multi_rhs_cg(A.csr.code, L.ptr(A.csr.rowptr), L.ptr(A.csr.colind),
+                                      L.ptr(A.csr.vals), n, kk, *tail)
+        L.check(fn, st)
         if kk != K:
             X[:, k0:k1].copy_(Xk)
     _record("multi_rhs_cg", info)

@@ -27,10 +27,72 @@ struct MrhsCols {
   int *conv;          // per column convergence flag
 };
 
-template <typename T, bool PREC>
+// Row access of the multi-RHS kernels: int32 CSR, or a diagonal-offset SELL
+// view of a stencil matrix (column = row + offset: no column or row-pointer
+// loads, so every load of a row is independent of the others).
+template <typename T>
+struct CsrRows {
+  const int32_t *rowptr, *colind;
+  const T *vals;
+  template <int VEC, int RB, typename G>
+  __device__ __forceinline__ void sum(int64_t row, const G &g, T (&s)[VEC]) const {
+    csr_row_vec<T, VEC, RB>(
+        colind, __ldg(rowptr + row), __ldg(rowptr + row + 1),
+        [&](int32_t k) { return splat<T, VEC>(__ldg(vals + k)); }, g, s);
+  }
+  template <typename G>
+  __device__ __forceinline__ T sum1(int64_t row, const G &g) const {
+    T ax = T(0);
+    for (int32_t k = rowptr[row]; k < rowptr[row + 1]; ++k) ax = fma(vals[k], g(colind[k]), ax);
+    return ax;
+  }
+};
+
+template <typename T, int W>
+struct DiagRows {
+  Sell<T> A;
+  template <int VEC, int RB, typename G>
+  __device__ __forceinline__ void sum(int64_t row, const G &g, T (&s)[VEC]) const {
+#pragma unroll
+    for (int u = 0; u < VEC; ++u) s[u] = T(0);
+    const T *__restrict__ vp = A.val + (row >> 5) * 32 * W + (row & 31);
+#pragma unroll
+    for (int j0 = 0; j0 < W; j0 += RB) {
+      T v[RB];
+      Pack<T, VEC> x[RB];
+#pragma unroll
+      for (int q = 0; q < RB; ++q) {
+        v[q] = T(0);
+        x[q] = splat<T, VEC>(T(0));
+        if (j0 + q < W) {
+          const int64_t c = row + A.off[j0 + q];
+          v[q] = __ldg(vp + 32 * (j0 + q));
+          if (c >= 0 && c < A.n_cols) x[q] = g((int32_t)c);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < RB; ++q) {
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) s[u] = fma(v[q], x[q].v[u], s[u]);
+      }
+    }
+  }
+  template <typename G>
+  __device__ __forceinline__ T sum1(int64_t row, const G &g) const {
+    T ax = T(0);
+    const T *__restrict__ vp = A.val + (row >> 5) * 32 * W + (row & 31);
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      const int64_t c = row + A.off[j];
+      if (c >= 0 && c < A.n_cols) ax = fma(__ldg(vp + 32 * j), g((int32_t)c), ax);
+    }
+    return ax;
+  }
+};
+
+template <typename T, bool PREC, typename M>
 __global__ void __launch_bounds__(1024)
-mrhs_init_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
-                 const T *__restrict__ vals, int64_t n, int K, const T *__restrict__ b,
+mrhs_init_kernel(M mat, int64_t n, int K, const T *__restrict__ b,
                  T *__restrict__ x, int guess, const T *__restrict__ dinv, T *__restrict__ r,
                  T *__restrict__ p_old, MrhsState *st, MrhsCols cs, double *partials,
                  double atol, double rtol) {
@@ -44,9 +106,7 @@ mrhs_init_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__
     T bv = b[o];
     T rv = bv;
     if (guess) {  // R = B - A X0
-      T ax = T(0);
-      for (int32_t k = rowptr[row]; k < rowptr[row + 1]; ++k)
-        ax = fma(vals[k], x[(int64_t)colind[k] * K + bi], ax);
+      const T ax = mat.sum1(row, [&](int32_t c) { return x[(int64_t)c * K + bi]; });
       rv = sub_rn(bv, ax);
     }
     r[o] = rv;
@@ -83,10 +143,9 @@ __global__ void zero_kernel(T *__restrict__ x, int64_t n) {
 
 // P = Z + beta P (pytorch_backend.py:2487) formed inside the gather, AP = A P,
 // per-column (P, AP); the last block forms alpha with (P, AP) <= 0 -> 1.
-template <typename T, bool PREC, int VEC, int RB>
+template <typename T, bool PREC, int VEC, int RB, typename M>
 __global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
-mrhs_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
-                 const T *__restrict__ vals, int64_t n, int K, const T *__restrict__ r,
+mrhs_spmv_kernel(M mat, int64_t n, int K, const T *__restrict__ r,
                  const T *__restrict__ dinv, const T *__restrict__ p_old, T *__restrict__ p_new,
                  T *__restrict__ Ap, MrhsState *st, MrhsCols cs, double *partials) {
   extern __shared__ double smem[];
@@ -101,9 +160,8 @@ mrhs_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__
   for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
        row += (int64_t)gridDim.x * ln.rpb) {
     T sum[VEC];
-    csr_row_vec<T, VEC, RB>(
-        colind, __ldg(rowptr + row), __ldg(rowptr + row + 1),
-        [&](int32_t k) { return splat<T, VEC>(__ldg(vals + k)); },
+    mat.template sum<VEC, RB>(
+        row,
         [&](int32_t ci) {
           const int64_t c = (int64_t)ci * K + ln.m0;
           const Pack<T, VEC> rv = vload<T, VEC, kLoadRO>(r + c);
@@ -233,11 +291,11 @@ static size_t mrhs_ws_bytes(size_t elem, int64_t n, int64_t K) {
 }
 
 
-template <typename T, bool PREC, int VEC>
-static int mrhs_loop(const int32_t *rowptr, const int32_t *colind, const T *vals, int64_t n, int K,
-                     const T *dinv, T *x, T *r, T *pA, T *pB, T *Ap, MrhsState *st, MrhsCols cs,
-                     double *const part[3], int64_t maxiter, cudaStream_t s) {
-  auto spmv = mrhs_spmv_kernel<T, PREC, VEC, kBatchRB>;
+template <typename T, bool PREC, int VEC, typename M>
+static int mrhs_loop(M mat, int64_t n, int K, const T *dinv, T *x, T *r, T *pA, T *pB, T *Ap,
+                     MrhsState *st, MrhsCols cs, double *const part[3], int64_t maxiter,
+                     cudaStream_t s) {
+  auto spmv = mrhs_spmv_kernel<T, PREC, VEC, kBatchRB, M>;
   auto upd = mrhs_update_kernel<T, PREC, VEC>;
   const int TB = batch_block(K, VEC);
   const size_t sm1 = batch_smem(1, TB, VEC), sm2 = batch_smem(2, TB, VEC);
@@ -247,8 +305,7 @@ static int mrhs_loop(const int32_t *rowptr, const int32_t *colind, const T *vals
     T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
     cudaEvent_t ev;
     profiler().begin(0, it, s, &ev);
-    SLA_LAUNCH(spmv, G1, TB, sm1, s, rowptr, colind, vals, n, K, r, dinv, p_old, p_new, Ap, st,
-               cs, part[1]);
+    SLA_LAUNCH(spmv, G1, TB, sm1, s, mat, n, K, r, dinv, p_old, p_new, Ap, st, cs, part[1]);
     profiler().end(0, s, ev);
     SLA_LAUNCH(upd, G2, TB, sm2, s, n, K, x, r, p_new, p_old, Ap, dinv, st, cs, part[2],
                (int)(it & 1));
@@ -256,9 +313,9 @@ static int mrhs_loop(const int32_t *rowptr, const int32_t *colind, const T *vals
   });
 }
 
-template <typename T, bool PREC>
-static int mrhs_impl(const int32_t *rowptr, const int32_t *colind, const T *vals, int64_t n, int K,
-                     const T *dinv, const T *b, T *x, bool guess, double atol, double rtol,
+template <typename T, bool PREC, typename M>
+static int mrhs_impl(M mat, int64_t n, int K, const T *dinv, const T *b, T *x, bool guess,
+                     double atol, double rtol,
                      int64_t maxiter, int64_t every, int64_t *iters_out, int32_t *conv_out,
                      void *ws, size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
   Carver c(ws, ws_bytes);
@@ -278,23 +335,21 @@ static int mrhs_impl(const int32_t *rowptr, const int32_t *colind, const T *vals
   init.check_every = every;
   SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(init), cudaMemcpyHostToDevice, s));
   {
-    auto init_fn = mrhs_init_kernel<T, PREC>;
+    auto init_fn = mrhs_init_kernel<T, PREC, M>;
     const int TB0 = batch_block(K, 1);
     const size_t sm0 = batch_smem(2, TB0, 1);
     const int G0 = occupancy_grid((const void *)init_fn, TB0, sm0);
-    SLA_LAUNCH(init_fn, G0, TB0, sm0, s, rowptr, colind, vals, n, K, b, x, guess ? 1 : 0, dinv, r,
-               pA, st, cs, part[0], atol, rtol);
+    SLA_LAUNCH(init_fn, G0, TB0, sm0, s, mat, n, K, b, x, guess ? 1 : 0, dinv, r, pA, st, cs,
+               part[0], atol, rtol);
   }
   if (!guess) SLA_LAUNCH(zero_kernel<T>, grid_for((int64_t)nk), kBlock, 0, s, x, (int64_t)nk);
   // 16-byte vector groups of columns where K and the caller's x allow it
   constexpr int kVec = 16 / sizeof(T);
   int rc;
   if (K % kVec == 0 && aligned16(x))
-    rc = mrhs_loop<T, PREC, kVec>(rowptr, colind, vals, n, K, dinv, x, r, pA, pB, Ap, st, cs, part,
-                                  maxiter, s);
+    rc = mrhs_loop<T, PREC, kVec>(mat, n, K, dinv, x, r, pA, pB, Ap, st, cs, part, maxiter, s);
   else
-    rc = mrhs_loop<T, PREC, 1>(rowptr, colind, vals, n, K, dinv, x, r, pA, pB, Ap, st, cs, part,
-                               maxiter, s);
+    rc = mrhs_loop<T, PREC, 1>(mat, n, K, dinv, x, r, pA, pB, Ap, st, cs, part, maxiter, s);
   SLA_TRY(rc);
   // a last even iteration's direction sits in pB
   SLA_LAUNCH(mrhs_xflush_kernel<T>, grid_for((int64_t)nk), kBlock, 0, s, n, K, x, pB, st, cs);
@@ -328,6 +383,50 @@ static int mrhs_impl(const int32_t *rowptr, const int32_t *colind, const T *vals
   return info->status;
 }
 
+static int mrhs_args_ok(int dtype, int64_t n, int64_t k, const void *b, void *x,
+                        sla_solve_info_t *info, int64_t check_every, void *workspace,
+                        size_t workspace_bytes) {
+  if (!b || !x || !info || n <= 0 || n >= INT32_MAX) return SLA_ERR_INVALID;
+  if (k < 1 || check_every < 1) return SLA_ERR_INVALID;
+  if (k > 1024) return SLA_ERR_UNSUPPORTED;
+  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
+  size_t need = 0;
+  SLA_TRY(sla_multi_rhs_cg_workspace(dtype, n, k, &need));
+  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  return SLA_OK;
+}
+
+// Dispatch on dtype and preconditioning for one row-access type.
+template <template <typename> class Mk>
+static int mrhs_run(int dtype, Mk<double> md, Mk<float> mf, int64_t n, int K, const void *dinv,
+                    const void *b, void *x, bool g, double atol, double rtol, int64_t maxiter,
+                    int64_t every, int64_t *iters_out, int32_t *conv_out, void *ws,
+                    size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
+  if (dtype == SLA_F64) {
+    if (dinv)
+      return mrhs_impl<double, true>(md, n, K, (const double *)dinv, (const double *)b,
+                                     (double *)x, g, atol, rtol, maxiter, every, iters_out,
+                                     conv_out, ws, ws_bytes, info, s);
+    return mrhs_impl<double, false>(md, n, K, nullptr, (const double *)b, (double *)x, g, atol,
+                                    rtol, maxiter, every, iters_out, conv_out, ws, ws_bytes,
+                                    info, s);
+  }
+  if (dtype == SLA_F32) {
+    if (dinv)
+      return mrhs_impl<float, true>(mf, n, K, (const float *)dinv, (const float *)b, (float *)x,
+                                    g, atol, rtol, maxiter, every, iters_out, conv_out, ws,
+                                    ws_bytes, info, s);
+    return mrhs_impl<float, false>(mf, n, K, nullptr, (const float *)b, (float *)x, g, atol,
+                                   rtol, maxiter, every, iters_out, conv_out, ws, ws_bytes, info,
+                                   s);
+  }
+  return SLA_ERR_INVALID;
+}
+
+template <int W> struct DiagW {
+  template <typename T> using type = DiagRows<T, W>;
+};
+
 }  // namespace sla
 
 using namespace sla;
@@ -347,40 +446,45 @@ int sla_multi_rhs_cg(int dtype, const int32_t *rowptr, const int32_t *colind, co
                      int64_t check_every, int64_t *iters_out, int32_t *converged_out,
                      void *workspace, size_t workspace_bytes, sla_solve_info_t *info,
                      sla_stream_t stream) {
-  if (!rowptr || !colind || !vals || !b || !x || !info || n <= 0 || n >= INT32_MAX)
-    return SLA_ERR_INVALID;
-  if (k < 1 || check_every < 1) return SLA_ERR_INVALID;
-  if (k > 1024) return SLA_ERR_UNSUPPORTED;
-  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
-  size_t need = 0;
-  SLA_TRY(sla_multi_rhs_cg_workspace(dtype, n, k, &need));
-  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  if (!rowptr || !colind || !vals) return SLA_ERR_INVALID;
+  SLA_TRY(mrhs_args_ok(dtype, n, k, b, x, info, check_every, workspace, workspace_bytes));
+  CsrRows<double> md{rowptr, colind, (const double *)vals};
+  CsrRows<float> mf{rowptr, colind, (const float *)vals};
+  return mrhs_run<CsrRows>(dtype, md, mf, n, (int)k, dinv, b, x, x_is_guess != 0, atol, rtol,
+                           maxiter, check_every, iters_out, converged_out, workspace,
+                           workspace_bytes, info, (cudaStream_t)stream);
+}
+
+int sla_multi_rhs_cg_diag(int dtype, const sla_sell_t *A, int64_t k, const void *dinv,
+                          const void *b, void *x, int x_is_guess, double atol, double rtol,
+                          int64_t maxiter, int64_t check_every, int64_t *iters_out,
+                          int32_t *converged_out, void *workspace, size_t workspace_bytes,
+                          sla_solve_info_t *info, sla_stream_t stream) {
+  if (!sell_ok(A) || A->n_diags <= 0 || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  const int64_t n = A->n_slots;
+  if (A->n_cols != n) return SLA_ERR_INVALID;  // square system
+  SLA_TRY(mrhs_args_ok(dtype, n, k, b, x, info, check_every, workspace, workspace_bytes));
   cudaStream_t s = (cudaStream_t)stream;
   const bool g = x_is_guess != 0;
-  const int K = (int)k;
-  if (dtype == SLA_F64) {
-    if (dinv)
-      return mrhs_impl<double, true>(rowptr, colind, (const double *)vals, n, K,
-                                     (const double *)dinv, (const double *)b, (double *)x, g,
-                                     atol, rtol, maxiter, check_every, iters_out, converged_out,
-                                     workspace, workspace_bytes, info, s);
-    return mrhs_impl<double, false>(rowptr, colind, (const double *)vals, n, K, nullptr,
-                                    (const double *)b, (double *)x, g, atol, rtol, maxiter,
-                                    check_every, iters_out, converged_out, workspace,
-                                    workspace_bytes, info, s);
+  switch (A->n_diags) {
+    case 5:
+      return mrhs_run<DiagW<5>::type>(dtype, {make_sell<double>(A)}, {make_sell<float>(A)}, n,
+                                      (int)k, dinv, b, x, g, atol, rtol, maxiter, check_every,
+                                      iters_out, converged_out, workspace, workspace_bytes, info,
+                                      s);
+    case 7:
+      return mrhs_run<DiagW<7>::type>(dtype, {make_sell<double>(A)}, {make_sell<float>(A)}, n,
+                                      (int)k, dinv, b, x, g, atol, rtol, maxiter, check_every,
+                                      iters_out, converged_out, workspace, workspace_bytes, info,
+                                      s);
+    case 27:
+      return mrhs_run<DiagW<27>::type>(dtype, {make_sell<double>(A)}, {make_sell<float>(A)}, n,
+                                       (int)k, dinv, b, x, g, atol, rtol, maxiter, check_every,
+                                       iters_out, converged_out, workspace, workspace_bytes,
+                                       info, s);
+    default:
+      return SLA_ERR_UNSUPPORTED;
   }
-  if (dtype == SLA_F32) {
-    if (dinv)
-      return mrhs_impl<float, true>(rowptr, colind, (const float *)vals, n, K, (const float *)dinv,
-                                    (const float *)b, (float *)x, g, atol, rtol, maxiter,
-                                    check_every, iters_out, converged_out, workspace,
-                                    workspace_bytes, info, s);
-    return mrhs_impl<float, false>(rowptr, colind, (const float *)vals, n, K, nullptr,
-                                   (const float *)b, (float *)x, g, atol, rtol, maxiter,
-                                   check_every, iters_out, converged_out, workspace,
-                                   workspace_bytes, info, s);
-  }
-  return SLA_ERR_INVALID;
 }
 
 }  // extern "C"
