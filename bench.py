@@ -497,7 +497,10 @@ def wl_mrhs(args, dev, local):
                      value, "column-iterations/s", ms, 1)
     line["config"] = {"workload": "multi_rhs_cg_poisson3d_7pt", "grid": [m, m, m], "n": n,
                       "rhs": K, "rtol": RTOL, "iterations_per_solve": iters // args.steps,
-                      "layout": "X, B and work vectors [n][16]; int32 CSR shared by the columns",
+                      "layout": "X, B and work vectors [n][16]; matrix "
+                                + ("diagonal-offset SELL (columns computed)"
+                                   if A.sell().diagonal_offsets else "int32 CSR")
+                                + ", shared by the columns",
                       "l2": "inputs larger than L2"}
     line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
                                   "achieved_gbs": round(iter_bytes * value / K / 1e9, 1),
