@@ -50,9 +50,11 @@ enum { kRunning = 0, kConverged = 1, kMaxiter = 2, kNonFinite = 3, kTimeout = 4 
 constexpr int kPBlock = SLA_PERSIST_BLOCK;
 constexpr int kPWarps = kPBlock / 32;
 
+// Every block of the persistent kernel sums the NV x gridDim partials in the
+// same order.
 template <int NV>
-__device__ __forceinline__ void reduce_partials_bs(double (&v)[NV], const double *parts,
-                                                   double *smem) {
+__device__ __forceinline__ void reduce_partials(double (&v)[NV], const double *parts,
+                                                double *smem) {
   const unsigned G = gridDim.x;
 #pragma unroll
   for (int k = 0; k < NV; ++k) v[k] = 0.0;
@@ -269,7 +271,7 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
     block_sum<1, kPBlock>(a1, smem);
     if (threadIdx.x == 0) partA[blockIdx.x] = a1[0];
     if (!grid_sync(&st->bar)) { done = kTimeout; break; }
-    reduce_partials_bs<1>(a1, partA, smem);
+    reduce_partials<1>(a1, partA, smem);
     const T alpha = (T)(rz / a1[0]);
     // phase B: x, r update and the two residual dots
     double a2[2] = {0.0, 0.0};
@@ -285,7 +287,7 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
     block_sum<2, kPBlock>(a2, smem);
     if (threadIdx.x == 0) { partB[blockIdx.x] = a2[0]; partB[gridDim.x + blockIdx.x] = a2[1]; }
     if (!grid_sync(&st->bar)) { done = kTimeout; break; }
-    reduce_partials_bs<2>(a2, partB, smem);
+    reduce_partials<2>(a2, partB, smem);
     rr = a2[0];
     beta = a2[1] / rz;
     rz = a2[1];

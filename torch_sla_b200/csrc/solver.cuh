@@ -1,23 +1,10 @@
-// Host-side polling and device-side reduction helpers shared by the
-// Krylov drivers.
+// Host-side polling of the device-resident Krylov loops (chunked launches
+// with one chunk in flight) shared by the drivers.
 #pragma once
 
 #include "sell.cuh"
 
 namespace sla {
-
-// Every block sums the NV x gridDim partials in the same order.
-template <int NV>
-__device__ __forceinline__ void reduce_partials(double (&v)[NV], const double *parts, double *smem) {
-  const unsigned G = gridDim.x;
-#pragma unroll
-  for (int k = 0; k < NV; ++k) v[k] = 0.0;
-  for (unsigned i = threadIdx.x; i < G; i += kBlock) {
-#pragma unroll
-    for (int k = 0; k < NV; ++k) v[k] += ld_l2(parts + k * G + i);
-  }
-  block_sum<NV, kBlock>(v, smem);
-}
 
 struct HostPoll {
   int *flags = nullptr;  // pinned
