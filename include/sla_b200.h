@@ -99,6 +99,9 @@ typedef struct {
 } sla_solve_info_t;
 
 /* ------------------------------------------------------------------ misc */
+/* Version of this interface; 2 since sla_sell_t carries n_cols, row_base
+ * and the diagonal offsets. _lib.py refuses a library with another. */
+#define SLA_ABI_VERSION 2
 int sla_abi_version(void);
 const char *sla_status_string(int status);
 /* Kernels this library has launched in this process (all devices). */

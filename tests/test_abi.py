@@ -35,7 +35,7 @@ def test_binding_table_matches_header():
 
 def test_status_strings_and_version():
     lib = L.lib()
-    assert lib.sla_abi_version() == 1
+    assert lib.sla_abi_version() == L.ABI_VERSION == 2
     assert lib.sla_status_string(L.SLA_ERR_UNSUPPORTED) == b"unsupported problem shape"
     assert lib.sla_status_string(L.SLA_NOT_CONVERGED).startswith(b"did not converge")
 
@@ -59,3 +59,33 @@ def test_workspace_queries(n, nnz):
     assert lib.sla_csr_build_workspace(n, nnz, ctypes.byref(need)) == 0 and need.value > 0
     assert lib.sla_sell_layout_workspace(n, ctypes.byref(need)) == 0 and need.value > 0
     assert lib.sla_bicgstab_workspace(2, n, ctypes.byref(need)) == L.SLA_ERR_INVALID
+
+
+def _view(**kw):
+    v = L.SellView()
+    v.n_slots, v.n_slices = kw.get("n_slots", 64), kw.get("n_slices", 2)
+    v.slice_ptr, v.val = 1 << 20, 1 << 20  # never dereferenced: rejected on the host
+    v.col = kw.get("col", None)
+    v.row_ids = kw.get("row_ids", None)
+    v.max_width = v.uniform_width = kw.get("width", 7)
+    v.n_cols, v.row_base = kw.get("n_cols", 64), kw.get("row_base", 0)
+    offs = kw.get("offsets", [-8, -4, -1, 0, 1, 4, 8])
+    v.n_diags = kw.get("n_diags", len(offs))
+    for i, o in enumerate(offs):
+        v.diag_offsets[i] = o
+    return v
+
+
+@pytest.mark.parametrize("bad", [
+    dict(offsets=[-8, -4, -1, 0, 1, 4, 8, 9, 10], width=9),   # 9 diagonals: no kernel for it
+    dict(offsets=[-4, -8, -1, 0, 1, 4, 8]),                    # offsets not ascending
+    dict(width=5),                                              # width != n_diags
+    dict(n_cols=0),                                             # no column bound
+    dict(row_ids=1 << 20, row_base=3),                          # row ids and a row base
+    dict(n_slices=3),                                           # n_slices != ceil(n_slots / 32)
+    dict(n_diags=0, col=None),                                  # explicit view without columns
+])
+def test_malformed_sell_views_are_rejected_on_the_host(bad):
+    """sla_spmv validates the view before any CUDA call: no GPU needed."""
+    v = _view(**bad)
+    assert L.lib().sla_spmv(L.SLA_F64, ctypes.byref(v), 1 << 20, 1 << 20, None) == L.SLA_ERR_INVALID

@@ -28,6 +28,7 @@ c_i32, c_i64, c_dbl, c_ptr, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_dou
 
 
 MAX_DIAGS = 32  # SLA_MAX_DIAGS
+ABI_VERSION = 2  # SLA_ABI_VERSION
 
 
 class SellView(ctypes.Structure):
@@ -145,6 +146,11 @@ def lib():
             f"torch_sla_b200: {LIB_PATH} is missing; build it with "
             "`python -m torch_sla_b200.build` (nvcc, sm_100a)")
     handle = ctypes.CDLL(LIB_PATH)
+    handle.sla_abi_version.restype = ctypes.c_int
+    if handle.sla_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"torch_sla_b200: {LIB_PATH} has interface version "
+                           f"{handle.sla_abi_version()}, this package needs {ABI_VERSION}; "
+                           "rebuild it with `python -m torch_sla_b200.build`")
     for name, (res, args) in _SIGNATURES.items():
         fn = getattr(handle, name, None)
         if fn is None:

@@ -103,7 +103,7 @@ void Profiler::resolve() {
 
 extern "C" {
 
-int sla_abi_version(void) { return 1; }
+int sla_abi_version(void) { return SLA_ABI_VERSION; }
 
 const char *sla_status_string(int status) {
   switch (status) {
