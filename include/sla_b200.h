@@ -157,6 +157,14 @@ int sla_sell_diag_probe(const int32_t *rowptr, const int32_t *colind,
  * has no entry on a diagonal). Every CSR entry of the listed rows must lie
  * on one of the n_diags ascending host-side offsets (SLA_ERR_INVALID
  * otherwise). Workspace as for the probe. Synchronises the stream. */
+/* Position of every CSR entry of rows 0..n_rows-1 in the diagonal-offset
+ * view with the given ascending host-side offsets:
+ * (row/32)*32*n_diags + 32*j + row%32. SLA_ERR_INVALID when an entry lies on
+ * none of them. Workspace as for the probe. Synchronises the stream. */
+int sla_sell_diag_positions(const int32_t *rowptr, const int32_t *colind,
+                            int64_t n_rows, const int32_t *offsets,
+                            int32_t n_diags, int64_t *pos, void *workspace,
+                            size_t workspace_bytes, sla_stream_t stream);
 int sla_sell_diag_fill(int dtype, const int32_t *rowptr, const int32_t *colind,
                        const void *vals, const int32_t *row_ids, int64_t n_slots,
                        const int32_t *offsets, int32_t n_diags, void *sell_val,
@@ -234,6 +242,14 @@ int sla_batched_values(int dtype, const void *val_batch, int64_t batch,
                        int64_t nnz_coo, const int64_t *src_index,
                        const int32_t *seg_ptr, int64_t nnz_csr, void *out,
                        sla_stream_t stream);
+/* The same values placed in the order of a diagonal-offset view of the
+ * pattern: out ([n_out][B], zero-filled first) receives member b's value of
+ * CSR entry e at (pos[e] * B + b); pos from sla_sell_diag_positions. */
+int sla_batched_values_at(int dtype, const void *val_batch, int64_t batch,
+                          int64_t nnz_coo, const int64_t *src_index,
+                          const int32_t *seg_ptr, int64_t nnz_csr,
+                          const int64_t *pos, int64_t n_out, void *out,
+                          sla_stream_t stream);
 int sla_batched_cg_workspace(int dtype, int64_t n, int64_t batch,
                              size_t *bytes);
 int sla_batched_cg(int dtype, const int32_t *rowptr, const int32_t *colind,
@@ -241,6 +257,15 @@ int sla_batched_cg(int dtype, const int32_t *rowptr, const int32_t *colind,
                    const void *b, void *x, double atol, double rtol,
                    int64_t maxiter, void *workspace, size_t workspace_bytes,
                    sla_solve_info_t *info, sla_stream_t stream);
+/* The same solve on a diagonal-offset view of the pattern (5, 7 or 27
+ * diagonals, square, no row ids; the view's own values are not used) with
+ * values in that view's order (sla_batched_values_at): no column or
+ * row-pointer loads in the SpMV. */
+int sla_batched_cg_diag(int dtype, const sla_sell_t *A, const void *vals_diag,
+                        int64_t batch, const void *b, void *x, double atol,
+                        double rtol, int64_t maxiter, void *workspace,
+                        size_t workspace_bytes, sla_solve_info_t *info,
+                        sla_stream_t stream);
 
 /* CG on K right-hand sides of one CSR matrix (batched_pcg_solve,
  * pytorch_backend.py:2352-2504; pytorch_solve with a 2-D b). b and x are

@@ -112,3 +112,18 @@ def test_diag_view_multi_rhs_matches_csr(dev):
         out.append(res)
     assert torch.equal(out[0].num_iters, out[1].num_iters)
     assert float((out[0].X - out[1].X).abs().max()) == 0.0
+
+
+def test_diag_view_batched_matches_csr(dev, monkeypatch):
+    """Batched same-pattern CG with values in the diagonal-offset order
+    against the CSR kernels: same iterations, same X up to zero signs."""
+    from torch_sla_b200._csr import DeviceCSR as DC
+    vb, r, c, sh, bb = P.diffusion_2d_batched(8, 40, seed=2)
+    args = (vb.to(dev), r.to(dev), c.to(dev), sh, bb.to(dev))
+    X_diag, info_diag = PB.batched_cg_same_pattern_info(*args, atol=0.0, rtol=1e-10)
+    assert DC(None, r.to(dev), c.to(dev), sh, keep_map=True,
+              dtype=torch.float64).diag_pattern() is not None
+    monkeypatch.setattr(DC, "diag_pattern", lambda self: None)
+    X_csr, info_csr = PB.batched_cg_same_pattern_info(*args, atol=0.0, rtol=1e-10)
+    assert info_diag.iterations == info_csr.iterations
+    assert float((X_diag - X_csr).abs().max()) == 0.0

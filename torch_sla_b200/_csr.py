@@ -140,14 +140,16 @@ class DeviceCSR:
             self._sell = s
         return s
 
-    def _diagonal_view(self, row_ids, n_slots, n_cols, vals, stream):
+    def _diag_offsets(self, row_ids, n_slots, stream):
+        """Ascending diagonal offsets of the listed rows when they fit a
+        diagonal-offset view (5, 7 or 27 diagonals, padding <= DIAG_MAX_PAD),
+        else None, plus the probe workspace."""
         if n_slots == 0 or self.nnz == 0:
-            return None
+            return None, None
         lib = L.lib()
-        dev = self.device
         need = ctypes.c_size_t(0)
         L.check("sla_sell_diag_probe_workspace", lib.sla_sell_diag_probe_workspace(ctypes.byref(need)))
-        ws = L.workspace(need.value, dev)
+        ws = L.workspace(need.value, self.device)
         offs = (L.c_i32 * L.MAX_DIAGS)()
         count = L.c_i32(0)
         L.check("sla_sell_diag_probe", lib.sla_sell_diag_probe(
@@ -155,24 +157,49 @@ class DeviceCSR:
             ctypes.byref(count), L.ptr(ws), ws.numel(), stream))
         w = int(count.value)
         if w not in self.DIAG_WIDTHS:
-            return None
+            return None, ws
         if row_ids is None:
             nnz_view = self.nnz
         else:
             rl = row_ids.to(torch.int64)
             nnz_view = int((self.rowptr[rl + 1] - self.rowptr[rl]).sum())
+        padded = (n_slots + 31) // 32 * 32 * w
+        if padded > (1.0 + self.DIAG_MAX_PAD) * max(nnz_view, 1):
+            return None, ws
+        return list(offs)[:w], ws
+
+    def diag_pattern(self):
+        """(offsets, positions) of the whole matrix as a diagonal-offset view
+        -- positions[k] is CSR entry k's place in that view -- or None."""
+        stream = L.stream_handle(self.device)
+        offs, ws = self._diag_offsets(None, self.shape[0], stream)
+        if offs is None or self.shape[0] != self.shape[1]:
+            return None
+        pos = torch.empty(max(self.nnz, 1), dtype=torch.int64, device=self.device)
+        arr = (L.c_i32 * L.MAX_DIAGS)(*offs)
+        L.check("sla_sell_diag_positions", L.lib().sla_sell_diag_positions(
+            L.ptr(self.rowptr), L.ptr(self.colind), self.shape[0], arr, len(offs), L.ptr(pos),
+            L.ptr(ws), ws.numel(), stream))
+        return offs, pos[: self.nnz]
+
+    def _diagonal_view(self, row_ids, n_slots, n_cols, vals, stream):
+        offs, ws = self._diag_offsets(row_ids, n_slots, stream)
+        if offs is None:
+            return None
+        lib = L.lib()
+        dev = self.device
+        w = len(offs)
         n_slices = (n_slots + 31) // 32
         padded = n_slices * 32 * w
-        if padded > (1.0 + self.DIAG_MAX_PAD) * max(nnz_view, 1):
-            return None
+        arr = (L.c_i32 * L.MAX_DIAGS)(*offs)
         sval = torch.empty(padded, dtype=self.dtype, device=dev)
         L.check("sla_sell_diag_fill", lib.sla_sell_diag_fill(
             self.code, L.ptr(self.rowptr), L.ptr(self.colind), L.ptr(vals), L.ptr(row_ids),
-            n_slots, offs, w, L.ptr(sval), L.ptr(ws), ws.numel(), stream))
+            n_slots, arr, w, L.ptr(sval), L.ptr(ws), ws.numel(), stream))
         slice_ptr = (torch.arange(n_slices + 1, device=dev, dtype=torch.int64) * (32 * w)).to(
             torch.int32)
         return Sell(slice_ptr, None, sval, n_slots, row_ids, max_width=w, uniform_width=w,
-                    n_cols=n_cols, offsets=list(offs)[:w])
+                    n_cols=n_cols, offsets=offs)
 
     def _explicit_view(self, row_ids, n_slots, n_cols, vals, stream):
         lib = L.lib()

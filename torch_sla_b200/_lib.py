@@ -69,6 +69,8 @@ _SIGNATURES = {
     "sla_sell_diag_probe_workspace": (ctypes.c_int, [_P(c_sz)]),
     "sla_sell_diag_probe": (ctypes.c_int, [c_ptr, c_ptr, c_ptr, c_i64, _P(c_i32), _P(c_i32),
                                            c_ptr, c_sz, c_ptr]),
+    "sla_sell_diag_positions": (ctypes.c_int, [c_ptr, c_ptr, c_i64, _P(c_i32), c_i32, c_ptr,
+                                               c_ptr, c_sz, c_ptr]),
     "sla_sell_diag_fill": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_i64,
                                           _P(c_i32), c_i32, c_ptr, c_ptr, c_sz, c_ptr]),
     "sla_jacobi_inverse": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_i64,
@@ -89,6 +91,11 @@ _SIGNATURES = {
                                     _P(SolveInfo), c_ptr]),
     "sla_batched_values": (ctypes.c_int, [ctypes.c_int, c_ptr, c_i64, c_i64, c_ptr, c_ptr,
                                           c_i64, c_ptr, c_ptr]),
+    "sla_batched_values_at": (ctypes.c_int, [ctypes.c_int, c_ptr, c_i64, c_i64, c_ptr, c_ptr,
+                                             c_i64, c_ptr, c_i64, c_ptr, c_ptr]),
+    "sla_batched_cg_diag": (ctypes.c_int, [ctypes.c_int, _P(SellView), c_ptr, c_i64, c_ptr,
+                                           c_ptr, c_dbl, c_dbl, c_i64, c_ptr, c_sz,
+                                           _P(SolveInfo), c_ptr]),
     "sla_batched_cg_workspace": (ctypes.c_int, [ctypes.c_int, c_i64, c_i64, _P(c_sz)]),
     "sla_batched_cg": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_i64, c_i64, c_ptr,
                                       c_ptr, c_dbl, c_dbl, c_i64, c_ptr, c_sz, _P(SolveInfo),

@@ -16,7 +16,7 @@ import torch
 from torch import Tensor
 
 from .. import _lib as L
-from .._csr import DeviceCSR, coo_value_grad
+from .._csr import DeviceCSR, Sell, coo_value_grad
 
 __all__ = [
     "SolveResult", "CachedSparseMatrix", "JacobiPreconditioner", "IdentityPreconditioner",
@@ -335,24 +335,41 @@ def batched_cg_same_pattern_info(val_batch: Tensor, row: Tensor, col: Tensor,
     stream = L.stream_handle(dev)
     X = torch.empty(Bn, n, dtype=val_batch.dtype, device=dev)
     info = L.SolveInfo()
+    # stencil patterns: values in the order of a diagonal-offset view, whose
+    # SpMV computes columns instead of loading them
+    diag = csr.diag_pattern()
+    if diag is not None:
+        offs, pos = diag
+        w = len(offs)
+        n_out = (n + 31) // 32 * 32 * w
+        view = Sell(torch.zeros(1, dtype=torch.int32, device=dev), None, None, n, None,
+                    max_width=w, uniform_width=w, n_cols=n, offsets=offs)
     # Members are coupled only through the "all converged" test; batches
     # beyond the kernel's 1024 lanes run as independent chunks.
     for s0 in range(0, Bn, _MAX_BATCH):
         vb = val_batch[s0:s0 + _MAX_BATCH].contiguous()
         bb = b_batch[s0:s0 + _MAX_BATCH].to(val_batch.dtype).contiguous()
         B = int(vb.shape[0])
-        vals = torch.empty(max(csr.nnz * B, 1), dtype=val_batch.dtype, device=dev)
-        L.check("sla_batched_values", lib.sla_batched_values(
-            code, L.ptr(vb), B, int(vb.shape[1]), L.ptr(csr.src_index), L.ptr(csr.seg_ptr),
-            csr.nnz, L.ptr(vals), stream))
         need = ctypes.c_size_t(0)
         L.check("sla_batched_cg_workspace", lib.sla_batched_cg_workspace(code, n, B, ctypes.byref(need)))
         ws = L.workspace(need.value, dev)
         xo = X[s0:s0 + B]
-        st = lib.sla_batched_cg(code, L.ptr(csr.rowptr), L.ptr(csr.colind), L.ptr(vals), n, B,
-                                L.ptr(bb), L.ptr(xo), float(atol), float(rtol), int(maxiter),
-                                L.ptr(ws), ws.numel(), ctypes.byref(info), stream)
-        L.check("sla_batched_cg", st)
+        tail = (L.ptr(bb), L.ptr(xo), float(atol), float(rtol), int(maxiter), L.ptr(ws),
+                ws.numel(), ctypes.byref(info), stream)
+        if diag is not None:
+            vals = torch.empty(max(n_out * B, 1), dtype=val_batch.dtype, device=dev)
+            L.check("sla_batched_values_at", lib.sla_batched_values_at(
+                code, L.ptr(vb), B, int(vb.shape[1]), L.ptr(csr.src_index), L.ptr(csr.seg_ptr),
+                csr.nnz, L.ptr(pos), n_out, L.ptr(vals), stream))
+            L.check("sla_batched_cg_diag", lib.sla_batched_cg_diag(
+                code, view.ref(), L.ptr(vals), B, *tail))
+        else:
+            vals = torch.empty(max(csr.nnz * B, 1), dtype=val_batch.dtype, device=dev)
+            L.check("sla_batched_values", lib.sla_batched_values(
+                code, L.ptr(vb), B, int(vb.shape[1]), L.ptr(csr.src_index), L.ptr(csr.seg_ptr),
+                csr.nnz, L.ptr(vals), stream))
+            L.check("sla_batched_cg", lib.sla_batched_cg(
+                code, L.ptr(csr.rowptr), L.ptr(csr.colind), L.ptr(vals), n, B, *tail))
     _record("batched_cg", info)
     return X, info
 

@@ -8,6 +8,8 @@
 // fixed order (rows of the block, then blocks), so results are
 // deterministic. Stops when every ||R_b|| <= max(atol, rtol*||b_b||), with
 // all members iterating until then, as the reference does.
+#include <type_traits>
+
 #include "batch.cuh"
 
 namespace sla {
@@ -26,10 +28,67 @@ struct BatchScalars {
   double *rz, *alpha, *beta, *tol, *rr, *alpha_prev;
 };
 
+// Row access of the batched kernels: CSR with [nnz][B] values, or a
+// diagonal-offset view of a stencil pattern with values [slot entry][B] in
+// the view's order (column = row + offset: no column or row-pointer loads).
 template <typename T>
+struct CsrBatch {
+  const int32_t *rowptr, *colind;
+  const T *vals;
+  template <int VEC, int RB, typename G>
+  __device__ __forceinline__ void sum(int64_t row, int B, int m0, const G &g, T (&s)[VEC]) const {
+    csr_row_vec<T, VEC, RB>(
+        colind, __ldg(rowptr + row), __ldg(rowptr + row + 1),
+        [&](int32_t k) { return vload<T, VEC, kLoadStream>(vals + (int64_t)k * B + m0); }, g, s);
+  }
+  // member bi's diagonal entry (0 when the row stores none)
+  __device__ __forceinline__ T diag(int64_t row, int B, int bi) const {
+    T d = T(0);
+    for (int32_t k = rowptr[row]; k < rowptr[row + 1]; ++k)
+      if (colind[k] == (int32_t)row) d = vals[(int64_t)k * B + bi];
+    return d;
+  }
+};
+
+template <typename T, int W>
+struct DiagBatch {
+  Sell<T> A;      // pattern: offsets and column bound (its own values unused)
+  const T *vals;  // [n_slices * 32 * W][B]
+  int j0;         // index of offset 0, -1 if none
+  template <int VEC, int RB, typename G>
+  __device__ __forceinline__ void sum(int64_t row, int B, int m0, const G &g, T (&s)[VEC]) const {
+#pragma unroll
+    for (int u = 0; u < VEC; ++u) s[u] = T(0);
+    const int64_t e0 = (row >> 5) * 32 * W + (row & 31);
+#pragma unroll
+    for (int jb = 0; jb < W; jb += RB) {
+      Pack<T, VEC> v[RB], x[RB];
+#pragma unroll
+      for (int q = 0; q < RB; ++q) {
+        v[q] = splat<T, VEC>(T(0));
+        x[q] = splat<T, VEC>(T(0));
+        if (jb + q < W) {
+          const int64_t c = row + A.off[jb + q];
+          v[q] = vload<T, VEC, kLoadStream>(vals + (e0 + 32 * (jb + q)) * B + m0);
+          if (c >= 0 && c < A.n_cols) x[q] = g((int32_t)c);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < RB; ++q) {
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) s[u] = fma(v[q].v[u], x[q].v[u], s[u]);
+      }
+    }
+  }
+  __device__ __forceinline__ T diag(int64_t row, int B, int bi) const {
+    if (j0 < 0) return T(0);
+    return vals[((row >> 5) * 32 * W + (row & 31) + 32 * j0) * B + bi];
+  }
+};
+
+template <typename T, typename M>
 __global__ void __launch_bounds__(1024)
-batch_init_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
-                  const T *__restrict__ vals, int64_t n, int B, const T *__restrict__ b_in,
+batch_init_kernel(M mat, int64_t n, int B, const T *__restrict__ b_in,
                   T *__restrict__ x, T *__restrict__ r, T *__restrict__ p_old, T *__restrict__ dinv,
                   BatchState *st, BatchScalars sc, double *partials, double atol, double rtol) {
   extern __shared__ double smem[];
@@ -38,9 +97,7 @@ batch_init_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict_
   double acc[2][1] = {{0.0}, {0.0}};
   for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
        row += (int64_t)gridDim.x * ln.rpb) {
-    T d = T(0);
-    for (int32_t k = rowptr[row]; k < rowptr[row + 1]; ++k)
-      if (colind[k] == (int32_t)row) d = vals[(int64_t)k * B + bi];
+    const T d = mat.diag(row, B, bi);
     T di = (fabs(d) > T(0)) ? T(1) / d : T(1);
     T bv = b_in[(int64_t)bi * n + row];
     int64_t o = row * B + bi;
@@ -68,10 +125,9 @@ batch_init_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict_
 
 // K_A: p = p_old * beta + D^-1 r formed inside the gather, Ap = A p, writes
 // p and Ap, per-member (p, Ap); the last block forms alpha.
-template <typename T, int VEC, int RB>
+template <typename T, int VEC, int RB, typename M>
 __global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
-batch_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
-                  const T *__restrict__ vals, int64_t n, int B, const T *__restrict__ r,
+batch_spmv_kernel(M mat, int64_t n, int B, const T *__restrict__ r,
                   const T *__restrict__ dinv, const T *__restrict__ p_old, T *__restrict__ p_new,
                   T *__restrict__ Ap, BatchState *st, BatchScalars sc, double *partials) {
   extern __shared__ double smem[];
@@ -86,9 +142,8 @@ batch_spmv_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict_
   for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
        row += (int64_t)gridDim.x * ln.rpb) {
     T sum[VEC];
-    csr_row_vec<T, VEC, RB>(
-        colind, __ldg(rowptr + row), __ldg(rowptr + row + 1),
-        [&](int32_t k) { return vload<T, VEC, kLoadStream>(vals + (int64_t)k * B + ln.m0); },
+    mat.template sum<VEC, RB>(
+        row, B, ln.m0,
         [&](int32_t ci) {
           const int64_t c = (int64_t)ci * B + ln.m0;
           const Pack<T, VEC> po = vload<T, VEC, kLoadRO>(p_old + c);
@@ -223,11 +278,11 @@ static size_t batch_ws_bytes(size_t elem, int64_t n, int64_t B) {
 // Row load batch of the vectorised SpMV: one dependent round trip covers a
 // row of up to RB entries (5- and 7-point stencils).
 
-template <typename T, int VEC>
-static int batched_loop(const int32_t *rowptr, const int32_t *colind, const T *vals, int64_t n,
-                        int B, T *xi, T *r, T *pA, T *pB, T *Ap, T *dinv, BatchState *st,
-                        BatchScalars sc, double *const part[3], int64_t maxiter, cudaStream_t s) {
-  auto spmv = batch_spmv_kernel<T, VEC, kBatchRB>;
+template <typename T, int VEC, typename M>
+static int batched_loop(M mat, int64_t n, int B, T *xi, T *r, T *pA, T *pB, T *Ap, T *dinv,
+                        BatchState *st, BatchScalars sc, double *const part[3], int64_t maxiter,
+                        cudaStream_t s) {
+  auto spmv = batch_spmv_kernel<T, VEC, kBatchRB, M>;
   auto upd = batch_update_kernel<T, VEC>;
   const int TB = batch_block(B, VEC);
   const size_t sm1 = batch_smem(1, TB, VEC), sm2 = batch_smem(2, TB, VEC);
@@ -237,8 +292,7 @@ static int batched_loop(const int32_t *rowptr, const int32_t *colind, const T *v
     T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
     cudaEvent_t ev;
     profiler().begin(0, it, s, &ev);
-    SLA_LAUNCH(spmv, G1, TB, sm1, s, rowptr, colind, vals, n, B, r, dinv, p_old, p_new, Ap, st,
-               sc, part[1]);
+    SLA_LAUNCH(spmv, G1, TB, sm1, s, mat, n, B, r, dinv, p_old, p_new, Ap, st, sc, part[1]);
     profiler().end(0, s, ev);
     profiler().begin(1, it, s, &ev);
     SLA_LAUNCH(upd, G2, TB, sm2, s, n, B, xi, r, p_new, p_old, Ap, dinv, st, sc, part[2],
@@ -248,10 +302,10 @@ static int batched_loop(const int32_t *rowptr, const int32_t *colind, const T *v
   });
 }
 
-template <typename T>
-static int batched_impl(const int32_t *rowptr, const int32_t *colind, const T *vals, int64_t n,
-                        int B, const T *b, T *x, double atol, double rtol, int64_t maxiter,
-                        void *ws, size_t ws_bytes, sla_solve_info_t *info, cudaStream_t s) {
+template <typename T, typename M>
+static int batched_impl(M mat, const T *vals, int64_t n, int B, const T *b, T *x, double atol,
+                        double rtol, int64_t maxiter, void *ws, size_t ws_bytes,
+                        sla_solve_info_t *info, cudaStream_t s) {
   Carver c(ws, ws_bytes);
   const size_t nb = (size_t)(n * B);
   T *r = c.take<T>(nb), *xi = c.take<T>(nb), *pA = c.take<T>(nb), *pB = c.take<T>(nb);
@@ -269,20 +323,19 @@ static int batched_impl(const int32_t *rowptr, const int32_t *colind, const T *v
   {
     const int TB0 = batch_block(B, 1);
     const size_t sm0 = batch_smem(2, TB0, 1);
-    const int G0 = occupancy_grid((const void *)batch_init_kernel<T>, TB0, sm0);
-    SLA_LAUNCH(batch_init_kernel<T>, G0, TB0, sm0, s, rowptr, colind, vals, n, B, b, xi, r, pA,
-               dinv, st, sc, part[0], atol, rtol);
+    auto init_fn = batch_init_kernel<T, M>;
+    const int G0 = occupancy_grid((const void *)init_fn, TB0, sm0);
+    SLA_LAUNCH(init_fn, G0, TB0, sm0, s, mat, n, B, b, xi, r, pA, dinv, st, sc, part[0], atol,
+               rtol);
   }
   // 16-byte vector groups of members where B allows it (the interleaved
   // buffers are all 256-byte aligned)
   constexpr int kVec = 16 / sizeof(T);
   int rc;
   if (B % kVec == 0 && aligned16(vals))
-    rc = batched_loop<T, kVec>(rowptr, colind, vals, n, B, xi, r, pA, pB, Ap, dinv, st, sc, part,
-                               maxiter, s);
+    rc = batched_loop<T, kVec>(mat, n, B, xi, r, pA, pB, Ap, dinv, st, sc, part, maxiter, s);
   else
-    rc = batched_loop<T, 1>(rowptr, colind, vals, n, B, xi, r, pA, pB, Ap, dinv, st, sc, part,
-                            maxiter, s);
+    rc = batched_loop<T, 1>(mat, n, B, xi, r, pA, pB, Ap, dinv, st, sc, part, maxiter, s);
   SLA_TRY(rc);
   // a last even iteration's direction sits in pB
   SLA_LAUNCH(batch_xflush_kernel<T>, grid_for(n * B), kBlock, 0, s, n, B, xi, pB, st, sc);
@@ -302,6 +355,19 @@ static int batched_impl(const int32_t *rowptr, const int32_t *colind, const T *v
   return info->status;
 }
 
+static int batched_args_ok(int dtype, int64_t n, int64_t batch, const void *b, void *x,
+                           sla_solve_info_t *info, void *workspace, size_t workspace_bytes) {
+  if (!b || !x || !info || n <= 0 || n >= INT32_MAX) return SLA_ERR_INVALID;
+  if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
+  if (batch < 1) return SLA_ERR_INVALID;
+  if (batch > kMaxBatch) return SLA_ERR_UNSUPPORTED;
+  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
+  size_t need = 0;
+  SLA_TRY(sla_batched_cg_workspace(dtype, n, batch, &need));
+  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  return SLA_OK;
+}
+
 }  // namespace sla
 
 using namespace sla;
@@ -319,23 +385,53 @@ int sla_batched_cg(int dtype, const int32_t *rowptr, const int32_t *colind,
                    const void *vals_interleaved, int64_t n, int64_t batch, const void *b, void *x,
                    double atol, double rtol, int64_t maxiter, void *workspace,
                    size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
-  if (!rowptr || !b || !x || !info || n <= 0 || n >= INT32_MAX) return SLA_ERR_INVALID;
-  if (batch < 1) return SLA_ERR_INVALID;
-  if (batch > kMaxBatch) return SLA_ERR_UNSUPPORTED;
-  info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
-  size_t need = 0;
-  SLA_TRY(sla_batched_cg_workspace(dtype, n, batch, &need));
-  if (workspace_bytes < need || !workspace) return SLA_ERR_WORKSPACE;
+  if (!rowptr || !colind) return SLA_ERR_INVALID;
+  SLA_TRY(batched_args_ok(dtype, n, batch, b, x, info, workspace, workspace_bytes));
   cudaStream_t s = (cudaStream_t)stream;
-  if (dtype == SLA_F64)
-    return batched_impl<double>(rowptr, colind, (const double *)vals_interleaved, n, (int)batch,
+  if (dtype == SLA_F64) {
+    const double *v = (const double *)vals_interleaved;
+    return batched_impl<double>(CsrBatch<double>{rowptr, colind, v}, v, n, (int)batch,
                                 (const double *)b, (double *)x, atol, rtol, maxiter, workspace,
                                 workspace_bytes, info, s);
-  if (dtype == SLA_F32)
-    return batched_impl<float>(rowptr, colind, (const float *)vals_interleaved, n, (int)batch,
-                               (const float *)b, (float *)x, atol, rtol, maxiter, workspace,
-                               workspace_bytes, info, s);
-  return SLA_ERR_INVALID;
+  }
+  const float *v = (const float *)vals_interleaved;
+  return batched_impl<float>(CsrBatch<float>{rowptr, colind, v}, v, n, (int)batch,
+                             (const float *)b, (float *)x, atol, rtol, maxiter, workspace,
+                             workspace_bytes, info, s);
+}
+
+int sla_batched_cg_diag(int dtype, const sla_sell_t *A, const void *vals_diag, int64_t batch,
+                        const void *b, void *x, double atol, double rtol, int64_t maxiter,
+                        void *workspace, size_t workspace_bytes, sla_solve_info_t *info,
+                        sla_stream_t stream) {
+  if (!A || A->n_diags <= 0 || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  sla_sell_t pat = *A;
+  if (!pat.val) pat.val = vals_diag;  // the pattern view needs no values of its own
+  if (!sell_ok(&pat) || !vals_diag) return SLA_ERR_INVALID;
+  const int64_t n = pat.n_slots;
+  if (pat.n_cols != n) return SLA_ERR_INVALID;  // square systems
+  SLA_TRY(batched_args_ok(dtype, n, batch, b, x, info, workspace, workspace_bytes));
+  int j0 = -1;
+  for (int j = 0; j < pat.n_diags; ++j)
+    if (pat.diag_offsets[j] == 0) j0 = j;
+  cudaStream_t s = (cudaStream_t)stream;
+  auto run = [&](auto tag, auto wtag) -> int {
+    using T = decltype(tag);
+    constexpr int W = decltype(wtag)::value;
+    const T *v = (const T *)vals_diag;
+    return batched_impl<T>(DiagBatch<T, W>{make_sell<T>(&pat), v, j0}, v, n, (int)batch,
+                           (const T *)b, (T *)x, atol, rtol, maxiter, workspace, workspace_bytes,
+                           info, s);
+  };
+  auto by_width = [&](auto tag) -> int {
+    switch (pat.n_diags) {
+      case 5: return run(tag, std::integral_constant<int, 5>{});
+      case 7: return run(tag, std::integral_constant<int, 7>{});
+      case 27: return run(tag, std::integral_constant<int, 27>{});
+      default: return SLA_ERR_UNSUPPORTED;
+    }
+  };
+  return dtype == SLA_F64 ? by_width(double(0)) : by_width(float(0));
 }
 
 }  // extern "C"

@@ -484,6 +484,29 @@ diag_fill_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__
   }
 }
 
+// Position of every CSR entry in a diagonal-offset view of all rows:
+// (row / 32) * 32 * W + 32 * j + row % 32, j the entry's diagonal.
+__global__ void __launch_bounds__(kBlock)
+diag_pos_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
+                int64_t n_rows, DiagOffsets D, int64_t *__restrict__ pos, int *bad) {
+  int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; r < n_rows; r += stride) {
+    const int64_t base = (r >> 5) * 32 * D.n + (r & 31);
+    for (int32_t k = rowptr[r]; k < rowptr[r + 1]; ++k) {
+      const int64_t d = (int64_t)colind[k] - r;
+      int lo = 0, hi = D.n - 1, j = -1;
+      while (lo <= hi) {
+        const int mid = (lo + hi) >> 1;
+        if (D.off[mid] == d) { j = mid; break; }
+        if (D.off[mid] < d) lo = mid + 1; else hi = mid - 1;
+      }
+      if (j < 0) { atomicExch(bad, 1); pos[k] = -1; continue; }
+      pos[k] = base + 32 * j;
+    }
+  }
+}
+
 }  // namespace sla
 
 using namespace sla;
@@ -660,6 +683,31 @@ int sla_sell_diag_fill(int dtype, const int32_t *rowptr, const int32_t *colind, 
   else
     SLA_LAUNCH(diag_fill_kernel<float>, grid_for(n_slots), kBlock, 0, s, rowptr, colind,
                (const float *)vals, row_ids, n_slots, D, (float *)sell_val, bad);
+  int hb = 0;
+  SLA_CUDA_TRY(cudaMemcpyAsync(&hb, bad, sizeof(int), cudaMemcpyDeviceToHost, s));
+  SLA_CUDA_TRY(cudaStreamSynchronize(s));
+  return hb ? SLA_ERR_INVALID : SLA_OK;
+}
+
+int sla_sell_diag_positions(const int32_t *rowptr, const int32_t *colind, int64_t n_rows,
+                            const int32_t *offsets, int32_t n_diags, int64_t *pos,
+                            void *workspace, size_t workspace_bytes, sla_stream_t stream) {
+  if (!rowptr || !offsets || n_rows < 0 || n_diags < 1 || n_diags > SLA_MAX_DIAGS)
+    return SLA_ERR_INVALID;
+  size_t need = 0;
+  sla_sell_diag_probe_workspace(&need);
+  if (!workspace || workspace_bytes < need) return SLA_ERR_WORKSPACE;
+  DiagOffsets D;
+  D.n = n_diags;
+  for (int i = 0; i < SLA_MAX_DIAGS; ++i) D.off[i] = i < n_diags ? offsets[i] : INT32_MAX;
+  for (int i = 1; i < n_diags; ++i)
+    if (D.off[i] <= D.off[i - 1]) return SLA_ERR_INVALID;
+  if (n_rows == 0) return SLA_OK;
+  if (!colind || !pos) return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  int *bad = (int *)workspace;
+  SLA_CUDA_TRY(cudaMemsetAsync(bad, 0, sizeof(int), s));
+  SLA_LAUNCH(diag_pos_kernel, grid_for(n_rows), kBlock, 0, s, rowptr, colind, n_rows, D, pos, bad);
   int hb = 0;
   SLA_CUDA_TRY(cudaMemcpyAsync(&hb, bad, sizeof(int), cudaMemcpyDeviceToHost, s));
   SLA_CUDA_TRY(cudaStreamSynchronize(s));

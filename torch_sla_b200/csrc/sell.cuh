@@ -93,7 +93,10 @@ constexpr int kRowBatch = 8;
 
 // Blocks per SM the SpMV-bearing kernels are compiled for (register cap):
 // enough warps to keep ~8 batched loads each in flight.
-constexpr int kSpmvMinBlocks = 4;
+#ifndef SLA_SPMV_MIN_BLOCKS
+#define SLA_SPMV_MIN_BLOCKS 4
+#endif
+constexpr int kSpmvMinBlocks = SLA_SPMV_MIN_BLOCKS;
 
 // Width spec of a view: the template value its kernels are launched with.
 inline int width_spec(const sla_sell_t *A) {

@@ -55,10 +55,13 @@ __global__ void coo_value_grad_kernel(const int64_t *__restrict__ row, const int
   }
 }
 
+// Per-member values gathered from the COO batch: out[(pos ? pos[e] : e) * batch + b]
+// = sum of the COO duplicates of CSR entry e (in input order) of member b.
 template <typename T>
 __global__ void batched_values_kernel(const T *__restrict__ vb, int64_t batch, int64_t nnz_coo,
                                       const int64_t *__restrict__ src, const int32_t *__restrict__ seg,
-                                      int64_t nnz_csr, T *__restrict__ out) {
+                                      int64_t nnz_csr, const int64_t *__restrict__ pos,
+                                      T *__restrict__ out) {
   int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (; t < nnz_csr * batch; t += stride) {
@@ -67,7 +70,7 @@ __global__ void batched_values_kernel(const T *__restrict__ vb, int64_t batch, i
     int32_t s0 = seg[e], s1 = seg[e + 1];
     T acc = v[src[s0]];
     for (int32_t q = s0 + 1; q < s1; ++q) acc = add_rn(acc, v[src[q]]);
-    out[t] = acc;
+    out[(pos ? pos[e] : e) * batch + bi] = acc;
   }
 }
 
@@ -113,13 +116,35 @@ int sla_batched_values(int dtype, const void *val_batch, int64_t batch, int64_t 
   if (dtype == SLA_F64)
     SLA_LAUNCH(batched_values_kernel<double>, grid_for(nnz_csr * batch), kBlock, 0, s,
                (const double *)val_batch, batch, nnz_coo, src_index, seg_ptr, nnz_csr,
-               (double *)out);
+               (const int64_t *)nullptr, (double *)out);
   else if (dtype == SLA_F32)
     SLA_LAUNCH(batched_values_kernel<float>, grid_for(nnz_csr * batch), kBlock, 0, s,
                (const float *)val_batch, batch, nnz_coo, src_index, seg_ptr, nnz_csr,
-               (float *)out);
+               (const int64_t *)nullptr, (float *)out);
   else
     return SLA_ERR_INVALID;
+  return SLA_OK;
+}
+
+int sla_batched_values_at(int dtype, const void *val_batch, int64_t batch, int64_t nnz_coo,
+                          const int64_t *src_index, const int32_t *seg_ptr, int64_t nnz_csr,
+                          const int64_t *pos, int64_t n_out, void *out, sla_stream_t stream) {
+  if (batch < 1 || nnz_coo < 0 || nnz_csr < 0 || n_out < 0 || !pos || !out)
+    return SLA_ERR_INVALID;
+  if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t elem = dtype == SLA_F64 ? 8 : 4;
+  SLA_CUDA_TRY(cudaMemsetAsync(out, 0, elem * (size_t)n_out * (size_t)batch, s));
+  if (nnz_csr == 0) return SLA_OK;
+  if (!val_batch || !src_index || !seg_ptr) return SLA_ERR_INVALID;
+  if (dtype == SLA_F64)
+    SLA_LAUNCH(batched_values_kernel<double>, grid_for(nnz_csr * batch), kBlock, 0, s,
+               (const double *)val_batch, batch, nnz_coo, src_index, seg_ptr, nnz_csr, pos,
+               (double *)out);
+  else
+    SLA_LAUNCH(batched_values_kernel<float>, grid_for(nnz_csr * batch), kBlock, 0, s,
+               (const float *)val_batch, batch, nnz_coo, src_index, seg_ptr, nnz_csr, pos,
+               (float *)out);
   return SLA_OK;
 }
 
