@@ -412,7 +412,8 @@ def wl_batched(args, dev, local):
     line["config"] = {"workload": "batched_cg_diffusion2d", "batch": B, "grid": [m, m],
                       "iterations_per_solve": iters // args.steps, "rtol": RTOL,
                       "forward_backward_ms": round(ms_fb / max(1, args.steps // 2), 2),
-                      "layout": "values [nnz][B], vectors [n][B]"}
+                      "layout": "vectors [n][B]; values [entry][B] in the order of a "
+                                "diagonal-offset view of the pattern (columns computed)"}
     line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
                                   "frac": round(iter_bytes * value / 1e9 / peak, 4)}
