@@ -106,6 +106,16 @@ def test_solver_config_scopes():
     assert _active_defaults() == {}
 
 
+def test_package_exposes_distributed_names_lazily():
+    """torch_sla.DSparseTensor / torch_sla.Partition are top-level names in
+    the reference (torch_sla/__init__.py); here they load on first access."""
+    from torch_sla_b200.distributed import DSparseTensor
+    assert T.DSparseTensor is DSparseTensor
+    assert T.Partition is PP.Partition
+    assert T.distributed.__name__ == "torch_sla_b200.distributed"
+    assert not hasattr(T, "no_such_name")
+
+
 def test_compute_on_cpu_tensors_raises():
     v, r, c, sh = P.poisson_2d_5pt(6)
     b = torch.ones(36, dtype=torch.float64)

@@ -25,7 +25,10 @@ __all__ = [
 
 
 def __getattr__(name):
+    # importlib rather than `from . import distributed`: the latter checks
+    # hasattr(package, "distributed") first, which re-enters this function.
     if name in ("DSparseTensor", "Partition", "distributed"):
-        from . import distributed
-        return distributed if name == "distributed" else getattr(distributed, name)
-    raise AttributeError(name)
+        import importlib
+        mod = importlib.import_module(__name__ + ".distributed")
+        return mod if name == "distributed" else getattr(mod, name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
