@@ -513,8 +513,66 @@ def wl_mrhs(args, dev, local):
     return line
 
 
+def wl_mixed(args, dev, local):
+    """Mixed-precision PCG (pytorch_solve(float32, mixed_precision=True)):
+    3-D 7-point 256^3, float32 matrix and Jacobi inverse, float64 vectors,
+    rtol 1e-8."""
+    from torch_sla_b200 import _lib as L
+    from torch_sla_b200 import problems as P
+    from torch_sla_b200.backends import pytorch_backend as PB
+    m = args.grid
+    n = m ** 3
+    v, r, c, sh = P.poisson_3d_7pt(m, dtype=torch.float32, device=dev)
+    b = P.rhs_normal(n, SEED, torch.float32).to(dev)
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    M = PB.Float32Preconditioner(PB.get_preconditioner(A, "jacobi"))
+    nnz = A.csr.nnz
+
+    def once():
+        return PB.pcg_solve_mixed_precision(A, b, atol=0.0, rtol=RTOL, maxiter=10000,
+                                            preconditioner=M).num_iters
+
+    for _ in range(args.warmup):
+        once()
+    L.profile_enable(True, 7)
+    l0 = L.launch_count()
+    ms, its, clk = timed(once, args.steps, dev, local)
+    launches = L.launch_count() - l0
+    ka_ms, ka_n = L.profile_read(0)
+    kb_ms, kb_n = L.profile_read(1)
+    L.profile_enable(False)
+    iters = sum(its)
+    value = iters / (ms / 1e3)
+    peak, _ = peaks()
+    # float32 matrix (8 B per entry with the int32 column), float64 vectors:
+    # 11 vector passes of 8 B plus two float32 inverse-diagonal passes
+    mat = matrix_bytes(nnz, n, V=4)
+    iter_bytes = mat + (11 * 8 + 2 * 4) * n
+    fm = sell_format(A.sell(), V=4)
+    line = base_line(args, "mixed-precision Jacobi-PCG iterations/s (256^3 7-point)", value,
+                     "iterations/s", ms, 1, dtype="f32 matrix / f64 vectors")
+    line["config"] = {"workload": "mixed_pcg_poisson3d_7pt", "grid": [m, m, m], "n": n,
+                      "nnz": nnz, "rtol": RTOL, "b": "N(0,1) seed 1, float32",
+                      "iterations_per_solve": iters // args.steps, "format": fm["format"],
+                      "l2": "inputs larger than L2; no flush", "parallelism": "single GPU"}
+    # K_A: matrix + r, p_old read, p_new, Ap written (8 B) + dinv (4 B)
+    line["roofline"] = roofline("mx_spmv_kernel", mat + (4 * 8 + 4) * n, ka_ms, ka_n,
+                                f"mx_spmv_kernel@mixed:{m}", fm["matrix_bytes"] + (4 * 8 + 4) * n)
+    line["roofline"]["update_kernel"] = {
+        "kernel": "mx_update_kernel", "avg_launch_ms": round(kb_ms / max(kb_n, 1), 5),
+        # r read/write, Ap, dinv; x two steps at odd iterations (mean 44 B per row)
+        "achieved": round(44 * n / (kb_ms / max(kb_n, 1) / 1e3) / 1e9, 1) if kb_n else None}
+    line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
+                                  "achieved_gbs": round(iter_bytes * value / 1e9, 1),
+                                  "frac": round(iter_bytes * value / 1e9 / peak, 4),
+                                  "bytes_formula": "8 nnz + 4 (N+1) + (11 * 8 + 2 * 4) N"}
+    line["gpu_launches"] = launches
+    line["clocks"] = clk
+    return line
+
+
 WORKLOADS = {"pcg7": wl_pcg7, "cg2d": wl_cg2d, "spmv": wl_spmv, "batched": wl_batched,
-             "bicgstab": wl_bicgstab, "mrhs": wl_mrhs}
+             "bicgstab": wl_bicgstab, "mrhs": wl_mrhs, "mixed": wl_mixed}
 
 
 # ------------------------------------------------------------ N GPUs
@@ -716,7 +774,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="pcg7",
-                    choices=["pcg7", "cg2d", "spmv", "batched", "bicgstab", "pcg27", "mrhs"])
+                    choices=["pcg7", "cg2d", "spmv", "batched", "bicgstab", "pcg27", "mrhs",
+                             "mixed"])
     ap.add_argument("--grid", type=int, default=M, help="grid edge per GPU (default 256)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

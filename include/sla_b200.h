@@ -100,8 +100,9 @@ typedef struct {
 
 /* ------------------------------------------------------------------ misc */
 /* Version of this interface; 2 since sla_sell_t carries n_cols, row_base
- * and the diagonal offsets. _lib.py refuses a library with another. */
-#define SLA_ABI_VERSION 2
+ * and the diagonal offsets, 3 since sla_pcg_mixed. _lib.py refuses a
+ * library with another. */
+#define SLA_ABI_VERSION 3
 int sla_abi_version(void);
 const char *sla_status_string(int status);
 /* Kernels this library has launched in this process (all devices). */
@@ -225,6 +226,30 @@ int sla_pcg_noalloc(int dtype, const sla_sell_t *A, const void *dinv,
                     const void *b, void *x, int x_is_guess, double atol,
                     double rtol, int64_t maxiter, int flags,
                     sla_solve_info_t *info, sla_stream_t stream);
+
+/* Mixed-precision PCG: pytorch_solve's float32 + mixed_precision branch
+ * (pytorch_backend.py:2278-2285) into pcg_solve_mixed_precision
+ * (:1176-1255). A is a float32 view; Ap = (double)(A (float)p) with float32
+ * accumulation; x (float64, [n]) and every vector, dot and update are
+ * float64; b is float32 or float64 (b_dtype). No start-of-iteration test:
+ * iteration i stops when ||r|| < max(atol, rtol*||b||) (||b|| = 0 counts
+ * as 1) after its r update, iterations = i + 1. p'Ap <= 0 stops before the
+ * update with SLA_BREAKDOWN (reason 5), iterations = i, the residual of the
+ * previous update and *pap_out = p'Ap (pap_out may be NULL). */
+enum {
+  SLA_MIXED_M_F32_NONE = 0,   /* z = (double)(float)r: 'none' run in float32
+                                 (pytorch_solve's M_f64 wrapper, :2281-2283) */
+  SLA_MIXED_M_F32_JACOBI = 1, /* z = (double)(dinv * (float)r), dinv float32 */
+  SLA_MIXED_M_F64_JACOBI = 2, /* z = dinv * r, dinv float64 (the default of
+                                 pcg_solve_mixed_precision, :1211-1216)      */
+  SLA_MIXED_M_F64_NONE = 3    /* z = r                                        */
+};
+int sla_pcg_mixed_workspace(int64_t n, size_t *bytes);
+int sla_pcg_mixed(const sla_sell_t *A, int precond, const void *dinv,
+                  int b_dtype, const void *b, double *x, int x_is_guess,
+                  double atol, double rtol, int64_t maxiter, void *workspace,
+                  size_t workspace_bytes, sla_solve_info_t *info,
+                  double *pap_out, sla_stream_t stream);
 
 /* Jacobi-PBiCGStab with torch-sla's half-step / full-step stopping tests and
  * 1e-30 breakdown guards (pbicgstab_solve, pytorch_backend.py:1508-1596). */

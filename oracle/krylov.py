@@ -81,6 +81,67 @@ def pcg(val, row, col, shape, b, *, x0=None, atol=1e-10, rtol=1e-6, maxiter=1000
     return x, maxiter, res, res < math.sqrt(tol_sq)
 
 
+def pcg_mixed(val, row, col, shape, b, *, x0=None, atol=1e-10, rtol=1e-6, maxiter=10000,
+              precond="jacobi"):
+    """pytorch_solve's float32 + mixed_precision branch (pytorch_backend.py:
+    2278-2285) into pcg_solve_mixed_precision (:1176-1255) with
+    MixedPrecisionMatrix (:1143-1173). precond 'jacobi' / 'none' is the
+    float32 preconditioner pytorch_solve wraps in M_f64 (r rounded to
+    float32, result widened); 'default' is the float64 Jacobi the function
+    builds when called without one (:1211-1216). Returns (x float64,
+    iterations, residual, converged, p'Ap of a p'Ap <= 0 stop or None)."""
+    n = shape[0]
+    A32 = csr(val.to(torch.float32), row, col, shape)
+
+    def mv(v):
+        return torch.mv(A32, v.to(torch.float32)).to(torch.float64)
+
+    if precond == "default":
+        d64 = torch.zeros(n, dtype=torch.float64)
+        m = row == col
+        d64.scatter_add_(0, row[m].to(torch.int64), val[m].to(torch.float64))
+        dinv64 = jacobi_inverse(d64, "eps")
+        apply_m = lambda v: dinv64 * v  # noqa: E731
+    else:
+        if precond == "none":
+            m32 = lambda v: v  # noqa: E731
+        else:
+            dinv32 = jacobi_inverse(diagonal(val.to(torch.float32), row, col, n), "eps")
+            m32 = lambda v: dinv32 * v  # noqa: E731
+        apply_m = lambda v: m32(v.to(torch.float32)).to(torch.float64)  # noqa: E731
+    if x0 is None:
+        x = torch.zeros(n, dtype=torch.float64)
+        r = b.to(torch.float64).clone()
+    else:
+        x = x0.to(torch.float64).clone()
+        r = b.to(torch.float64) - mv(x)
+    z = apply_m(r)
+    p = z.clone()
+    rz_old = torch.vdot(r, z)
+    b_norm = torch.norm(b.to(torch.float64))
+    if b_norm == 0:
+        b_norm = 1.0
+    tol = max(atol, rtol * b_norm)
+    residual = torch.norm(r).item()
+    for i in range(maxiter):
+        Ap = mv(p)
+        pAp = torch.vdot(p, Ap)
+        if pAp <= 0:
+            return x, i, residual, False, float(pAp)
+        alpha = rz_old / pAp
+        x.add_(p, alpha=alpha.item())
+        r.add_(Ap, alpha=-alpha.item())
+        residual = torch.norm(r).item()
+        if residual < tol:
+            return x, i + 1, residual, True, None
+        z = apply_m(r)
+        rz_new = torch.vdot(r, z)
+        beta = rz_new / rz_old
+        p.mul_(beta.item()).add_(z)
+        rz_old = rz_new
+    return x, maxiter, residual, False, None
+
+
 def csr_diagonal(A):
     """Diagonal of a torch CPU CSR matrix."""
     crow, colv, vals = A.crow_indices(), A.col_indices(), A.values()
@@ -277,12 +338,18 @@ def batched_pcg(val, row, col, shape, B, *, X0=None, atol=1e-10, rtol=1e-6, maxi
 
 # -------------------------------------------------------- adjoints
 def adjoint(val, row, col, shape, u, gradu, *, method="cg", atol=1e-10, rtol=1e-10,
-            maxiter=10000, precond="jacobi"):
+            maxiter=10000, precond="jacobi", mixed_precision=False):
     """SparseLinearSolvePyTorch.backward (linear_solve.py:303-324):
-    A^T gradb = gradu on the swapped pattern, gradval = -gradb[row]*u[col]."""
-    fn = pcg if method == "cg" else pbicgstab
+    A^T gradb = gradu on the swapped pattern, gradval = -gradb[row]*u[col].
+    With mixed_precision (float32 CG) the adjoint solve is the mixed PCG and
+    gradb is cast back to the value dtype (linear_solve.py:319-320)."""
+    if mixed_precision and method == "cg" and val.dtype == torch.float32:
+        fn = pcg_mixed
+    else:
+        fn = pcg if method == "cg" else pbicgstab
     gradb = fn(val, col, row, (shape[1], shape[0]), gradu, atol=atol, rtol=rtol,
                maxiter=maxiter, precond=precond)[0]
+    gradb = gradb.to(val.dtype)
     gradval = -gradb[row.to(torch.int64)] * u[col.to(torch.int64)]
     return gradval, gradb
 

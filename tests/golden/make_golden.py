@@ -111,6 +111,59 @@ def single(ref_path):
     bicg_case("bicg_ad2d12_maxiter", spec, prob.val, prob.row, prob.col, prob.shape, b, atol=0.0,
               rtol=1e-12, maxiter=5, preconditioner="jacobi")
 
+    # mixed-precision PCG: pytorch_solve(float32, mixed_precision=True) and
+    # pcg_solve_mixed_precision with its own float64 Jacobi default
+    def mixed_case(name, spec, v, r, c, shape, b, precond, **kw):
+        A = PB.CachedSparseMatrix(v, r, c, shape)
+        if precond is None:
+            M_f64 = None
+        else:
+            M = PB.get_preconditioner(A, precond)
+            M_f64 = lambda t, _M=M: _M(t.to(torch.float32)).to(torch.float64)  # noqa: E731
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            res = PB.pcg_solve_mixed_precision(A, b, preconditioner=M_f64, **kw)
+            x_ps = (PB.pytorch_solve(v, r, c, shape, b, method="cg", preconditioner=precond,
+                                     mixed_precision=True, **kw) if precond else None)
+        out[name] = {**spec, "b": b.clone(), "kw": dict(kw), "precond": precond,
+                     "x": res.x.clone(), "iters": int(res.num_iters),
+                     "residual": float(res.residual), "converged": bool(res.converged),
+                     "x_pytorch_solve": None if x_ps is None else x_ps.clone()}
+
+    v, r, c, sh = P.poisson_3d_7pt(12)
+    b = P.rhs_normal(sh[0], 1).float()
+    mixed_case("mixed_3d12_jacobi", gen("poisson_3d_7pt", 12, dtype=torch.float32), v.float(),
+               r, c, sh, b, "jacobi", atol=0.0, rtol=1e-8, maxiter=10000)
+    mixed_case("mixed_3d12_default", gen("poisson_3d_7pt", 12, dtype=torch.float32), v.float(),
+               r, c, sh, b, None, atol=0.0, rtol=1e-8, maxiter=10000)
+    v, r, c, sh = P.poisson_2d_5pt(20)
+    b = P.rhs_uniform_pm1(sh[0], 0).float()
+    mixed_case("mixed_2d20_none", gen("poisson_2d_5pt", 20, dtype=torch.float32), v.float(),
+               r, c, sh, b, "none", atol=1e-12, rtol=1e-9, maxiter=10000)
+    x0 = P.rhs_normal(sh[0], 5)
+    mixed_case("mixed_2d20_x0", gen("poisson_2d_5pt", 20, dtype=torch.float32), v.float(),
+               r, c, sh, b, "jacobi", x0=x0, atol=0.0, rtol=1e-9, maxiter=10000)
+    mixed_case("mixed_2d20_maxiter", gen("poisson_2d_5pt", 20, dtype=torch.float32), v.float(),
+               r, c, sh, b, "jacobi", atol=0.0, rtol=1e-9, maxiter=7)
+    # indefinite (Laplacian - shift*I, one negative eigenvalue): p'Ap <= 0
+    # stops the solve after an even (10) and an odd (9) number of iterations
+    for m, shift, seed in ((10, 0.3, 1), (12, 0.2, 0)):
+        v, r, c, sh = P.poisson_2d_5pt(m)
+        vi = v.float().clone()
+        vi[r == c] -= shift
+        mixed_case(f"mixed_indef_2d{m}", coo(vi, r, c, sh), vi, r, c, sh,
+                   P.rhs_normal(sh[0], seed).float(), "jacobi", atol=0.0, rtol=1e-9, maxiter=500)
+    v, r, c, sh = P.poisson_3d_7pt(6)
+    vg = v.float().clone().requires_grad_(True)
+    bg = P.rhs_normal(sh[0], 3).float().requires_grad_(True)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        x = spsolve(vg, r, c, sh, bg, backend="pytorch", method="cg", mixed_precision=True)
+    (x * x).sum().backward()
+    out["mixed_adj_3d6"] = {**gen("poisson_3d_7pt", 6, dtype=torch.float32),
+                            "b": bg.detach().clone(), "x": x.detach().clone(),
+                            "grad_val": vg.grad.clone(), "grad_b": bg.grad.clone()}
+
     # multi-RHS CG: pytorch_solve with a 2-D b ('none' -- its 'jacobi' closure
     # does not broadcast over columns) and batched_cg_solve's column Jacobi
     v, r, c, sh = P.poisson_2d_5pt(24)

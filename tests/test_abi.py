@@ -35,7 +35,7 @@ def test_binding_table_matches_header():
 
 def test_status_strings_and_version():
     lib = L.lib()
-    assert lib.sla_abi_version() == L.ABI_VERSION == 2
+    assert lib.sla_abi_version() == L.ABI_VERSION == 3
     assert lib.sla_status_string(L.SLA_ERR_UNSUPPORTED) == b"unsupported problem shape"
     assert lib.sla_status_string(L.SLA_NOT_CONVERGED).startswith(b"did not converge")
 
@@ -46,6 +46,9 @@ def test_invalid_arguments_are_rejected_before_any_device_work():
     assert lib.sla_pcg(1, None, None, None, None, 0, 0.0, 1e-8, 10, 0, None, 0,
                        ctypes.byref(info), None) == L.SLA_ERR_INVALID
     assert lib.sla_spmv(7, None, None, None, None) == L.SLA_ERR_INVALID
+    assert lib.sla_pcg_mixed(None, L.SLA_MIXED_M_F32_JACOBI, None, L.SLA_F32, None, None, 0,
+                             0.0, 1e-8, 10, None, 0, ctypes.byref(info), None,
+                             None) == L.SLA_ERR_INVALID
     assert lib.sla_csr_build(1, None, None, None, 10, 0, 5, None, None, None, None, None,
                              None, None, 0, None) == L.SLA_ERR_INVALID
     assert lib.sla_shard_cg(None, None, None, 1, None, None, None, None, None, 0.0, 0.0, 1, 10,

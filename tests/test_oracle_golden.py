@@ -40,6 +40,38 @@ def test_oracle_pcg_config1_full_size(golden):
     assert float(x.sum()) == pytest.approx(case["x_sum"], rel=1e-12)
 
 
+MIXED = ["mixed_3d12_jacobi", "mixed_3d12_default", "mixed_2d20_none", "mixed_2d20_x0",
+         "mixed_2d20_maxiter", "mixed_indef_2d10", "mixed_indef_2d12"]
+
+
+@pytest.mark.parametrize("name", MIXED)
+def test_oracle_mixed_pcg_matches_reference(golden, name):
+    """pcg_solve_mixed_precision / pytorch_solve(mixed_precision=True)."""
+    case = golden[name]
+    v, r, c, sh = case_inputs(case)
+    pc = case["precond"] or "default"
+    x, it, res, conv, pap = K.pcg_mixed(v, r, c, sh, case["b"], precond=pc, **case["kw"])
+    assert it == case["iters"]
+    assert conv == case["converged"]
+    assert x.dtype == torch.float64 and torch.equal(x, case["x"])
+    assert res == pytest.approx(case["residual"], rel=1e-12)
+    assert (pap is not None) == name.startswith("mixed_indef")
+    if case["x_pytorch_solve"] is not None:
+        assert torch.equal(case["x_pytorch_solve"], case["x"])
+
+
+def test_oracle_mixed_adjoint_matches_reference(golden):
+    """spsolve(float32, mixed_precision=True) forward and adjoint."""
+    case = golden["mixed_adj_3d6"]
+    v, r, c, sh = case_inputs(case)
+    x = K.pcg_mixed(v, r, c, sh, case["b"], atol=1e-10, rtol=1e-10, maxiter=10000)[0]
+    u = x.to(torch.float32)
+    assert torch.equal(u, case["x"])
+    gval, gb = K.adjoint(v, r, c, sh, u, 2 * u, method="cg", mixed_precision=True)
+    assert gb.dtype == torch.float32 and torch.equal(gb, case["grad_b"])
+    assert torch.equal(gval, case["grad_val"])
+
+
 @pytest.mark.parametrize("name", ["bicg_cd3d10_jacobi", "bicg_ad2d12_none", "bicg_ad2d12_maxiter"])
 def test_oracle_bicgstab_matches_reference(golden, name):
     case = golden[name]

@@ -22,13 +22,15 @@ SLA_ERR_INVALID, SLA_ERR_CUDA, SLA_ERR_NCCL = -1, -2, -3
 SLA_ERR_TIMEOUT, SLA_ERR_UNSUPPORTED, SLA_ERR_WORKSPACE, SLA_ERR_INDEX = -4, -5, -6, -7
 SLA_JACOBI_EPS, SLA_JACOBI_CLAMP, SLA_JACOBI_NONZERO = 0, 1, 2
 SLA_PCG_AUTO, SLA_PCG_STREAMED, SLA_PCG_PERSISTENT = 0, 1, 2
+SLA_MIXED_M_F32_NONE, SLA_MIXED_M_F32_JACOBI, SLA_MIXED_M_F64_JACOBI, SLA_MIXED_M_F64_NONE = (
+    0, 1, 2, 3)
 
 c_i32, c_i64, c_dbl, c_ptr, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_double,
                                     ctypes.c_void_p, ctypes.c_size_t)
 
 
 MAX_DIAGS = 32  # SLA_MAX_DIAGS
-ABI_VERSION = 2  # SLA_ABI_VERSION
+ABI_VERSION = 3  # SLA_ABI_VERSION
 
 
 class SellView(ctypes.Structure):
@@ -85,6 +87,10 @@ _SIGNATURES = {
     "sla_pcg_noalloc": (ctypes.c_int, [ctypes.c_int, _P(SellView), c_ptr, c_ptr, c_ptr,
                                        ctypes.c_int, c_dbl, c_dbl, c_i64, ctypes.c_int,
                                        _P(SolveInfo), c_ptr]),
+    "sla_pcg_mixed_workspace": (ctypes.c_int, [c_i64, _P(c_sz)]),
+    "sla_pcg_mixed": (ctypes.c_int, [_P(SellView), ctypes.c_int, c_ptr, ctypes.c_int, c_ptr,
+                                     c_ptr, ctypes.c_int, c_dbl, c_dbl, c_i64, c_ptr, c_sz,
+                                     _P(SolveInfo), _P(c_dbl), c_ptr]),
     "sla_bicgstab_workspace": (ctypes.c_int, [ctypes.c_int, c_i64, _P(c_sz)]),
     "sla_bicgstab": (ctypes.c_int, [ctypes.c_int, _P(SellView), c_ptr, c_ptr, c_ptr,
                                     ctypes.c_int, c_dbl, c_dbl, c_i64, c_ptr, c_sz,

@@ -22,6 +22,7 @@ __all__ = [
     "SolveResult", "CachedSparseMatrix", "JacobiPreconditioner", "IdentityPreconditioner",
     "jacobi_preconditioner", "get_preconditioner", "pcg_solve_optimized", "pcg_solve_fused",
     "pbicgstab_solve", "pytorch_solve", "batched_cg_same_pattern", "last_solve_info",
+    "MixedPrecisionMatrix", "pcg_solve_mixed_precision",
 ]
 
 
@@ -115,9 +116,9 @@ def get_preconditioner(A: CachedSparseMatrix, name: str = "jacobi",
                        mixed_precision: bool = False, method: str = "cg"):
     """'jacobi' and 'none' (pytorch_backend.py:855-929). 'auto' resolves to
     'jacobi', the only preconditioner of the B200 path."""
-    if mixed_precision:
-        raise NotImplementedError("torch_sla_b200: mixed-precision preconditioning is not "
-                                  "part of the B200 path")
+    if mixed_precision and A.dtype == torch.float64:
+        raise NotImplementedError("torch_sla_b200: float32 application of a float64 "
+                                  "preconditioner is not part of the B200 path")
     if name is None or name == "none":
         return IdentityPreconditioner()
     if name in ("jacobi", "auto"):
@@ -180,6 +181,102 @@ def pcg_solve_fused(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int
     return pcg_solve_optimized(A, b, x0=x0, atol=atol, rtol=rtol, maxiter=maxiter, preconditioner=M)
 
 
+# ------------------------------------------------------ mixed-precision PCG
+class MixedPrecisionMatrix:
+    """float32 matrix with float64 input and output (pytorch_backend.py:1143-1173):
+    x is rounded to float32, multiplied in float32 and the result widened."""
+
+    def __init__(self, val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int],
+                 cached: Optional[CachedSparseMatrix] = None):
+        self.shape = (int(shape[0]), int(shape[1]))
+        self.device = val.device
+        self.n = self.shape[0]
+        self.val, self.row, self.col = val, row, col
+        # a float32 CachedSparseMatrix of the same COO is reused as is
+        self.A32 = (cached if cached is not None and cached.dtype == torch.float32
+                    else CachedSparseMatrix(val.to(torch.float32), row, col, self.shape))
+        self._dinv64 = None
+
+    def matvec(self, x_f64: Tensor) -> Tensor:
+        return self.A32.matvec(x_f64.to(torch.float32)).to(torch.float64)
+
+    def jacobi_inverse64(self) -> Tensor:
+        """1/d with |d| < 100 eps(float64) -> 1, d the float64 sum of the
+        diagonal entries (pytorch_backend.py:1156-1158, 1211-1216)."""
+        if self._dinv64 is None:
+            A64 = CachedSparseMatrix(self.val.to(torch.float64), self.row, self.col, self.shape)
+            self._dinv64 = A64.csr.jacobi_inverse(L.SLA_JACOBI_EPS)
+        return self._dinv64
+
+
+class Float32Preconditioner:
+    """pytorch_solve's M_f64 (pytorch_backend.py:2281-2283): applies a
+    float32 preconditioner to r rounded to float32 and widens the result."""
+
+    def __init__(self, inner):
+        self.inner = inner
+
+    def __call__(self, r: Tensor) -> Tensor:
+        return self.inner(r.to(torch.float32)).to(torch.float64)
+
+
+def _mixed_mode(preconditioner, Am: MixedPrecisionMatrix):
+    """(SLA_MIXED_M_* mode, inverse diagonal) of a preconditioner argument."""
+    if preconditioner is None:
+        return L.SLA_MIXED_M_F64_JACOBI, Am.jacobi_inverse64()
+    if isinstance(preconditioner, Float32Preconditioner):
+        inner = preconditioner.inner
+        if isinstance(inner, IdentityPreconditioner):
+            return L.SLA_MIXED_M_F32_NONE, None
+        if isinstance(inner, JacobiPreconditioner) and inner.dinv.dtype == torch.float32:
+            return L.SLA_MIXED_M_F32_JACOBI, inner.dinv
+    elif isinstance(preconditioner, IdentityPreconditioner):
+        return L.SLA_MIXED_M_F64_NONE, None
+    elif isinstance(preconditioner, JacobiPreconditioner):
+        # dinv * r with float64 r promotes to float64: the widened inverse
+        return L.SLA_MIXED_M_F64_JACOBI, preconditioner.dinv.to(torch.float64)
+    raise NotImplementedError("torch_sla_b200: mixed-precision PCG accepts the preconditioners "
+                              "built by get_preconditioner ('jacobi', 'none') only")
+
+
+def pcg_solve_mixed_precision(A: CachedSparseMatrix, b: Tensor, x0: Optional[Tensor] = None,
+                              atol: float = 1e-10, rtol: float = 1e-6, maxiter: int = 10000,
+                              preconditioner: Callable[[Tensor], Tensor] = None) -> SolveResult:
+    """Mixed-precision PCG (pytorch_backend.py:1176-1255): float32 SpMV,
+    float64 vectors, dots and updates; stops when ||r|| < max(atol, rtol||b||)
+    after an update; p'Ap <= 0 stops with a warning. x is float64."""
+    L.require_cuda(b, x0)
+    if b.dim() != 1 or b.shape[0] != A.n:
+        raise ValueError(f"torch_sla_b200: b must have shape [{A.n}]")
+    Am = MixedPrecisionMatrix(A.val, A.row, A.col, A.shape, cached=A)
+    mode, dinv = _mixed_mode(preconditioner, Am)
+    if b.dtype not in (torch.float32, torch.float64):
+        b = b.to(torch.float64)
+    b = b.contiguous()
+    lib = L.lib()
+    need = ctypes.c_size_t(0)
+    L.check("sla_pcg_mixed_workspace", lib.sla_pcg_mixed_workspace(A.n, ctypes.byref(need)))
+    ws = L.workspace(need.value, A.device)
+    x = (x0.to(torch.float64).clone().contiguous() if x0 is not None
+         else torch.empty(A.n, dtype=torch.float64, device=A.device))
+    info = L.SolveInfo()
+    pap = ctypes.c_double(0.0)
+    st = lib.sla_pcg_mixed(Am.A32.sell().ref(), int(mode), L.ptr(dinv), L.dtype_code(b.dtype),
+                           L.ptr(b), L.ptr(x), int(x0 is not None), float(atol), float(rtol),
+                           int(maxiter), L.ptr(ws), ws.numel(), ctypes.byref(info),
+                           ctypes.byref(pap), L.stream_handle(A.device))
+    L.check("sla_pcg_mixed", st)
+    _record("pcg_mixed", info)
+    if info.status == L.SLA_BREAKDOWN:
+        warnings.warn(f"PCG: Matrix not positive definite (p'Ap = {pap.value:.2e})")
+        return SolveResult(x, int(info.iterations), float(info.residual), False)
+    converged = info.status == L.SLA_OK
+    if not converged:
+        warnings.warn(f"Mixed PCG did not converge in {maxiter} iterations "
+                      f"(residual={info.residual:.2e})")
+    return SolveResult(x, int(info.iterations), float(info.residual), converged)
+
+
 def _bicgstab_core(A: CachedSparseMatrix, b: Tensor, x0, dinv, atol, rtol, maxiter):
     L.require_cuda(b, x0)
     b = b.to(A.dtype).contiguous()
@@ -225,8 +322,10 @@ def pytorch_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int],
             return batched_pcg_solve(A_mat, b, X0=x0, atol=atol, rtol=rtol, maxiter=maxiter,
                                      preconditioner=M).X
         if mixed_precision and val.dtype == torch.float32:
-            raise NotImplementedError("torch_sla_b200: mixed-precision PCG is not part of the "
-                                      "B200 path")
+            A = CachedSparseMatrix(val, row, col, shape)
+            M = Float32Preconditioner(get_preconditioner(A, preconditioner))
+            return pcg_solve_mixed_precision(A, b, x0=x0, atol=atol, rtol=rtol, maxiter=maxiter,
+                                             preconditioner=M).x
         return pcg_solve_fused(val, row, col, shape, b, x0=x0, atol=atol, rtol=rtol,
                                maxiter=maxiter, preconditioner=preconditioner).x
     if method == "bicgstab":
