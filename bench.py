@@ -363,12 +363,17 @@ def wl_spmv(args, dev, local):
                                           "algorithmic_bytes": alg, "format": fm["format"],
                                           "format_bytes": fb,
                                           "format_frac": round(fb / sec / 1e9 / peak, 4),
-                                          "clocks": clk}
+                                          "clocks": clk, "_ms": ms, "_reps": reps}
         del csr, sell, x, y
     line = base_line(args, "SpMV HBM GB/s (256^3 7-point, fp64)", res["f64"]["achieved_gbs"],
                      "GB/s", res["f64"]["us_per_spmv"] / 1e3 * args.steps, 1)
+    f64 = res["f64"]
+    line["roofline"] = roofline("spmv_kernel", f64["algorithmic_bytes"], f64.pop("_ms"),
+                                f64.pop("_reps"), f"spmv_kernel@spmv:{m}", f64["format_bytes"])
+    res["f32"].pop("_ms"), res["f32"].pop("_reps")
     line["config"] = {"workload": "spmv_poisson3d_7pt", "grid": [m, m, m], "sweep": res,
                       "l2": "inputs larger than L2"}
+    line["clocks"] = f64["clocks"]
     return line
 
 
@@ -507,8 +512,13 @@ def wl_mrhs(args, dev, local):
                                   "achieved_gbs": round(iter_bytes * value / K / 1e9, 1),
                                   "frac": round(iter_bytes * value / K / 1e9 / peak, 4),
                                   "bytes_formula": "12 nnz + 4 (N+1) + 13 * 16 * 8 N"}
-    line["roofline"] = roofline("mrhs_spmv_kernel", nnz * 12 + 4 * (n + 1) + 5 * K * 8 * n + 8 * n,
-                                ka_ms, ka_n, "mrhs_spmv_kernel@mrhs:128x16")
+    # K_A reads the matrix and the search directions P (formed by
+    # mrhs_pform_kernel), writes AP
+    sell = A.sell()
+    fm = sell_format(sell)
+    line["roofline"] = roofline("mrhs_spmv_kernel", nnz * 12 + 4 * (n + 1) + 2 * K * 8 * n,
+                                ka_ms, ka_n, "mrhs_spmv_kernel@mrhs:128x16",
+                                fm["matrix_bytes"] + 2 * K * 8 * n)
     line["clocks"] = clk
     return line
 

@@ -22,7 +22,8 @@ __all__ = [
     "SolveResult", "CachedSparseMatrix", "JacobiPreconditioner", "IdentityPreconditioner",
     "jacobi_preconditioner", "get_preconditioner", "pcg_solve_optimized", "pcg_solve_fused",
     "pbicgstab_solve", "pytorch_solve", "batched_cg_same_pattern", "last_solve_info",
-    "MixedPrecisionMatrix", "pcg_solve_mixed_precision",
+    "MixedPrecisionMatrix", "pcg_solve_mixed_precision", "sparse_matvec", "extract_diagonal",
+    "pcg_solve", "cg_solve", "bicgstab_solve", "batched_pcg_solve", "batched_cg_solve",
 ]
 
 
@@ -342,6 +343,50 @@ def pytorch_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int],
     raise ValueError(f"Unknown method: {method}. Available: cg, bicgstab, gmres, minres, lsqr, lsmr")
 
 
+# ------------------------------------------------- legacy / helper entries
+def sparse_matvec(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int],
+                  x: Tensor) -> Tensor:
+    """y = A @ x from COO, values taken in x's dtype (pytorch_backend.py:2153-2158)."""
+    L.require_cuda(val, x)
+    return DeviceCSR(val.to(x.dtype), row, col, tuple(shape)).matvec(x)
+
+
+def extract_diagonal(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int]) -> Tensor:
+    """Sum of the diagonal COO entries, length min(shape) (pytorch_backend.py:2161-2167)."""
+    L.require_cuda(val)
+    n = min(int(shape[0]), int(shape[1]))
+    return DeviceCSR(val, row, col, tuple(shape)).diagonal()[:n]
+
+
+def pcg_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int], b: Tensor,
+              x0: Optional[Tensor] = None, atol: float = 1e-10, rtol: float = 1e-6,
+              maxiter: int = 10000, M_inv: Optional[Tensor] = None,
+              callback: Optional[Callable] = None) -> Tuple[Tensor, int, float]:
+    """Legacy interface (pytorch_backend.py:2170-2186): Jacobi PCG; M_inv and
+    callback are accepted and unused, as in torch-sla."""
+    res = pcg_solve_fused(val, row, col, shape, b, x0=x0, atol=atol, rtol=rtol, maxiter=maxiter,
+                          preconditioner="jacobi")
+    return res.x, res.num_iters, res.residual
+
+
+def cg_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int], b: Tensor,
+             x0: Optional[Tensor] = None, atol: float = 1e-10, rtol: float = 1e-6,
+             maxiter: int = 10000, callback: Optional[Callable] = None) -> Tuple[Tensor, int, float]:
+    """pytorch_backend.py:2189-2204 ('auto' preconditioner, which is Jacobi here)."""
+    res = pcg_solve_fused(val, row, col, shape, b, x0=x0, atol=atol, rtol=rtol, maxiter=maxiter,
+                          preconditioner="auto")
+    return res.x, res.num_iters, res.residual
+
+
+def bicgstab_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int], b: Tensor,
+                   x0: Optional[Tensor] = None, atol: float = 1e-10, rtol: float = 1e-6,
+                   maxiter: int = 10000,
+                   callback: Optional[Callable] = None) -> Tuple[Tensor, int, float]:
+    """pytorch_backend.py:2207-2221 ('auto' preconditioner, which is Jacobi here)."""
+    return pbicgstab_solve(val, row, col, shape, b, x0=x0, atol=atol, rtol=rtol, maxiter=maxiter,
+                           preconditioner="auto")
+
+
 # ----------------------------------------------------------- multi-RHS CG
 class BatchSolveResult(NamedTuple):
     """Result of the multi-RHS solve (pytorch_backend.py:2344-2349)."""
@@ -413,6 +458,18 @@ def batched_pcg_solve(A: CachedSparseMatrix, B: Tensor, X0: Optional[Tensor] = N
         n_failed = int((~converged).sum().item())
         warnings.warn(f"Batched PCG: {n_failed}/{K} RHS did not converge in {maxiter} iterations")
     return BatchSolveResult(X, iters.to(torch.int32).to(A.device), residuals, converged)
+
+
+def batched_cg_solve(val: Tensor, row: Tensor, col: Tensor, shape: Tuple[int, int], B: Tensor,
+                     X0: Optional[Tensor] = None, atol: float = 1e-10, rtol: float = 1e-6,
+                     maxiter: int = 10000, preconditioner: str = "jacobi",
+                     check_interval: int = 50) -> BatchSolveResult:
+    """Multi-RHS CG from COO (pytorch_backend.py:2507-2572). 'jacobi' is
+    1/diag with infinite entries set to 1, applied column by column."""
+    A = CachedSparseMatrix(val, row, col, shape)
+    M = None if preconditioner == "jacobi" else get_preconditioner(A, preconditioner)
+    return batched_pcg_solve(A, B, X0=X0, atol=atol, rtol=rtol, maxiter=maxiter,
+                             preconditioner=M, check_interval=check_interval)
 
 
 # ----------------------------------------------------------------- batched

@@ -147,6 +147,9 @@ template <> __device__ __forceinline__ float sub_rn(float a, float b) { return _
 template <typename U> __device__ __forceinline__ U ld_stream(const U *p) { return __ldcs(p); }
 // L1-bypassing loads for data written by other blocks of the same launch.
 template <typename U> __device__ __forceinline__ U ld_l2(const U *p) { return __ldcg(p); }
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
 
 // Deterministic block sum of NV doubles (fixed shuffle + fixed smem order).
 // Every thread returns with v[] holding the block total. smem: NV*BS/32.

@@ -141,8 +141,53 @@ __global__ void zero_kernel(T *__restrict__ x, int64_t n) {
   for (; i < n; i += stride) x[i] = T(0);
 }
 
-// P = Z + beta P (pytorch_backend.py:2487) formed inside the gather, AP = A P,
-// per-column (P, AP); the last block forms alpha with (P, AP) <= 0 -> 1.
+// P = Z + beta P (pytorch_backend.py:2487) is formed once per row by
+// mrhs_pform_kernel and K_A gathers it (SLA_MRHS_SPLIT 1), or K_A forms it
+// inside the gather, every row recomputing it for each of its entries
+// (SLA_MRHS_SPLIT 0). Measured on 128^3 7-point x 16 columns fp64: the
+// split costs one more [n][K] pass but halves the loads per gathered entry,
+// K_A 366 -> 184 us, 26.5 k -> 29.0 k column-iterations/s; 7-entry load
+// batches on the split gather: 28.6 k.
+#ifndef SLA_MRHS_SPLIT
+#define SLA_MRHS_SPLIT 1
+#endif
+constexpr bool kMrhsSplit = SLA_MRHS_SPLIT != 0;
+
+template <typename T, bool PREC, int VEC>
+__device__ __forceinline__ Pack<T, VEC> mrhs_p(const T *__restrict__ r, const T *__restrict__ dinv,
+                                               const T *__restrict__ p_old, int64_t c, int32_t ci,
+                                               const T (&beta)[VEC]) {
+  const Pack<T, VEC> rv = vload<T, VEC, kLoadRO>(r + c);
+  const Pack<T, VEC> po = vload<T, VEC, kLoadRO>(p_old + c);
+  const T d = PREC ? __ldg(dinv + ci) : T(1);
+  Pack<T, VEC> out;
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) {
+    const T z = PREC ? mul_rn(d, rv.v[u]) : rv.v[u];
+    out.v[u] = add_rn(z, mul_rn(beta[u], po.v[u]));
+  }
+  return out;
+}
+
+template <typename T, bool PREC, int VEC>
+__global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
+mrhs_pform_kernel(int64_t n, int K, const T *__restrict__ r, const T *__restrict__ dinv,
+                  const T *__restrict__ p_old, T *__restrict__ p_new, const MrhsState *st,
+                  MrhsCols cs) {
+  if (*(volatile const int *)&st->done) return;
+  const BatchLane ln(K, VEC);
+  T beta[VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) beta[u] = (T)cs.beta[ln.m0 + u];
+  for (int64_t row = (int64_t)blockIdx.x * ln.rpb + ln.rl; row < n;
+       row += (int64_t)gridDim.x * ln.rpb) {
+    const int64_t o = row * K + ln.m0;
+    vstore(p_new + o, mrhs_p<T, PREC, VEC>(r, dinv, p_old, o, (int32_t)row, beta));
+  }
+}
+
+// AP = A P, per-column (P, AP); the last block forms alpha with
+// (P, AP) <= 0 -> 1.
 template <typename T, bool PREC, int VEC, int RB, typename M>
 __global__ void __launch_bounds__(VEC == 1 ? 1024 : kBatchThreads, VEC == 1 ? 1 : kBatchMinBlocks)
 mrhs_spmv_kernel(M mat, int64_t n, int K, const T *__restrict__ r,
@@ -164,31 +209,20 @@ mrhs_spmv_kernel(M mat, int64_t n, int K, const T *__restrict__ r,
         row,
         [&](int32_t ci) {
           const int64_t c = (int64_t)ci * K + ln.m0;
-          const Pack<T, VEC> rv = vload<T, VEC, kLoadRO>(r + c);
-          const Pack<T, VEC> po = vload<T, VEC, kLoadRO>(p_old + c);
-          const T d = PREC ? __ldg(dinv + ci) : T(1);
-          Pack<T, VEC> out;
-#pragma unroll
-          for (int u = 0; u < VEC; ++u) {
-            const T z = PREC ? mul_rn(d, rv.v[u]) : rv.v[u];
-            out.v[u] = add_rn(z, mul_rn(beta[u], po.v[u]));
-          }
-          return out;
+          if constexpr (kMrhsSplit) return vload<T, VEC, kLoadRO>(p_new + c);
+          else return mrhs_p<T, PREC, VEC>(r, dinv, p_old, c, ci, beta);
         },
         sum);
     const int64_t o = row * K + ln.m0;
-    const Pack<T, VEC> rv = vload<T, VEC, kLoadRO>(r + o);
-    const Pack<T, VEC> po = vload<T, VEC, kLoadRO>(p_old + o);
-    const T d = PREC ? __ldg(dinv + row) : T(1);
     Pack<T, VEC> pn, ap;
+    if constexpr (kMrhsSplit) pn = vload<T, VEC, kLoadRO>(p_new + o);
+    else pn = mrhs_p<T, PREC, VEC>(r, dinv, p_old, o, (int32_t)row, beta);
 #pragma unroll
     for (int u = 0; u < VEC; ++u) {
-      const T z = PREC ? mul_rn(d, rv.v[u]) : rv.v[u];
-      pn.v[u] = add_rn(z, mul_rn(beta[u], po.v[u]));
       ap.v[u] = sum[u];
       acc[0][u] += (double)pn.v[u] * (double)sum[u];
     }
-    vstore(p_new + o, pn);
+    if constexpr (!kMrhsSplit) vstore(p_new + o, pn);
     vstore(Ap + o, ap);
   }
   if (!batch_reduce<1, VEC>(acc, K, smem, partials, &st->counter[1])) return;
@@ -301,9 +335,12 @@ static int mrhs_loop(M mat, int64_t n, int K, const T *dinv, T *x, T *r, T *pA, 
   const size_t sm1 = batch_smem(1, TB, VEC), sm2 = batch_smem(2, TB, VEC);
   const int G1 = occupancy_grid((const void *)spmv, TB, sm1);
   const int G2 = occupancy_grid((const void *)upd, TB, sm2);
+  auto pform = mrhs_pform_kernel<T, PREC, VEC>;
+  const int G0 = kMrhsSplit ? occupancy_grid((const void *)pform, TB, 0) : 0;
   return run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
     T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
     cudaEvent_t ev;
+    if (kMrhsSplit) SLA_LAUNCH(pform, G0, TB, 0, s, n, K, r, dinv, p_old, p_new, st, cs);
     profiler().begin(0, it, s, &ev);
     SLA_LAUNCH(spmv, G1, TB, sm1, s, mat, n, K, r, dinv, p_old, p_new, Ap, st, cs, part[1]);
     profiler().end(0, s, ev);
