@@ -203,6 +203,7 @@ def wl_pcg7(args, dev, local):
     launches = L.launch_count() - l0
     ka_ms, ka_n = L.profile_read(0)
     kb_ms, kb_n = L.profile_read(1)
+    kp_ms, kp_n = L.profile_read(2)
     L.profile_enable(False)
     iters = sum(its)
     value = iters / (ms / 1e3)
@@ -216,12 +217,19 @@ def wl_pcg7(args, dev, local):
                       "format": fm["format"],
                       "l2": "inputs larger than L2 (0.9-1.4 GB matrix); no flush",
                       "parallelism": "single GPU"}
-    line["roofline"] = roofline("cg_spmv_kernel", matrix_bytes(nnz, n) + 5 * 8 * n, ka_ms, ka_n,
-                                f"cg_spmv_kernel@pcg7:{m}", fm["matrix_bytes"] + 5 * 8 * n)
+    # K_A: the SpMV over the search direction p (formed by cg_pform_kernel):
+    # matrix + p read once + Ap written
+    line["roofline"] = roofline("cg_spmv_split_kernel", matrix_bytes(nnz, n) + 2 * 8 * n, ka_ms,
+                                ka_n, f"cg_spmv_split_kernel@pcg7:{m}",
+                                fm["matrix_bytes"] + 2 * 8 * n)
     line["roofline"]["update_kernel"] = {
         "kernel": "cg_update_kernel", "avg_launch_ms": round(kb_ms / max(kb_n, 1), 5),
         # 4 vector passes at even, 8 at odd iterations (x updated two steps at a time)
         "achieved": round(6 * 8 * n / (kb_ms / max(kb_n, 1) / 1e3) / 1e9, 1) if kb_n else None}
+    line["roofline"]["pform_kernel"] = {
+        "kernel": "cg_pform_kernel", "avg_launch_ms": round(kp_ms / max(kp_n, 1), 5),
+        # r, dinv, p_old read, p written
+        "achieved": round(4 * 8 * n / (kp_ms / max(kp_n, 1) / 1e3) / 1e9, 1) if kp_n else None}
     line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
                                   "frac": round(iter_bytes * value / 1e9 / peak, 4),

@@ -3,14 +3,17 @@
 // at the start of iteration i stop if (r,r) < max(atol, rtol*||b||)^2 and
 // report i iterations.
 //
-// Streamed path, two kernels per iteration (large systems):
-//   K_A  p_new = p_old*beta + M^{-1} r    (computed inside the SpMV gather)
-//        Ap = A p_new, write p_new and Ap, partial (p_new, Ap)
+// Streamed path (large systems), per iteration:
+//   K_P  p_new = p_old*beta + M^{-1} r             (streaming pass)
+//   K_A  Ap = A p_new, partial (p_new, Ap)
 //        last block: alpha = (r,z) / (p,Ap)
 //   K_B  x += alpha p ; r -= alpha Ap ; partial (r,r), (r, M^{-1} r)
 //        last block: beta, convergence / maxiter bookkeeping
-// HBM per iteration: matrix + 12 vector passes (r, dinv, p_old read and
-// p_new, Ap written by K_A; x, p, r, Ap, dinv read and x, r written by K_B).
+// (or, with SLA_CG_SPLIT 0, K_P fused into K_A's gather). HBM per
+// iteration: matrix + 12 vector passes on average (r, dinv, p_old read and
+// p_new written by K_P; p_new read and Ap written by K_A; r, Ap, dinv read
+// and r written by K_B, plus x, p, p_prev read and x written at every
+// other iteration).
 // The scalar recurrences stay on the device; the host polls a pinned flag
 // once per chunk of iterations with one chunk in flight.
 //
@@ -144,6 +147,113 @@ cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
 template <typename T> struct Pair;
 template <> struct Pair<double> { using type = double2; };
 template <> struct Pair<float> { using type = float2; };
+
+// Split K_A (SLA_CG_SPLIT 1, the default): p_new = p_old*beta + M^{-1} r is
+// formed once per row by cg_pform_kernel (a streaming pass) and K_A is a
+// plain SpMV over p_new with the L2 prefetch of the next slice's values;
+// same arithmetic, same row sums and dot order as the fused K_A
+// (SLA_CG_SPLIT 0), which forms p inside the gather, once per entry.
+// Measured on 256^3 7-point fp64: fused K_A 284.5 us; split 265.7 us for
+// both kernels (one more vector pass, but the SpMV streams at ~7 TB/s
+// once its gathers are a single vector): 2400 -> 2535 it/s.
+#ifndef SLA_CG_SPLIT
+#define SLA_CG_SPLIT 1
+#endif
+constexpr bool kCgSplit = SLA_CG_SPLIT != 0;
+
+template <typename T, bool PREC, bool VEC>
+__global__ void __launch_bounds__(kBlock)
+cg_pform_kernel(int64_t n, const T *__restrict__ r, const T *__restrict__ dinv,
+                const T *__restrict__ p_old, T *__restrict__ p_new, const CgState *st) {
+  if (*(volatile const int *)&st->done) return;
+  const T beta = (T)st->beta;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  auto pf = [&](T pc, T rc, T dc) { return add_rn(mul_rn(pc, beta), PREC ? mul_rn(dc, rc) : rc); };
+  int64_t tail = 0;
+  if (VEC) {
+    using V = typename Pair<T>::type;
+    const int64_t n2 = n >> 1;
+    for (int64_t i = tid; i < n2; i += stride) {
+      const V rv = __ldcs((const V *)r + i), pv = __ldcs((const V *)p_old + i);
+      V dv = rv;
+      if (PREC) dv = __ldg((const V *)dinv + i);
+      V out;
+      out.x = pf(pv.x, rv.x, dv.x);
+      out.y = pf(pv.y, rv.y, dv.y);
+      ((V *)p_new)[i] = out;
+    }
+    tail = n2 * 2;
+  }
+  for (int64_t i = tail + tid; i < n; i += stride)
+    p_new[i] = pf(p_old[i], r[i], PREC ? dinv[i] : T(0));
+}
+
+template <typename T, int WS>
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
+cg_spmv_split_kernel(Sell<T> A, const T *__restrict__ p, T *__restrict__ Ap, CgState *st,
+                     double *partials) {
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->done) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  PlainGather<T> g{p};
+  double acc[1] = {0.0};
+  for_each_slice<WS, true>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
+    int64_t row = s * 32 + lane;
+    if (row < A.n_slots) {
+      const T pn = __ldg(p + row);
+      Ap[row] = sum;
+      acc[0] += (double)pn * (double)sum;
+    }
+  });
+  if (last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem) && threadIdx.x == 0) {
+    st->pAp = acc[0];
+    st->alpha = st->rz / acc[0];
+  }
+}
+
+// K_A of one iteration, fused or split.
+template <typename T, bool PREC, int WS>
+struct KaLaunch {
+  int grid = 0, grid_p = 0;
+  bool vec = false;
+  void init(int64_t n, const void *r, const void *dinv, const void *pA, const void *pB) {
+    if (kCgSplit) {
+      grid = occupancy_grid((const void *)cg_spmv_split_kernel<T, WS>);
+      grid_p = occupancy_grid((const void *)cg_pform_kernel<T, PREC, true>);
+      vec = aligned16(r, pA, pB) && (!PREC || aligned16(dinv));
+    } else {
+      grid = occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS>);
+    }
+  }
+  // prof: time the launches with the sampling profiler (class 0 the SpMV,
+  // class 2 the p-forming pass).
+  int run(int64_t it, bool prof, const Sell<T> &A, const T *r, const T *dinv, const T *p_old,
+          T *p_new, T *Ap, CgState *st, double *part, cudaStream_t s) const {
+    cudaEvent_t ev;
+    if (kCgSplit) {
+      const int64_t n = A.n_slots;
+      if (prof) profiler().begin(2, it, s, &ev);
+      if (vec)
+        SLA_LAUNCH((cg_pform_kernel<T, PREC, true>), grid_p, kBlock, 0, s, n, r, dinv, p_old, p_new, st);
+      else
+        SLA_LAUNCH((cg_pform_kernel<T, PREC, false>), grid_p, kBlock, 0, s, n, r, dinv, p_old, p_new, st);
+      if (prof) profiler().end(2, s, ev);
+      if (prof) profiler().begin(0, it, s, &ev);
+      SLA_LAUNCH((cg_spmv_split_kernel<T, WS>), grid, kBlock, 0, s, A, (const T *)p_new, Ap, st, part);
+      if (prof) profiler().end(0, s, ev);
+    } else {
+      if (prof) profiler().begin(0, it, s, &ev);
+      SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS>), grid, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap,
+                 st, part);
+      if (prof) profiler().end(0, s, ev);
+    }
+    return SLA_OK;
+  }
+};
 
 // r -= alpha Ap (torch addcmul_ rounding) and the two dots.
 template <typename T, bool PREC>
@@ -373,16 +483,14 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
     g_launches.fetch_add(1, std::memory_order_relaxed);
     profiler().end(0, s, ev);
   } else {
-    const int grid_a = occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS>);
+    KaLaunch<T, PREC, WS> ka;
+    ka.init(n, r, dinv, pA, pB);
     const bool vec = aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv));
     SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
       T *p_old = (it & 1) ? pB : pA;
       T *p_new = (it & 1) ? pA : pB;
       cudaEvent_t ev;
-      profiler().begin(0, it, s, &ev);
-      SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS>), grid_a, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap,
-                 st, part0);
-      profiler().end(0, s, ev);
+      SLA_TRY(ka.run(it, true, A, r, dinv, p_old, p_new, Ap, st, part0, s));
       profiler().begin(1, it, s, &ev);
       SLA_TRY((update_launch<T, PREC>(vec, it, n, x, r, p_new, p_old, Ap, dinv, st, part1, s)));
       profiler().end(1, s, ev);
@@ -475,13 +583,14 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
                                              dim3(coop_grid), dim3(kPBlock), args, 0, s));
     g_launches.fetch_add(1, std::memory_order_relaxed);
   } else {
+    KaLaunch<T, PREC, WS> ka;
+    ka.init(n, r, dinv, pA, pB);
     for (int64_t it = 0; it < maxiter;) {
       int64_t chunk = maxiter - it < 8 ? maxiter - it : 8;
       for (int64_t j = 0; j < chunk; ++j, ++it) {
         T *p_old = (it & 1) ? pB : pA;
         T *p_new = (it & 1) ? pA : pB;
-        SLA_LAUNCH((cg_spmv_kernel<T, PREC, WS>), occupancy_grid((const void *)cg_spmv_kernel<T, PREC, WS>),
-                   kBlock, 0, s, A, r, dinv, p_old, p_new, Ap, st, part0);
+        SLA_TRY(ka.run(it, false, A, r, dinv, p_old, p_new, Ap, st, part0, s));
         const bool vec = aligned16(x, r, pA, pB, Ap) && (!PREC || aligned16(dinv));
         SLA_TRY((update_launch<T, PREC>(vec, it, n, x, r, p_new, p_old, Ap, dinv, st, part1, s)));
       }
