@@ -683,7 +683,7 @@ def run_sharded(args, world, rank, local):
     interior_frac = plan.sell_int.n_slots / max(n_loc, 1)
     fm_int = sell_format(plan.sell_int, V)
     exchange = (("halo values and dot products stored into peer GPUs' memory by the solver "
-                 f"kernels (CUDA IPC over NVLink), {2 if method == 'cg' else 3} launches per "
+                 f"kernels (CUDA IPC over NVLink), 3 launches per "
                  "iteration") if plan.p2p is not None else
                 "NCCL grouped send/recv halo + allreduce per reduction point")
     mat = matrix_bytes(nnz, n_loc)

@@ -148,18 +148,11 @@ template <typename T> struct Pair;
 template <> struct Pair<double> { using type = double2; };
 template <> struct Pair<float> { using type = float2; };
 
-// Split K_A (SLA_CG_SPLIT 1, the default): p_new = p_old*beta + M^{-1} r is
-// formed once per row by cg_pform_kernel (a streaming pass) and K_A is a
-// plain SpMV over p_new with the L2 prefetch of the next slice's values;
-// same arithmetic, same row sums and dot order as the fused K_A
-// (SLA_CG_SPLIT 0), which forms p inside the gather, once per entry.
-// Measured on 256^3 7-point fp64: fused K_A 284.5 us; split 265.7 us for
-// both kernels (one more vector pass, but the SpMV streams at ~7 TB/s
-// once its gathers are a single vector): 2400 -> 2535 it/s.
-#ifndef SLA_CG_SPLIT
-#define SLA_CG_SPLIT 1
-#endif
-constexpr bool kCgSplit = SLA_CG_SPLIT != 0;
+// Split K_A (kCgSplit): p_new = p_old*beta + M^{-1} r is formed once per row
+// by cg_pform_kernel (a streaming pass) and K_A is a plain SpMV over p_new
+// with the L2 prefetch of the next slice's values; same arithmetic, same
+// row sums and dot order as the fused K_A, which forms p inside the gather,
+// once per entry.
 
 template <typename T, bool PREC, bool VEC>
 __global__ void __launch_bounds__(kBlock)
@@ -222,7 +215,7 @@ struct KaLaunch {
   bool vec = false;
   void init(int64_t n, const void *r, const void *dinv, const void *pA, const void *pB) {
     if (kCgSplit) {
-      grid = occupancy_grid((const void *)cg_spmv_split_kernel<T, WS>);
+      grid = spmv_grid();
       grid_p = occupancy_grid((const void *)cg_pform_kernel<T, PREC, true>);
       vec = aligned16(r, pA, pB) && (!PREC || aligned16(dinv));
     } else {

@@ -163,6 +163,56 @@ mx_spmv_kernel(Sell<float> A, const double *__restrict__ r, const void *dinv,
   }
 }
 
+// Split K_A (kCgSplit): a streaming pass forms p (float64) and its float32
+// rounding once per row; the SpMV then gathers the float32 copy (4 bytes
+// per entry instead of r, p_old and the inverse diagonal). Same values as
+// the gather above: (float)p of the same float64 p.
+template <int MODE>
+__global__ void __launch_bounds__(kBlock)
+mx_pform_kernel(int64_t n, const double *__restrict__ r, const void *dinv,
+                const double *__restrict__ p_old, double *__restrict__ p_new,
+                float *__restrict__ p32, const MixState *st) {
+  if (*(volatile const int *)&st->done) return;
+  const MxPGather<MODE> g{r, dinv, p_old, st->beta};
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const double pv = g.p((int32_t)i);
+    p_new[i] = pv;
+    p32[i] = __double2float_rn(pv);
+  }
+}
+
+template <int WS>
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
+mx_spmv_split_kernel(Sell<float> A, const float *__restrict__ p32, const double *__restrict__ p,
+                     double *__restrict__ Ap, MixState *st, double *partials) {
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->done) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  PlainGather<float> g{p32};
+  double acc[1] = {0.0};
+  for_each_slice<WS, true>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    const float sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
+    const int64_t row = s * 32 + lane;
+    if (row < A.n_slots) {
+      const double ap = (double)sum;
+      Ap[row] = ap;
+      acc[0] += __ldg(p + row) * ap;
+    }
+  });
+  if (last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem) && threadIdx.x == 0) {
+    st->pAp = acc[0];
+    if (acc[0] <= 0.0) {
+      st->done = kMxNotSPD;
+      st->iters_out = st->iter;
+    } else {
+      st->alpha = st->rz / acc[0];
+    }
+  }
+}
+
 template <int MODE>
 __device__ __forceinline__ void mx_rupd(double &ri, double api, double alpha, const void *dinv,
                                         int64_t i, double (&acc)[2]) {
@@ -240,8 +290,8 @@ mx_xflush_kernel(int64_t n, double *__restrict__ x, const double *__restrict__ p
 
 static size_t mx_ws_bytes(int64_t n) {
   const size_t G = (size_t)solver_grid();
-  return 4 * align_up(sizeof(double) * (size_t)n) + 2 * align_up(4 * G * sizeof(double)) +
-         align_up(sizeof(MixState));
+  return 4 * align_up(sizeof(double) * (size_t)n) + align_up(sizeof(float) * (size_t)n) +
+         2 * align_up(4 * G * sizeof(double)) + align_up(sizeof(MixState));
 }
 
 template <int MODE>
@@ -268,6 +318,7 @@ static int pcg_mixed_impl(const sla_sell_t *Ad, const void *dinv, int b_dtype, c
   Carver c(ws, ws_bytes);
   double *r = c.take<double>(n), *pA = c.take<double>(n), *pB = c.take<double>(n),
          *Ap = c.take<double>(n);
+  float *p32 = c.take<float>(n);
   const int G = solver_grid();
   double *part0 = c.take<double>(4 * (size_t)G), *part1 = c.take<double>(4 * (size_t)G);
   MixState *st = c.take<MixState>(1);
@@ -284,16 +335,28 @@ static int pcg_mixed_impl(const sla_sell_t *Ad, const void *dinv, int b_dtype, c
   else
     SLA_LAUNCH((mx_init_kernel<double, MODE>), grid_for(n), kBlock, 0, s, n, (const double *)b, x,
                guess ? Ap : nullptr, dinv, r, pA, st, part0, atol, rtol);
-  const int grid_a = occupancy_grid((const void *)mx_spmv_kernel<MODE, WS>);
+  const int grid_a = kCgSplit ? spmv_grid()
+                              : occupancy_grid((const void *)mx_spmv_kernel<MODE, WS>);
+  const int grid_p = occupancy_grid((const void *)mx_pform_kernel<MODE>);
   const bool vec = aligned16(x, r, pA, pB, Ap);
   SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
     double *p_old = (it & 1) ? pB : pA;
     double *p_new = (it & 1) ? pA : pB;
     cudaEvent_t ev;
-    profiler().begin(0, it, s, &ev);
-    SLA_LAUNCH((mx_spmv_kernel<MODE, WS>), grid_a, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap, st,
-               part0);
-    profiler().end(0, s, ev);
+    if (kCgSplit) {
+      profiler().begin(2, it, s, &ev);
+      SLA_LAUNCH((mx_pform_kernel<MODE>), grid_p, kBlock, 0, s, n, r, dinv, p_old, p_new, p32, st);
+      profiler().end(2, s, ev);
+      profiler().begin(0, it, s, &ev);
+      SLA_LAUNCH((mx_spmv_split_kernel<WS>), grid_a, kBlock, 0, s, A, (const float *)p32,
+                 (const double *)p_new, Ap, st, part0);
+      profiler().end(0, s, ev);
+    } else {
+      profiler().begin(0, it, s, &ev);
+      SLA_LAUNCH((mx_spmv_kernel<MODE, WS>), grid_a, kBlock, 0, s, A, r, dinv, p_old, p_new, Ap,
+                 st, part0);
+      profiler().end(0, s, ev);
+    }
     profiler().begin(1, it, s, &ev);
     SLA_TRY((mx_update_launch<MODE>(vec, it, n, x, r, p_new, p_old, Ap, dinv, st, part1, s)));
     profiler().end(1, s, ev);

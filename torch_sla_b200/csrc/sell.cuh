@@ -98,6 +98,23 @@ constexpr int kRowBatch = 8;
 #endif
 constexpr int kSpmvMinBlocks = SLA_SPMV_MIN_BLOCKS;
 
+// CG search direction: formed by a streaming pass before a plain SpMV
+// (SLA_CG_SPLIT 1), or inside the SpMV's gather, once per entry (0).
+// Measured on 256^3 7-point fp64: fused K_A 284.5 us; split 265.7 us for
+// both kernels (one more vector pass, but the SpMV streams at ~7 TB/s once
+// its gathers are a single vector): 2400 -> 2535 it/s.
+#ifndef SLA_CG_SPLIT
+#define SLA_CG_SPLIT 1
+#endif
+constexpr bool kCgSplit = SLA_CG_SPLIT != 0;
+
+// Grid of the SpMV kernels whose blocks also reduce a dot product: the
+// resident blocks their launch bounds guarantee (kSpmvMinBlocks per SM),
+// whatever registers an instantiation ends up with, so the summation order
+// of the dot -- and with it every iterate -- is the same for every layout
+// of a matrix.
+inline int spmv_grid() { return kSpmvMinBlocks * device_info().sm_count; }
+
 
 // Width spec of a view: the template value its kernels are launched with.
 inline int width_spec(const sla_sell_t *A) {

@@ -238,6 +238,71 @@ shard_cg_p2p_spmv(Sell<T> AI, Sell<T> AB, int32_t n_own, const int32_t *__restri
   if (threadIdx.x == 0) R->pap[0] = acc[0];
 }
 
+// Split form of K_A (SLA_CG_SPLIT, as in the single-GPU CG): a streaming
+// pass forms p_new for every owned row and sends the neighbours' halo share,
+// then the cooperative SpMV gathers p_new. Both kernels take the same stop
+// decision from the summed residual; only the SpMV records it.
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+shard_cg_p2p_pform(int64_t n, const int32_t *__restrict__ send_index, const T *__restrict__ r,
+                   const T *__restrict__ dinv, const T *__restrict__ p_old, T *__restrict__ p_new,
+                   const ShardState *st, const CgRed *R, long long k, long long every,
+                   double atol, double rtol, P2PDev<T> P) {
+  if (*(volatile const int *)&st->stopped) return;
+  if (cg_stop(R, k, every, cg_tol(R, atol, rtol))) return;
+  ShardP<T, PREC> inner{r, dinv, p_old, (T)cg_beta(R, k)};
+  p2p_send_halo(P, send_index, inner, P.seq + (unsigned long long)(k + 1));
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p_new[i] = inner((int32_t)i);
+}
+
+template <typename T, int WS>
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
+shard_cg_p2p_spmv_split(Sell<T> AI, Sell<T> AB, int32_t n_own, const T *__restrict__ p,
+                        T *__restrict__ Ap, ShardState *st, CgRed *R, double *partials,
+                        long long k, long long every, double atol, double rtol, P2PDev<T> P) {
+  constexpr int WSB = boundary_spec(WS);
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  if (cg_stop(R, k, every, cg_tol(R, atol, rtol))) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) { st->stopped = 1; st->iters = k; }
+    return;
+  }
+  const unsigned long long seq = P.seq + (unsigned long long)(k + 1);
+  PlainGather<T> inner{p};
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[1] = {0.0};
+  auto emit = [&](const Sell<T> &A, int64_t s, T sum) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int32_t row = (int32_t)slot_row(A, slot);
+      const T pn = __ldg(p + row);
+      Ap[row] = sum;
+      acc[0] += (double)pn * (double)sum;
+    }
+  };
+  for_each_slice<WS, true>(AI, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    emit(AI, s, sell_row_at<WS>(AI, s, sbase, swidth, lane, inner));
+  });
+  if (!p2p_wait_halo(P, seq)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  HaloGatherL2<T, PlainGather<T>> g{inner, P.halo, n_own};
+  for_each_slice<WSB>(AB, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    emit(AB, s, sell_row_at<WSB>(AB, s, sbase, swidth, lane, g));
+  });
+  if (!last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem)) return;
+  if (!p2p_allreduce<1>(P, 1, (int)(k & 1), seq, acc)) {
+    if (threadIdx.x == 0) st->stopped = kStopTimeout;
+    return;
+  }
+  if (threadIdx.x == 0) R->pap[0] = acc[0];
+}
+
 template <typename T, bool PREC>
 __global__ void __launch_bounds__(kBlock)
 shard_cg_p2p_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
@@ -506,13 +571,15 @@ static int shard_cg_p2p_impl(P2PPlan *pp, const sla_halo_plan_t *plan, const sla
   SLA_LAUNCH((shard_cg_p2p_init<T, PREC>), grid_for(no), kBlock, 0, s, no, b, x, dinv, r, pA, st,
              R, part[0], P);
   // co-resident grid for the kernel whose blocks wait on other GPUs
-  const void *ka = (const void *)shard_cg_p2p_spmv<T, PREC, WS>;
+  const void *ka = kCgSplit ? (const void *)shard_cg_p2p_spmv_split<T, WS>
+                            : (const void *)shard_cg_p2p_spmv<T, PREC, WS>;
   int per_sm = 0;
   SLA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ka, kBlock, 0));
   if (per_sm < 1) return SLA_ERR_UNSUPPORTED;
   int ga = per_sm * device_info().sm_count;
   if (ga > G) ga = G;
   const int gu = occupancy_grid((const void *)shard_cg_p2p_update<T, PREC>);
+  const int gp = occupancy_grid((const void *)shard_cg_p2p_pform<T, PREC>);
   const int32_t n_own = (int32_t)no;
   SLA_TRY(shard_loop(pp->comm, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
     T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
@@ -520,9 +587,19 @@ static int shard_cg_p2p_impl(P2PPlan *pp, const sla_halo_plan_t *plan, const sla
     void *args[] = {&AI, &AB, (void *)&n_own, (void *)&plan->send_index, (void *)&r,
                     (void *)&dinv, (void *)&p_old, (void *)&p_new, (void *)&Ap, (void *)&st,
                     (void *)&R, (void *)&part[1], &kk, &ev_, (void *)&atol, (void *)&rtol, &P};
+    void *args_split[] = {&AI, &AB, (void *)&n_own, (void *)&p_new, (void *)&Ap, (void *)&st,
+                          (void *)&R, (void *)&part[1], &kk, &ev_, (void *)&atol, (void *)&rtol,
+                          &P};
     cudaEvent_t e;
+    if (kCgSplit) {
+      profiler().begin(2, k, s, &e);
+      SLA_LAUNCH((shard_cg_p2p_pform<T, PREC>), gp, kBlock, 0, s, no, plan->send_index, r, dinv,
+                 p_old, p_new, st, R, kk, ev_, atol, rtol, P);
+      profiler().end(2, s, e);
+    }
     profiler().begin(0, k, s, &e);
-    SLA_CUDA_TRY(cudaLaunchCooperativeKernel(ka, dim3(ga), dim3(kBlock), args, 0, s));
+    SLA_CUDA_TRY(cudaLaunchCooperativeKernel(ka, dim3(ga), dim3(kBlock),
+                                             kCgSplit ? args_split : args, 0, s));
     g_launches.fetch_add(1, std::memory_order_relaxed);
     profiler().end(0, s, e);
     profiler().begin(1, k, s, &e);

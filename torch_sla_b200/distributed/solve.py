@@ -7,8 +7,9 @@ grouped NCCL send/recv while the interior rows compute, and the dot products
 of each reduction point are combined by one small ncclAllReduce (CG: 2 per
 iteration; BiCGStab: 3). On a single node both solvers instead store halo
 values and dot products straight into the other GPUs' memory from inside
-their kernels (sla_shard_cg_p2p: two launches per iteration,
-sla_shard_bicgstab_p2p: three). The stopping test runs every 10 iterations on
+their kernels (sla_shard_cg_p2p: three launches per iteration -- the search
+direction and the halo send, the SpMV, the update; sla_shard_bicgstab_p2p:
+three). The stopping test runs every 10 iterations on
 the allreduced norms, as in the reference.
 """
 from __future__ import annotations
