@@ -163,7 +163,8 @@ def pcg_solve_optimized(A: CachedSparseMatrix, b: Tensor, x0: Optional[Tensor] =
                         preconditioner: Callable[[Tensor], Tensor] = None,
                         check_interval: int = 50) -> SolveResult:
     """Jacobi-PCG with the start-of-iteration stopping test
-    (pytorch_backend.py:1262-1362), fused into two kernels per iteration."""
+    (pytorch_backend.py:1262-1362): per iteration a search-direction pass, an
+    SpMV and an update kernel (one cooperative kernel for small systems)."""
     dinv = _as_dinv(preconditioner, A)
     x, info = _pcg_core(A, b, x0, dinv, atol, rtol, maxiter)
     converged = info.status == L.SLA_OK

@@ -225,10 +225,11 @@ __device__ __forceinline__ T sell_row_at(const Sell<T> &A, int64_t s, int32_t ba
 //
 // PF (uniform layouts): while a slice runs, prefetch into L2 the values of
 // the warp's next slice (no registers held). Measured on the 256^3 7-point
-// fp64 SpMV: 183 -> 171 us, where the streamed values are half the loads;
-// no gain in the solver kernels, whose three gathered vectors per entry
-// keep the load pipe full without it (CG K_A 285 us either way, BiCGStab
-// K1 147 -> 151 us), so only the plain SpMV turns it on.
+// fp64 SpMV: 183 -> 171 us, where the streamed values are half the loads.
+// Kernels that gather one stored vector (the plain SpMV, the CG SpMV over a
+// formed search direction) turn it on; it gains nothing where each entry
+// gathers three vectors (the fused CG K_A stayed at 285 us, BiCGStab K1
+// went 147 -> 151 us).
 template <int WS, bool PF = false, typename T, typename Body>
 __device__ __forceinline__ void for_each_slice(const Sell<T> &A, int64_t warp, int64_t nwarps,
                                                int lane, Body body) {

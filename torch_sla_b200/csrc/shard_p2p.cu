@@ -8,13 +8,16 @@ namespace sla {
 // ============================================================ peer-memory path
 // Single-node path of the shard CG: halo values and dot products travel as
 // stores into the other GPUs' memory (CUDA IPC mappings over NVLink /
-// NVSwitch) from inside the solver kernels. An iteration is two launches:
-//   K_A  stop test; send this rank's share of the neighbours' halo (the
-//        search direction computed on the fly) straight into their halo
-//        buffers, the last block raising an arrival sequence number;
-//        interior rows; wait for the neighbours' arrivals; boundary rows;
-//        (p, Ap) summed over the grid and then over the ranks in rank order
+// NVSwitch) from inside the solver kernels. An iteration is three launches:
+//   K_P  stop test; form the search direction p; send this rank's share of
+//        the neighbours' halo straight into their halo buffers, the last
+//        block raising an arrival sequence number
+//   K_A  stop test; interior rows; wait for the neighbours' arrivals;
+//        boundary rows; (p, Ap) summed over the grid and then over the
+//        ranks in rank order
 //   K_B  x / r update, (r, r) and (r, z) summed the same way.
+// (With SLA_CG_SPLIT 0, K_P's work runs at the start of K_A, p computed on
+// the fly inside the gathers.)
 // K_A is a cooperative launch (all blocks co-resident), so no block can
 // wait on a block that has not started; every wait is bounded (wait_ns of
 // the descriptor, default kWaitLimitNs on the GPU's global timer)
