@@ -558,6 +558,7 @@ def wl_mixed(args, dev, local):
     launches = L.launch_count() - l0
     ka_ms, ka_n = L.profile_read(0)
     kb_ms, kb_n = L.profile_read(1)
+    kp_ms, kp_n = L.profile_read(2)
     L.profile_enable(False)
     iters = sum(its)
     value = iters / (ms / 1e3)
@@ -573,13 +574,18 @@ def wl_mixed(args, dev, local):
                       "nnz": nnz, "rtol": RTOL, "b": "N(0,1) seed 1, float32",
                       "iterations_per_solve": iters // args.steps, "format": fm["format"],
                       "l2": "inputs larger than L2; no flush", "parallelism": "single GPU"}
-    # K_A: matrix + r, p_old read, p_new, Ap written (8 B) + dinv (4 B)
-    line["roofline"] = roofline("mx_spmv_kernel", mat + (4 * 8 + 4) * n, ka_ms, ka_n,
-                                f"mx_spmv_kernel@mixed:{m}", fm["matrix_bytes"] + (4 * 8 + 4) * n)
+    # K_A: matrix + the float32 copy of p gathered (4 B) + p read at its own
+    # row for the dot (8 B) + Ap written (8 B)
+    line["roofline"] = roofline("mx_spmv_split_kernel", mat + 20 * n, ka_ms, ka_n,
+                                f"mx_spmv_split_kernel@mixed:{m}", fm["matrix_bytes"] + 20 * n)
     line["roofline"]["update_kernel"] = {
         "kernel": "mx_update_kernel", "avg_launch_ms": round(kb_ms / max(kb_n, 1), 5),
         # r read/write, Ap, dinv; x two steps at odd iterations (mean 44 B per row)
         "achieved": round(44 * n / (kb_ms / max(kb_n, 1) / 1e3) / 1e9, 1) if kb_n else None}
+    line["roofline"]["pform_kernel"] = {
+        "kernel": "mx_pform_kernel", "avg_launch_ms": round(kp_ms / max(kp_n, 1), 5),
+        # r, p_old (8 B), dinv (4 B) read; p (8 B) and its float32 copy (4 B) written
+        "achieved": round(32 * n / (kp_ms / max(kp_n, 1) / 1e3) / 1e9, 1) if kp_n else None}
     line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
                                   "frac": round(iter_bytes * value / 1e9 / peak, 4),
