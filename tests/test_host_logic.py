@@ -116,6 +116,38 @@ def test_package_exposes_distributed_names_lazily():
     assert not hasattr(T, "no_such_name")
 
 
+def test_mixed_precision_preconditioner_modes():
+    """pcg_solve_mixed_precision's z = M r rule for each preconditioner form
+    (pytorch_backend.py:1211-1216, 2281-2283) maps to one kernel mode."""
+    from torch_sla_b200 import _lib as L
+    from torch_sla_b200.backends import pytorch_backend as PB
+
+    class FakeMixed:  # stands in for MixedPrecisionMatrix (no device here)
+        def jacobi_inverse64(self):
+            return "dinv64"
+
+    def jacobi(dtype):
+        M = PB.JacobiPreconditioner.__new__(PB.JacobiPreconditioner)
+        M.dinv = torch.ones(3, dtype=dtype)
+        return M
+
+    Am = FakeMixed()
+    assert PB._mixed_mode(None, Am) == (L.SLA_MIXED_M_F64_JACOBI, "dinv64")
+    mode, d = PB._mixed_mode(PB.Float32Preconditioner(jacobi(torch.float32)), Am)
+    assert mode == L.SLA_MIXED_M_F32_JACOBI and d.dtype == torch.float32
+    assert PB._mixed_mode(PB.Float32Preconditioner(PB.IdentityPreconditioner()), Am) == (
+        L.SLA_MIXED_M_F32_NONE, None)
+    assert PB._mixed_mode(PB.IdentityPreconditioner(), Am) == (L.SLA_MIXED_M_F64_NONE, None)
+    mode, d = PB._mixed_mode(jacobi(torch.float32), Am)  # dinv * r promotes to float64
+    assert mode == L.SLA_MIXED_M_F64_JACOBI and d.dtype == torch.float64
+    with pytest.raises(NotImplementedError):
+        PB._mixed_mode(lambda r: r, Am)
+    # the float32 wrapper rounds r before the preconditioner and widens after
+    r = torch.tensor([1.0 + 2.0 ** -40, -3.0], dtype=torch.float64)
+    z = PB.Float32Preconditioner(PB.IdentityPreconditioner())(r)
+    assert z.dtype == torch.float64 and z[0] == 1.0 and z[1] == -3.0
+
+
 def test_compute_on_cpu_tensors_raises():
     v, r, c, sh = P.poisson_2d_5pt(6)
     b = torch.ones(36, dtype=torch.float64)
