@@ -13,10 +13,11 @@ Other workloads (--workload): cg2d (2-D 256^2 plain CG, rtol 1e-10,
 persistent kernel), spmv (256^3 SpMV fp64 and fp32), batched (64 x 512^2
 same-pattern CG, rtol 1e-8, with backward), bicgstab (192^3 convection-
 diffusion, Jacobi BiCGStab), pcg27 (27-point variable-coefficient 256^3 per
-GPU), mrhs (128^3 7-point with 16 right-hand sides, multi-RHS CG).
+GPU), mrhs (128^3 7-point with 16 right-hand sides, multi-RHS CG), mixed
+(256^3 7-point mixed-precision PCG: float32 matrix, float64 vectors).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                  [--workload pcg7|cg2d|spmv|batched|bicgstab|pcg27|mrhs] [--grid M]
+                  [--workload pcg7|cg2d|spmv|batched|bicgstab|pcg27|mrhs|mixed] [--grid M]
 """
 from __future__ import annotations
 
