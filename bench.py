@@ -158,24 +158,42 @@ def sell_format(sell, V=8):
 
 
 def roofline(kernel, alg_bytes, ms_total, launches, traffic_key, format_bytes=None):
-    """achieved = algorithmic bytes (int32 CSR definition) / mean launch time;
-    format_* = the same time against the bytes the layout in use must move
-    (below the CSR figure for a diagonal-offset view, hence frac > format_frac
-    there)."""
+    """Roofline of one kernel from its in-situ CUDA-event mean launch time.
+
+    achieved / frac: the bytes this kernel must move per launch in the
+    layout it runs on (the matrix as stored, padding included, plus its
+    vectors) over the mean launch time -- for the diagonal-offset view these
+    are values only, no column array, and they match the ncu-measured DRAM
+    traffic within a few per cent. alg_achieved / alg_frac: the same time
+    against the int32-CSR algorithmic bytes (nnz (V+4) + 4 (N+1) + vectors),
+    which read above 1 where the layout stores less than int32 CSR does.
+    traffic_frac: the ncu DRAM bytes of one launch (profiles/traffic.txt)
+    over the same time."""
     peak, kind = peaks()
     avg = ms_total / max(launches, 1)
-    ach = alg_bytes / (avg / 1e3) / 1e9 if launches else None
-    out = {"kernel": kernel, "bound": "hbm", "achieved": None if ach is None else round(ach, 1),
-           "peak": peak, "unit": "GB/s", "frac": None if ach is None else round(ach / peak, 4),
-           "traffic": read_traffic(traffic_key), "traffic_key": traffic_key,
-           "algorithmic_bytes": int(alg_bytes),
-           "avg_launch_ms": round(avg, 5), "sampled_launches": launches,
-           "peak_kind": "measured (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else kind}
-    if format_bytes is not None and launches:
-        fa = format_bytes / (avg / 1e3) / 1e9
-        out.update({"format_bytes": int(format_bytes), "format_achieved": round(fa, 1),
-                    "format_frac": round(fa / peak, 4)})
-    return out
+    sec = avg / 1e3
+    basis = format_bytes if format_bytes is not None else alg_bytes
+    traffic = read_traffic(traffic_key)
+
+    def gbs(nbytes):
+        return nbytes / sec / 1e9 if launches and nbytes is not None else None
+
+    def rnd(v, d):
+        return None if v is None else round(v, d)
+
+    ach, alg, tr = gbs(basis), gbs(alg_bytes), gbs(traffic)
+    return {"kernel": kernel, "bound": "hbm", "achieved": rnd(ach, 1), "peak": peak,
+            "unit": "GB/s", "frac": rnd(ach / peak if ach else None, 4),
+            "traffic": traffic, "traffic_key": traffic_key,
+            "traffic_frac": rnd(tr / peak if tr else None, 4),
+            "bytes": int(basis),
+            "bytes_basis": ("layout (matrix as stored + vectors)" if format_bytes is not None
+                            else "int32 CSR (nnz (V+4) + 4 (N+1) + vectors)"),
+            "alg_bytes": int(alg_bytes), "alg_achieved": rnd(alg, 1),
+            "alg_frac": rnd(alg / peak if alg else None, 4),
+            "avg_launch_ms": round(avg, 5), "sampled_launches": launches,
+            "peak_kind": ("measured (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured"
+                          else kind)}
 
 
 # ----------------------------------------------------- single-GPU workloads
@@ -233,12 +251,13 @@ def wl_pcg7(args, dev, local):
         "achieved": round(4 * 8 * n / (kp_ms / max(kp_n, 1) / 1e3) / 1e9, 1) if kp_n else None}
     line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
-                                  "frac": round(iter_bytes * value / 1e9 / peak, 4),
-                                  "frac_of_8tbs": round(iter_bytes * value / 8e12, 4),
+                                  "alg_frac": round(iter_bytes * value / 1e9 / peak, 4),
+                                  "alg_frac_of_8tbs": round(iter_bytes * value / 8e12, 4),
                                   "bytes_formula": "12 nnz + 4 (N+1) + 13 * 8 N",
-                                  "format_bytes_per_iter": fm["matrix_bytes"] + 12 * 8 * n,
-                                  "format_frac": round((fm["matrix_bytes"] + 12 * 8 * n) * value
-                                                       / 1e9 / peak, 4)}
+                                  "layout_bytes_per_iter": fm["matrix_bytes"] + 12 * 8 * n,
+                                  "frac": round((fm["matrix_bytes"] + 12 * 8 * n) * value
+                                                / 1e9 / peak, 4)}
+    line["roofline"]["explicit"] = explicit_pcg7(A, b, Mj, n, nnz, m)
     if not args.no_e2e:
         line["e2e"] = e2e_pcg7(args, v, r, c, b_host, sh, dev)
     line["gpu_launches"] = launches
@@ -246,6 +265,29 @@ def wl_pcg7(args, dev, local):
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_pcg(A, b_host, args.cpu_seconds)
     return line
+
+
+def explicit_pcg7(A, b, Mj, n, nnz, m):
+    """The same solve on the explicit int32-column SELL view, the layout
+    every non-stencil matrix takes: its SpMV K_A timed in situ (CUDA events
+    on the launching stream) over two solves. Its bytes are the int32-CSR
+    algorithmic bytes up to the slice padding."""
+    from torch_sla_b200 import _lib as L
+    from torch_sla_b200.backends import pytorch_backend as PB
+    sell = A.csr.sell(diagonal=False)
+    fm = sell_format(sell)
+    PB._pcg_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000, sell=sell)
+    L.profile_enable(True, 7)
+    its = [PB._pcg_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000, sell=sell)[1].iterations
+           for _ in range(2)]
+    ka_ms, ka_n = L.profile_read(0)
+    L.profile_enable(False)
+    out = roofline("cg_spmv_split_kernel (explicit int32-column SELL)",
+                   matrix_bytes(nnz, n) + 2 * 8 * n, ka_ms, ka_n,
+                   f"cg_spmv_split_kernel@pcg7-explicit:{m}", fm["matrix_bytes"] + 2 * 8 * n)
+    out.update(format=fm["format"], padded_nnz=sell.padded_nnz, iterations_per_solve=its[0])
+    del sell
+    return out
 
 
 def e2e_pcg7(args, v, r, c, b_host, sh, dev):
@@ -343,7 +385,9 @@ def wl_cg2d(args, dev, local):
 
 
 def wl_spmv(args, dev, local):
-    """SpMV sweep: y = A x on the 256^3 7-point matrix, fp64 and fp32."""
+    """SpMV sweep: y = A x on the 256^3 7-point matrix, fp64 and fp32, on the
+    diagonal-offset view the solvers pick for this stencil and on the explicit
+    int32-column view every other pattern takes."""
     from torch_sla_b200 import problems as P
     from torch_sla_b200._csr import DeviceCSR, spmv
     res = {}
@@ -353,33 +397,37 @@ def wl_spmv(args, dev, local):
     for dt, V in ((torch.float64, 8), (torch.float32, 4)):
         v, r, c, sh = P.poisson_3d_7pt(m, dtype=dt, device=dev)
         csr = DeviceCSR(v, r, c, sh)
-        sell = csr.sell()
         del v, r, c
         x = P.rhs_normal(n, SEED, dt).to(dev)
         y = torch.empty_like(x)
-        reps = 50
-        for _ in range(5):
-            spmv(sell, x, n, y)
-        ms, _, clk = timed(lambda: spmv(sell, x, n, y), reps, dev, local)
-        alg = matrix_bytes(csr.nnz, n, V) + 2 * V * n
-        fm = sell_format(sell, V)
-        fb = fm["matrix_bytes"] + 2 * V * n
-        sec = ms / reps / 1e3
-        res["f64" if V == 8 else "f32"] = {"us_per_spmv": round(sec * 1e6, 2),
-                                          "achieved_gbs": round(alg / sec / 1e9, 1),
-                                          "frac": round(alg / sec / 1e9 / peak, 4),
-                                          "frac_of_8tbs": round(alg / sec / 8e12, 4),
-                                          "algorithmic_bytes": alg, "format": fm["format"],
-                                          "format_bytes": fb,
-                                          "format_frac": round(fb / sec / 1e9 / peak, 4),
-                                          "clocks": clk, "_ms": ms, "_reps": reps}
-        del csr, sell, x, y
-    line = base_line(args, "SpMV HBM GB/s (256^3 7-point, fp64)", res["f64"]["achieved_gbs"],
-                     "GB/s", res["f64"]["us_per_spmv"] / 1e3 * args.steps, 1)
+        for diagonal in (True, False):
+            sell = csr.sell(diagonal=diagonal)
+            reps = 50
+            for _ in range(5):
+                spmv(sell, x, n, y)
+            ms, _, clk = timed(lambda: spmv(sell, x, n, y), reps, dev, local)
+            alg = matrix_bytes(csr.nnz, n, V) + 2 * V * n
+            fm = sell_format(sell, V)
+            fb = fm["matrix_bytes"] + 2 * V * n
+            sec = ms / reps / 1e3
+            key = ("f64" if V == 8 else "f32") + ("" if diagonal else "_explicit")
+            res[key] = {"us_per_spmv": round(sec * 1e6, 2),
+                        "achieved_gbs": round(fb / sec / 1e9, 1),
+                        "frac": round(fb / sec / 1e9 / peak, 4), "bytes": fb,
+                        "format": fm["format"],
+                        "alg_bytes": alg, "alg_achieved_gbs": round(alg / sec / 1e9, 1),
+                        "alg_frac": round(alg / sec / 1e9 / peak, 4),
+                        "alg_frac_of_8tbs": round(alg / sec / 8e12, 4),
+                        "clocks": clk, "_ms": ms, "_reps": reps}
+            del sell
+        del csr, x, y
     f64 = res["f64"]
-    line["roofline"] = roofline("spmv_kernel", f64["algorithmic_bytes"], f64.pop("_ms"),
-                                f64.pop("_reps"), f"spmv_kernel@spmv:{m}", f64["format_bytes"])
-    res["f32"].pop("_ms"), res["f32"].pop("_reps")
+    line = base_line(args, "SpMV HBM GB/s (256^3 7-point, fp64)", f64["achieved_gbs"],
+                     "GB/s", f64["us_per_spmv"] / 1e3 * args.steps, 1)
+    line["roofline"] = roofline("spmv_kernel", f64["alg_bytes"], f64.pop("_ms"),
+                                f64.pop("_reps"), f"spmv_kernel@spmv:{m}", f64["bytes"])
+    for k, d in res.items():
+        d.pop("_ms", None), d.pop("_reps", None)
     line["config"] = {"workload": "spmv_poisson3d_7pt", "grid": [m, m, m], "sweep": res,
                       "l2": "inputs larger than L2"}
     line["clocks"] = f64["clocks"]
@@ -430,7 +478,7 @@ def wl_batched(args, dev, local):
                                 "diagonal-offset view of the pattern (columns computed)"}
     line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
-                                  "frac": round(iter_bytes * value / 1e9 / peak, 4)}
+                                  "alg_frac": round(iter_bytes * value / 1e9 / peak, 4)}
     line["roofline"] = roofline("batch_spmv_kernel",
                                 B * nnz * 8 + 4 * nnz + 4 * (n + 1) + 5 * B * 8 * n, ka_ms, ka_n,
                                 f"batch_spmv_kernel@batched:{B}x{m}")
@@ -469,7 +517,7 @@ def wl_bicgstab(args, dev, local):
                       "iterations_per_solve": iters // args.steps}
     line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
-                                  "frac": round(iter_bytes * value / 1e9 / peak, 4),
+                                  "alg_frac": round(iter_bytes * value / 1e9 / peak, 4),
                                   "bytes_formula": "2 (12 nnz + 4 (N+1)) + 25 * 8 N"}
     fm = sell_format(A.sell())
     line["config"]["format"] = fm["format"]
@@ -519,7 +567,7 @@ def wl_mrhs(args, dev, local):
                       "l2": "inputs larger than L2"}
     line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
                                   "achieved_gbs": round(iter_bytes * value / K / 1e9, 1),
-                                  "frac": round(iter_bytes * value / K / 1e9 / peak, 4),
+                                  "alg_frac": round(iter_bytes * value / K / 1e9 / peak, 4),
                                   "bytes_formula": "12 nnz + 4 (N+1) + 13 * 16 * 8 N"}
     # K_A reads the matrix and the search directions P (formed by
     # mrhs_pform_kernel), writes AP
@@ -589,7 +637,7 @@ def wl_mixed(args, dev, local):
         "achieved": round(32 * n / (kp_ms / max(kp_n, 1) / 1e3) / 1e9, 1) if kp_n else None}
     line["iteration_roofline"] = {"bytes_per_iter": iter_bytes,
                                   "achieved_gbs": round(iter_bytes * value / 1e9, 1),
-                                  "frac": round(iter_bytes * value / 1e9 / peak, 4),
+                                  "alg_frac": round(iter_bytes * value / 1e9 / peak, 4),
                                   "bytes_formula": "8 nnz + 4 (N+1) + (11 * 8 + 2 * 4) N"}
     line["gpu_launches"] = launches
     line["clocks"] = clk
@@ -660,12 +708,17 @@ def run_sharded(args, world, rank, local):
     torch.cuda.synchronize()
     dist.barrier()
     L.profile_enable(True, 7)
+    if plan.p2p is not None:
+        plan.p2p_timers(reset=True)
     l0 = L.launch_count()
     ms_local, outs, clk = timed(lambda: once()[1], args.steps, dev, local)
     dist.barrier()
     launches = L.launch_count() - l0
     ka_ms, ka_n = L.profile_read(0)
+    kb_ms, kb_n = L.profile_read(1)
+    kp_ms, kp_n = L.profile_read(2)
     L.profile_enable(False)
+    timers = plan.p2p_timers(reset=True) if plan.p2p is not None else None
     t = torch.tensor([ms_local], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
@@ -686,6 +739,8 @@ def run_sharded(args, world, rank, local):
     dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e_ms = float(te.item())
 
+    halo = halo_report(D, plan, world, dev, m, timers, (kp_ms, kp_n), (ka_ms, ka_n),
+                       (kb_ms, kb_n), method)
     V = 8
     interior_frac = plan.sell_int.n_slots / max(n_loc, 1)
     fm_int = sell_format(plan.sell_int, V)
@@ -699,21 +754,29 @@ def run_sharded(args, world, rank, local):
                   "fp64 Jacobi-PCG iterations/s (3-D 27-point, 256^3 unknowns per GPU)")
         iter_bytes = mat + 13 * V * n_loc
         if plan.p2p is not None:
-            # one kernel covers every owned row (halo send, interior, boundary)
-            ka_bytes = mat + 5 * V * n_loc
+            # K_A covers every owned row (interior, halo wait, boundary,
+            # cross-rank sum) over the search direction K_P formed: matrix +
+            # p gathered + Ap written
+            ka_bytes = mat + 2 * V * n_loc
             ka_fmt = (fm_int["matrix_bytes"] + sell_format(plan.sell_bnd, V)["matrix_bytes"]
-                      + 5 * V * n_loc)
-            kname, rows = "shard_cg_p2p_spmv", "all rows, halo send and cross-rank sum fused"
+                      + 2 * V * n_loc)
+            kname, rows = "shard_cg_p2p_spmv_split", "all rows, halo wait and cross-rank sum"
         else:
             ka_bytes = (mat + 5 * V * n_loc) * interior_frac
             ka_fmt = fm_int["matrix_bytes"] + 5 * V * plan.sell_int.n_slots
             kname, rows = "shard_cg_spmv", "interior rows"
     else:
         metric = "fp64 Jacobi-BiCGStab iterations/s (convection-diffusion, 192^3 per GPU)"
-        ka_bytes = (mat + 6 * V * n_loc) * interior_frac
-        ka_fmt = fm_int["matrix_bytes"] + 6 * V * plan.sell_int.n_slots
         iter_bytes = 2 * mat + 25 * V * n_loc
-        kname, rows = "shard_bi_k1", "interior rows"
+        if plan.p2p is not None:
+            ka_bytes = mat + 6 * V * n_loc
+            ka_fmt = (fm_int["matrix_bytes"] + sell_format(plan.sell_bnd, V)["matrix_bytes"]
+                      + 6 * V * n_loc)
+            kname, rows = "shard_bi_p2p_k1", "all rows, halo wait and cross-rank sum"
+        else:
+            ka_bytes = (mat + 6 * V * n_loc) * interior_frac
+            ka_fmt = fm_int["matrix_bytes"] + 6 * V * plan.sell_int.n_slots
+            kname, rows = "shard_bi_k1", "interior rows"
     peak, _ = peaks()
     if rank == 0:
         line = base_line(args, metric, value, "iterations/s", ms, world)
@@ -731,7 +794,7 @@ def run_sharded(args, world, rank, local):
         line["iteration_roofline"] = {"bytes_per_iter_per_gpu": iter_bytes,
                                       "achieved_gbs_per_gpu":
                                           round(iter_bytes * value / world / 1e9, 1),
-                                      "frac": round(iter_bytes * value / world / 1e9 / peak, 4)}
+                                      "alg_frac": round(iter_bytes * value / world / 1e9 / peak, 4)}
         line["roofline"] = roofline(f"{kname} ({rows})", ka_bytes, ka_ms, ka_n,
                                     f"{kname}@{wl}-shard:{m}", ka_fmt)
         line["e2e"] = {"value": round(sum(e_its) * world / (e_ms / 1e3), 3),
@@ -740,6 +803,7 @@ def run_sharded(args, world, rank, local):
                        "ms_per_step": round(e_ms / e_steps, 3), "steps": e_steps,
                        "api": "DSparseTensor.solve_distributed_shard, b from pinned host "
                               "memory, x read back; shard setup done once before timing"}
+        line["halo"] = halo
         line["gpu_launches"] = launches
         line["clocks"] = clk
         print(json.dumps(line), flush=True)
@@ -747,6 +811,75 @@ def run_sharded(args, world, rank, local):
     destroy_all()
     dist.barrier()
     dist.destroy_process_group()
+
+
+# Peer copy over NVLink measured on this pool's B200s (GB/s per direction);
+# nominal NVLink 5 is 900 GB/s per direction per GPU.
+NVLINK_PEER_GBS = 770.0
+
+
+def halo_report(D, plan, world, dev, m, timers, kp, ka, kb, method):
+    """Where the time of a sharded iteration goes, max over ranks: the
+    in-situ CUDA-event means of the solver's kernels (K_P forms p and sends
+    the halo, K_A the SpMV with the halo wait and the cross-rank (p,Ap) sum,
+    K_B the update and the (r,r),(r,z) sum), the GPU-timer breakdown the
+    peer-memory kernels record while profiling (mean per block: halo stores
+    + fence in K_P, halo-arrival wait in K_A; the two cross-rank sums in the
+    last block), and a standalone halo_exchange (NCCL grouped send/recv of
+    one m^2 layer per neighbour, the reference's exchange step) timed over
+    50 calls with CUDA events."""
+    import torch.distributed as dist
+    from torch_sla_b200.distributed import halo_exchange
+
+    def mean(t):
+        return t[0] / t[1] * 1e3 if t[1] else 0.0
+    vals = [mean(kp), mean(ka), mean(kb)]
+    if timers and timers["iterations"]:
+        it = timers["iterations"]
+        vals += [timers["send_ns"] / max(timers["kp_blocks"], 1) / 1e3,
+                 timers["wait_ns"] / max(timers["ka_blocks"], 1) / 1e3,
+                 timers["sum_pap_ns"] / it / 1e3, timers["sum_rr_ns"] / it / 1e3]
+    else:
+        vals += [-1.0, -1.0, -1.0, -1.0]
+    ex_us = -1.0
+    bytes_nb = m * m * 8
+    if world > 1:
+        xl = torch.zeros(plan.n_owned + plan.n_halo, dtype=torch.float64, device=dev)
+        for _ in range(5):
+            halo_exchange(D, xl)
+        torch.cuda.synchronize()
+        dist.barrier()
+        reps = 50
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            halo_exchange(D, xl)
+        e1.record()
+        torch.cuda.synchronize()
+        ex_us = e0.elapsed_time(e1) * 1e3 / reps
+    vals.append(ex_us)
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    v = [round(float(a), 2) for a in t.tolist()]
+    out = {"reduction": "max over ranks", "kernel_us": {"K_P": v[0], "K_A": v[1], "K_B": v[2]}
+           if method == "cg" else {"K1": v[1]},
+           "bytes_per_neighbour": bytes_nb,
+           "neighbours_per_rank": "1 (end slabs) / 2 (middle slabs)" if world > 2 else
+           ("1" if world == 2 else "0")}
+    if v[3] >= 0:
+        out["peer_memory_us_per_iteration"] = {
+            "halo_send_per_block": v[3], "halo_wait_per_block": v[4],
+            "cross_rank_sum_pap": v[5], "cross_rank_sum_rr": v[6],
+            "timer": "GPU global timer in the solver kernels (profiling on)"}
+    if world > 1 and v[7] > 0:
+        gbs = bytes_nb / (v[7] / 1e6) / 1e9
+        out["halo_exchange"] = {
+            "api": "torch_sla_b200.distributed.halo_exchange (NCCL grouped send/recv)",
+            "us_per_exchange": v[7], "gbs_per_direction_per_neighbour": round(gbs, 1),
+            "nvlink_frac": round(gbs / NVLINK_PEER_GBS, 4),
+            "nvlink_peak": f"{NVLINK_PEER_GBS} GB/s peer copy per direction (measured on this "
+                           "pool); 900 nominal"}
+    return out
 
 
 # --------------------------------------------------------- reference arm
@@ -781,8 +914,14 @@ def run_reference(args):
     value = its / dt
     line = base_line(args, METRIC, value, "iterations/s", dt * 1e3, world)
     line["impl"] = "reference"
+    # the same config keys as the B200 arm's line for this workload
     line["config"] = {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [m * world, m, m],
-                      "n_per_slab": n, "rtol": RTOL, "parallelism": "host CPU"}
+                      "n": n * world, "rtol": RTOL, "b": "N(0,1) seed 1",
+                      "parallelism": "host CPU"}
+    if world > 1:
+        line["config"]["n_per_gpu"] = n
+    else:
+        line["config"]["nnz"] = int(Acpu.values().numel())
     sample = (f"{per_step} PCG iterations per step on one 256^3 slab; x{world} slabs" if world > 1
               else f"{per_step} PCG iterations per step on the 256^3 system")
     line["cpu_baseline"] = {"value": round(value, 3), "unit": "iterations/s", "cores": cores,

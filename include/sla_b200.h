@@ -100,9 +100,10 @@ typedef struct {
 
 /* ------------------------------------------------------------------ misc */
 /* Version of this interface; 2 since sla_sell_t carries n_cols, row_base
- * and the diagonal offsets, 3 since sla_pcg_mixed. _lib.py refuses a
+ * and the diagonal offsets, 3 since sla_pcg_mixed, 4 since
+ * sla_p2p_profile_read (and one-rank peer-memory plans). _lib.py refuses a
  * library with another. */
-#define SLA_ABI_VERSION 3
+#define SLA_ABI_VERSION 4
 int sla_abi_version(void);
 const char *sla_status_string(int status);
 /* Kernels this library has launched in this process (all devices). */
@@ -215,12 +216,15 @@ int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b,
  * SLA_PCG_NOALLOC_SCRATCH_BYTES (16 MiB), held on every GPU that loads the
  * library until the process exits; that fits n <= 500,000 rows in float64
  * (1,000,000 in float32) on a 148-SM B200. Larger n returns
- * SLA_ERR_UNSUPPORTED. The caller still provides A, dinv, b and x. The first
- * call on a device resolves the array's device address on that device, so
- * make that first call before any stream capture. All calls share the one
- * array: calls that overlap on the GPU (other streams, other host threads)
- * race and must be serialised by the caller. No cudaMalloc/cudaFree or other
- * allocating routine is called. */
+ * SLA_ERR_UNSUPPORTED. The caller still provides A, dinv, b and x. Each
+ * call resolves the array's device address on the current device
+ * (cudaGetSymbolAddress), so make the first call on a device before any
+ * stream capture. The call blocks the host until the solve has finished (it
+ * reads the convergence flag back every 8 iterations on the streamed path
+ * and the final state at the end). All calls share the one array: calls that
+ * overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller. No cudaMalloc/cudaFree or other allocating
+ * routine is called. */
 #define SLA_PCG_NOALLOC_SCRATCH_BYTES (16u << 20)
 int sla_pcg_noalloc(int dtype, const sla_sell_t *A, const void *dinv,
                     const void *b, void *x, int x_is_guess, double atol,
@@ -384,7 +388,7 @@ int sla_shard_bicgstab(void *comm_halo, void *comm_reduce,
                        size_t workspace_bytes, sla_solve_info_t *info,
                        sla_stream_t stream);
 
-/* Peer-memory shard CG (single node, 2..8 ranks; the same algorithm and
+/* Peer-memory shard CG (single node, 1..8 ranks; the same algorithm and
  * stopping rule as sla_shard_cg, distributed/solve.py:279-350). Halo values
  * and dot products are stored by the solver kernels directly into the other
  * GPUs' memory through CUDA IPC mappings, so an iteration is two kernel
@@ -392,7 +396,9 @@ int sla_shard_bicgstab(void *comm_halo, void *comm_reduce,
  * sla_p2p_create is collective over `comm` (NCCL is used once to trade the
  * IPC handles and agree): it maps every rank's exchange buffer and returns
  * *p2p_out = NULL with SLA_OK on every rank when any rank cannot (more than
- * 8 ranks, peer mapping refused, a halo permutation in the plan). The handle
+ * 8 ranks, peer mapping refused, a halo permutation in the plan). One rank
+ * maps nothing and runs the same kernels, its cross-rank sums covering
+ * itself. The handle
  * owns its device buffer; sla_p2p_destroy is collective (it waits until
  * every rank is past its last remote store). Every cross-GPU wait inside the
  * kernels is bounded; a peer that stops answering ends the solve with
@@ -400,6 +406,15 @@ int sla_shard_bicgstab(void *comm_halo, void *comm_reduce,
  * with the same arguments, as with sla_shard_cg. */
 int sla_p2p_create(void *comm, const sla_halo_plan_t *plan, int dtype, void **p2p_out);
 int sla_p2p_destroy(void *p2p);
+/* Instrumentation of the peer-memory CG (no counterpart in torch-sla): while
+ * profiling is on (sla_profile_enable), the solver kernels add GPU-timer
+ * nanoseconds into per-plan slots, copied to out[0..n_out) (zeros past the
+ * 7 slots) and cleared when reset != 0: 0 halo send (K_P, summed over
+ * blocks), 1 halo-arrival wait (K_A, summed over blocks), 2 cross-rank
+ * (p,Ap) sum (K_A last block), 3 cross-rank (r,r),(r,z) sum (K_B last
+ * block), 4 K_A blocks summed over launches, 5 K_A launches, 6 K_P blocks
+ * summed over launches. Synchronises the device. */
+int sla_p2p_profile_read(void *p2p, int reset, unsigned long long *out, int n_out);
 int sla_shard_cg_p2p(void *p2p, const sla_halo_plan_t *plan, int dtype,
                      const sla_sell_t *A_interior, const sla_sell_t *A_boundary,
                      const void *dinv, const void *b, void *x, double atol,

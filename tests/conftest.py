@@ -11,6 +11,16 @@ if REPO not in sys.path:
 GOLDEN = os.path.join(REPO, "tests", "golden")
 
 
+def torch_sla_path():
+    """Directory holding an installed torch-sla package: $TORCH_SLA_REF, then
+    baseline/_ref (the offline install beside this repository); None when
+    neither has it."""
+    for cand in (os.environ.get("TORCH_SLA_REF"), os.path.join(REPO, "baseline", "_ref")):
+        if cand and os.path.isdir(os.path.join(cand, "torch_sla")):
+            return cand
+    return None
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and libsla_b200.so")
 

@@ -1,8 +1,10 @@
 """Generate the golden fixtures of the parity tests by running torch-sla itself.
 
-Run in the build container, where the reference source tree is importable:
+Run where the reference source tree is importable:
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /root/reference
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py <torch-sla source tree>
+
+(the tree may also come from the TORCH_SLA_REF environment variable).
 
 It writes tests/golden/golden.pt (single-process solvers, SpMV, adjoints,
 partition maps) and tests/golden/golden_shard.pt (the reference's
@@ -324,7 +326,9 @@ def shard(ref_path, out_path, world=2, port=29631):
 
 
 if __name__ == "__main__":
-    ref_path = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_path = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TORCH_SLA_REF")
+    if not ref_path:
+        sys.exit("usage: make_golden.py <torch-sla source tree> (or set TORCH_SLA_REF)")
     torch.save(single(ref_path), os.path.join(HERE, "golden.pt"))
     shard(ref_path, os.path.join(HERE, "golden_shard.pt"))
     print("wrote", os.listdir(HERE))

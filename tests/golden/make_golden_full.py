@@ -1,0 +1,303 @@
+"""Full-size golden fixtures: torch-sla itself run at the benchmark sizes.
+
+The small fixtures (make_golden.py) pin every code path at sizes the oracle
+finishes in seconds. This script pins the solver workloads at the sizes the
+throughput figures are quoted on, by running torch-sla's own pytorch backend
+on the host CPU (minutes to tens of minutes each):
+
+  pcg7_256_f64   3-D 7-point Poisson 256^3, b ~ N(0,1) seed 1, Jacobi PCG,
+                 rtol 1e-8 (pcg_solve_optimized, pytorch_backend.py:1262) plus
+                 the SpMV y = A x (CachedSparseMatrix.matvec, :154) in fp64
+  pcg7_256_f32   the same system in float32 (pcg_solve_optimized on a float32
+                 CachedSparseMatrix), rtol 1e-8, plus the float32 SpMV
+  bicg_cd192     192^3 upwind convection-diffusion, b ~ U(0,1) seed 3, Jacobi
+                 BiCGStab rtol 1e-8 (pbicgstab_solve, :1508)
+  batched_64x512 64 x 512^2 variable-coefficient diffusion, forward and
+                 backward through spsolve_batch_same_layout (batch_solve.py:46)
+                 with batched_cg_same_pattern (:2575) at rtol 1e-8, loss sum x^2
+  shard27_<m>_P<P>  27-point variable-coefficient system on a (m P) x m x m
+                 grid under a P-rank gloo group: DSparseTensor.partition +
+                 solve (distributed/solve.py:279 cg_shard), b ~ N(0,1) seed 4
+
+Only compact summaries are stored (a few hundred KB in all): iteration
+counts, norms, the true relative residual, per-member norms, and the values
+at a seeded sample of indices. Every fixture names the generator its
+inputs come from (torch_sla_b200.problems), so the GPU tests rebuild the
+inputs without the reference.
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden_full.py \
+        <torch-sla source tree> [case ...]
+
+The tree may also come from the TORCH_SLA_REF environment variable.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import time
+import warnings
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+OUT = os.path.join(HERE, "full")
+sys.path.insert(0, REPO)
+
+from torch_sla_b200 import problems as P  # noqa: E402
+
+SAMPLE = 4096
+SAMPLE_SEED = 99
+
+
+def _ref(path):
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    import torch_sla
+    return torch_sla
+
+
+def sample_idx(n: int, k: int = SAMPLE, seed: int = SAMPLE_SEED) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    k = min(k, n)
+    return torch.randperm(n, generator=g)[:k].sort().values
+
+
+def summary(x: torch.Tensor, idx: torch.Tensor) -> dict:
+    xf = x.reshape(-1)
+    return {"idx": idx.clone(), "at": xf[idx].clone(), "norm": float(xf.double().norm()),
+            "sum": float(xf.double().sum()), "absmax": float(xf.double().abs().max())}
+
+
+def save(name: str, d: dict):
+    os.makedirs(OUT, exist_ok=True)
+    torch.save(d, os.path.join(OUT, f"{name}.pt"))
+    print(f"[{time.strftime('%H:%M:%S')}] wrote {name}", flush=True)
+
+
+def true_residual(A, x, b) -> float:
+    r = b.double() - A.matvec(x).double()
+    return float(r.norm() / b.double().norm())
+
+
+def case_pcg7(ref, dtype):
+    from torch_sla.backends import pytorch_backend as PB
+    m = 256
+    n = m ** 3
+    v, r, c, sh = P.poisson_3d_7pt(m, dtype=dtype)
+    b = P.rhs_normal(n, 1, dtype)
+    rtol = 1e-8
+    t0 = time.perf_counter()
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    t_csr = time.perf_counter() - t0
+    del v, r, c
+    xs = P.rhs_normal(n, 1, dtype)  # the SpMV sweep's x (seed 1)
+    y = A.matvec(xs)
+    M = PB.get_preconditioner(A, "jacobi")
+    t0 = time.perf_counter()
+    res = PB.pcg_solve_optimized(A, b, atol=0.0, rtol=rtol, maxiter=10000, preconditioner=M)
+    t_solve = time.perf_counter() - t0
+    idx = sample_idx(n)
+    tag = "f64" if dtype == torch.float64 else "f32"
+    save(f"pcg7_256_{tag}", {
+        "gen": ("poisson_3d_7pt", (m,), {"dtype": dtype}), "rhs": ("rhs_normal", n, 1, dtype),
+        "atol": 0.0, "rtol": rtol, "preconditioner": "jacobi", "maxiter": 10000,
+        "iters": int(res.num_iters), "converged": bool(res.converged),
+        "residual": float(res.residual), "true_rel_residual": true_residual(A, res.x, b),
+        "x": summary(res.x, idx), "spmv_x": ("rhs_normal", n, 1, dtype),
+        "spmv_y": summary(y, idx),
+        "cpu": {"threads": torch.get_num_threads(), "csr_build_s": t_csr,
+                "solve_s": t_solve}})
+
+
+def case_bicg192(ref):
+    from torch_sla.backends import pytorch_backend as PB
+    m = 192
+    v, r, c, sh = P.convdiff_3d_upwind(m)
+    b = P.rhs_uniform01(sh[0], 3)
+    t0 = time.perf_counter()
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        x, it, resid = PB.pbicgstab_solve(v, r, c, sh, b, atol=0.0, rtol=1e-8, maxiter=10000,
+                                          preconditioner="jacobi")
+    t_solve = time.perf_counter() - t0
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    save("bicg_cd192", {
+        "gen": ("convdiff_3d_upwind", (m,), {}), "rhs": ("rhs_uniform01", sh[0], 3),
+        "atol": 0.0, "rtol": 1e-8, "preconditioner": "jacobi", "maxiter": 10000,
+        "iters": int(it), "residual": float(resid), "true_rel_residual": true_residual(A, x, b),
+        "x": summary(x, sample_idx(sh[0])),
+        "cpu": {"threads": torch.get_num_threads(), "solve_s": t_solve}})
+
+
+class _CountNorms:
+    """Counts torch.linalg.vector_norm calls: batched_cg_same_pattern calls it
+    once for ||b_i|| and once per iteration (its stop test), so a solve of k
+    iterations makes k + 1 calls."""
+
+    def __init__(self):
+        self.calls = 0
+        self._orig = torch.linalg.vector_norm
+
+    def __enter__(self):
+        orig = self._orig
+
+        def counted(*a, **k):
+            self.calls += 1
+            return orig(*a, **k)
+        torch.linalg.vector_norm = counted
+        return self
+
+    def __exit__(self, *exc):
+        torch.linalg.vector_norm = self._orig
+
+
+def case_batched(ref):
+    from torch_sla.backends import pytorch_backend as PB
+    from torch_sla.batch_solve import spsolve_batch_same_layout
+    B, m = 64, 512
+    vb, r, c, sh, bb = P.diffusion_2d_batched(B, m, seed=2)
+    rtol = 1e-8
+    # spsolve_batch_same_layout takes no rtol and batched_cg_same_pattern
+    # defaults to 1e-6; the workload is specified at 1e-8, so the module
+    # attribute the autograd Function imports at call time (batch_solve.py:72,
+    # :135) is bound to the same function with rtol = 1e-8 and a counter.
+    orig = PB.batched_cg_same_pattern
+    iters = []
+
+    def at_rtol(*a, **k):
+        k["rtol"] = rtol
+        with _CountNorms() as cnt:
+            out = orig(*a, **k)
+        iters.append(cnt.calls - 1)
+        return out
+
+    PB.batched_cg_same_pattern = at_rtol
+    try:
+        vg = vb.clone().requires_grad_(True)
+        bg = bb.clone().requires_grad_(True)
+        t0 = time.perf_counter()
+        U = spsolve_batch_same_layout(vg, r, c, sh, bg, method="cg", atol=0.0, maxiter=10000)
+        t_fwd = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        (U * U).sum().backward()
+        t_bwd = time.perf_counter() - t0
+    finally:
+        PB.batched_cg_same_pattern = orig
+    U = U.detach()
+    # true residual per member: A_i u_i - b_i
+    AU = torch.zeros_like(U)
+    AU.index_add_(1, r, vb * U[:, c])
+    rel = ((AU - bb).norm(dim=1) / bb.norm(dim=1))
+    n, nnz = sh[0], r.numel()
+    save("batched_64x512", {
+        "gen": ("diffusion_2d_batched", (B, m), {"seed": 2}), "atol": 0.0, "rtol": rtol,
+        "maxiter": 10000, "iters_forward": iters[0], "iters_adjoint": iters[1],
+        "true_rel_residual": rel.clone(),
+        "U": summary(U, sample_idx(B * n)),
+        "U_member_norm": U.norm(dim=1).clone(),
+        "grad_val": summary(vg.grad, sample_idx(B * nnz)),
+        "grad_val_member_norm": vg.grad.norm(dim=1).clone(),
+        "grad_b": summary(bg.grad, sample_idx(B * n, seed=SAMPLE_SEED + 1)),
+        "grad_b_member_norm": bg.grad.norm(dim=1).clone(),
+        "cpu": {"threads": torch.get_num_threads(), "forward_s": t_fwd, "backward_s": t_bwd}})
+
+
+# ------------------------------------------------------------ shard solves
+def _shard27_worker(rank, world, port, ref_path, m, threads, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.set_num_threads(threads)
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        _ref(ref_path)
+        from torch.distributed.device_mesh import init_device_mesh
+        from torch_sla import DSparseTensor, SparseTensor, solve, SolverConfig
+        mesh = init_device_mesh("cpu", (world,))
+        dims = (m * world, m, m)
+        n = dims[0] * dims[1] * dims[2]
+        v, r, c = P.stencil27_rows(dims, 0, dims[0], seed=4)
+        b = P.rhs_normal(n, 4)
+        A = SparseTensor(v, r, c, (n, n))
+        D = DSparseTensor.partition(A, mesh, partition_method="simple")
+        calls = [0]
+        inner = D._shard_matvec
+
+        def counted(x, _inner=inner):
+            calls[0] += 1
+            return _inner(x)
+
+        D._shard_matvec = counted
+        b_dt = D.scatter(b)
+        t0 = time.perf_counter()
+        with SolverConfig(method="cg", atol=0.0, rtol=1e-8, maxiter=10000,
+                          preconditioner="jacobi"):
+            x_dt = solve(D, b_dt)
+        t_solve = time.perf_counter() - t0
+        x = x_dt.full_tensor()
+        if rank == 0:
+            # cg_shard: one matvec for the initial residual, one per iteration
+            ax = torch.sparse_coo_tensor(torch.stack([r, c]), v, (n, n)).coalesce() @ x
+            rel = float((ax - b).norm() / b.norm())
+            torch.save({"gen": ("stencil27_rows", (dims, 0, dims[0]), {"seed": 4}),
+                        "rhs": ("rhs_normal", n, 4), "dims": dims, "P": world, "m": m,
+                        "atol": 0.0, "rtol": 1e-8, "preconditioner": "jacobi",
+                        "iters": calls[0] - 1, "true_rel_residual": rel,
+                        "x": summary(x, sample_idx(n)),
+                        "cpu": {"threads_per_rank": threads, "solve_s": t_solve}}, out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def case_shard27(ref_path, m, world, port):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    threads = max(1, (os.cpu_count() or 2) // world)
+    os.makedirs(OUT, exist_ok=True)
+    out_path = os.path.join(OUT, f"shard27_{m}_P{world}.pt")
+    procs = [ctx.Process(target=_shard27_worker,
+                         args=(rk, world, port, ref_path, m, threads, out_path))
+             for rk in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=7200)
+        assert p.exitcode == 0, f"shard worker exited with {p.exitcode}"
+    print(f"[{time.strftime('%H:%M:%S')}] wrote shard27_{m}_P{world}", flush=True)
+
+
+CASES = ["bicg_cd192", "pcg7_256_f64", "shard27_32_P2", "shard27_32_P4", "shard27_64_P2",
+         "shard27_64_P4", "batched_64x512", "pcg7_256_f32"]
+
+
+def main():
+    args = sys.argv[1:]
+    ref_path = os.environ.get("TORCH_SLA_REF")
+    if args and os.path.isdir(args[0]):
+        ref_path, args = args[0], args[1:]
+    if not ref_path:
+        sys.exit("usage: make_golden_full.py <torch-sla source tree> [case ...] "
+                 "(or set TORCH_SLA_REF)")
+    torch.set_num_threads(os.cpu_count() or 1)
+    ref = _ref(ref_path)
+    for name in args or CASES:
+        t0 = time.perf_counter()
+        if name == "pcg7_256_f64":
+            case_pcg7(ref, torch.float64)
+        elif name == "pcg7_256_f32":
+            case_pcg7(ref, torch.float32)
+        elif name == "bicg_cd192":
+            case_bicg192(ref)
+        elif name == "batched_64x512":
+            case_batched(ref)
+        elif name.startswith("shard27_"):
+            _, m, pw = name.split("_")
+            case_shard27(ref_path, int(m), int(pw[1:]), 29700 + int(pw[1:]) + int(m))
+        else:
+            sys.exit(f"unknown case {name}")
+        print(f"  {name}: {time.perf_counter() - t0:.1f} s", flush=True)
+
+
+if __name__ == "__main__":
+    main()

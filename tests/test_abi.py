@@ -35,7 +35,7 @@ def test_binding_table_matches_header():
 
 def test_status_strings_and_version():
     lib = L.lib()
-    assert lib.sla_abi_version() == L.ABI_VERSION == 3
+    assert lib.sla_abi_version() == L.ABI_VERSION == 4
     assert lib.sla_status_string(L.SLA_ERR_UNSUPPORTED) == b"unsupported problem shape"
     assert lib.sla_status_string(L.SLA_NOT_CONVERGED).startswith(b"did not converge")
 
@@ -92,3 +92,29 @@ def test_malformed_sell_views_are_rejected_on_the_host(bad):
     """sla_spmv validates the view before any CUDA call: no GPU needed."""
     v = _view(**bad)
     assert L.lib().sla_spmv(L.SLA_F64, ctypes.byref(v), 1 << 20, 1 << 20, None) == L.SLA_ERR_INVALID
+
+
+@pytest.mark.parametrize("width,offsets", [(7, [-65536, -256, -1, 0, 1, 256, 65536]),
+                                           (27, list(range(-13, 14)))])
+def test_views_whose_int32_offsets_would_wrap_are_refused(width, offsets):
+    """A uniform view addresses entry j of slice s as 32*width*s + 32*j + lane
+    in int32; a view with more than 2^31 padded entries is refused with
+    SLA_ERR_UNSUPPORTED before any device work (a stencil matrix with nnz just
+    below the CSR builder's 2^31 limit would otherwise wrap once padded)."""
+    n_slots = (2 ** 31) // (32 * width) * 32 + 32  # one slice past the limit
+    v = _view(n_slots=n_slots, n_slices=(n_slots + 31) // 32, width=width, offsets=offsets,
+              n_cols=n_slots)
+    lib = L.lib()
+    assert lib.sla_spmv(L.SLA_F64, ctypes.byref(v), 1 << 20, 1 << 20, None) == L.SLA_ERR_UNSUPPORTED
+    info = L.SolveInfo()
+    assert lib.sla_pcg(L.SLA_F64, ctypes.byref(v), None, 1 << 20, 1 << 20, 0, 0.0, 1e-8, 10, 0,
+                       1 << 20, 1 << 40, ctypes.byref(info), None) == L.SLA_ERR_UNSUPPORTED
+    # one slice fewer fits: the same view is then only refused for other reasons
+    # (here the missing workspace), never for its size
+    ok = _view(n_slots=n_slots - 32, n_slices=(n_slots - 32 + 31) // 32, width=width,
+               offsets=offsets, n_cols=n_slots - 32)
+    assert lib.sla_pcg(L.SLA_F64, ctypes.byref(ok), None, 1 << 20, 1 << 20, 0, 0.0, 1e-8, 10, 0,
+                       None, 0, ctypes.byref(info), None) == L.SLA_ERR_WORKSPACE
+    arr = (L.c_i32 * L.MAX_DIAGS)(*offsets)
+    assert lib.sla_sell_diag_fill(L.SLA_F64, 1 << 20, 1 << 20, 1 << 20, None, n_slots, arr,
+                                  width, 1 << 20, None, 0, None) == L.SLA_ERR_UNSUPPORTED

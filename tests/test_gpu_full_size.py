@@ -1,0 +1,138 @@
+"""Parity at the benchmark sizes against torch-sla itself.
+
+The fixtures in tests/golden/full/ were made by running torch-sla's own
+pytorch backend on the host CPU at the workload sizes (make_golden_full.py
+beside them): the 3-D 7-point Poisson system with 256^3 unknowns (Jacobi PCG
+in fp64 and fp32, and the SpMV), the 192^3 upwind convection-diffusion
+system (Jacobi BiCGStab) and the batch of 64 variable-coefficient 512^2
+diffusion systems (batched CG forward and its adjoint backward). Each stores
+the iteration counts, the true relative residual, norms and the values at a
+seeded sample of 4096 indices.
+
+Gates, as the north-star parity bar states them:
+  * iteration count within +-3 % of torch-sla's;
+  * the true relative residual ||b - A x|| / ||b|| at or below rtol;
+  * SpMV within 1e-13 relative (fp64) / 1e-5 (fp32) at the sampled rows;
+  * gradients of the batched adjoint within 1e-8 relative.
+The solution itself is compared at the sampled indices (max-norm relative to
+the largest entry); its tolerance is stated per test with the reason.
+"""
+import math
+import os
+import warnings
+
+import pytest
+import torch
+
+import torch_sla_b200 as T
+from torch_sla_b200 import problems as P
+from torch_sla_b200.backends import pytorch_backend as PB
+
+pytestmark = pytest.mark.gpu
+
+FULL = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "full")
+
+
+def fixture(name):
+    return torch.load(os.path.join(FULL, f"{name}.pt"), weights_only=False)
+
+
+def iters_close(got, want):
+    return abs(got - want) <= max(1, math.ceil(0.03 * want))
+
+
+def sampled_rel(x, summ):
+    """max |x[idx] - ref[idx]| / max |ref[idx]| over the fixture's sample."""
+    got = x.reshape(-1)[summ["idx"].to(x.device)].double().cpu()
+    ref = summ["at"].double()
+    return float((got - ref).abs().max() / ref.abs().max())
+
+
+def true_rel_residual(A, x, b):
+    return float((b.double() - (A @ x).double()).norm() / b.double().norm())
+
+
+@pytest.mark.parametrize("tag", ["f64", "f32"])
+def test_pcg7_256_matches_reference(dev, tag):
+    """3-D 7-point Poisson 256^3, b ~ N(0,1) seed 1, Jacobi PCG to rtol 1e-8
+    (pcg_solve_optimized, pytorch_backend.py:1262-1362), plus y = A x with
+    x ~ N(0,1) seed 1 (CachedSparseMatrix.matvec, :154-161)."""
+    ref = fixture(f"pcg7_256_{tag}")
+    dtype = torch.float64 if tag == "f64" else torch.float32
+    m = 256
+    n = m ** 3
+    v, r, c, sh = P.poisson_3d_7pt(m, dtype=dtype, device=dev)
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    # SpMV at the sampled rows
+    x_s = P.rhs_normal(n, 1, dtype).to(dev)
+    y = A.matvec(x_s)
+    spmv_tol = 1e-13 if tag == "f64" else 1e-5
+    assert sampled_rel(y, ref["spmv_y"]) <= spmv_tol
+    del x_s, y
+    b = P.rhs_normal(n, 1, dtype).to(dev)
+    M = PB.get_preconditioner(A, "jacobi")
+    res = PB.pcg_solve_optimized(A, b, atol=0.0, rtol=ref["rtol"], maxiter=10000,
+                                 preconditioner=M)
+    assert res.converged == ref["converged"]
+    assert iters_close(res.num_iters, ref["iters"]), (res.num_iters, ref["iters"])
+    St = T.SparseTensor(v, r, c, sh)
+    tr = true_rel_residual(St, res.x, b)
+    assert tr <= ref["rtol"], (tr, ref["true_rel_residual"])
+    # Both solves stop on the same recursive-residual test; the iterates
+    # differ only by the rounding of the inner products (summation order).
+    # fp64: those differences stay far below the 1e-8 stopping tolerance;
+    # fp32: both carry float32 rounding of order 1e-7 per operation.
+    x_tol = 1e-8 if tag == "f64" else 1e-3
+    e = sampled_rel(res.x, ref["x"])
+    assert e <= x_tol, e
+    assert float(res.x.double().norm()) == pytest.approx(ref["x"]["norm"], rel=x_tol)
+
+
+def test_bicgstab_cd192_matches_reference(dev):
+    """192^3 upwind convection-diffusion, b ~ U(0,1) seed 3, Jacobi BiCGStab
+    to rtol 1e-8 (pbicgstab_solve, pytorch_backend.py:1508-1596)."""
+    ref = fixture("bicg_cd192")
+    v, r, c, sh = P.convdiff_3d_upwind(192, device=dev)
+    b = P.rhs_uniform01(sh[0], 3).to(dev)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        x, it, res = T.pbicgstab_solve(v, r, c, sh, b, atol=0.0, rtol=1e-8, maxiter=10000,
+                                       preconditioner="jacobi")
+    assert iters_close(it, ref["iters"]), (it, ref["iters"])
+    tr = true_rel_residual(T.SparseTensor(v, r, c, sh), x, b)
+    assert tr <= ref["rtol"], (tr, ref["true_rel_residual"])
+    # BiCGStab's iterates depend on the rounding of its inner products more
+    # than CG's (its count moves by several iterations with the summation
+    # order alone), so two solves to rtol 1e-8 agree to about the tolerance
+    # the stopping test guarantees, scaled by the system's conditioning.
+    e = sampled_rel(x, ref["x"])
+    assert e <= 1e-6, e
+
+
+def test_batched_64x512_forward_and_adjoint_match_reference(dev):
+    """64 x 512^2 diffusion, batched CG to rtol 1e-8 forward and backward
+    through spsolve_batch_same_layout (batch_solve.py:46-177), loss sum x^2."""
+    ref = fixture("batched_64x512")
+    vb, r, c, sh, bb = P.diffusion_2d_batched(64, 512, seed=2)
+    vb, r, c, bb = vb.to(dev), r.to(dev), c.to(dev), bb.to(dev)
+    vg = vb.clone().requires_grad_(True)
+    bg = bb.clone().requires_grad_(True)
+    U = T.spsolve_batch_same_layout(vg, r, c, sh, bg, method="cg", atol=0.0, rtol=ref["rtol"],
+                                    maxiter=10000)
+    it_fwd = PB.last_solve_info()["iterations"]
+    (U * U).sum().backward()
+    it_adj = PB.last_solve_info()["iterations"]
+    assert iters_close(it_fwd, ref["iters_forward"]), (it_fwd, ref["iters_forward"])
+    assert iters_close(it_adj, ref["iters_adjoint"]), (it_adj, ref["iters_adjoint"])
+    U = U.detach()
+    AU = torch.zeros_like(U)
+    AU.index_add_(1, r, vb * U[:, c])
+    rel = ((AU - bb).norm(dim=1) / bb.norm(dim=1)).cpu()
+    assert float(rel.max()) <= ref["rtol"], (float(rel.max()), float(ref["true_rel_residual"].max()))
+    eu = sampled_rel(U, ref["U"])
+    eg_val = sampled_rel(vg.grad, ref["grad_val"])
+    eg_b = sampled_rel(bg.grad, ref["grad_b"])
+    assert eu <= 1e-8, eu
+    assert eg_val <= 1e-8 and eg_b <= 1e-8, (eg_val, eg_b)
+    gn = vg.grad.norm(dim=1).cpu()
+    assert torch.allclose(gn, ref["grad_val_member_norm"], rtol=1e-8, atol=0)

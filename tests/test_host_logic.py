@@ -243,9 +243,10 @@ def test_gloo_two_ranks_partition_scatter_gather(tmp_path):
 
 
 def test_patch_install_into_reference():
-    ref = "/root/reference"
-    if not os.path.isdir(os.path.join(ref, "torch_sla")):
-        pytest.skip("torch-sla source tree not present")
+    from conftest import torch_sla_path
+    ref = torch_sla_path()
+    if ref is None:
+        pytest.skip("torch-sla not found (set TORCH_SLA_REF or install it into baseline/_ref)")
     import subprocess
     import sys
     code = (

@@ -45,7 +45,7 @@ def _noalloc_pcg(A, dinv, b, atol, rtol, flags):
     return x, info
 
 
-@pytest.mark.parametrize("flags", [L.SLA_PCG_AUTO, L.SLA_PCG_STREAMED])
+@pytest.mark.parametrize("flags", [L.SLA_PCG_AUTO, L.SLA_PCG_STREAMED, L.SLA_PCG_PERSISTENT])
 @pytest.mark.parametrize("case", ["poisson3d_jacobi", "poisson2d_none", "poisson3d_f32"])
 def test_noalloc_matches_workspace_entry_point(case, flags):
     if not torch.cuda.is_available():
@@ -85,3 +85,50 @@ def test_noalloc_refuses_systems_beyond_its_array():
                                  1e-8, 100, 0, ctypes.byref(info), L.stream_handle(dev))
     assert st == L.SLA_ERR_UNSUPPORTED
     assert float(x.abs().max()) == 0.0
+
+
+def _f32_row_limit():
+    """Largest float32 row count whose PCG scratch (sla_pcg_workspace) fits
+    the library's fixed array."""
+    lib = L.lib()
+    need = ctypes.c_size_t(0)
+
+    def fits(n):
+        L.check("sla_pcg_workspace", lib.sla_pcg_workspace(L.SLA_F32, n, ctypes.byref(need)))
+        return need.value <= L.SLA_PCG_NOALLOC_SCRATCH_BYTES
+
+    lo, hi = 1, 1 << 24
+    while hi - lo > 1:
+        mid = (lo + hi) // 2
+        lo, hi = (mid, hi) if fits(mid) else (lo, mid)
+    return lo
+
+
+def test_noalloc_float32_size_limit():
+    """float32 systems just under the array's limit solve and match sla_pcg;
+    one row more is refused without touching x."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    dev = torch.device("cuda", 0)
+    n_max = _f32_row_limit()
+    for n in (n_max, n_max + 1):
+        # diagonally dominant 1-D three-point system: converges in a few tens
+        # of iterations at any n
+        v, r, c = P.grid_coo((n,), 4.0, P.axis_edges(1, -1.0), torch.float32, dev)
+        A = PB.CachedSparseMatrix(v, r, c, (n, n))
+        dinv = PB.get_preconditioner(A, "jacobi").dinv
+        b = P.rhs_normal(n, 3, torch.float32).to(dev)
+        if n == n_max:
+            x_ref, info_ref = _workspace_pcg(A, dinv, b, 0.0, 1e-6, L.SLA_PCG_AUTO)
+            x, info = _noalloc_pcg(A, dinv, b, 0.0, 1e-6, L.SLA_PCG_AUTO)
+            assert info.status == info_ref.status == 0
+            assert info.iterations == info_ref.iterations
+            assert float((x - x_ref).abs().max() / x_ref.abs().max()) <= 1e-5
+        else:
+            x = torch.zeros_like(b)
+            info = L.SolveInfo()
+            st = L.lib().sla_pcg_noalloc(L.SLA_F32, A.sell().ref(), L.ptr(dinv), L.ptr(b),
+                                         L.ptr(x), 0, 0.0, 1e-6, 100, L.SLA_PCG_AUTO,
+                                         ctypes.byref(info), L.stream_handle(dev))
+            assert st == L.SLA_ERR_UNSUPPORTED
+            assert float(x.abs().max()) == 0.0

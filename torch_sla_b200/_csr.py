@@ -166,6 +166,8 @@ class DeviceCSR:
         padded = (n_slots + 31) // 32 * 32 * w
         if padded > (1.0 + self.DIAG_MAX_PAD) * max(nnz_view, 1):
             return None, ws
+        if padded > 2 ** 31 - 1:  # entry offsets are int32 in the kernels
+            return None, ws
         return list(offs)[:w], ws
 
     def diag_pattern(self):

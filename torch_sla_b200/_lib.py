@@ -22,6 +22,7 @@ SLA_ERR_INVALID, SLA_ERR_CUDA, SLA_ERR_NCCL = -1, -2, -3
 SLA_ERR_TIMEOUT, SLA_ERR_UNSUPPORTED, SLA_ERR_WORKSPACE, SLA_ERR_INDEX = -4, -5, -6, -7
 SLA_JACOBI_EPS, SLA_JACOBI_CLAMP, SLA_JACOBI_NONZERO = 0, 1, 2
 SLA_PCG_AUTO, SLA_PCG_STREAMED, SLA_PCG_PERSISTENT = 0, 1, 2
+SLA_PCG_NOALLOC_SCRATCH_BYTES = 16 << 20  # size of sla_pcg_noalloc's fixed device array
 SLA_MIXED_M_F32_NONE, SLA_MIXED_M_F32_JACOBI, SLA_MIXED_M_F64_JACOBI, SLA_MIXED_M_F64_NONE = (
     0, 1, 2, 3)
 
@@ -30,7 +31,7 @@ c_i32, c_i64, c_dbl, c_ptr, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_dou
 
 
 MAX_DIAGS = 32  # SLA_MAX_DIAGS
-ABI_VERSION = 3  # SLA_ABI_VERSION
+ABI_VERSION = 4  # SLA_ABI_VERSION
 
 
 class SellView(ctypes.Structure):
@@ -134,6 +135,8 @@ _SIGNATURES = {
                                           c_ptr]),
     "sla_p2p_create": (ctypes.c_int, [c_ptr, _P(HaloPlan), ctypes.c_int, _P(c_ptr)]),
     "sla_p2p_destroy": (ctypes.c_int, [c_ptr]),
+    "sla_p2p_profile_read": (ctypes.c_int, [c_ptr, ctypes.c_int, _P(ctypes.c_ulonglong),
+                                            ctypes.c_int]),
     "sla_shard_cg_p2p": (ctypes.c_int, [c_ptr, _P(HaloPlan), ctypes.c_int, _P(SellView),
                                         _P(SellView), c_ptr, c_ptr, c_ptr, c_dbl, c_dbl, c_i64,
                                         c_i64, c_ptr, c_sz, _P(SolveInfo), c_ptr]),

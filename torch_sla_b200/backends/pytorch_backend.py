@@ -138,12 +138,14 @@ def _as_dinv(preconditioner, A: CachedSparseMatrix):
                               "built by get_preconditioner ('jacobi', 'none') only")
 
 
-def _pcg_core(A: CachedSparseMatrix, b: Tensor, x0, dinv, atol, rtol, maxiter, flags=0):
+def _pcg_core(A: CachedSparseMatrix, b: Tensor, x0, dinv, atol, rtol, maxiter, flags=0,
+              sell=None):
+    """sla_pcg on A's SELL view (or on `sell`, another view of the same rows)."""
     L.require_cuda(b, x0)
     if b.dim() != 1 or b.shape[0] != A.n:
         raise ValueError(f"torch_sla_b200: b must have shape [{A.n}]")
     b = b.to(A.dtype).contiguous()
-    sell = A.sell()
+    sell = A.sell() if sell is None else sell
     lib = L.lib()
     need = ctypes.c_size_t(0)
     L.check("sla_pcg_workspace", lib.sla_pcg_workspace(A.csr.code, A.n, ctypes.byref(need)))

@@ -407,7 +407,8 @@ int sla_batched_cg_diag(int dtype, const sla_sell_t *A, const void *vals_diag, i
   if (!A || A->n_diags <= 0 || A->row_ids || A->row_base) return SLA_ERR_INVALID;
   sla_sell_t pat = *A;
   if (!pat.val) pat.val = vals_diag;  // the pattern view needs no values of its own
-  if (!sell_ok(&pat) || !vals_diag) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(&pat));
+  if (!vals_diag) return SLA_ERR_INVALID;
   const int64_t n = pat.n_slots;
   if (pat.n_cols != n) return SLA_ERR_INVALID;  // square systems
   SLA_TRY(batched_args_ok(dtype, n, batch, b, x, info, workspace, workspace_bytes));

@@ -270,7 +270,8 @@ int sla_bicgstab_workspace(int dtype, int64_t n, size_t *bytes) {
 int sla_bicgstab(int dtype, const sla_sell_t *A, const void *dinv, const void *b, void *x,
                  int x_is_guess, double atol, double rtol, int64_t maxiter, void *workspace,
                  size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
-  if (!sell_ok(A) || !b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(A));
+  if (!b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
   if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
   info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;

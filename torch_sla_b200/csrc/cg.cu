@@ -19,7 +19,6 @@
 //
 // Persistent path (small systems, vectors L2-resident): the same two phases
 // in one cooperative launch separated by a bounded grid barrier.
-#include <mutex>
 
 #include "solver.cuh"
 
@@ -510,28 +509,19 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
 // a device address; the address is resolved per device with
 // cudaGetSymbolAddress and passed to the kernels.
 static __device__ __align__(256) unsigned char g_pcg_noalloc_scratch[SLA_PCG_NOALLOC_SCRATCH_BYTES];
-constexpr int kMaxDevices = 64;
 
-// Device address of the scratch array on the current device, resolved once
-// per device (the first call on a device does this set-up).
+// Device address of the scratch array on the current device. It is resolved
+// on every call (cudaGetSymbolAddress is cheap next to a solve), so an
+// address can never go stale, e.g. after a cudaDeviceReset reloads the module.
 static int noalloc_scratch(void **out) {
-  static std::mutex mu;
-  static void *addr[kMaxDevices] = {};
-  int dev = 0;
-  SLA_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kMaxDevices) return SLA_ERR_UNSUPPORTED;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void *p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_pcg_noalloc_scratch);
-    if (e != cudaSuccess || !p) {
-      fprintf(stderr, "[sla_b200] cudaGetSymbolAddress(pcg scratch) failed: %s\n",
-              cudaGetErrorString(e));
-      return SLA_ERR_CUDA;
-    }
-    addr[dev] = p;
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_pcg_noalloc_scratch);
+  if (e != cudaSuccess || !p) {
+    fprintf(stderr, "[sla_b200] cudaGetSymbolAddress(pcg scratch) failed: %s\n",
+            cudaGetErrorString(e));
+    return SLA_ERR_CUDA;
   }
-  *out = addr[dev];
+  *out = p;
   return SLA_OK;
 }
 
@@ -566,7 +556,9 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
     int cap = per_sm * dev.sm_count;
     coop_grid = want < cap ? want : cap;
     if (coop_grid < 1) coop_grid = 1;
-    persistent = per_sm > 0;
+    // the same rule as pcg_impl: AUTO keeps large systems on the streamed path
+    bool small = n <= (int64_t)(1 << 20);
+    persistent = per_sm > 0 && (flags == SLA_PCG_PERSISTENT || small);
   }
   if (flags == SLA_PCG_PERSISTENT && !persistent) return SLA_ERR_UNSUPPORTED;
   if (persistent) {
@@ -620,7 +612,8 @@ int sla_pcg_workspace(int dtype, int64_t n, size_t *bytes) {
 int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b, void *x,
             int x_is_guess, double atol, double rtol, int64_t maxiter, int flags, void *workspace,
             size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
-  if (!sell_ok(A) || !b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(A));
+  if (!b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
   if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
   if (flags < 0 || flags > 2) return SLA_ERR_INVALID;
@@ -651,7 +644,8 @@ int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b, voi
 int sla_pcg_noalloc(int dtype, const sla_sell_t *A, const void *dinv, const void *b, void *x,
                     int x_is_guess, double atol, double rtol, int64_t maxiter, int flags,
                     sla_solve_info_t *info, sla_stream_t stream) {
-  if (!sell_ok(A) || !b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(A));
+  if (!b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
   if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
   if (flags < 0 || flags > 2) return SLA_ERR_INVALID;

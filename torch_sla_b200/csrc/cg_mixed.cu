@@ -393,7 +393,8 @@ int sla_pcg_mixed(const sla_sell_t *A, int precond, const void *dinv, int b_dtyp
                   double *x, int x_is_guess, double atol, double rtol, int64_t maxiter,
                   void *workspace, size_t workspace_bytes, sla_solve_info_t *info,
                   double *pap_out, sla_stream_t stream) {
-  if (!sell_ok(A) || !b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(A));
+  if (!b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
   if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
   if (b_dtype != SLA_F32 && b_dtype != SLA_F64) return SLA_ERR_INVALID;

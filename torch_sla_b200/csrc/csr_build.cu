@@ -660,6 +660,8 @@ int sla_sell_diag_fill(int dtype, const int32_t *rowptr, const int32_t *colind, 
                        sla_stream_t stream) {
   if (!rowptr || !offsets || n_slots < 0 || n_diags < 1 || n_diags > SLA_MAX_DIAGS)
     return SLA_ERR_INVALID;
+  // the view's entries are addressed with int32 offsets
+  if ((n_slots + 31) / 32 * 32 * (int64_t)n_diags > (int64_t)INT32_MAX) return SLA_ERR_UNSUPPORTED;
   size_t need = 0;
   sla_sell_diag_probe_workspace(&need);
   if (!workspace || workspace_bytes < need) return SLA_ERR_WORKSPACE;

@@ -497,7 +497,8 @@ int sla_multi_rhs_cg_diag(int dtype, const sla_sell_t *A, int64_t k, const void 
                           int64_t maxiter, int64_t check_every, int64_t *iters_out,
                           int32_t *converged_out, void *workspace, size_t workspace_bytes,
                           sla_solve_info_t *info, sla_stream_t stream) {
-  if (!sell_ok(A) || A->n_diags <= 0 || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(A));
+  if (A->n_diags <= 0 || A->row_ids || A->row_base) return SLA_ERR_INVALID;
   const int64_t n = A->n_slots;
   if (A->n_cols != n) return SLA_ERR_INVALID;  // square system
   SLA_TRY(mrhs_args_ok(dtype, n, k, b, x, info, check_every, workspace, workspace_bytes));

@@ -66,6 +66,15 @@ inline Sell<T> make_sell(const sla_sell_t *A) {
 
 inline bool diag_width_supported(int w) { return w == 5 || w == 7 || w == 27; }
 
+// Entry offsets of a uniform-width view (diagonal-offset or uniform explicit)
+// are computed in int32 as 32 * width * slice + 32 * entry + lane: the
+// padded entry count must stay below 2^31. Non-uniform explicit views carry
+// their offsets in int32 slice pointers, bounded when they were built.
+inline bool sell_offsets_fit(const sla_sell_t *A) {
+  const int64_t w = A->uniform_width > 0 ? A->uniform_width : A->n_diags;
+  return w <= 0 || A->n_slices * 32 * w <= (int64_t)INT32_MAX;
+}
+
 inline bool sell_ok(const sla_sell_t *A) {
   if (!A) return false;
   if (A->n_slots < 0 || A->n_slices != (A->n_slots + 31) / 32) return false;
@@ -84,6 +93,14 @@ inline bool sell_ok(const sla_sell_t *A) {
   if (A->n_diags < 0) return false;
   if (A->n_slices > 0 && (!A->slice_ptr || !A->col || !A->val)) return false;
   return true;
+}
+
+// SLA_OK for a valid view, SLA_ERR_UNSUPPORTED when its int32 entry
+// offsets would wrap, SLA_ERR_INVALID otherwise.
+inline int sell_check(const sla_sell_t *A) {
+  if (!A) return SLA_ERR_INVALID;
+  if (A->n_slices >= 0 && !sell_offsets_fit(A)) return SLA_ERR_UNSUPPORTED;
+  return sell_ok(A) ? SLA_OK : SLA_ERR_INVALID;
 }
 
 // Entries per load batch: a batch issues all its column/value loads, then all

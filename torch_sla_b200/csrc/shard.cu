@@ -664,7 +664,8 @@ int sla_shard_spmv(void *comm, const sla_halo_plan_t *plan, int dtype, const sla
                    void *recvbuf, sla_stream_t stream) {
   Comm *c = (Comm *)comm;
   if (!c || !c->nccl || !plan_ok(plan) || !x_local || !y_owned) return SLA_ERR_INVALID;
-  if (!sell_ok(A_interior) || !sell_ok(A_boundary)) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(A_interior));
+  SLA_TRY(sell_check(A_boundary));
   if (A_boundary->n_diags > 0) return SLA_ERR_UNSUPPORTED;
   if (A_interior->n_diags > 0 && A_interior->n_cols > plan->n_owned + plan->n_halo)
     return SLA_ERR_INVALID;
@@ -723,7 +724,8 @@ int sla_shard_rmatvec(void *comm, const sla_halo_plan_t *plan, int dtype, const 
                       const void *y_owned, void *w_local, void *sendbuf, void *recvbuf,
                       sla_stream_t stream) {
   Comm *c = (Comm *)comm;
-  if (!c || !c->nccl || !plan_ok(plan) || !sell_ok(AT) || !w_local) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(AT));
+  if (!c || !c->nccl || !plan_ok(plan) || !w_local) return SLA_ERR_INVALID;
   if (AT->n_slots != plan->n_owned + plan->n_halo || AT->row_ids || AT->row_base)
     return SLA_ERR_INVALID;
   if (AT->n_diags > 0 && AT->n_cols > plan->n_owned) return SLA_ERR_INVALID;

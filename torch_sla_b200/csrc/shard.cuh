@@ -273,7 +273,9 @@ inline int shard_args_ok(void *ch, void *cr, const sla_halo_plan_t *plan, const 
                          const sla_sell_t *Ab, const void *b, void *x, sla_solve_info_t *info,
                          int64_t every) {
   if (!ch || !cr || !((Comm *)ch)->nccl || !((Comm *)cr)->nccl) return SLA_ERR_INVALID;
-  if (!plan_ok(plan) || !sell_ok(Ai) || !sell_ok(Ab) || !info || every < 1) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(Ai));
+  SLA_TRY(sell_check(Ab));
+  if (!plan_ok(plan) || !info || every < 1) return SLA_ERR_INVALID;
   if (Ab->n_diags > 0) return SLA_ERR_UNSUPPORTED;
   // interior gathers read owned vectors only
   if (Ai->n_diags > 0 && Ai->n_cols > plan->n_owned) return SLA_ERR_INVALID;

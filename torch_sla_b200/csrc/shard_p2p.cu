@@ -34,6 +34,9 @@ struct P2PHeader {
   unsigned long long arrive[kP2PMaxRanks];
   unsigned long long red_flag[2][kRedPoints][kP2PMaxRanks];
   double red_val[2][kRedPoints][kP2PMaxRanks][kRedValues];
+  // instrumentation of this rank's solver kernels, written only while the
+  // library's profiling is on (kTimer* slots, nanoseconds summed)
+  unsigned long long timers[8];
   unsigned send_count;
   unsigned pad[63];
 };
@@ -49,7 +52,20 @@ struct P2PDev {
   const T *halo;                 // my halo buffer (written by the neighbours)
   unsigned long long seq;        // epoch << 32
   unsigned long long wait_ns;    // bound of every wait on another GPU
+  unsigned long long *timers;    // &local->timers while profiling, else null
 };
+
+// Timer slots (sums over launches; per-block slots also over the blocks):
+//   kTimerSend   K_P, every block: storing its share of the neighbours' halo
+//                and the system-scope fence that makes the stores visible
+//   kTimerWait   K_A, every block: waiting for the neighbours' arrivals
+//   kTimerRedA   K_A, the last block: the cross-rank (p, Ap) sum
+//   kTimerRedB   K_B, the last block: the cross-rank (r,r), (r,z) sum
+//   kTimerBlocks K_A: blocks per launch summed (divides kTimerWait)
+//   kTimerIters  K_A launches that ran (iterations)
+//   kTimerSendBlocks K_P: blocks per launch summed (divides kTimerSend)
+enum { kTimerSend = 0, kTimerWait, kTimerRedA, kTimerRedB, kTimerBlocks, kTimerIters,
+       kTimerSendBlocks, kTimerCount };
 
 struct P2PPlan {
   Comm *comm = nullptr;
@@ -86,6 +102,20 @@ __device__ __forceinline__ bool wait_seq(const unsigned long long *p, unsigned l
     __nanosleep(32);
   }
   return true;
+}
+
+template <typename T>
+__device__ __forceinline__ unsigned long long p2p_tic(const P2PDev<T> &P) {
+  return P.timers ? global_ns() : 0ull;
+}
+// Adds the time since t0 to a timer slot (thread 0 of the calling block).
+template <typename T>
+__device__ __forceinline__ void p2p_toc(const P2PDev<T> &P, int slot, unsigned long long t0) {
+  if (P.timers && threadIdx.x == 0) atomicAdd(P.timers + slot, global_ns() - t0);
+}
+template <typename T>
+__device__ __forceinline__ void p2p_count(const P2PDev<T> &P, int slot, unsigned long long v) {
+  if (P.timers && threadIdx.x == 0) atomicAdd(P.timers + slot, v);
 }
 
 // This block's share of the halo values of all neighbours, then the arrival
@@ -225,19 +255,27 @@ shard_cg_p2p_spmv(Sell<T> AI, Sell<T> AB, int32_t n_own, const int32_t *__restri
   for_each_slice<WS>(AI, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     emit(AI, s, sell_row_at<WS>(AI, s, sbase, swidth, lane, inner));
   });
+  const unsigned long long tw = p2p_tic(P);
   if (!p2p_wait_halo(P, seq)) {
     if (threadIdx.x == 0) st->stopped = kStopTimeout;
     return;
+  }
+  p2p_toc(P, kTimerWait, tw);
+  if (blockIdx.x == 0) {
+    p2p_count(P, kTimerBlocks, gridDim.x);
+    p2p_count(P, kTimerIters, 1);
   }
   HaloGatherL2<T, ShardP<T, PREC>> g{inner, P.halo, n_own};
   for_each_slice<WSB>(AB, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     emit(AB, s, sell_row_at<WSB>(AB, s, sbase, swidth, lane, g));
   });
   if (!last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem)) return;
+  const unsigned long long tr = p2p_tic(P);
   if (!p2p_allreduce<1>(P, 1, (int)(k & 1), seq, acc)) {
     if (threadIdx.x == 0) st->stopped = kStopTimeout;
     return;
   }
+  p2p_toc(P, kTimerRedA, tr);
   if (threadIdx.x == 0) R->pap[0] = acc[0];
 }
 
@@ -254,7 +292,10 @@ shard_cg_p2p_pform(int64_t n, const int32_t *__restrict__ send_index, const T *_
   if (*(volatile const int *)&st->stopped) return;
   if (cg_stop(R, k, every, cg_tol(R, atol, rtol))) return;
   ShardP<T, PREC> inner{r, dinv, p_old, (T)cg_beta(R, k)};
+  const unsigned long long t0 = p2p_tic(P);
   p2p_send_halo(P, send_index, inner, P.seq + (unsigned long long)(k + 1));
+  p2p_toc(P, kTimerSend, t0);
+  if (blockIdx.x == 0) p2p_count(P, kTimerSendBlocks, gridDim.x);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     p_new[i] = inner((int32_t)i);
@@ -290,19 +331,27 @@ shard_cg_p2p_spmv_split(Sell<T> AI, Sell<T> AB, int32_t n_own, const T *__restri
   for_each_slice<WS, true>(AI, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     emit(AI, s, sell_row_at<WS>(AI, s, sbase, swidth, lane, inner));
   });
+  const unsigned long long tw = p2p_tic(P);
   if (!p2p_wait_halo(P, seq)) {
     if (threadIdx.x == 0) st->stopped = kStopTimeout;
     return;
+  }
+  p2p_toc(P, kTimerWait, tw);
+  if (blockIdx.x == 0) {
+    p2p_count(P, kTimerBlocks, gridDim.x);
+    p2p_count(P, kTimerIters, 1);
   }
   HaloGatherL2<T, PlainGather<T>> g{inner, P.halo, n_own};
   for_each_slice<WSB>(AB, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     emit(AB, s, sell_row_at<WSB>(AB, s, sbase, swidth, lane, g));
   });
   if (!last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem)) return;
+  const unsigned long long tr = p2p_tic(P);
   if (!p2p_allreduce<1>(P, 1, (int)(k & 1), seq, acc)) {
     if (threadIdx.x == 0) st->stopped = kStopTimeout;
     return;
   }
+  p2p_toc(P, kTimerRedA, tr);
   if (threadIdx.x == 0) R->pap[0] = acc[0];
 }
 
@@ -329,10 +378,12 @@ shard_cg_p2p_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__
     acc[1] += (double)ri * (double)zi;
   }
   if (!last_block_sum<2, kBlock>(acc, partials, &st->counter[3], smem)) return;
+  const unsigned long long tr = p2p_tic(P);
   if (!p2p_allreduce<2>(P, 2, (int)(k & 1), P.seq + (unsigned long long)(k + 1), acc)) {
     if (threadIdx.x == 0) st->stopped = kStopTimeout;
     return;
   }
+  p2p_toc(P, kTimerRedB, tr);
   if (threadIdx.x == 0) {
     R->loc[k & 1][0] = acc[0];
     R->loc[k & 1][1] = acc[1];
@@ -544,6 +595,9 @@ static P2PDev<T> p2p_dev(const P2PPlan *pp) {
   d.halo = (const T *)(pp->local + p2p_halo_offset());
   d.seq = pp->epoch << 32;
   d.wait_ns = pp->wait_ns;
+  d.timers = profiler().enabled
+                 ? (unsigned long long *)(pp->local + offsetof(P2PHeader, timers))
+                 : nullptr;
   return d;
 }
 
@@ -792,7 +846,9 @@ int sla_p2p_create(void *comm, const sla_halo_plan_t *plan, int dtype, void **p2
   if (!c || !c->nccl || !plan_ok(plan)) return SLA_ERR_INVALID;
   if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
   const int world = c->nranks, me = c->rank;
-  if (world < 2 || world > kP2PMaxRanks) return SLA_OK;  // same answer on every rank
+  // one rank has no peer to map but runs the same kernels (its cross-rank
+  // sums cover itself), so one and several GPUs time the same code
+  if (world < 1 || world > kP2PMaxRanks) return SLA_OK;  // same answer on every rank
   P2PPlan *pp = new P2PPlan();
   pp->comm = c;
   pp->world = world;
@@ -833,6 +889,18 @@ int sla_p2p_create(void *comm, const sla_halo_plan_t *plan, int dtype, void **p2
     if (sec > 0.0) pp->wait_ns = (unsigned long long)(sec * 1e9);
   }
   *p2p_out = pp;
+  return SLA_OK;
+}
+
+int sla_p2p_profile_read(void *p2p, int reset, unsigned long long *out, int n_out) {
+  P2PPlan *pp = (P2PPlan *)p2p;
+  if (!pp || !out || n_out < 0) return SLA_ERR_INVALID;
+  unsigned long long t[kTimerCount] = {};
+  char *dev = pp->local + offsetof(P2PHeader, timers);
+  SLA_CUDA_TRY(cudaDeviceSynchronize());
+  SLA_CUDA_TRY(cudaMemcpy(t, dev, sizeof(t), cudaMemcpyDeviceToHost));
+  if (reset) SLA_CUDA_TRY(cudaMemset(dev, 0, sizeof(t)));
+  for (int i = 0; i < n_out; ++i) out[i] = i < kTimerCount ? t[i] : 0ull;
   return SLA_OK;
 }
 

@@ -81,7 +81,8 @@ using namespace sla;
 extern "C" {
 
 int sla_spmv(int dtype, const sla_sell_t *A, const void *x, void *y, sla_stream_t stream) {
-  if (!sell_ok(A) || (A->n_slots > 0 && (!x || !y))) return SLA_ERR_INVALID;
+  SLA_TRY(sell_check(A));
+  if (A->n_slots > 0 && (!x || !y)) return SLA_ERR_INVALID;
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype == SLA_F64) return spmv_launch<double>(A, x, y, s);
   if (dtype == SLA_F32) return spmv_launch<float>(A, x, y, s);

@@ -185,10 +185,12 @@ class _ShardPlan:
 
     def enable_p2p(self) -> None:
         """Map the peer-memory exchange buffers of the shard CG (collective;
-        stays None when any rank cannot, or TORCH_SLA_B200_P2P=0)."""
+        stays None when any rank cannot, or TORCH_SLA_B200_P2P=0). A one-rank
+        group gets a plan too: it maps no peer and runs the same kernels as
+        several ranks do."""
         if self.p2p is not None or os.environ.get("TORCH_SLA_B200_P2P", "1") == "0":
             return
-        if not dist.is_initialized() or dist.get_world_size(self._group) < 2:
+        if not dist.is_initialized():
             return
         from .comm import communicators, register_p2p
         h = ctypes.c_void_p()
@@ -198,6 +200,17 @@ class _ShardPlan:
         if h.value:
             self.p2p = h
             register_p2p(h)
+
+    def p2p_timers(self, reset: bool = True) -> dict | None:
+        """Device-timer readings of the peer-memory CG kernels since the last
+        reset (recorded only while profiling is on; None without a plan)."""
+        if self.p2p is None:
+            return None
+        out = (ctypes.c_ulonglong * 8)()
+        L.check("sla_p2p_profile_read", L.lib().sla_p2p_profile_read(self.p2p, int(reset), out, 8))
+        keys = ("send_ns", "wait_ns", "sum_pap_ns", "sum_rr_ns", "ka_blocks", "iterations",
+                "kp_blocks")
+        return {k: int(out[i]) for i, k in enumerate(keys)}
 
     def dinv(self, kind: str):
         if kind not in self._dinv:
