@@ -18,6 +18,7 @@ GPU), mrhs (128^3 7-point with 16 right-hand sides, multi-RHS CG), mixed
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                   [--workload pcg7|cg2d|spmv|batched|bicgstab|pcg27|mrhs|mixed] [--grid M]
+                  [--layout auto|explicit]
 """
 from __future__ import annotations
 
@@ -154,7 +155,9 @@ def sell_format(sell, V=8):
     if sell.diagonal_offsets:
         return {"format": f"SELL-32 diagonal-offset ({sell.uniform_width} diagonals, "
                           "no column array)", "matrix_bytes": sell.padded_nnz * V}
-    return {"format": "SELL-32 int32 (sigma=1)", "matrix_bytes": sell.padded_nnz * (V + 4)}
+    rows = 4 * sell.n_slots if sell.row_ids is not None else 0  # row ids of a sorted view
+    return {"format": f"SELL-32 int32 (sigma={getattr(sell, 'sigma', 1)})",
+            "matrix_bytes": sell.padded_nnz * (V + 4) + rows}
 
 
 def roofline(kernel, alg_bytes, ms_total, launches, traffic_key, format_bytes=None):
@@ -210,9 +213,11 @@ def wl_pcg7(args, dev, local):
     A = PB.CachedSparseMatrix(v, r, c, sh)
     Mj = PB.get_preconditioner(A, "jacobi")
     nnz = A.csr.nnz
+    # --layout explicit: the whole solve on the int32-column view
+    view = A.csr.sell(diagonal=False) if args.layout == "explicit" else A.sell()
 
     def solve_once():
-        return PB._pcg_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000)[1].iterations
+        return PB._pcg_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000, sell=view)[1].iterations
 
     for _ in range(args.warmup):
         solve_once()
@@ -228,7 +233,7 @@ def wl_pcg7(args, dev, local):
     value = iters / (ms / 1e3)
     peak, kind = peaks()
     iter_bytes = matrix_bytes(nnz, n) + 13 * 8 * n
-    fm = sell_format(A.sell())
+    fm = sell_format(view)
     line = base_line(args, METRIC, value, "iterations/s", ms, 1)
     line["config"] = {"workload": "jacobi_pcg_poisson3d_7pt", "grid": [m, m, m], "n": n,
                       "nnz": nnz, "rtol": RTOL, "b": "N(0,1) seed 1",
@@ -238,8 +243,9 @@ def wl_pcg7(args, dev, local):
                       "parallelism": "single GPU"}
     # K_A: the SpMV over the search direction p (formed by cg_pform_kernel):
     # matrix + p read once + Ap written
+    tkey = "pcg7-explicit" if args.layout == "explicit" else "pcg7"
     line["roofline"] = roofline("cg_spmv_split_kernel", matrix_bytes(nnz, n) + 2 * 8 * n, ka_ms,
-                                ka_n, f"cg_spmv_split_kernel@pcg7:{m}",
+                                ka_n, f"cg_spmv_split_kernel@{tkey}:{m}",
                                 fm["matrix_bytes"] + 2 * 8 * n)
     line["roofline"]["update_kernel"] = {
         "kernel": "cg_update_kernel", "avg_launch_ms": round(kb_ms / max(kb_n, 1), 5),
@@ -257,7 +263,8 @@ def wl_pcg7(args, dev, local):
                                   "layout_bytes_per_iter": fm["matrix_bytes"] + 12 * 8 * n,
                                   "frac": round((fm["matrix_bytes"] + 12 * 8 * n) * value
                                                 / 1e9 / peak, 4)}
-    line["roofline"]["explicit"] = explicit_pcg7(A, b, Mj, n, nnz, m)
+    if args.layout != "explicit":
+        line["roofline"]["explicit"] = explicit_pcg7(A, b, Mj, n, nnz, m)
     if not args.no_e2e:
         line["e2e"] = e2e_pcg7(args, v, r, c, b_host, sh, dev)
     line["gpu_launches"] = launches
@@ -361,7 +368,9 @@ def wl_cg2d(args, dev, local):
                      ms / args.steps, "ms/solve", ms, 1, hib=False)
     line["config"] = {"workload": "cg_poisson2d_5pt_256", "n": sh[0], "nnz": A.csr.nnz,
                       "iterations_per_solve": its[0], "preconditioner": "none",
-                      "kernel": "cg_persistent_kernel (one cooperative launch per solve)",
+                      "kernel": "cg_cluster_kernel (one thread-block cluster per solve: "
+                                "values, search direction and partial sums in distributed "
+                                "shared memory, cluster barriers)",
                       "iterations_per_s": round(sum(its) / (ms / 1e3), 1)}
     line["gpu_launches"] = L.launch_count() - l0
     # unpreconditioned CG: matrix + 11 vector passes per iteration; the
@@ -369,9 +378,18 @@ def wl_cg2d(args, dev, local):
     # for comparison (the kernel is bound by its two grid barriers per
     # iteration, not by bandwidth)
     per_iter = matrix_bytes(A.csr.nnz, sh[0]) + 11 * 8 * sh[0]
-    line["roofline"] = roofline("cg_persistent_kernel", per_iter * its[0], ms, args.steps,
-                                "cg_persistent_kernel@cg2d:256")
-    line["roofline"]["note"] = "L2-resident; one launch per solve"
+    line["roofline"] = roofline("cg_cluster_kernel", per_iter * its[0], ms, args.steps,
+                                "cg_cluster_kernel@cg2d:256")
+    line["roofline"]["note"] = ("one launch per solve; the matrix and search direction live in "
+                                "shared memory, so HBM is not the bound: latency of the three "
+                                "cluster barriers per iteration is")
+    # the cooperative-grid kernel on the same solve, for comparison
+    l1 = L.launch_count()
+    ms_p, its_p, _ = timed(lambda: PB._pcg_core(A, b, None, None, 0.0, 1e-10, 10000,
+                                                L.SLA_PCG_PERSISTENT)[1].iterations,
+                           args.steps, dev, local)
+    line["config"]["persistent_grid_kernel"] = {"ms_per_solve": round(ms_p / args.steps, 3),
+                                                "iterations_per_solve": its_p[0]}
     line["clocks"] = clk
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
@@ -421,6 +439,7 @@ def wl_spmv(args, dev, local):
                         "clocks": clk, "_ms": ms, "_reps": reps}
             del sell
         del csr, x, y
+    res["irregular"] = spmv_irregular(dev, local, peak)
     f64 = res["f64"]
     line = base_line(args, "SpMV HBM GB/s (256^3 7-point, fp64)", f64["achieved_gbs"],
                      "GB/s", f64["us_per_spmv"] / 1e3 * args.steps, 1)
@@ -432,6 +451,41 @@ def wl_spmv(args, dev, local):
                       "l2": "inputs larger than L2"}
     line["clocks"] = f64["clocks"]
     return line
+
+
+def spmv_irregular(dev, local, peak, n=4_000_000, avg=16.0):
+    """fp64 SpMV on a matrix with power-law row lengths (problems.powerlaw_coo:
+    4M rows, about 16 entries per row, the longest 1025): the SELL-32 view in
+    row order (sigma = 1) against the view sorted by length inside windows
+    of sigma rows (SELL-32-sigma), with padding ratios and the bytes each
+    layout moves."""
+    from torch_sla_b200 import problems as P
+    from torch_sla_b200._csr import DeviceCSR, spmv
+    v, r, c, sh = P.powerlaw_coo(n, avg)
+    csr = DeviceCSR(v.to(dev), r.to(dev), c.to(dev), sh)
+    del v, r, c
+    x = P.rhs_normal(n, SEED).to(dev)
+    y = torch.empty_like(x)
+    out = {"matrix": f"power-law row lengths, n={n}, nnz={csr.nnz}, "
+                     f"longest row {int((csr.rowptr[1:] - csr.rowptr[:-1]).max())}"}
+    for sigma in (1, 1024, 4096):
+        sell = csr.sell(sigma=sigma)
+        for _ in range(5):
+            spmv(sell, x, n, y)
+        ms, _, _ = timed(lambda: spmv(sell, x, n, y), 50, dev, local)
+        sec = ms / 50 / 1e3
+        fm = sell_format(sell)
+        fb = fm["matrix_bytes"] + 2 * 8 * n
+        alg = matrix_bytes(csr.nnz, n) + 2 * 8 * n
+        out[f"sigma{sigma}"] = {"us_per_spmv": round(sec * 1e6, 2),
+                                "padding": round(sell.padded_nnz / csr.nnz, 3),
+                                "bytes": fb, "achieved_gbs": round(fb / sec / 1e9, 1),
+                                "frac": round(fb / sec / 1e9 / peak, 4),
+                                "alg_bytes": alg, "alg_frac": round(alg / sec / 1e9 / peak, 4)}
+        del sell
+    out["auto_sigma"] = csr.sell().sigma
+    del csr, x, y
+    return out
 
 
 def wl_batched(args, dev, local):
@@ -941,6 +995,8 @@ def main():
                     choices=["pcg7", "cg2d", "spmv", "batched", "bicgstab", "pcg27", "mrhs",
                              "mixed"])
     ap.add_argument("--grid", type=int, default=M, help="grid edge per GPU (default 256)")
+    ap.add_argument("--layout", default="auto", choices=["auto", "explicit"],
+                    help="pcg7: the SELL view the solver picks, or the int32-column view")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)

@@ -57,9 +57,15 @@ enum {
 
 /* Solver path selection for sla_pcg (flags argument). */
 enum {
-  SLA_PCG_AUTO = 0,        /* persistent kernel for small systems, else streamed */
-  SLA_PCG_STREAMED = 1,    /* two fused kernels per iteration                     */
-  SLA_PCG_PERSISTENT = 2   /* one cooperative launch for the whole solve          */
+  SLA_PCG_AUTO = 0,        /* small systems: the cluster kernel when the system
+                              fits one thread-block cluster, else the persistent
+                              kernel; larger systems streamed                     */
+  SLA_PCG_STREAMED = 1,    /* three kernels per iteration                         */
+  SLA_PCG_PERSISTENT = 2,  /* one cooperative launch for the whole solve          */
+  SLA_PCG_CLUSTER = 3      /* one thread-block cluster for the whole solve (the
+                              vectors and a diagonal-offset view in distributed
+                              shared memory); SLA_ERR_UNSUPPORTED when it does
+                              not fit                                             */
 };
 
 /* SELL-32 (SELL-C-sigma with C = 32, sigma = 1) matrix view. Slice s holds
@@ -142,6 +148,20 @@ int sla_sell_fill(int dtype, const int32_t *rowptr, const int32_t *colind,
                   const void *vals, const int32_t *row_ids, int64_t n_slots,
                   const int32_t *slice_ptr, int32_t *sell_col, void *sell_val,
                   sla_stream_t stream);
+/* SELL-32-sigma row order (no counterpart in torch-sla, whose CSR SpMV
+ * serves any pattern, pytorch_backend.py:154-161): order[t] lists the rows
+ * of the view (row_ids, or 0..n_slots-1 when row_ids is NULL) with each
+ * window of sigma consecutive entries sorted by decreasing row length, equal
+ * lengths kept in ascending order, and every full window rotated by
+ * (window index mod sigma/32) slices so that the widest slices of
+ * successive windows fall on different slice positions. Passed as the row_ids of
+ * sla_sell_layout / sla_sell_fill it groups rows of similar length into each
+ * 32-row slice, so irregular patterns pad less. sigma is a power of two in
+ * [32, 4096]. The solver and SpMV kernels accept such a view for the whole
+ * matrix: its row_ids must be a permutation of 0..n-1. */
+int sla_sell_sigma_order(const int32_t *rowptr, const int32_t *row_ids,
+                         int64_t n_slots, int32_t sigma, int32_t *order,
+                         sla_stream_t stream);
 
 /* Distinct diagonal offsets (col - row) of the CSR rows listed in row_ids
  * (or rows 0..n_slots-1). Writes up to SLA_MAX_DIAGS ascending offsets to
@@ -199,7 +219,10 @@ int sla_coo_value_grad(int dtype, const int64_t *row, const int64_t *col,
 /* Jacobi-PCG / CG with torch-sla's stopping rule: stop at the start of
  * iteration i when (r,r) < max(atol, rtol*||b||)^2, iterations = i
  * (pcg_solve_optimized, pytorch_backend.py:1262-1362). dinv == NULL selects
- * preconditioner='none'. x holds the initial guess when x_is_guess != 0. */
+ * preconditioner='none'. x holds the initial guess when x_is_guess != 0.
+ * A covers all n rows: row_base 0, and row_ids NULL (slot i is row i) or a
+ * permutation of 0..n-1 (a SELL-32-sigma order, sla_sell_sigma_order); the
+ * same holds for sla_bicgstab and sla_pcg_mixed. */
 int sla_pcg_workspace(int dtype, int64_t n, size_t *bytes);
 int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b,
             void *x, int x_is_guess, double atol, double rtol,

@@ -9,9 +9,13 @@ on the host CPU (minutes to tens of minutes each):
                  rtol 1e-8 (pcg_solve_optimized, pytorch_backend.py:1262) plus
                  the SpMV y = A x (CachedSparseMatrix.matvec, :154) in fp64
   pcg7_256_f32   the same system in float32 (pcg_solve_optimized on a float32
-                 CachedSparseMatrix), rtol 1e-8, plus the float32 SpMV
+                 CachedSparseMatrix), rtol 1e-8, plus the float32 SpMV;
+                 pcg7_256_f32_envelope adds the counts with torch.vdot
+                 accumulating in float64 and summing in permuted orders
   bicg_cd192     192^3 upwind convection-diffusion, b ~ U(0,1) seed 3, Jacobi
-                 BiCGStab rtol 1e-8 (pbicgstab_solve, :1508)
+                 BiCGStab rtol 1e-8 (pbicgstab_solve, :1508); bicg_cd192_envelope
+                 adds the counts of the same solve with torch.vdot summing in
+                 four permuted orders (the spread rounding alone causes)
   batched_64x512 64 x 512^2 variable-coefficient diffusion, forward and
                  backward through spsolve_batch_same_layout (batch_solve.py:46)
                  with batched_cg_same_pattern (:2575) at rtol 1e-8, loss sum x^2
@@ -128,6 +132,73 @@ def case_bicg192(ref):
         "iters": int(it), "residual": float(resid), "true_rel_residual": true_residual(A, x, b),
         "x": summary(x, sample_idx(sh[0])),
         "cpu": {"threads": torch.get_num_threads(), "solve_s": t_solve}})
+
+
+def case_bicg192_envelope(ref, seeds=(0, 1, 2, 3)):
+    """BiCGStab's iteration count moves with the rounding of its inner
+    products alone: re-run torch-sla's pbicgstab_solve on the 192^3 system
+    with torch.vdot summing in `seeds` permuted orders and store the counts
+    beside the reference's own (iters_envelope, first entry the unpermuted
+    count)."""
+    from torch_sla.backends import pytorch_backend as PB
+    path = os.path.join(OUT, "bicg_cd192.pt")
+    d = torch.load(path, weights_only=False)
+    m = 192
+    v, r, c, sh = P.convdiff_3d_upwind(m)
+    b = P.rhs_uniform01(sh[0], 3)
+    orig = torch.vdot
+    counts = [int(d["iters"])]
+    for seed in seeds:
+        perm = torch.randperm(sh[0], generator=torch.Generator().manual_seed(seed))
+        torch.vdot = lambda a, bb, perm=perm: (a[perm] * bb[perm]).sum()
+        try:
+            with warnings.catch_warnings():
+                warnings.simplefilter("ignore")
+                _, it, _ = PB.pbicgstab_solve(v, r, c, sh, b, atol=0.0, rtol=1e-8,
+                                              maxiter=10000, preconditioner="jacobi")
+        finally:
+            torch.vdot = orig
+        counts.append(int(it))
+        print(f"  permuted dot order {seed}: {it} iterations", flush=True)
+    d["iters_envelope"] = counts
+    save("bicg_cd192", d)
+
+
+def case_pcg7_f32_envelope(ref, seeds=(0, 1)):
+    """float32 PCG's iteration count depends on how its float32 inner
+    products round (torch.vdot accumulating 16.7M float32 terms): re-run
+    torch-sla's pcg_solve_optimized on the float32 256^3 system with
+    torch.vdot (a) accumulating in float64 and rounding the result to float32
+    once, and (b) summing in float32 in `seeds` permuted orders; store the
+    counts beside the reference's own (iters_envelope, first entry the
+    unmodified count)."""
+    from torch_sla.backends import pytorch_backend as PB
+    path = os.path.join(OUT, "pcg7_256_f32.pt")
+    d = torch.load(path, weights_only=False)
+    m = 256
+    n = m ** 3
+    v, r, c, sh = P.poisson_3d_7pt(m, dtype=torch.float32)
+    b = P.rhs_normal(n, 1, torch.float32)
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    del v, r, c
+    M = PB.get_preconditioner(A, "jacobi")
+    orig = torch.vdot
+    counts = [int(d["iters"])]
+    variants = [("float64-accumulated", lambda a, bb: (a.double() * bb.double()).sum().to(a.dtype))]
+    for seed in seeds:
+        perm = torch.randperm(n, generator=torch.Generator().manual_seed(seed))
+        variants.append((f"permuted {seed}", lambda a, bb, perm=perm: (a[perm] * bb[perm]).sum()))
+    for name, fn in variants:
+        torch.vdot = fn
+        try:
+            res = PB.pcg_solve_optimized(A, b, atol=0.0, rtol=1e-8, maxiter=10000,
+                                         preconditioner=M)
+        finally:
+            torch.vdot = orig
+        counts.append(int(res.num_iters))
+        print(f"  dot {name}: {res.num_iters} iterations", flush=True)
+    d["iters_envelope"] = counts
+    save("pcg7_256_f32", d)
 
 
 class _CountNorms:
@@ -268,7 +339,8 @@ def case_shard27(ref_path, m, world, port):
 
 
 CASES = ["bicg_cd192", "pcg7_256_f64", "shard27_32_P2", "shard27_32_P4", "shard27_64_P2",
-         "shard27_64_P4", "batched_64x512", "pcg7_256_f32"]
+         "shard27_64_P4", "batched_64x512", "pcg7_256_f32", "bicg_cd192_envelope",
+         "shard27_128_P2", "pcg7_256_f32_envelope"]
 
 
 def main():
@@ -289,6 +361,10 @@ def main():
             case_pcg7(ref, torch.float32)
         elif name == "bicg_cd192":
             case_bicg192(ref)
+        elif name == "bicg_cd192_envelope":
+            case_bicg192_envelope(ref)
+        elif name == "pcg7_256_f32_envelope":
+            case_pcg7_f32_envelope(ref)
         elif name == "batched_64x512":
             case_batched(ref)
         elif name.startswith("shard27_"):

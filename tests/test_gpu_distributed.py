@@ -310,7 +310,8 @@ def _worker_shard27(rank, world, port, out_dir, names):
 
 
 SHARD27 = {1: ["shard27_32_P2", "shard27_32_P4", "shard27_64_P2", "shard27_64_P4"],
-           2: ["shard27_32_P2", "shard27_64_P2"], 4: ["shard27_32_P4", "shard27_64_P4"]}
+           2: ["shard27_32_P2", "shard27_64_P2"],
+           4: ["shard27_32_P4", "shard27_64_P4"]}
 
 
 @pytest.mark.parametrize("world", [1, 2, 4])

@@ -74,10 +74,21 @@ def test_pcg7_256_matches_reference(dev, tag):
     res = PB.pcg_solve_optimized(A, b, atol=0.0, rtol=ref["rtol"], maxiter=10000,
                                  preconditioner=M)
     assert res.converged == ref["converged"]
-    assert iters_close(res.num_iters, ref["iters"]), (res.num_iters, ref["iters"])
+    # fp64: the count itself; float32: torch-sla's count moves with how its
+    # float32 inner products round (iters_envelope: the reference re-run with
+    # torch.vdot accumulating in float64, and summing in permuted orders),
+    # and this solver accumulates every dot in float64
+    env = ref.get("iters_envelope", [ref["iters"]])
+    lo, hi = min(env), max(env)
+    assert math.floor(0.97 * lo) <= res.num_iters <= math.ceil(1.03 * hi), (res.num_iters, env)
     St = T.SparseTensor(v, r, c, sh)
     tr = true_rel_residual(St, res.x, b)
-    assert tr <= ref["rtol"], (tr, ref["true_rel_residual"])
+    if tag == "f64":
+        assert tr <= ref["rtol"], (tr, ref["true_rel_residual"])
+    else:
+        # float32: the recursive residual reaches rtol 1e-8, the true one
+        # stops at the float32 floor (torch-sla: 7.3e-6); no worse than that
+        assert tr <= 1.5 * ref["true_rel_residual"], (tr, ref["true_rel_residual"])
     # Both solves stop on the same recursive-residual test; the iterates
     # differ only by the rounding of the inner products (summation order).
     # fp64: those differences stay far below the 1e-8 stopping tolerance;
@@ -98,7 +109,12 @@ def test_bicgstab_cd192_matches_reference(dev):
         warnings.simplefilter("ignore")
         x, it, res = T.pbicgstab_solve(v, r, c, sh, b, atol=0.0, rtol=1e-8, maxiter=10000,
                                        preconditioner="jacobi")
-    assert iters_close(it, ref["iters"]), (it, ref["iters"])
+    # torch-sla's own count moves with the summation order of its inner
+    # products (iters_envelope: the reference re-run with torch.vdot summing
+    # in permuted orders); the count must lie within +-3 % of that spread
+    env = ref.get("iters_envelope", [ref["iters"]])
+    lo, hi = min(env), max(env)
+    assert math.floor(0.97 * lo) <= it <= math.ceil(1.03 * hi), (it, env)
     tr = true_rel_residual(T.SparseTensor(v, r, c, sh), x, b)
     assert tr <= ref["rtol"], (tr, ref["true_rel_residual"])
     # BiCGStab's iterates depend on the rounding of its inner products more

@@ -122,7 +122,7 @@ PCG_CASES = ["pcg_2d32_none", "pcg_3d16_jacobi", "pcg_3d16_jacobi_f32", "pcg_2d1
              "pcg_2d32_maxiter"]
 
 
-@pytest.mark.parametrize("flags", [L.SLA_PCG_STREAMED, L.SLA_PCG_PERSISTENT])
+@pytest.mark.parametrize("flags", [L.SLA_PCG_STREAMED, L.SLA_PCG_PERSISTENT, L.SLA_PCG_CLUSTER])
 @pytest.mark.parametrize("name", PCG_CASES)
 def test_pcg_matches_reference(dev, golden, name, flags):
     case = golden[name]
@@ -153,6 +153,35 @@ def test_pcg_config1_full_size_persistent(dev, golden):
     assert float(res.x.sum()) == pytest.approx(ref["x_sum"], rel=1e-7)
     true_res = (b - T.SparseTensor(v, r, c, sh) @ res.x).norm() / b.norm()
     assert float(true_res) < 2e-10
+
+
+@pytest.mark.parametrize("flags", [L.SLA_PCG_CLUSTER, L.SLA_PCG_PERSISTENT])
+def test_pcg_config1_full_size_small_system_kernels(dev, golden, flags):
+    """The 2-D 256^2 system (plain CG, rtol 1e-10) on the thread-block-cluster
+    kernel (values, search direction and partial sums in distributed shared
+    memory) and on the cooperative-grid kernel."""
+    ref = golden["pcg_2d256_none"]
+    v, r, c, sh = P.poisson_2d_5pt(256, device=dev)
+    b = P.rhs_uniform_pm1(sh[0], 0).to(dev)
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    x, info = PB._pcg_core(A, b, None, None, 0.0, 1e-10, 10000, flags)
+    assert info.status == 0 and iters_close(info.iterations, ref["iters"]), info.iterations
+    assert float(x.sum()) == pytest.approx(ref["x_sum"], rel=1e-7)
+    true_res = (b - T.SparseTensor(v, r, c, sh) @ x).norm() / b.norm()
+    assert float(true_res) < 2e-10
+    x2, _ = PB._pcg_core(A, b, None, None, 0.0, 1e-10, 10000, flags)
+    assert torch.equal(x, x2)  # deterministic: fixed summation order
+
+
+def test_pcg_cluster_refuses_systems_that_do_not_fit(dev):
+    """More rows than one cluster holds in shared memory: SLA_ERR_UNSUPPORTED
+    with the cluster flag (AUTO then runs the cooperative-grid kernel)."""
+    v, r, c, sh = P.poisson_3d_7pt(48, device=dev)  # 110,592 rows, 7 diagonals
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    b = P.rhs_normal(sh[0], 1).to(dev)
+    with pytest.raises(L.SlaError) as e:
+        PB._pcg_core(A, b, None, None, 0.0, 1e-8, 100, L.SLA_PCG_CLUSTER)
+    assert e.value.status == L.SLA_ERR_UNSUPPORTED
 
 
 def test_pcg_deterministic(dev):

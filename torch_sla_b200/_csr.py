@@ -40,6 +40,7 @@ class Sell:
         self.uniform_width = int(uniform_width)
         self.n_cols = int(n_cols)
         self.offsets = list(offsets) if offsets else []
+        self.sigma = 1  # rows sorted by length inside windows of sigma rows (explicit views)
         arr = (L.c_i32 * L.MAX_DIAGS)(*self.offsets)
         self.view = L.SellView(self.n_slots, self.n_slices, L.ptr(slice_ptr), L.ptr(col),
                                L.ptr(val), L.ptr(self.row_ids), self.max_width,
@@ -110,16 +111,30 @@ class DeviceCSR:
     # may add over the rows' own entries
     DIAG_MAX_PAD = 0.10
 
+    # SELL-32-sigma: an explicit view of all rows sorts the rows by length
+    # inside windows of SIGMA rows when the sigma = 1 layout pads more than
+    # SIGMA_PAD over the stored entries, and keeps the sorted layout when it
+    # moves at least SIGMA_GAIN fewer bytes per SpMV (row ids read and the
+    # scattered row writes charged to it)
+    SIGMA = 4096
+    SIGMA_PAD = 0.10
+    SIGMA_GAIN = 0.05
+
     def sell(self, row_ids: torch.Tensor | None = None, values: torch.Tensor | None = None,
-             n_cols: int | None = None, diagonal: bool = True) -> Sell:
+             n_cols: int | None = None, diagonal: bool = True,
+             sigma: int | None = None) -> Sell:
         """SELL-32 view of all rows (row_ids=None) or of the listed rows.
 
         When the rows' columns lie on 5, 7 or 27 diagonals (stencil
         matrices) the view stores no column indices (diagonal-offset
         layout); `n_cols` bounds the columns the kernels may touch (default:
         the matrix's column count) and must exceed every stored column of
-        the rows. diagonal=False forces the explicit layout."""
-        cacheable = row_ids is None and values is None and n_cols is None and diagonal
+        the rows. diagonal=False forces the explicit layout. sigma (explicit
+        views of all rows): 1 keeps row order, a power of two in [32, 4096]
+        sorts rows by length inside windows of that many rows (SELL-C-sigma),
+        None picks between them by the bytes each layout moves."""
+        cacheable = (row_ids is None and values is None and n_cols is None and diagonal
+                     and sigma is None)
         if cacheable and self._sell is not None:
             return self._sell
         vals = self.vals if values is None else values
@@ -135,7 +150,7 @@ class DeviceCSR:
         stream = L.stream_handle(dev)
         s = self._diagonal_view(row_ids, n_slots, n_cols, vals, stream) if diagonal else None
         if s is None:
-            s = self._explicit_view(row_ids, n_slots, n_cols, vals, stream)
+            s = self._explicit_view(row_ids, n_slots, n_cols, vals, stream, sigma)
         if cacheable:
             self._sell = s
         return s
@@ -203,7 +218,17 @@ class DeviceCSR:
         return Sell(slice_ptr, None, sval, n_slots, row_ids, max_width=w, uniform_width=w,
                     n_cols=n_cols, offsets=offs)
 
-    def _explicit_view(self, row_ids, n_slots, n_cols, vals, stream):
+    def sigma_order(self, sigma: int, row_ids: torch.Tensor | None = None) -> torch.Tensor:
+        """Rows of the view (row_ids, or all rows) sorted by decreasing length
+        inside windows of `sigma` rows (sla_sell_sigma_order)."""
+        n_slots = self.shape[0] if row_ids is None else int(row_ids.numel())
+        order = torch.empty(max(n_slots, 1), dtype=torch.int32, device=self.device)[:n_slots]
+        L.check("sla_sell_sigma_order", L.lib().sla_sell_sigma_order(
+            L.ptr(self.rowptr), L.ptr(row_ids), n_slots, int(sigma), L.ptr(order),
+            L.stream_handle(self.device)))
+        return order
+
+    def _explicit_view(self, row_ids, n_slots, n_cols, vals, stream, sigma=None):
         lib = L.lib()
         dev = self.device
         n_slices = (n_slots + 31) // 32
@@ -220,6 +245,25 @@ class DeviceCSR:
                 ctypes.byref(padded), ctypes.byref(widest), L.ptr(ws), ws.numel(), stream))
 
         layout(0)
+        used_sigma = 1
+        if row_ids is None and n_slots > 0 and sigma != 1:
+            want = sigma if sigma is not None else self.SIGMA
+            if sigma is not None or padded.value > (1.0 + self.SIGMA_PAD) * max(self.nnz, 1):
+                V = torch.empty((), dtype=self.dtype).element_size()
+                plain_bytes = padded.value * (V + 4)
+                plain = padded.value
+                order = self.sigma_order(want)
+                row_ids = order
+                layout(0)
+                # row id loads (4 B) and the scattered row writes (up to a
+                # 32 B sector for an 8 B value) are charged to the sorted view
+                sorted_bytes = padded.value * (V + 4) + 28 * n_slots
+                if sigma is None and sorted_bytes > (1.0 - self.SIGMA_GAIN) * plain_bytes:
+                    row_ids = None
+                    layout(0)
+                    assert padded.value == plain
+                else:
+                    used_sigma = want
         uniform = 0
         w = int(widest.value)
         # pad every slice to the widest one when that costs <= 3 % more
@@ -232,8 +276,10 @@ class DeviceCSR:
         L.check("sla_sell_fill", lib.sla_sell_fill(
             self.code, L.ptr(self.rowptr), L.ptr(self.colind), L.ptr(vals), L.ptr(row_ids), n_slots,
             L.ptr(slice_ptr), L.ptr(scol), L.ptr(sval), stream))
-        return Sell(slice_ptr, scol, sval, n_slots, row_ids, max_width=widest.value,
+        view = Sell(slice_ptr, scol, sval, n_slots, row_ids, max_width=widest.value,
                     uniform_width=uniform, n_cols=n_cols)
+        view.sigma = used_sigma
+        return view
 
     # --------------------------------------------------------------- helpers
     def jacobi_inverse(self, rule: int, n_rows: int | None = None) -> torch.Tensor:

@@ -21,7 +21,7 @@ SLA_OK, SLA_NOT_CONVERGED, SLA_BREAKDOWN = 0, 1, 2
 SLA_ERR_INVALID, SLA_ERR_CUDA, SLA_ERR_NCCL = -1, -2, -3
 SLA_ERR_TIMEOUT, SLA_ERR_UNSUPPORTED, SLA_ERR_WORKSPACE, SLA_ERR_INDEX = -4, -5, -6, -7
 SLA_JACOBI_EPS, SLA_JACOBI_CLAMP, SLA_JACOBI_NONZERO = 0, 1, 2
-SLA_PCG_AUTO, SLA_PCG_STREAMED, SLA_PCG_PERSISTENT = 0, 1, 2
+SLA_PCG_AUTO, SLA_PCG_STREAMED, SLA_PCG_PERSISTENT, SLA_PCG_CLUSTER = 0, 1, 2, 3
 SLA_PCG_NOALLOC_SCRATCH_BYTES = 16 << 20  # size of sla_pcg_noalloc's fixed device array
 SLA_MIXED_M_F32_NONE, SLA_MIXED_M_F32_JACOBI, SLA_MIXED_M_F64_JACOBI, SLA_MIXED_M_F64_NONE = (
     0, 1, 2, 3)
@@ -69,6 +69,7 @@ _SIGNATURES = {
                                        c_ptr, c_sz, c_ptr]),
     "sla_sell_fill": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr,
                                      c_ptr, c_ptr, c_ptr]),
+    "sla_sell_sigma_order": (ctypes.c_int, [c_ptr, c_ptr, c_i64, c_i32, c_ptr, c_ptr]),
     "sla_sell_diag_probe_workspace": (ctypes.c_int, [_P(c_sz)]),
     "sla_sell_diag_probe": (ctypes.c_int, [c_ptr, c_ptr, c_ptr, c_i64, _P(c_i32), _P(c_i32),
                                            c_ptr, c_sz, c_ptr]),

@@ -106,8 +106,9 @@ bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T 
   double acc[1] = {0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-    int64_t row = s * 32 + lane;
-    if (row < A.n_slots) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int64_t row = slot_row(A, slot);
       p_new[row] = g.pval((int32_t)row);
       v_new[row] = sum;
       acc[0] += (double)rhat[row] * (double)sum;
@@ -130,8 +131,9 @@ bicg_k2(Sell<T> A, const T *__restrict__ r, const T *__restrict__ v, const T *__
   double acc[3] = {0.0, 0.0, 0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-    int64_t row = s * 32 + lane;
-    if (row < A.n_slots) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int64_t row = slot_row(A, slot);
       T si = g.sval((int32_t)row);
       t[row] = sum;
       acc[0] += (double)si * (double)si;
@@ -271,7 +273,7 @@ int sla_bicgstab(int dtype, const sla_sell_t *A, const void *dinv, const void *b
                  int x_is_guess, double atol, double rtol, int64_t maxiter, void *workspace,
                  size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
   SLA_TRY(sell_check(A));
-  if (!b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  if (!b || !x || !info || A->row_base) return SLA_ERR_INVALID;
   if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
   info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;

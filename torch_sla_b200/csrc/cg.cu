@@ -20,6 +20,8 @@
 // Persistent path (small systems, vectors L2-resident): the same two phases
 // in one cooperative launch separated by a bounded grid barrier.
 
+#include <cooperative_groups.h>
+
 #include "solver.cuh"
 
 namespace sla {
@@ -129,8 +131,9 @@ cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
   double acc[1] = {0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-    int64_t row = s * 32 + lane;
-    if (row < A.n_slots) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int64_t row = slot_row(A, slot);
       T pn = g((int32_t)row);
       p_new[row] = pn;
       Ap[row] = sum;
@@ -194,8 +197,9 @@ cg_spmv_split_kernel(Sell<T> A, const T *__restrict__ p, T *__restrict__ Ap, CgS
   double acc[1] = {0.0};
   for_each_slice<WS, true>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-    int64_t row = s * 32 + lane;
-    if (row < A.n_slots) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int64_t row = slot_row(A, slot);
       const T pn = __ldg(p + row);
       Ap[row] = sum;
       acc[0] += (double)pn * (double)sum;
@@ -362,8 +366,9 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
     double a1[1] = {0.0};
     for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
       T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-      int64_t row = s * 32 + lane;
-      if (row < n) {
+      const int64_t slot = s * 32 + lane;
+      if (slot < n) {
+        const int64_t row = slot_row(A, slot);
         T pn = g((int32_t)row);
         p_new[row] = pn;
         Ap[row] = sum;
@@ -405,6 +410,164 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
   }
 }
 
+// ------------------------------------------------- thread-block cluster CG
+// Small stencil systems run inside ONE thread-block cluster (16 CTAs of 1024
+// threads where the GPU allows that cluster size, else 8): CTA c owns R
+// consecutive rows (R a multiple of 32, at most 4 per thread) and keeps
+// their matrix values (diagonal-offset view), their search direction and
+// their Jacobi inverse in shared memory, x and r in registers. The SpMV reads
+// the search direction of rows owned by other CTAs through distributed
+// shared memory, and the three synchronisation points of an iteration
+// (search direction published; (p, Ap) partials; (r, r) and (r, z) partials)
+// are hardware cluster barriers rather than grid barriers through global
+// memory. Every CTA sums the per-CTA partials in rank order, so all CTAs
+// take the same decisions. Same recurrences and roundings as the streamed
+// path (x updated every iteration: the same roundings as its deferred
+// two-step update).
+constexpr int kClThreads = 1024;
+constexpr int kClRowsPerThread = 4;
+constexpr int kClRowsMax = kClThreads * kClRowsPerThread;
+
+template <typename T, bool PREC, int W>
+__global__ void __launch_bounds__(kClThreads, 1)
+cg_cluster_kernel(Sell<T> A, int64_t n, int32_t R, T *__restrict__ x, const T *__restrict__ r_in,
+                  const T *__restrict__ dinv, CgState *st) {
+  namespace cgx = cooperative_groups;
+  cgx::cluster_group cl = cgx::this_cluster();
+  extern __shared__ __align__(16) unsigned char cl_smem[];
+  T *sv = reinterpret_cast<T *>(cl_smem);                  // [R * W] values
+  T *sp = sv + (size_t)R * W;                               // [R] search direction
+  T *sd = sp + R;                                           // [R] Jacobi inverse (PREC)
+  double *red = reinterpret_cast<double *>(sd + (PREC ? R : 0));  // [4] this CTA's partials
+  double *tot = red + 4;                                    // [kClMaxCtas][2] gathered partials
+  double *wsm = tot + 2 * 16;                               // block_sum scratch [2][32]
+  const int tid = threadIdx.x;
+  const unsigned me = cl.block_rank();
+  const unsigned ncta = cl.num_blocks();
+  const int64_t r0 = (int64_t)me * R;
+  const int64_t vend = A.n_slices * 32 * W;
+  for (int64_t i = tid; i < (int64_t)R * W; i += kClThreads)
+    sv[i] = (r0 * W + i < vend) ? A.val[r0 * W + i] : T(0);
+  if (PREC)
+    for (int i = tid; i < R; i += kClThreads) sd[i] = (r0 + i < n) ? dinv[r0 + i] : T(0);
+  T xr[kClRowsPerThread], rv[kClRowsPerThread], ap[kClRowsPerThread], pv[kClRowsPerThread];
+#pragma unroll
+  for (int q = 0; q < kClRowsPerThread; ++q) {
+    const int lr = tid + q * kClThreads;
+    const int64_t row = r0 + lr;
+    const bool ok = lr < R && row < n;
+    xr[q] = ok ? x[row] : T(0);
+    rv[q] = ok ? r_in[row] : T(0);
+    pv[q] = T(0);
+    ap[q] = T(0);
+  }
+  double rz = st->rz, rr = st->rr;
+  const double tol_sq = st->tol_sq;
+  const long long maxiter = st->maxiter;
+  int done = st->done;
+  long long iters = done == kRunning ? maxiter : st->iters_out;
+  double beta = 0.0;
+  __syncthreads();
+  for (long long k = 0; done == kRunning && k < maxiter; ++k) {
+    // 1: p = M^{-1} r + beta p, published to the cluster
+#pragma unroll
+    for (int q = 0; q < kClRowsPerThread; ++q) {
+      const int lr = tid + q * kClThreads;
+      if (lr < R && r0 + lr < n) {
+        const T z = PREC ? mul_rn(sd[lr], rv[q]) : rv[q];
+        pv[q] = add_rn(mul_rn(pv[q], (T)beta), z);
+        sp[lr] = pv[q];
+      }
+    }
+    cl.sync();
+    // 2: Ap and (p, Ap); columns owned by another CTA come over DSMEM
+    double a1[1] = {0.0};
+#pragma unroll
+    for (int q = 0; q < kClRowsPerThread; ++q) {
+      const int lr = tid + q * kClThreads;
+      const int64_t row = r0 + lr;
+      if (lr < R && row < n) {
+        const T *vp = sv + (size_t)(lr >> 5) * 32 * W + (lr & 31);
+        T sum = T(0);
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+          const int64_t c = row + A.off[j];
+          const int64_t lc = c - r0;
+          T pc = T(0);
+          if (lc >= 0 && lc < R) {
+            pc = sp[lc];
+          } else if (c >= 0 && c < A.n_cols) {
+            const unsigned owner = (unsigned)((int32_t)c / R);
+            pc = cl.map_shared_rank(sp, owner)[(int32_t)c - (int32_t)owner * R];
+          }
+          sum = fma(vp[32 * j], pc, sum);
+        }
+        ap[q] = sum;
+        a1[0] += (double)pv[q] * (double)sum;
+      }
+    }
+    block_sum<1, kClThreads>(a1, wsm);
+    if (tid == 0) red[0] = a1[0];
+    cl.sync();
+    if (tid < (int)ncta) tot[tid] = cl.map_shared_rank(red, tid)[0];
+    __syncthreads();
+    double pap = 0.0;
+    for (unsigned c = 0; c < ncta; ++c) pap += tot[c];
+    const T alpha = (T)(rz / pap);
+    // 3: x, r update and the two residual dots
+    double a2[2] = {0.0, 0.0};
+#pragma unroll
+    for (int q = 0; q < kClRowsPerThread; ++q) {
+      const int lr = tid + q * kClThreads;
+      if (lr < R && r0 + lr < n) {
+        xr[q] = add_rn(xr[q], mul_rn(alpha, pv[q]));
+        rv[q] = sub_rn(rv[q], mul_rn(alpha, ap[q]));
+        const T z = PREC ? mul_rn(sd[lr], rv[q]) : rv[q];
+        a2[0] += (double)rv[q] * (double)rv[q];
+        a2[1] += (double)rv[q] * (double)z;
+      }
+    }
+    block_sum<2, kClThreads>(a2, wsm);
+    if (tid == 0) {
+      red[1] = a2[0];
+      red[2] = a2[1];
+    }
+    cl.sync();
+    if (tid < (int)ncta) {
+      const double *o = cl.map_shared_rank(red, tid);
+      tot[2 * tid] = o[1];
+      tot[2 * tid + 1] = o[2];
+    }
+    __syncthreads();
+    double s_rr = 0.0, s_rz = 0.0;
+    for (unsigned c = 0; c < ncta; ++c) {
+      s_rr += tot[2 * c];
+      s_rz += tot[2 * c + 1];
+    }
+    __syncthreads();  // tot is rewritten in the next iteration
+    rr = s_rr;
+    beta = s_rz / rz;
+    rz = s_rz;
+    const long long it = k + 1;
+    if (rr < tol_sq) { done = kConverged; iters = it; }
+    else if (!isfinite(rr)) { done = kNonFinite; iters = maxiter; }
+    else if (it >= maxiter) { done = kMaxiter; iters = maxiter; }
+  }
+#pragma unroll
+  for (int q = 0; q < kClRowsPerThread; ++q) {
+    const int lr = tid + q * kClThreads;
+    if (lr < R && r0 + lr < n) x[r0 + lr] = xr[q];
+  }
+  if (me == 0 && tid == 0) {
+    st->rr = rr;
+    st->rz = rz;
+    st->done = done;
+    st->iters_out = iters;
+    st->iter = 0;  // x is complete: no pending deferred step
+  }
+  cl.sync();  // no CTA leaves while another may still read its shared memory
+}
+
 // K_B of iteration `it`: x is updated at odd iterations only (see
 // cg_update_kernel); p_new / p_old are that iteration's directions.
 template <typename T, bool PREC>
@@ -419,6 +582,60 @@ static int update_launch(bool vec, int64_t it, int64_t n, T *x, T *r, const T *p
   const bool odd = (it & 1) != 0;
   if (vec) return odd ? go(cg_update_kernel<T, PREC, true, true>) : go(cg_update_kernel<T, PREC, true, false>);
   return odd ? go(cg_update_kernel<T, PREC, false, true>) : go(cg_update_kernel<T, PREC, false, false>);
+}
+
+// Launch of cg_cluster_kernel when the system fits one cluster: a
+// diagonal-offset view (columns computed, values only in shared memory) with
+// at most kClRowsMax rows per CTA and the CTA's values, search direction and
+// Jacobi inverse within the shared-memory limit. *launched tells the caller
+// whether it ran (false: use another path).
+template <typename T, bool PREC, int WS>
+static int cluster_launch(const Sell<T> &A, int64_t n, T *x, T *r, const T *dinv, CgState *st,
+                          cudaStream_t s, bool *launched) {
+  *launched = false;
+  if constexpr (WS <= kDiagSpec) {
+    return SLA_OK;
+  } else {
+    constexpr int W = WS - kDiagSpec;
+    auto kern = cg_cluster_kernel<T, PREC, W>;
+    int dev = 0, max_smem = 0;
+    SLA_CUDA_TRY(cudaGetDevice(&dev));
+    SLA_CUDA_TRY(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    for (int cl : {16, 8}) {
+      const int64_t R = (n + (int64_t)cl * 32 - 1) / ((int64_t)cl * 32) * 32;
+      if (R > kClRowsMax) return SLA_OK;  // a smaller cluster only holds fewer rows
+      const size_t smem = (size_t)R * W * sizeof(T) + (size_t)R * sizeof(T) * (PREC ? 2 : 1) +
+                          (4 + 2 * 16 + 2 * 32) * sizeof(double);
+      if (smem > (size_t)max_smem) return SLA_OK;
+      SLA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem));
+      if (cl > 8)
+        SLA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(cl);
+      cfg.blockDim = dim3(kClThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = s;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = cl;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int fits = 0;
+      if (cudaOccupancyMaxActiveClusters(&fits, kern, &cfg) != cudaSuccess || fits < 1) {
+        cudaGetLastError();  // this cluster size is refused here: try the next
+        continue;
+      }
+      const int32_t R32 = (int32_t)R;
+      SLA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, A, n, R32, x, (const T *)r, dinv, st));
+      g_launches.fetch_add(1, std::memory_order_relaxed);
+      *launched = true;
+      return SLA_OK;
+    }
+    return SLA_OK;
+  }
 }
 
 static size_t cg_ws_bytes(size_t elem, int64_t n) {
@@ -464,8 +681,18 @@ static int pcg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool 
     persistent = per_sm > 0 && (flags == SLA_PCG_PERSISTENT || small);
   }
   if (flags == SLA_PCG_PERSISTENT && !persistent) return SLA_ERR_UNSUPPORTED;
+  bool clustered = false;
+  if (flags == SLA_PCG_CLUSTER || (flags == SLA_PCG_AUTO && persistent)) {
+    cudaEvent_t ev;
+    profiler().begin(0, 0, s, &ev);
+    SLA_TRY((cluster_launch<T, PREC, WS>(A, n, x, r, dinv, st, s, &clustered)));
+    profiler().end(0, s, ev);
+    if (flags == SLA_PCG_CLUSTER && !clustered) return SLA_ERR_UNSUPPORTED;
+  }
 
-  if (persistent) {
+  if (clustered) {
+    // the whole solve ran in the cluster kernel
+  } else if (persistent) {
     int64_t nn = n;
     void *args[] = {&A, &nn, &x, &r, (void *)&dinv, &pA, &pB, &Ap, &st, &part0, &part1};
     cudaEvent_t ev;
@@ -561,7 +788,14 @@ static int pcg_noalloc_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *
     persistent = per_sm > 0 && (flags == SLA_PCG_PERSISTENT || small);
   }
   if (flags == SLA_PCG_PERSISTENT && !persistent) return SLA_ERR_UNSUPPORTED;
-  if (persistent) {
+  bool clustered = false;
+  if (flags == SLA_PCG_CLUSTER || (flags == SLA_PCG_AUTO && persistent)) {
+    SLA_TRY((cluster_launch<T, PREC, WS>(A, n, x, r, dinv, st, s, &clustered)));
+    if (flags == SLA_PCG_CLUSTER && !clustered) return SLA_ERR_UNSUPPORTED;
+  }
+  if (clustered) {
+    // the whole solve ran in the cluster kernel
+  } else if (persistent) {
     int64_t nn = n;
     void *args[] = {&A, &nn, &x, &r, (void *)&dinv, &pA, &pB, &Ap, &st, &part0, &part1};
     SLA_CUDA_TRY(cudaLaunchCooperativeKernel((const void *)cg_persistent_kernel<T, PREC, WS>,
@@ -613,10 +847,10 @@ int sla_pcg(int dtype, const sla_sell_t *A, const void *dinv, const void *b, voi
             int x_is_guess, double atol, double rtol, int64_t maxiter, int flags, void *workspace,
             size_t workspace_bytes, sla_solve_info_t *info, sla_stream_t stream) {
   SLA_TRY(sell_check(A));
-  if (!b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  if (!b || !x || !info || A->row_base) return SLA_ERR_INVALID;
   if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
-  if (flags < 0 || flags > 2) return SLA_ERR_INVALID;
+  if (flags < 0 || flags > 3) return SLA_ERR_INVALID;
   info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
   size_t need = 0;
   SLA_TRY(sla_pcg_workspace(dtype, A->n_slots, &need));
@@ -645,10 +879,10 @@ int sla_pcg_noalloc(int dtype, const sla_sell_t *A, const void *dinv, const void
                     int x_is_guess, double atol, double rtol, int64_t maxiter, int flags,
                     sla_solve_info_t *info, sla_stream_t stream) {
   SLA_TRY(sell_check(A));
-  if (!b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  if (!b || !x || !info || A->row_base) return SLA_ERR_INVALID;
   if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
-  if (flags < 0 || flags > 2) return SLA_ERR_INVALID;
+  if (flags < 0 || flags > 3) return SLA_ERR_INVALID;
   if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
   info->iterations = 0; info->residual = 0; info->status = 0; info->reason = 0;
   size_t need = cg_ws_bytes(dtype == SLA_F64 ? 8 : 4, A->n_slots);

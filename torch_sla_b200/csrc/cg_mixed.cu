@@ -90,8 +90,8 @@ mx_matvec_kernel(Sell<float> A, const double *__restrict__ x, double *__restrict
   MxRound g{x};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     const float sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-    const int64_t row = s * 32 + lane;
-    if (row < A.n_slots) y[row] = (double)sum;
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) y[slot_row(A, slot)] = (double)sum;
   });
 }
 
@@ -143,8 +143,9 @@ mx_spmv_kernel(Sell<float> A, const double *__restrict__ r, const void *dinv,
   double acc[1] = {0.0};
   for_each_slice<WS>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     const float sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-    const int64_t row = s * 32 + lane;
-    if (row < A.n_slots) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int64_t row = slot_row(A, slot);
       const double pn = g.p((int32_t)row);
       const double ap = (double)sum;
       p_new[row] = pn;
@@ -195,8 +196,9 @@ mx_spmv_split_kernel(Sell<float> A, const float *__restrict__ p32, const double 
   double acc[1] = {0.0};
   for_each_slice<WS, true>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
     const float sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-    const int64_t row = s * 32 + lane;
-    if (row < A.n_slots) {
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int64_t row = slot_row(A, slot);
       const double ap = (double)sum;
       Ap[row] = ap;
       acc[0] += __ldg(p + row) * ap;
@@ -394,7 +396,7 @@ int sla_pcg_mixed(const sla_sell_t *A, int precond, const void *dinv, int b_dtyp
                   void *workspace, size_t workspace_bytes, sla_solve_info_t *info,
                   double *pap_out, sla_stream_t stream) {
   SLA_TRY(sell_check(A));
-  if (!b || !x || !info || A->row_ids || A->row_base) return SLA_ERR_INVALID;
+  if (!b || !x || !info || A->row_base) return SLA_ERR_INVALID;
   if (A->n_diags > 0 && A->n_cols > A->n_slots) return SLA_ERR_INVALID;  // square system
   if (A->n_slots <= 0 || A->n_slots >= INT32_MAX) return SLA_ERR_INVALID;
   if (b_dtype != SLA_F32 && b_dtype != SLA_F64) return SLA_ERR_INVALID;

@@ -374,6 +374,63 @@ __global__ void sell_fill_kernel(const int32_t *__restrict__ rowptr, const int32
   }
 }
 
+// ------------------------------------------------------------- SELL-C-sigma
+// Row order of a SELL-32-sigma view: inside each window of sigma consecutive
+// rows (of the listed rows, or of all rows) the rows are sorted by decreasing
+// length, equal lengths in ascending row order, so each 32-row slice holds
+// rows of similar length and pads less. One block per window sorts the keys
+// (INT32_MAX - length) << 32 | position in shared memory (bitonic network,
+// sigma a power of two in [32, 4096]). The sorted window is then rotated by
+// (window mod sigma/32) slices: the widest slice of window w sits at slice
+// w mod (sigma/32) of the window, not always at its start, so the kernels'
+// grid-stride slice walks (whose warp count is a multiple of 32) do not hand
+// every window's widest slice to the same few warps. The last window, when
+// partial, is not rotated.
+constexpr int kSigmaMax = 4096;
+
+__global__ void __launch_bounds__(1024)
+sigma_order_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ row_ids,
+                   int64_t n_slots, int sigma, int32_t *__restrict__ order) {
+  extern __shared__ unsigned long long key[];
+  const int64_t w0 = (int64_t)blockIdx.x * sigma;
+  for (int i = threadIdx.x; i < sigma; i += blockDim.x) {
+    const int64_t t = w0 + i;
+    unsigned long long k = ~0ull;  // empty positions sort last
+    if (t < n_slots) {
+      const int64_t r = row_ids ? row_ids[t] : t;
+      const unsigned len = (unsigned)(rowptr[r + 1] - rowptr[r]);
+      k = ((unsigned long long)(0x7fffffffu - len) << 32) | (unsigned)i;
+    }
+    key[i] = k;
+  }
+  __syncthreads();
+  for (int size = 2; size <= sigma; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < sigma; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const unsigned long long a = key[i], b = key[j];
+          if ((a > b) == ((i & size) == 0)) {
+            key[i] = b;
+            key[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const bool full = w0 + sigma <= n_slots;
+  const int rot = full ? (int)(blockIdx.x % (unsigned)(sigma / 32)) * 32 : 0;
+  for (int i = threadIdx.x; i < sigma; i += blockDim.x) {
+    const int64_t t = w0 + i;
+    if (t < n_slots) {
+      const int k = (i - rot + sigma) & (sigma - 1);
+      const int64_t src = w0 + (int64_t)(key[k] & 0xffffffffull);
+      order[t] = row_ids ? row_ids[src] : (int32_t)src;
+    }
+  }
+}
+
 template <typename T>
 __global__ void jacobi_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
                               const T *__restrict__ vals, int64_t n, int rule, T *__restrict__ dinv) {
@@ -594,6 +651,19 @@ int sla_sell_fill(int dtype, const int32_t *rowptr, const int32_t *colind, const
                (float *)sell_val);
   else
     return SLA_ERR_INVALID;
+  return SLA_OK;
+}
+
+int sla_sell_sigma_order(const int32_t *rowptr, const int32_t *row_ids, int64_t n_slots,
+                         int32_t sigma, int32_t *order, sla_stream_t stream) {
+  if (!rowptr || !order || n_slots < 0 || n_slots >= INT32_MAX) return SLA_ERR_INVALID;
+  if (sigma < 32 || sigma > kSigmaMax || (sigma & (sigma - 1))) return SLA_ERR_INVALID;
+  if (n_slots == 0) return SLA_OK;
+  const int64_t windows = (n_slots + sigma - 1) / sigma;
+  const int threads = sigma < 1024 ? sigma : 1024;
+  SLA_LAUNCH(sigma_order_kernel, (unsigned)windows, threads,
+             (size_t)sigma * sizeof(unsigned long long), (cudaStream_t)stream, rowptr, row_ids,
+             n_slots, (int)sigma, order);
   return SLA_OK;
 }
 

@@ -80,7 +80,8 @@ def _transpose_view(D):
         st = D._local_tensor
         nl = plan.n_owned + plan.n_halo
         plan.csr_t = DeviceCSR(st.values, st.col_indices, st.row_indices, (nl, plan.n_owned))
-        plan.sell_t = plan.csr_t.sell()
+        # sla_shard_rmatvec writes slot i to row i: no SELL-C-sigma reordering
+        plan.sell_t = plan.csr_t.sell(sigma=1)
         plan.rev_send = torch.empty(max(plan.n_halo, 1), dtype=plan.dtype, device=plan.device)
         plan.rev_recv = torch.empty(max(plan.n_send, 1), dtype=plan.dtype, device=plan.device)
     return plan

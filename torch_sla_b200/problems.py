@@ -212,3 +212,42 @@ def stencil27_rows(dims, z0: int, nz_local: int, seed: int = 4, dtype=torch.floa
     col = torch.cat([p] + cols)
     val = torch.cat([diag] + vals).to(dtype)
     return val, row, col
+
+
+# ------------------------------------------------------------ irregular rows
+def powerlaw_coo(n: int, avg: float = 16.0, shape_a: float = 1.5, seed: int = 5,
+                 band: int = 1024, spd: bool = False, dtype=torch.float64, device="cpu"):
+    """Sparse n x n matrix with power-law (Pareto, shape `shape_a`) row
+    lengths of mean about `avg`, capped at min(n, 64 avg): the skewed row
+    lengths of FEM meshes with refined regions or of graph matrices. Half of
+    a row's columns lie within +-`band` of the diagonal, half anywhere;
+    off-diagonal values are -U(0.1, 1). Every row also holds a diagonal
+    entry equal to the sum of its off-diagonal magnitudes plus 1. With
+    spd=True the off-diagonal part is symmetrised first (B + B^T), making
+    the matrix symmetric positive definite. Duplicate (row, col) pairs are
+    left in the COO (summed when it is converted). Seeded CPU generator:
+    identical on every device. Returns (val, row, col, shape)."""
+    g = torch.Generator().manual_seed(seed)
+    cap = int(min(n, 64 * avg))
+    xm = avg * (shape_a - 1.0) / shape_a
+    u = torch.rand(n, generator=g, dtype=torch.float64).clamp_min(1e-12)
+    lens = (xm * u.pow(-1.0 / shape_a)).floor().clamp(1, cap).to(torch.int64)
+    rows = torch.repeat_interleave(torch.arange(n), lens)
+    m = rows.numel()
+    near = torch.rand(m, generator=g) < 0.5
+    off = torch.randint(-band, band + 1, (m,), generator=g)
+    far = torch.randint(0, n, (m,), generator=g)
+    cols = torch.where(near, (rows + off).clamp(0, n - 1), far)
+    keep = cols != rows
+    rows, cols = rows[keep], cols[keep]
+    vals = -(0.1 + 0.9 * torch.rand(rows.numel(), generator=g, dtype=torch.float64))
+    if spd:
+        rows, cols = torch.cat([rows, cols]), torch.cat([cols, rows])
+        vals = torch.cat([vals, vals])
+    diag = torch.ones(n, dtype=torch.float64)
+    diag.index_add_(0, rows, vals.abs())
+    idx = torch.arange(n)
+    val = torch.cat([diag, vals]).to(dtype)
+    row = torch.cat([idx, rows])
+    col = torch.cat([idx, cols])
+    return val.to(device), row.to(device), col.to(device), (n, n)
