@@ -309,8 +309,9 @@ def _worker_shard27(rank, world, port, out_dir, names):
         dist.destroy_process_group()
 
 
-SHARD27 = {1: ["shard27_32_P2", "shard27_32_P4", "shard27_64_P2", "shard27_64_P4"],
-           2: ["shard27_32_P2", "shard27_64_P2"],
+SHARD27 = {1: ["shard27_32_P2", "shard27_32_P4", "shard27_64_P2", "shard27_64_P4",
+               "shard27_128_P2"],
+           2: ["shard27_32_P2", "shard27_64_P2", "shard27_128_P2"],
            4: ["shard27_32_P4", "shard27_64_P4"]}
 
 
