@@ -751,10 +751,12 @@ def run_sharded(args, world, rank, local):
     nnz = plan.csr.nnz
     method = "bicgstab" if wl == "bicgstab" else "cg"
 
+    maxiter = args.maxiter or 100000
+
     def once(bb=None):
         x = D.solve_distributed_shard(b if bb is None else bb, method=method,
                                       preconditioner="jacobi", atol=0.0, rtol=RTOL,
-                                      maxiter=100000)
+                                      maxiter=maxiter)
         return x, D._last_info["iterations"]
 
     for _ in range(args.warmup):
@@ -842,6 +844,8 @@ def run_sharded(args, world, rank, local):
                           "iterations_per_solve": iters // args.steps,
                           "partition": "z-slabs (partition_simple), one-layer halos",
                           "halo_bytes_per_neighbour": m * m * V, "check_every": 10,
+                          "maxiter": maxiter,
+                          "stopped_at_maxiter": iters // args.steps >= maxiter,
                           "format": fm_int["format"] + " interior rows; explicit boundary rows",
                           "l2": "inputs larger than L2",
                           "parallelism": f"row-sharded x{world} ({exchange})"}
@@ -1000,6 +1004,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--maxiter", type=int, default=0,
+                    help="sharded solves: iteration cap per step (the metric stays iterations/s; "
+                         "torch-sla's shard BiCGStab converges slowly at N > 1)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -420,13 +420,53 @@ cg_persistent_kernel(Sell<T> A, int64_t n, T *__restrict__ x, T *__restrict__ r,
 // shared memory, and the three synchronisation points of an iteration
 // (search direction published; (p, Ap) partials; (r, r) and (r, z) partials)
 // are hardware cluster barriers rather than grid barriers through global
-// memory. Every CTA sums the per-CTA partials in rank order, so all CTAs
-// take the same decisions. Same recurrences and roundings as the streamed
+// memory. Partial sums go through warp butterflies in a fixed order, each
+// CTA pushes its total into every CTA's shared memory before the barrier,
+// and every warp then sums the per-CTA totals the same way, so all CTAs
+// take the same decisions with one CTA barrier per reduction. Same recurrences and roundings as the streamed
 // path (x updated every iteration: the same roundings as its deferred
 // two-step update).
 constexpr int kClThreads = 1024;
 constexpr int kClRowsPerThread = 4;
 constexpr int kClRowsMax = kClThreads * kClRowsPerThread;
+
+constexpr int kClMaxCtas = 16;
+
+// Sum over a warp in a fixed butterfly order: every lane gets the same total.
+__device__ __forceinline__ double warp_total(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+// Cluster-wide total of NV doubles per thread, identical in every thread of
+// every CTA: warp butterflies, the 32 warp totals summed by warp 0 the same
+// way, the CTA total stored into slot `me` of every CTA's `tot` (DSMEM), one
+// cluster barrier, then every warp sums the ncta slots with a butterfly.
+// wsm: NV x 32 doubles of this CTA. One CTA barrier and one cluster barrier.
+template <int NV>
+__device__ __forceinline__ void cluster_total(double (&v)[NV], double *wsm, double *tot,
+                                              cooperative_groups::cluster_group &cl,
+                                              unsigned me, unsigned ncta) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const double w = warp_total(v[k]);
+    if (lane == 0) wsm[k * 32 + warp] = w;
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const double t = warp_total(wsm[k * 32 + lane]);
+      if (lane < (int)ncta) cl.map_shared_rank(tot, lane)[k * kClMaxCtas + me] = t;
+    }
+  }
+  cl.sync();
+#pragma unroll
+  for (int k = 0; k < NV; ++k)
+    v[k] = warp_total(lane < (int)ncta ? tot[k * kClMaxCtas + lane] : 0.0);
+}
 
 template <typename T, bool PREC, int W>
 __global__ void __launch_bounds__(kClThreads, 1)
@@ -438,26 +478,32 @@ cg_cluster_kernel(Sell<T> A, int64_t n, int32_t R, T *__restrict__ x, const T *_
   T *sv = reinterpret_cast<T *>(cl_smem);                  // [R * W] values
   T *sp = sv + (size_t)R * W;                               // [R] search direction
   T *sd = sp + R;                                           // [R] Jacobi inverse (PREC)
-  double *red = reinterpret_cast<double *>(sd + (PREC ? R : 0));  // [4] this CTA's partials
-  double *tot = red + 4;                                    // [kClMaxCtas][2] gathered partials
-  double *wsm = tot + 2 * 16;                               // block_sum scratch [2][32]
+  double *tot_a = reinterpret_cast<double *>(sd + (PREC ? R : 0));  // [kClMaxCtas] (p,Ap)
+  double *tot_b = tot_a + kClMaxCtas;                       // [2][kClMaxCtas] (r,r), (r,z)
+  double *wsm_a = tot_b + 2 * kClMaxCtas;                   // [32] warp totals, (p,Ap)
+  double *wsm_b = wsm_a + 32;                               // [2][32] warp totals, (r,r), (r,z)
   const int tid = threadIdx.x;
   const unsigned me = cl.block_rank();
   const unsigned ncta = cl.num_blocks();
-  const int64_t r0 = (int64_t)me * R;
+  const int32_t n32 = (int32_t)n;
+  const int32_t r0 = (int32_t)me * R;
   const int64_t vend = A.n_slices * 32 * W;
   for (int64_t i = tid; i < (int64_t)R * W; i += kClThreads)
-    sv[i] = (r0 * W + i < vend) ? A.val[r0 * W + i] : T(0);
+    sv[i] = ((int64_t)r0 * W + i < vend) ? A.val[(int64_t)r0 * W + i] : T(0);
   if (PREC)
-    for (int i = tid; i < R; i += kClThreads) sd[i] = (r0 + i < n) ? dinv[r0 + i] : T(0);
+    for (int i = tid; i < R; i += kClThreads) sd[i] = (r0 + i < n32) ? dinv[r0 + i] : T(0);
+  int32_t off[W];
+#pragma unroll
+  for (int j = 0; j < W; ++j) off[j] = A.off[j];
+  const int32_t ncols = (int32_t)A.n_cols;
   T xr[kClRowsPerThread], rv[kClRowsPerThread], ap[kClRowsPerThread], pv[kClRowsPerThread];
+  bool own[kClRowsPerThread];
 #pragma unroll
   for (int q = 0; q < kClRowsPerThread; ++q) {
     const int lr = tid + q * kClThreads;
-    const int64_t row = r0 + lr;
-    const bool ok = lr < R && row < n;
-    xr[q] = ok ? x[row] : T(0);
-    rv[q] = ok ? r_in[row] : T(0);
+    own[q] = lr < R && r0 + lr < n32;
+    xr[q] = own[q] ? x[r0 + lr] : T(0);
+    rv[q] = own[q] ? r_in[r0 + lr] : T(0);
     pv[q] = T(0);
     ap[q] = T(0);
   }
@@ -472,33 +518,34 @@ cg_cluster_kernel(Sell<T> A, int64_t n, int32_t R, T *__restrict__ x, const T *_
     // 1: p = M^{-1} r + beta p, published to the cluster
 #pragma unroll
     for (int q = 0; q < kClRowsPerThread; ++q) {
-      const int lr = tid + q * kClThreads;
-      if (lr < R && r0 + lr < n) {
+      if (own[q]) {
+        const int lr = tid + q * kClThreads;
         const T z = PREC ? mul_rn(sd[lr], rv[q]) : rv[q];
         pv[q] = add_rn(mul_rn(pv[q], (T)beta), z);
         sp[lr] = pv[q];
       }
     }
     cl.sync();
-    // 2: Ap and (p, Ap); columns owned by another CTA come over DSMEM
+    // 2: Ap (ascending diagonals, one FMA chain per row as in the streamed
+    // path; columns owned by another CTA over DSMEM) and (p, Ap)
     double a1[1] = {0.0};
 #pragma unroll
     for (int q = 0; q < kClRowsPerThread; ++q) {
-      const int lr = tid + q * kClThreads;
-      const int64_t row = r0 + lr;
-      if (lr < R && row < n) {
-        const T *vp = sv + (size_t)(lr >> 5) * 32 * W + (lr & 31);
+      if (own[q]) {
+        const int lr = tid + q * kClThreads;
+        const int32_t row = r0 + lr;
+        const T *vp = sv + (lr >> 5) * 32 * W + (lr & 31);
         T sum = T(0);
 #pragma unroll
         for (int j = 0; j < W; ++j) {
-          const int64_t c = row + A.off[j];
-          const int64_t lc = c - r0;
+          const int32_t c = row + off[j];
+          const int32_t lc = c - r0;
           T pc = T(0);
-          if (lc >= 0 && lc < R) {
+          if ((uint32_t)lc < (uint32_t)R) {
             pc = sp[lc];
-          } else if (c >= 0 && c < A.n_cols) {
-            const unsigned owner = (unsigned)((int32_t)c / R);
-            pc = cl.map_shared_rank(sp, owner)[(int32_t)c - (int32_t)owner * R];
+          } else if ((uint32_t)c < (uint32_t)ncols) {
+            const int32_t owner = c / R;
+            pc = cl.map_shared_rank(sp, owner)[c - owner * R];
           }
           sum = fma(vp[32 * j], pc, sum);
         }
@@ -506,20 +553,14 @@ cg_cluster_kernel(Sell<T> A, int64_t n, int32_t R, T *__restrict__ x, const T *_
         a1[0] += (double)pv[q] * (double)sum;
       }
     }
-    block_sum<1, kClThreads>(a1, wsm);
-    if (tid == 0) red[0] = a1[0];
-    cl.sync();
-    if (tid < (int)ncta) tot[tid] = cl.map_shared_rank(red, tid)[0];
-    __syncthreads();
-    double pap = 0.0;
-    for (unsigned c = 0; c < ncta; ++c) pap += tot[c];
-    const T alpha = (T)(rz / pap);
+    cluster_total<1>(a1, wsm_a, tot_a, cl, me, ncta);
+    const T alpha = (T)(rz / a1[0]);
     // 3: x, r update and the two residual dots
     double a2[2] = {0.0, 0.0};
 #pragma unroll
     for (int q = 0; q < kClRowsPerThread; ++q) {
-      const int lr = tid + q * kClThreads;
-      if (lr < R && r0 + lr < n) {
+      if (own[q]) {
+        const int lr = tid + q * kClThreads;
         xr[q] = add_rn(xr[q], mul_rn(alpha, pv[q]));
         rv[q] = sub_rn(rv[q], mul_rn(alpha, ap[q]));
         const T z = PREC ? mul_rn(sd[lr], rv[q]) : rv[q];
@@ -527,37 +568,18 @@ cg_cluster_kernel(Sell<T> A, int64_t n, int32_t R, T *__restrict__ x, const T *_
         a2[1] += (double)rv[q] * (double)z;
       }
     }
-    block_sum<2, kClThreads>(a2, wsm);
-    if (tid == 0) {
-      red[1] = a2[0];
-      red[2] = a2[1];
-    }
-    cl.sync();
-    if (tid < (int)ncta) {
-      const double *o = cl.map_shared_rank(red, tid);
-      tot[2 * tid] = o[1];
-      tot[2 * tid + 1] = o[2];
-    }
-    __syncthreads();
-    double s_rr = 0.0, s_rz = 0.0;
-    for (unsigned c = 0; c < ncta; ++c) {
-      s_rr += tot[2 * c];
-      s_rz += tot[2 * c + 1];
-    }
-    __syncthreads();  // tot is rewritten in the next iteration
-    rr = s_rr;
-    beta = s_rz / rz;
-    rz = s_rz;
+    cluster_total<2>(a2, wsm_b, tot_b, cl, me, ncta);
+    rr = a2[0];
+    beta = a2[1] / rz;
+    rz = a2[1];
     const long long it = k + 1;
     if (rr < tol_sq) { done = kConverged; iters = it; }
     else if (!isfinite(rr)) { done = kNonFinite; iters = maxiter; }
     else if (it >= maxiter) { done = kMaxiter; iters = maxiter; }
   }
 #pragma unroll
-  for (int q = 0; q < kClRowsPerThread; ++q) {
-    const int lr = tid + q * kClThreads;
-    if (lr < R && r0 + lr < n) x[r0 + lr] = xr[q];
-  }
+  for (int q = 0; q < kClRowsPerThread; ++q)
+    if (own[q]) x[r0 + tid + q * kClThreads] = xr[q];
   if (me == 0 && tid == 0) {
     st->rr = rr;
     st->rz = rz;
@@ -601,11 +623,11 @@ static int cluster_launch(const Sell<T> &A, int64_t n, T *x, T *r, const T *dinv
     int dev = 0, max_smem = 0;
     SLA_CUDA_TRY(cudaGetDevice(&dev));
     SLA_CUDA_TRY(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-    for (int cl : {16, 8}) {
+    for (int cl : {kClMaxCtas, 8}) {
       const int64_t R = (n + (int64_t)cl * 32 - 1) / ((int64_t)cl * 32) * 32;
       if (R > kClRowsMax) return SLA_OK;  // a smaller cluster only holds fewer rows
       const size_t smem = (size_t)R * W * sizeof(T) + (size_t)R * sizeof(T) * (PREC ? 2 : 1) +
-                          (4 + 2 * 16 + 2 * 32) * sizeof(double);
+                          (3 * kClMaxCtas + 3 * 32) * sizeof(double);
       if (smem > (size_t)max_smem) return SLA_OK;
       SLA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         (int)smem));
