@@ -222,6 +222,67 @@ shard_cg_spmv(Sell<T> A, int32_t n_own, const T *__restrict__ r, const T *__rest
   }
 }
 
+// Split form of the NCCL-path K_A (SLA_CG_SPLIT, as on one GPU and on the
+// peer-memory path): a streaming pass takes the stop decision and forms
+// p_new = p_old*beta + M^{-1} r once per owned row; the send rows are then
+// packed from p_new, and the interior and boundary SpMVs gather p_new (and
+// the received halo) instead of recomputing p for every entry.
+template <typename T, bool PREC>
+__global__ void __launch_bounds__(kBlock)
+shard_cg_pform(int64_t n, const T *__restrict__ r, const T *__restrict__ dinv,
+               const T *__restrict__ p_old, T *__restrict__ p_new, ShardState *st,
+               const CgRed *R, long long k, long long every, double atol, double rtol) {
+  if (*(volatile int *)&st->stopped) return;
+  if (cg_stop(R, k, every, cg_tol(R, atol, rtol))) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) { st->stopped = 1; st->iters = k; }
+    return;
+  }
+  ShardP<T, PREC> inner{r, dinv, p_old, (T)cg_beta(R, k)};
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p_new[i] = inner((int32_t)i);
+}
+
+template <typename T>
+__global__ void shard_pack_rows(const int32_t *__restrict__ idx, int64_t n,
+                                const T *__restrict__ src, T *__restrict__ out,
+                                const ShardState *st) {
+  if (*(volatile const int *)&st->stopped) return;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = src[idx[i]];
+}
+
+template <typename T, bool HALO, int WS>
+__global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
+shard_cg_spmv_split(Sell<T> A, int32_t n_own, const T *__restrict__ p,
+                    const T *__restrict__ phalo, T *__restrict__ Ap, ShardState *st, CgRed *R,
+                    double *partials) {
+  __shared__ double smem[kWarps];
+  if (*(volatile int *)&st->stopped) return;
+  PlainGather<T> inner{p};
+  HaloGather<T, PlainGather<T>> g{inner, phalo, n_own};
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  double acc[1] = {0.0};
+  for_each_slice<WS, !HALO>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+    T sum = HALO ? sell_row_at<WS>(A, s, sbase, swidth, lane, g)
+                 : sell_row_at<WS>(A, s, sbase, swidth, lane, inner);
+    const int64_t slot = s * 32 + lane;
+    if (slot < A.n_slots) {
+      const int32_t row = (int32_t)slot_row(A, slot);
+      Ap[row] = sum;
+      acc[0] += (double)__ldg(p + row) * (double)sum;
+    }
+  });
+  if (last_block_sum<1, kBlock>(acc, partials, &st->counter[HALO ? 2 : 1], smem) &&
+      threadIdx.x == 0) {
+    if (!HALO) st->pap_int = acc[0];
+    else R->pap[0] = st->pap_int + acc[0];
+  }
+}
+
 template <typename T, bool PREC>
 __global__ void __launch_bounds__(kBlock)
 shard_cg_update(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ p,
@@ -444,11 +505,43 @@ static int shard_cg_impl(Comm *ch, Comm *cr, const sla_halo_plan_t *plan, const 
              part[0]);
   SLA_NCCL_TRY(ncclAllReduce(R->init, R->init, 2, ncclFloat64, ncclSum, cr->nccl, s));
   const T *hsrc = plan->halo_src ? halo : recvbuf;
-  const int gi = occupancy_grid((const void *)shard_cg_spmv<T, PREC, false, WS>);
-  const int gb = occupancy_grid((const void *)shard_cg_spmv<T, PREC, true, boundary_spec(WS)>);
+  const int gi = kCgSplit ? spmv_grid()
+                          : occupancy_grid((const void *)shard_cg_spmv<T, PREC, false, WS>);
+  const int gb = kCgSplit ? spmv_grid()
+                          : occupancy_grid((const void *)shard_cg_spmv<T, PREC, true,
+                                                                       boundary_spec(WS)>);
   const int gu = occupancy_grid((const void *)shard_cg_update<T, PREC>);
+  const int gp = occupancy_grid((const void *)shard_cg_pform<T, PREC>);
   SLA_TRY(shard_loop(cr, maxiter, every, &st->stopped, s, [&](int64_t k) -> int {
     T *p_old = (k & 1) ? pB : pA, *p_new = (k & 1) ? pA : pB;
+    if (kCgSplit) {
+      cudaEvent_t ev;
+      profiler().begin(2, k, s, &ev);
+      SLA_LAUNCH((shard_cg_pform<T, PREC>), gp, kBlock, 0, s, no, r, dinv, p_old, p_new, st, R,
+                 (long long)k, (long long)every, atol, rtol);
+      profiler().end(2, s, ev);
+      SLA_LAUNCH(shard_pack_rows<T>, ns > 0 ? grid_for(ns) : 1, kBlock, 0, s, plan->send_index,
+                 ns, (const T *)p_new, sendbuf, st);
+      SLA_TRY(halo_enqueue<T>(ch, plan, sendbuf, recvbuf, s));
+      profiler().begin(0, k, s, &ev);
+      SLA_LAUNCH((shard_cg_spmv_split<T, false, WS>), gi, kBlock, 0, s, AI, (int32_t)no,
+                 (const T *)p_new, hsrc, Ap, st, R, part[1]);
+      profiler().end(0, s, ev);
+      SLA_CUDA_TRY(cudaStreamWaitEvent(s, ch->ev_halo, 0));
+      if (plan->halo_src && nh > 0)
+        SLA_LAUNCH(halo_unpack_kernel<T>, grid_for(nh), kBlock, 0, s, recvbuf, plan->halo_src, nh,
+                   halo, &st->stopped);
+      SLA_LAUNCH((shard_cg_spmv_split<T, true, boundary_spec(WS)>), gb, kBlock, 0, s, AB,
+                 (int32_t)no, (const T *)p_new, hsrc, Ap, st, R, part[2]);
+      SLA_NCCL_TRY(ncclAllReduce(R->pap, R->pap, 1, ncclFloat64, ncclSum, cr->nccl, s));
+      profiler().begin(1, k, s, &ev);
+      SLA_LAUNCH((shard_cg_update<T, PREC>), gu, kBlock, 0, s, no, x, r, p_new, p_old, Ap, dinv,
+                 st, R, part[3], (long long)k);
+      profiler().end(1, s, ev);
+      SLA_NCCL_TRY(ncclAllReduce(R->loc[k & 1], R->loc[k & 1], 2, ncclFloat64, ncclSum,
+                                 cr->nccl, s));
+      return SLA_OK;
+    }
     if (ns > 0)
       SLA_LAUNCH((shard_cg_pack<T, PREC>), grid_for(ns), kBlock, 0, s, plan->send_index, ns, r,
                  dinv, p_old, sendbuf, st, R, (long long)k, (long long)every, atol, rtol);
