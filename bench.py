@@ -818,9 +818,10 @@ def run_sharded(args, world, rank, local):
                       + 2 * V * n_loc)
             kname, rows = "shard_cg_p2p_spmv_split", "all rows, halo wait and cross-rank sum"
         else:
-            ka_bytes = (mat + 5 * V * n_loc) * interior_frac
-            ka_fmt = fm_int["matrix_bytes"] + 5 * V * plan.sell_int.n_slots
-            kname, rows = "shard_cg_spmv", "interior rows"
+            # interior-row SpMV over the search direction the K_P pass formed
+            ka_bytes = (mat + 2 * V * n_loc) * interior_frac
+            ka_fmt = fm_int["matrix_bytes"] + 2 * V * plan.sell_int.n_slots
+            kname, rows = "shard_cg_spmv_split", "interior rows"
     else:
         metric = "fp64 Jacobi-BiCGStab iterations/s (convection-diffusion, 192^3 per GPU)"
         iter_bytes = 2 * mat + 25 * V * n_loc
@@ -990,6 +991,10 @@ def run_reference(args):
 
 
 def main():
+    # the JSON line must be the only output on stdout: keep NCCL's version
+    # banner (NCCL_DEBUG=VERSION) off it; an explicit INFO or TRACE stays
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+        os.environ["NCCL_DEBUG"] = "WARN"
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
