@@ -991,10 +991,11 @@ def run_reference(args):
 
 
 def main():
-    # the JSON line must be the only output on stdout: keep NCCL's version
-    # banner (NCCL_DEBUG=VERSION) off it; an explicit INFO or TRACE stays
-    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-        os.environ["NCCL_DEBUG"] = "WARN"
+    # the JSON line must be the only output on stdout: NCCL prints its
+    # version banner there at NCCL_DEBUG=VERSION and WARN, so those are
+    # unset (no NCCL log at all); an explicit INFO or TRACE stays
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("VERSION", "WARN"):
+        del os.environ["NCCL_DEBUG"]
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
