@@ -484,7 +484,23 @@ def spmv_irregular(dev, local, peak, n=4_000_000, avg=16.0):
                                 "alg_bytes": alg, "alg_frac": round(alg / sec / 1e9 / peak, 4)}
         del sell
     out["auto_sigma"] = csr.sell().sigma
-    del csr, x, y
+    # the matvec view: long rows by the warp-per-row CSR pass, the rest sorted
+    hv = csr.spmv_view()
+    for _ in range(5):
+        spmv(hv, x, n, y)
+    ms, _, _ = timed(lambda: spmv(hv, x, n, y), 50, dev, local)
+    sec = ms / 50 / 1e3
+    n_long = int(hv.long_rows.numel()) if hv.long_rows is not None else 0
+    long_nnz = (int((csr.rowptr[hv.long_rows.long() + 1] - csr.rowptr[hv.long_rows.long()]).sum())
+                if n_long else 0)
+    fb = sell_format(hv)["matrix_bytes"] + long_nnz * 12 + n_long * 12 + 2 * 8 * n
+    out["hybrid"] = {"us_per_spmv": round(sec * 1e6, 2), "long_rows": n_long,
+                     "long_row_entries": long_nnz,
+                     "padding": round((hv.padded_nnz + long_nnz) / csr.nnz, 3), "bytes": fb,
+                     "achieved_gbs": round(fb / sec / 1e9, 1),
+                     "frac": round(fb / sec / 1e9 / peak, 4),
+                     "alg_frac": round((matrix_bytes(csr.nnz, n) + 16 * n) / sec / 1e9 / peak, 4)}
+    del csr, x, y, hv
     return out
 
 

@@ -107,9 +107,10 @@ typedef struct {
 /* ------------------------------------------------------------------ misc */
 /* Version of this interface; 2 since sla_sell_t carries n_cols, row_base
  * and the diagonal offsets, 3 since sla_pcg_mixed, 4 since
- * sla_p2p_profile_read (and one-rank peer-memory plans). _lib.py refuses a
+ * sla_p2p_profile_read (and one-rank peer-memory plans), 5 since
+ * sla_spmv_rows_csr. _lib.py refuses a
  * library with another. */
-#define SLA_ABI_VERSION 4
+#define SLA_ABI_VERSION 5
 int sla_abi_version(void);
 const char *sla_status_string(int status);
 /* Kernels this library has launched in this process (all devices). */
@@ -205,6 +206,18 @@ int sla_jacobi_inverse(int dtype, const int32_t *rowptr, const int32_t *colind,
  * sparse_tensor/matmul.py:10-85). */
 int sla_spmv(int dtype, const sla_sell_t *A, const void *x, void *y,
              sla_stream_t stream);
+/* y[r] = sum over CSR row r for the n_rows rows listed in `rows` (int32 CSR
+ * of sla_csr_build), one warp per row: lane l sums entries l, l+32, ... in
+ * ascending order, then the 32 lane sums are combined in a fixed butterfly
+ * order. With sla_spmv over a SELL view of the remaining rows it forms the
+ * hybrid SpMV of irregular patterns, whose long rows would otherwise keep one
+ * lane of a slice busy while the rest of the grid idles. No counterpart in
+ * torch-sla (its CSR torch.mv serves any pattern, pytorch_backend.py:154-161);
+ * a long row's sum is ordered differently from a sequential one (agrees to
+ * rounding). */
+int sla_spmv_rows_csr(int dtype, const int32_t *rowptr, const int32_t *colind,
+                      const void *vals, const int32_t *rows, int64_t n_rows,
+                      const void *x, void *y, sla_stream_t stream);
 
 /* g[k] = -sum_c a[row[k]*K + c] * b[col[k]*K + c] for every COO entry k,
  * repeated for `batch` independent problems laid out back to back: the

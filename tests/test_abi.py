@@ -35,7 +35,7 @@ def test_binding_table_matches_header():
 
 def test_status_strings_and_version():
     lib = L.lib()
-    assert lib.sla_abi_version() == L.ABI_VERSION == 4
+    assert lib.sla_abi_version() == L.ABI_VERSION == 5
     assert lib.sla_status_string(L.SLA_ERR_UNSUPPORTED) == b"unsupported problem shape"
     assert lib.sla_status_string(L.SLA_NOT_CONVERGED).startswith(b"did not converge")
 

@@ -41,6 +41,7 @@ class Sell:
         self.n_cols = int(n_cols)
         self.offsets = list(offsets) if offsets else []
         self.sigma = 1  # rows sorted by length inside windows of sigma rows (explicit views)
+        self.long_rows = None  # hybrid SpMV views: rows summed by the warp-per-row CSR pass
         arr = (L.c_i32 * L.MAX_DIAGS)(*self.offsets)
         self.view = L.SellView(self.n_slots, self.n_slices, L.ptr(slice_ptr), L.ptr(col),
                                L.ptr(val), L.ptr(self.row_ids), self.max_width,
@@ -299,16 +300,58 @@ class DeviceCSR:
         d.index_add_(0, rows[mask], self.vals[mask])
         return d
 
+    # hybrid SpMV (matvec only): rows longer than LONG_ROW_MIN entries, and
+    # longer than LONG_ROW_AVG times the average row, go to a warp-per-row
+    # CSR pass (sla_spmv_rows_csr) over the CSR arrays themselves; the other
+    # rows form a SELL-32-sigma view
+    LONG_ROW_MIN = 64
+    LONG_ROW_AVG = 8
+
+    def spmv_view(self) -> Sell:
+        """The view `matvec` runs on: the solvers' view (`sell()`), or, when
+        that is a length-sorted explicit view whose longest rows exceed the
+        long-row threshold, a hybrid: a SELL-32-sigma view of the shorter rows
+        plus the list of long rows (`view.long_rows`) for the warp-per-row
+        pass. Long rows are summed lane-strided (agrees with the sequential
+        sum to rounding); every other row is bitwise the same as in `sell()`."""
+        if getattr(self, "_spmv_view", None) is not None:
+            return self._spmv_view
+        base = self.sell()
+        view = base
+        if base.sigma > 1 and self.vals is not None:
+            lens = (self.rowptr[1:] - self.rowptr[:-1]).to(torch.int64)
+            avg = max(1.0, self.nnz / max(self.shape[0], 1))
+            limit = max(self.LONG_ROW_MIN, int(self.LONG_ROW_AVG * avg + 0.999))
+            long_mask = lens > limit
+            n_long = int(long_mask.sum())
+            if n_long > 0:
+                rows = torch.arange(self.shape[0], device=self.device, dtype=torch.int32)
+                short = rows[~long_mask]
+                order = self.sigma_order(self.SIGMA, row_ids=short) if short.numel() else short
+                view = self._explicit_view(order, int(short.numel()), self.shape[1], self.vals,
+                                           L.stream_handle(self.device), sigma=1)
+                view.sigma = self.SIGMA
+                view.long_rows = rows[long_mask].contiguous()
+                view.csr_arrays = (self.rowptr, self.colind, self.vals)
+        self._spmv_view = view
+        return view
+
     def matvec(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        return spmv(self.sell(), x, self.shape[0], out)
+        return spmv(self.spmv_view(), x, self.shape[0], out)
 
 
 def spmv(sell: Sell, x: torch.Tensor, n_out: int, out: torch.Tensor | None = None) -> torch.Tensor:
     x = x.contiguous()
     if out is None:
         out = torch.empty(n_out, dtype=x.dtype, device=x.device)
-    L.check("sla_spmv", L.lib().sla_spmv(L.dtype_code(x.dtype), sell.ref(), L.ptr(x), L.ptr(out),
-                                         L.stream_handle(x.device)))
+    code, stream = L.dtype_code(x.dtype), L.stream_handle(x.device)
+    L.check("sla_spmv", L.lib().sla_spmv(code, sell.ref(), L.ptr(x), L.ptr(out), stream))
+    long_rows = getattr(sell, "long_rows", None)
+    if long_rows is not None:
+        rowptr, colind, vals = sell.csr_arrays
+        L.check("sla_spmv_rows_csr", L.lib().sla_spmv_rows_csr(
+            code, L.ptr(rowptr), L.ptr(colind), L.ptr(vals), L.ptr(long_rows),
+            int(long_rows.numel()), L.ptr(x), L.ptr(out), stream))
     return out
 
 

@@ -31,7 +31,7 @@ c_i32, c_i64, c_dbl, c_ptr, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_dou
 
 
 MAX_DIAGS = 32  # SLA_MAX_DIAGS
-ABI_VERSION = 4  # SLA_ABI_VERSION
+ABI_VERSION = 5  # SLA_ABI_VERSION
 
 
 class SellView(ctypes.Structure):
@@ -80,6 +80,8 @@ _SIGNATURES = {
     "sla_jacobi_inverse": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_i64,
                                           ctypes.c_int, c_ptr, c_ptr]),
     "sla_spmv": (ctypes.c_int, [ctypes.c_int, _P(SellView), c_ptr, c_ptr, c_ptr]),
+    "sla_spmv_rows_csr": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_ptr, c_ptr, c_i64, c_ptr,
+                                         c_ptr, c_ptr]),
     "sla_coo_value_grad": (ctypes.c_int, [ctypes.c_int, c_ptr, c_ptr, c_i64, c_ptr, c_ptr,
                                           c_i64, c_i64, c_i64, c_i64, c_ptr, c_ptr]),
     "sla_pcg_workspace": (ctypes.c_int, [ctypes.c_int, c_i64, _P(c_sz)]),

@@ -21,6 +21,44 @@ __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks) spmv_kernel(Sell<T> A,
   });
 }
 
+// y[r] for the CSR rows listed in `rows`, one warp per row: lane l takes the
+// row's entries l, l + 32, l + 64, ... in ascending order (four in flight per
+// lane), then a fixed butterfly adds the 32 lane sums. The long rows of a
+// hybrid SpMV: a row walked by one lane of a SELL slice would keep that warp
+// busy long after the others finished.
+template <typename T>
+__global__ void __launch_bounds__(kBlock)
+spmv_rows_csr_kernel(const int32_t *__restrict__ rowptr, const int32_t *__restrict__ colind,
+                     const T *__restrict__ vals, const int32_t *__restrict__ rows, int64_t n_rows,
+                     const T *__restrict__ x, T *__restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t i = warp; i < n_rows; i += nwarps) {
+    const int32_t r = __ldg(rows + i);
+    const int32_t k1 = __ldg(rowptr + r + 1);
+    int32_t k = __ldg(rowptr + r) + lane;
+    T acc = T(0);
+    for (; k + 96 < k1; k += 128) {
+      int32_t c[4];
+      T v[4], xv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        c[u] = ld_stream(colind + k + 32 * u);
+        v[u] = ld_stream(vals + k + 32 * u);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) xv[u] = __ldg(x + c[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc = fma(v[u], xv[u], acc);
+    }
+    for (; k < k1; k += 32) acc = fma(ld_stream(vals + k), __ldg(x + ld_stream(colind + k)), acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+    if (lane == 0) y[r] = acc;
+  }
+}
+
 template <typename T>
 int spmv_launch(const sla_sell_t *A, const void *x, void *y, cudaStream_t s) {
   Sell<T> a = make_sell<T>(A);
@@ -79,6 +117,27 @@ __global__ void batched_values_kernel(const T *__restrict__ vb, int64_t batch, i
 using namespace sla;
 
 extern "C" {
+
+int sla_spmv_rows_csr(int dtype, const int32_t *rowptr, const int32_t *colind, const void *vals,
+                      const int32_t *rows, int64_t n_rows, const void *x, void *y,
+                      sla_stream_t stream) {
+  if (n_rows < 0 || (n_rows > 0 && (!rowptr || !colind || !vals || !rows || !x || !y)))
+    return SLA_ERR_INVALID;
+  if (dtype != SLA_F32 && dtype != SLA_F64) return SLA_ERR_INVALID;
+  if (n_rows == 0) return SLA_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t want = (n_rows + kWarps - 1) / kWarps;
+  if (dtype == SLA_F64) {
+    const int g = occupancy_grid((const void *)spmv_rows_csr_kernel<double>);
+    SLA_LAUNCH(spmv_rows_csr_kernel<double>, want < g ? (int)want : g, kBlock, 0, s, rowptr,
+               colind, (const double *)vals, rows, n_rows, (const double *)x, (double *)y);
+  } else {
+    const int g = occupancy_grid((const void *)spmv_rows_csr_kernel<float>);
+    SLA_LAUNCH(spmv_rows_csr_kernel<float>, want < g ? (int)want : g, kBlock, 0, s, rowptr,
+               colind, (const float *)vals, rows, n_rows, (const float *)x, (float *)y);
+  }
+  return SLA_OK;
+}
 
 int sla_spmv(int dtype, const sla_sell_t *A, const void *x, void *y, sla_stream_t stream) {
   SLA_TRY(sell_check(A));
