@@ -492,6 +492,11 @@ cg_cluster_kernel(Sell<T> A, int64_t n, int32_t R, T *__restrict__ x, const T *_
     sv[i] = ((int64_t)r0 * W + i < vend) ? A.val[(int64_t)r0 * W + i] : T(0);
   if (PREC)
     for (int i = tid; i < R; i += kClThreads) sd[i] = (r0 + i < n32) ? dinv[r0 + i] : T(0);
+  // slots of rows past n are never written by the loop, but a row near n
+  // reaches them through the local branch of the gather (a column >= n
+  // inside this CTA's range, with value 0): they must hold 0, not whatever
+  // an earlier kernel left in shared memory (0 * NaN would be NaN)
+  for (int i = tid; i < R; i += kClThreads) sp[i] = T(0);
   int32_t off[W];
 #pragma unroll
   for (int j = 0; j < W; ++j) off[j] = A.off[j];
