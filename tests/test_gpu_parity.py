@@ -173,6 +173,23 @@ def test_pcg_config1_full_size_small_system_kernels(dev, golden, flags):
     assert torch.equal(x, x2)  # deterministic: fixed summation order
 
 
+@pytest.mark.parametrize("m", [100, 200, 203])
+def test_pcg_cluster_partial_last_tile(dev, m):
+    """n = m^2 not a multiple of the cluster's 16 x 32-row tiling: the last
+    CTA holds row slots past n, which rows near n reach through their local
+    gathers (with a zero value). Repeated solves, after kernels that leave
+    other data in shared memory, must match the streamed path."""
+    v, r, c, sh = P.poisson_2d_5pt(m, device=dev)
+    b = P.rhs_uniform_pm1(sh[0], 0).to(dev)
+    A = PB.CachedSparseMatrix(v, r, c, sh)
+    xs, info_s = PB._pcg_core(A, b, None, None, 0.0, 1e-10, 10000, L.SLA_PCG_STREAMED)
+    for _ in range(3):
+        y = T.SparseTensor(v, r, c, sh) @ b  # other kernels in between
+        xc, info_c = PB._pcg_core(A, b, None, None, 0.0, 1e-10, 10000, L.SLA_PCG_CLUSTER)
+        assert info_c.status == 0 and iters_close(info_c.iterations, info_s.iterations)
+        assert rel(xc, xs) < 1e-8 and bool(torch.isfinite(y).all())
+
+
 def test_pcg_cluster_refuses_systems_that_do_not_fit(dev):
     """More rows than one cluster holds in shared memory: SLA_ERR_UNSUPPORTED
     with the cluster flag (AUTO then runs the cooperative-grid kernel)."""
