@@ -643,8 +643,11 @@ def wl_mrhs(args, dev, local):
     # mrhs_pform_kernel), writes AP
     sell = A.sell()
     fm = sell_format(sell)
-    line["roofline"] = roofline("mrhs_spmv_kernel", nnz * 12 + 4 * (n + 1) + 2 * K * 8 * n,
-                                ka_ms, ka_n, "mrhs_spmv_kernel@mrhs:128x16",
+    # 7-point diagonal view: P tiles staged in shared memory by bulk copies
+    kname = ("mrhs_spmv_tile_kernel" if sell.diagonal_offsets and sell.uniform_width in (5, 7)
+             else "mrhs_spmv_kernel")
+    line["roofline"] = roofline(kname, nnz * 12 + 4 * (n + 1) + 2 * K * 8 * n,
+                                ka_ms, ka_n, f"{kname}@mrhs:128x16",
                                 fm["matrix_bytes"] + 2 * K * 8 * n)
     line["clocks"] = clk
     return line

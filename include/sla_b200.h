@@ -349,7 +349,11 @@ int sla_multi_rhs_cg(int dtype, const int32_t *rowptr, const int32_t *colind,
 /* The same solve with the matrix given as a diagonal-offset SELL view
  * (n_diags 5, 7 or 27, square, no row ids): no column or row-pointer loads
  * in the SpMV. Same results as sla_multi_rhs_cg on the same matrix up to
- * the sign of zero sums. */
+ * the sign of zero sums. Views with offsets (-a,-b,-1,0,1,b,a) or
+ * (-b,-1,0,1,b) and K a multiple of 16 bytes' worth of values stage each
+ * tile of P in shared memory with bulk copies; a copy that never completes
+ * within the bounded wait stops the solve with SLA_ERR_TIMEOUT (info->reason
+ * 4). */
 int sla_multi_rhs_cg_diag(int dtype, const sla_sell_t *A, int64_t k,
                           const void *dinv, const void *b, void *x,
                           int x_is_guess, double atol, double rtol,

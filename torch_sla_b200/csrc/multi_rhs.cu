@@ -32,6 +32,7 @@ struct MrhsCols {
 // loads, so every load of a row is independent of the others).
 template <typename T>
 struct CsrRows {
+  static constexpr int kWidth = 0;
   const int32_t *rowptr, *colind;
   const T *vals;
   template <int VEC, int RB, typename G>
@@ -50,6 +51,7 @@ struct CsrRows {
 
 template <typename T, int W>
 struct DiagRows {
+  static constexpr int kWidth = W;
   Sell<T> A;
   template <int VEC, int RB, typename G>
   __device__ __forceinline__ void sum(int64_t row, const G &g, T (&s)[VEC]) const {
@@ -232,6 +234,213 @@ mrhs_spmv_kernel(M mat, int64_t n, int K, const T *__restrict__ r,
   }
 }
 
+// ------------------------------------------------ SpMM over staged P tiles
+// For a diagonal-offset view whose offsets are [-b, -1, 0, 1, b] (W = 5) or
+// [-a, -b, -1, 0, 1, b, a] (W = 7) -- 2-D and 3-D structured grids -- the rows
+// a tile of rpb consecutive rows r0 .. r0+rpb-1 gathers from lie in at most
+// five contiguous ranges of P ([n][K] rows): r0-1 .. r0+rpb (the rows and
+// their +-1 neighbours) and r0 -+ b, r0 -+ a (rpb rows each); the tile's
+// matrix values are the contiguous SELL slices that hold its rows. One
+// thread of the block copies all of it into shared memory with bulk copies
+// (cp.async.bulk, completion counted on an mbarrier), double-buffered so
+// that the next tile streams in while this one computes; the block then
+// reads nothing else from global memory, and one barrier per tile both
+// releases the buffer and agrees on a timeout. Each row sums its entries in
+// ascending diagonal order from the same values as mrhs_spmv_kernel. Waits
+// are bounded (kWaitLimitNs); a timeout stops the solve with state 4.
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes,
+                                              uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for phase `parity` of an mbarrier.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  return true;
+}
+
+constexpr int kMrhsTimeout = 4;  // MrhsState::done when a tile never arrived
+
+// Elements of one staged tile: P rows (range 0 holds rpb + 2 rows, r0-1 ..
+// r0+rpb, the others rpb rows each), then the values of the SELL slices the
+// tile's rows span (at most (rpb + 31) / 32 + 1 slices of 32 W entries).
+inline size_t tile_p_rows(int W, int rpb) { return (size_t)(W == 7 ? 5 : 3) * rpb + 2; }
+inline size_t tile_elems(int W, int rpb, int K) {
+  return tile_p_rows(W, rpb) * K + (size_t)((rpb + 31) / 32 + 1) * 32 * W;
+}
+
+template <typename T, bool PREC, int VEC, int W>
+__global__ void __launch_bounds__(kBatchThreads, kBatchMinBlocks)
+mrhs_spmv_tile_kernel(Sell<T> A, int64_t n, int K, const T *__restrict__ p, T *__restrict__ Ap,
+                      MrhsState *st, MrhsCols cs, double *partials) {
+  extern __shared__ __align__(128) unsigned char mt_smem[];
+  __shared__ uint64_t bar[2];
+  __shared__ int s_stop;
+  if (threadIdx.x == 0) {
+    // one read for the whole block: a block of this launch that timed out
+    // may set st->done while others start
+    s_stop = *(volatile int *)&st->done;
+    if (!s_stop) {
+      mbar_init(&bar[0], 1);
+      mbar_init(&bar[1], 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+  }
+  __syncthreads();
+  if (s_stop) return;
+  const BatchLane ln(K, VEC);
+  const int rpb = ln.rpb;
+  constexpr int NR = W == 7 ? 5 : 3;  // P ranges
+  const int TR = NR * rpb + 2;
+  T *const buf0 = reinterpret_cast<T *>(mt_smem);
+  const size_t buf_elems = (size_t)TR * K + (size_t)((rpb + 31) / 32 + 1) * 32 * W;
+  double *red = reinterpret_cast<double *>(buf0 + 2 * buf_elems);
+  const int64_t b_off = -(int64_t)A.off[W == 7 ? 1 : 0];
+  const int64_t a_off = W == 7 ? -(int64_t)A.off[0] : 0;
+  // first buffer row of each range: A (r0-1..), B (-b), C (+b), D (-a), E (+a)
+  const int base_b = rpb + 2, base_c = 2 * rpb + 2, base_d = 3 * rpb + 2, base_e = 4 * rpb + 2;
+  const int64_t ntiles = (n + rpb - 1) / rpb;
+  const size_t row_bytes = (size_t)K * sizeof(T);
+  // thread 0: copy the P ranges and the values of tile t into buffer q
+  auto issue = [&](int64_t t, int q) {
+    const int64_t r0 = t * rpb;
+    const int64_t lo[5] = {r0 - 1, r0 - b_off, r0 + b_off, r0 - a_off, r0 + a_off};
+    const int cnt[5] = {rpb + 2, rpb, rpb, rpb, rpb};
+    const int dst[5] = {0, base_b, base_c, base_d, base_e};
+    int64_t g0[5], g1[5];
+    const int64_t last = (r0 + rpb < n ? r0 + rpb : n) - 1;
+    const int64_t s_lo = r0 >> 5, s_hi = last >> 5;
+    const uint32_t vbytes = (uint32_t)((s_hi - s_lo + 1) * 32 * W * sizeof(T));
+    uint32_t bytes = vbytes;
+#pragma unroll
+    for (int k = 0; k < NR; ++k) {
+      g0[k] = lo[k] < 0 ? 0 : lo[k];
+      g1[k] = lo[k] + cnt[k] > n ? n : lo[k] + cnt[k];
+      if (g1[k] > g0[k]) bytes += (uint32_t)((g1[k] - g0[k]) * row_bytes);
+    }
+    T *b = buf0 + q * buf_elems;
+    mbar_expect_tx(&bar[q], bytes);
+    bulk_copy_g2s(b + (size_t)TR * K, A.val + s_lo * 32 * W, vbytes, &bar[q]);
+#pragma unroll
+    for (int k = 0; k < NR; ++k)
+      if (g1[k] > g0[k])
+        bulk_copy_g2s(b + (size_t)(dst[k] + (g0[k] - lo[k])) * K, p + g0[k] * K,
+                      (uint32_t)((g1[k] - g0[k]) * row_bytes), &bar[q]);
+  };
+  double acc[1][VEC];
+#pragma unroll
+  for (int u = 0; u < VEC; ++u) acc[0][u] = 0.0;
+  uint32_t phase = 0u;  // bit q: parity of buffer q's next phase
+  int64_t t = blockIdx.x;
+  if (t < ntiles && threadIdx.x == 0) issue(t, 0);
+  int q = 0;
+  bool failed = false, pending_other = false;
+  for (; t < ntiles; t += gridDim.x, q ^= 1) {
+    const int64_t tn = t + gridDim.x;
+    pending_other = tn < ntiles;
+    if (pending_other && threadIdx.x == 0) {
+      // buffer q^1 was last read before the previous iteration's barrier
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(tn, q ^ 1);
+    }
+    const bool ok = mbar_wait_bounded(&bar[q], (phase >> q) & 1u);
+    phase ^= 1u << q;
+    const int64_t row = t * rpb + ln.rl;
+    if (ok && row < n) {
+      const T *tile = buf0 + q * buf_elems;
+      const T *vp = tile + (size_t)TR * K + ((row >> 5) - ((t * rpb) >> 5)) * 32 * W + (row & 31);
+      int idx[W];
+      if constexpr (W == 7) {
+        idx[0] = base_d; idx[1] = base_b; idx[2] = 0; idx[3] = 1; idx[4] = 2;
+        idx[5] = base_c; idx[6] = base_e;
+      } else {
+        idx[0] = base_b; idx[1] = 0; idx[2] = 1; idx[3] = 2; idx[4] = base_c;
+      }
+      T sum[VEC];
+#pragma unroll
+      for (int u = 0; u < VEC; ++u) sum[u] = T(0);
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const T v = vp[32 * j];
+        const int64_t c = row + A.off[j];
+        Pack<T, VEC> xv = splat<T, VEC>(T(0));
+        if (c >= 0 && c < A.n_cols)
+          xv = vload<T, VEC>(tile + (size_t)(idx[j] + ln.rl) * K + ln.m0);
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) sum[u] = fma(v, xv.v[u], sum[u]);
+      }
+      const Pack<T, VEC> pn = vload<T, VEC>(tile + (size_t)(1 + ln.rl) * K + ln.m0);
+      Pack<T, VEC> ap;
+#pragma unroll
+      for (int u = 0; u < VEC; ++u) {
+        ap.v[u] = sum[u];
+        acc[0][u] += (double)pn.v[u] * (double)sum[u];
+      }
+      vstore(Ap + row * K + ln.m0, ap);
+    }
+    // releases buffer q for the copy issued at the top of the next step,
+    // and agrees on a timeout
+    if (__syncthreads_or(!ok)) {
+      failed = true;
+      break;
+    }
+  }
+  if (failed) {
+    // wait (bounded) for the copy still in flight into the other buffer
+    if (pending_other) mbar_wait_bounded(&bar[q ^ 1], (phase >> (q ^ 1)) & 1u);
+    if (threadIdx.x == 0) st->done = kMrhsTimeout;
+  }
+  if (!batch_reduce<1, VEC>(acc, K, red, partials, &st->counter[1])) return;
+  for (int c = threadIdx.x; c < K; c += blockDim.x) {
+    const double pap = red[c];
+    cs.alpha[c] = cs.rz[c] / (pap > 0.0 ? pap : 1.0);
+  }
+}
+
+// Offsets of a view the staged-tile SpMM serves: [-b, -1, 0, 1, b] or
+// [-a, -b, -1, 0, 1, b, a] with 1 < b < a.
+template <typename T>
+inline bool tile_offsets_ok(const CsrRows<T> &) { return false; }
+template <typename T, int W>
+inline bool tile_offsets_ok(const DiagRows<T, W> &m) {
+  const int32_t *o = m.A.off;
+  if (W == 5) return o[1] == -1 && o[2] == 0 && o[3] == 1 && o[4] == -o[0] && o[4] > 1;
+  if (W == 7)
+    return o[2] == -1 && o[3] == 0 && o[4] == 1 && o[5] == -o[1] && o[6] == -o[0] && o[5] > 1 &&
+           o[6] > o[5];
+  return false;
+}
+
 // X is updated at odd iterations only, X = (X + alpha_prev P_prev) + alpha P
 // (the same two roundings as two single steps), while both directions sit
 // in the ping-pong buffers; mrhs_xflush_kernel applies a step left pending.
@@ -337,12 +546,39 @@ static int mrhs_loop(M mat, int64_t n, int K, const T *dinv, T *x, T *r, T *pA, 
   const int G2 = occupancy_grid((const void *)upd, TB, sm2);
   auto pform = mrhs_pform_kernel<T, PREC, VEC>;
   const int G0 = kMrhsSplit ? occupancy_grid((const void *)pform, TB, 0) : 0;
+  // staged-tile SpMM (TMA bulk copies of the gathered P ranges) where the
+  // view's offsets allow it
+  const void *tk = nullptr;
+  size_t smt = 0;
+  int Gt = 0;
+  if constexpr (kMrhsSplit && VEC > 1) {
+    if (tile_offsets_ok(mat) && aligned16(pA, pB, Ap) && (K * sizeof(T)) % 16 == 0) {
+      constexpr int Wv = M::kWidth;
+      if constexpr (Wv == 5 || Wv == 7) {
+        tk = (const void *)mrhs_spmv_tile_kernel<T, PREC, VEC, Wv>;
+        const int rpb = TB / (K / VEC);
+        smt = 2 * tile_elems(Wv, rpb, K) * sizeof(T) + sm1;
+        SLA_CUDA_TRY(cudaFuncSetAttribute(tk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smt));
+        Gt = occupancy_grid(tk, TB, smt);
+      }
+    }
+  }
   return run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
     T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
     cudaEvent_t ev;
     if (kMrhsSplit) SLA_LAUNCH(pform, G0, TB, 0, s, n, K, r, dinv, p_old, p_new, st, cs);
     profiler().begin(0, it, s, &ev);
-    SLA_LAUNCH(spmv, G1, TB, sm1, s, mat, n, K, r, dinv, p_old, p_new, Ap, st, cs, part[1]);
+    if (tk) {
+      if constexpr (kMrhsSplit && VEC > 1) {
+        if constexpr (M::kWidth == 5 || M::kWidth == 7) {
+          SLA_LAUNCH((mrhs_spmv_tile_kernel<T, PREC, VEC, M::kWidth>), Gt, TB, smt, s, mat.A, n,
+                     K, (const T *)p_new, Ap, st, cs, part[1]);
+        }
+      }
+    } else {
+      SLA_LAUNCH(spmv, G1, TB, sm1, s, mat, n, K, r, dinv, p_old, p_new, Ap, st, cs, part[1]);
+    }
     profiler().end(0, s, ev);
     SLA_LAUNCH(upd, G2, TB, sm2, s, n, K, x, r, p_new, p_old, Ap, dinv, st, cs, part[2],
                (int)(it & 1));
@@ -416,7 +652,7 @@ static int mrhs_impl(M mat, int64_t n, int K, const T *dinv, const T *b, T *x, b
   info->iterations = out.done == 0 ? maxiter : out.iters_out;
   info->residual = worst;
   info->reason = out.done;
-  info->status = all ? SLA_OK : SLA_NOT_CONVERGED;
+  info->status = out.done == kMrhsTimeout ? SLA_ERR_TIMEOUT : all ? SLA_OK : SLA_NOT_CONVERGED;
   return info->status;
 }
 
