@@ -57,24 +57,30 @@ def test_fp32_spmv_views_across_sizes(dev, grid):
     assert float((yr - y_ref.double()).abs().max() / y_ref.double().abs().max()) < 1e-5
 
 
-def test_diag_view_row_subset_bounded_columns(dev):
+@pytest.mark.parametrize("dtype,r0", [(torch.float64, 0), (torch.float32, 0),
+                                      (torch.float32, 5)])
+def test_diag_view_row_subset_bounded_columns(dev, dtype, r0):
     """A view of interior rows whose columns stay below n_cols (the shard
-    interior case): rows with a column >= n_cols are left out."""
+    interior case): rows with a column >= n_cols are left out. A run of rows
+    starting at an odd row (row_base 5) puts the float32 two-rows-per-lane
+    kernel's row pairs and gathers off 8-byte alignment."""
     v, r, c, sh = P.poisson_3d_7pt((10, 24, 24))  # 24 x 24 layers (padding ~5 %)
-    csr = DeviceCSR(v.to(dev), r.to(dev), c.to(dev), sh)
+    csr = DeviceCSR(v.to(dtype).to(dev), r.to(dev), c.to(dev), sh)
     n_cols = 576 * 7  # first 7 z-layers
-    rows = torch.arange(0, 576 * 6, dtype=torch.int32, device=dev)  # never reach layer 7
+    rows = torch.arange(r0, 576 * 6, dtype=torch.int32, device=dev)  # never reach layer 7
     d = csr.sell(row_ids=rows, n_cols=n_cols)
     e = csr.sell(row_ids=rows, diagonal=False)
-    assert d.diagonal_offsets
-    x = P.rhs_normal(sh[0], 2).to(dev)
-    yd = torch.zeros(sh[0], dtype=torch.float64, device=dev)
+    assert d.diagonal_offsets and d.row_ids is None and d.row_base == r0
+    x = P.rhs_normal(sh[0], 2, dtype).to(dev)
+    yd = torch.zeros(sh[0], dtype=dtype, device=dev)
     ye = torch.zeros_like(yd)
     from torch_sla_b200 import _lib as L
+    code = L.SLA_F64 if dtype == torch.float64 else L.SLA_F32
     for s, y in ((d, yd), (e, ye)):
-        L.check("sla_spmv", L.lib().sla_spmv(L.SLA_F64, s.ref(), L.ptr(x), L.ptr(y),
+        L.check("sla_spmv", L.lib().sla_spmv(code, s.ref(), L.ptr(x), L.ptr(y),
                                              L.stream_handle(dev)))
     assert torch.equal(yd, ye)
+    assert float(yd[:r0].abs().sum()) == 0  # rows outside the view untouched
 
 
 def test_scattered_pattern_keeps_explicit_columns(dev):

@@ -101,6 +101,13 @@ inline bool aligned16(const P *p, R... rest) {
   return (((uintptr_t)p) & 15u) == 0 && aligned16(rest...);
 }
 
+// True when every pointer is 8-byte aligned (float2 paths).
+inline bool aligned8() { return true; }
+template <typename P, typename... R>
+inline bool aligned8(const P *p, R... rest) {
+  return (((uintptr_t)p) & 7u) == 0 && aligned8(rest...);
+}
+
 inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
 
 // Carve sub-buffers out of a caller-provided workspace.
