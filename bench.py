@@ -265,6 +265,7 @@ def wl_pcg7(args, dev, local):
                                                 / 1e9 / peak, 4)}
     if args.layout != "explicit":
         line["roofline"]["explicit"] = explicit_pcg7(A, b, Mj, n, nnz, m)
+        line["float32"] = float32_pcg7(v, r, c, sh, b_host, dev, m, local)
     if not args.no_e2e:
         line["e2e"] = e2e_pcg7(args, v, r, c, b_host, sh, dev)
     line["gpu_launches"] = launches
@@ -294,6 +295,34 @@ def explicit_pcg7(A, b, Mj, n, nnz, m):
                    f"cg_spmv_split_kernel@pcg7-explicit:{m}", fm["matrix_bytes"] + 2 * 8 * n)
     out.update(format=fm["format"], padded_nnz=sell.padded_nnz, iterations_per_solve=its[0])
     del sell
+    return out
+
+
+def float32_pcg7(v, r, c, sh, b_host, dev, m, local):
+    """The same system in float32 (torch-sla's float32 PCG; this solver
+    accumulates its dots in float64): iterations/s over two solves timed with
+    CUDA events, and its SpMV K_A in situ. K_A bytes: float32 values + p
+    read + Ap written (4-byte words)."""
+    from torch_sla_b200 import _lib as L
+    from torch_sla_b200.backends import pytorch_backend as PB
+    n = sh[0]
+    A = PB.CachedSparseMatrix(v.float(), r, c, sh)
+    b = b_host.float().to(dev)
+    Mj = PB.get_preconditioner(A, "jacobi")
+    sell = A.sell()
+    fm = sell_format(sell, V=4)
+    PB._pcg_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000, sell=sell)
+    L.profile_enable(True, 7)
+    ms, its, _ = timed(lambda: PB._pcg_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000,
+                                            sell=sell)[1].iterations, 2, dev, local)
+    ka_ms, ka_n = L.profile_read(0)
+    L.profile_enable(False)
+    out = {"iterations_per_solve": its[0], "iterations_per_s": round(sum(its) / (ms / 1e3), 1),
+           "format": fm["format"]}
+    out["roofline"] = roofline("cg_spmv_split_kernel (float32)",
+                               matrix_bytes(A.csr.nnz, n, V=4) + 2 * 4 * n, ka_ms, ka_n,
+                               f"cg_spmv_split_kernel@pcg7-f32:{m}", fm["matrix_bytes"] + 2 * 4 * n)
+    del A, b, Mj, sell
     return out
 
 

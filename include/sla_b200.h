@@ -43,7 +43,8 @@ enum {
   SLA_ERR_NCCL = -3,       /* an NCCL call failed                           */
   SLA_ERR_TIMEOUT = -4,    /* a bounded device-side wait gave up            */
   SLA_ERR_UNSUPPORTED = -5,/* shape outside the supported envelope          */
-  SLA_ERR_WORKSPACE = -6,  /* workspace smaller than *_workspace() asked    */
+  SLA_ERR_WORKSPACE = -6,  /* workspace smaller than *_workspace() asked,
+                              or not 16-byte aligned                        */
   SLA_ERR_INDEX = -7       /* a COO index lies outside the matrix shape     */
 };
 

@@ -118,3 +118,17 @@ def test_views_whose_int32_offsets_would_wrap_are_refused(width, offsets):
     arr = (L.c_i32 * L.MAX_DIAGS)(*offsets)
     assert lib.sla_sell_diag_fill(L.SLA_F64, 1 << 20, 1 << 20, 1 << 20, None, n_slots, arr,
                                   width, 1 << 20, None, 0, None) == L.SLA_ERR_UNSUPPORTED
+
+
+def test_misaligned_workspace_is_refused_on_the_host():
+    """Solver workspaces are carved into 256-byte aligned arrays from their
+    base, which the vector loads need 16-byte aligned: a base off that
+    alignment is refused with SLA_ERR_WORKSPACE before any device work."""
+    v = _view()
+    info = L.SolveInfo()
+    lib = L.lib()
+    need = ctypes.c_size_t(0)
+    assert lib.sla_bicgstab_workspace(L.SLA_F64, 64, ctypes.byref(need)) == 0
+    assert lib.sla_bicgstab(L.SLA_F64, ctypes.byref(v), None, 1 << 20, 1 << 20, 0, 0.0, 1e-8,
+                            10, (1 << 20) + 8, need.value, ctypes.byref(info),
+                            None) == L.SLA_ERR_WORKSPACE

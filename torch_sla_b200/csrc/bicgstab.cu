@@ -5,13 +5,17 @@
 // reference does after `break`).
 //
 // Three kernels per iteration; s = r - alpha v is never stored:
-//   K1  p = r + beta (p - omega v) (own rows and inside the gather),
+//   K1  p = r + beta q (own rows and inside the gather),
 //       v = A M^{-1} p, partial (r_hat, v)          -> alpha
 //   K2  t = A M^{-1} (r - alpha v) (gather),
 //       partials (s,s), (t,t), (t,s)                -> exit mode / omega
 //   K3  x += alpha M^{-1} p [+ omega M^{-1} s], r = s - omega t,
+//       q = p - omega v for the next K1,
 //       partials (r,r), (r_hat, r)                  -> convergence, next rho
-// HBM per iteration: 2 x matrix + 19 vector passes.
+// q holds the reference's (p - omega * v), rounded exactly as it rounds it;
+// K3 reads p and v anyway, and storing q lets K1 gather three vectors per
+// entry (r, q, dinv) instead of four. HBM per iteration: 2 x matrix + 19
+// vector passes.
 #include "solver.cuh"
 
 namespace sla {
@@ -29,12 +33,11 @@ struct BicgState {
 enum { bRunning = 0, bConverged = 1, bMaxiter = 2, bRho = 3, bTT = 4, bOmega = 5 };
 
 template <typename T, bool PREC>
-struct PGather {  // p_hat = M^{-1}(r + beta (p - omega v))
-  const T *r, *p, *v, *dinv;
-  T beta, omega;
+struct PGather {  // p_hat = M^{-1}(r + beta q), q = p - omega v
+  const T *r, *q, *dinv;
+  T beta;
   __device__ __forceinline__ T pval(int32_t c) const {
-    T t = sub_rn(__ldg(p + c), mul_rn(omega, __ldg(v + c)));
-    return add_rn(__ldg(r + c), mul_rn(beta, t));
+    return add_rn(__ldg(r + c), mul_rn(beta, __ldg(q + c)));
   }
   __device__ __forceinline__ T operator()(int32_t c) const {
     T pc = pval(c);
@@ -58,7 +61,7 @@ struct SGather {  // s_hat = M^{-1}(r - alpha v)
 template <typename T>
 __global__ void __launch_bounds__(kBlock)
 bicg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T *__restrict__ Ax,
-                 T *__restrict__ r, T *__restrict__ rhat, T *__restrict__ p, T *__restrict__ v,
+                 T *__restrict__ r, T *__restrict__ rhat, T *__restrict__ q,
                  BicgState *st, double *partials, double atol, double rtol) {
   __shared__ double smem[2 * kWarps];
   double acc[2] = {0.0, 0.0};
@@ -70,8 +73,7 @@ bicg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T 
     if (!Ax) x[i] = T(0);
     r[i] = ri;
     rhat[i] = ri;
-    p[i] = T(0);
-    v[i] = T(0);
+    q[i] = T(0);  // p = v = 0
     acc[0] += (double)ri * (double)ri;
     acc[1] += (double)bi * (double)bi;
   }
@@ -93,13 +95,13 @@ bicg_init_kernel(int64_t n, const T *__restrict__ b, T *__restrict__ x, const T 
 
 template <typename T, bool PREC, int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
-bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T *__restrict__ p_old,
-        const T *__restrict__ v_old, const T *__restrict__ dinv, T *__restrict__ p_new,
-        T *__restrict__ v_new, BicgState *st, double *partials) {
+bicg_k1(Sell<T> A, const T *__restrict__ r, const T *__restrict__ rhat, const T *__restrict__ q,
+        const T *__restrict__ dinv, T *__restrict__ p_new, T *__restrict__ v_new, BicgState *st,
+        double *partials) {
   __shared__ double smem[kWarps];
   if (*(volatile int *)&st->done) return;
   const double beta = (st->rho_new / st->rho_old) * (st->alpha / st->omega);
-  PGather<T, PREC> g{r, p_old, v_old, dinv, (T)beta, (T)st->omega};
+  PGather<T, PREC> g{r, q, dinv, (T)beta};
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -161,7 +163,7 @@ template <typename T, bool PREC>
 __global__ void __launch_bounds__(kBlock)
 bicg_k3(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ rhat,
         const T *__restrict__ p, const T *__restrict__ v, const T *__restrict__ t,
-        const T *__restrict__ dinv, BicgState *st, double *partials) {
+        const T *__restrict__ dinv, T *__restrict__ q, BicgState *st, double *partials) {
   __shared__ double smem[2 * kWarps];
   if (*(volatile int *)&st->done) return;
   const int mode = st->mode;
@@ -170,10 +172,13 @@ bicg_k3(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ r
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (; i < n; i += stride) {
-    T ph = PREC ? mul_rn(dinv[i], p[i]) : p[i];
+    const T pi = p[i];
+    T ph = PREC ? mul_rn(dinv[i], pi) : pi;
     T xi = add_rn(x[i], mul_rn(alpha, ph));
     if (mode == 0) {
-      T si = sub_rn(r[i], mul_rn(alpha, v[i]));
+      const T vi = v[i];
+      q[i] = sub_rn(pi, mul_rn(omega, vi));
+      T si = sub_rn(r[i], mul_rn(alpha, vi));
       T sh = PREC ? mul_rn(dinv[i], si) : si;
       xi = add_rn(xi, mul_rn(omega, sh));
       T ri = sub_rn(si, mul_rn(omega, t[i]));
@@ -201,7 +206,7 @@ bicg_k3(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ r
 
 static size_t bicg_ws_bytes(size_t elem, int64_t n) {
   size_t G = (size_t)solver_grid();
-  return 7 * align_up(elem * (size_t)n) + 4 * align_up(4 * G * sizeof(double)) +
+  return 6 * align_up(elem * (size_t)n) + 4 * align_up(4 * G * sizeof(double)) +
          align_up(sizeof(BicgState));
 }
 
@@ -212,8 +217,8 @@ static int bicg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool
   Sell<T> A = make_sell<T>(Ad);
   const int64_t n = A.n_slots;
   Carver c(ws, ws_bytes);
-  T *r = c.take<T>(n), *rhat = c.take<T>(n), *pA = c.take<T>(n), *pB = c.take<T>(n);
-  T *vA = c.take<T>(n), *vB = c.take<T>(n), *t = c.take<T>(n);
+  T *r = c.take<T>(n), *rhat = c.take<T>(n), *p = c.take<T>(n), *q = c.take<T>(n);
+  T *v = c.take<T>(n), *t = c.take<T>(n);
   const int G = solver_grid();
   double *part[4];
   for (int k = 0; k < 4; ++k) part[k] = c.take<double>(4 * (size_t)G);
@@ -224,23 +229,20 @@ static int bicg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool
   SLA_CUDA_TRY(cudaMemcpyAsync(st, &init, sizeof(BicgState), cudaMemcpyHostToDevice, s));
   if (guess) SLA_TRY(spmv_launch<T>(Ad, x, t, s));
   SLA_LAUNCH(bicg_init_kernel<T>, grid_for(n), kBlock, 0, s, n, b, x, guess ? t : nullptr, r, rhat,
-             pA, vA, st, part[0], atol, rtol);
+             q, st, part[0], atol, rtol);
   const int g1 = occupancy_grid((const void *)bicg_k1<T, PREC, WS>);
   const int g2 = occupancy_grid((const void *)bicg_k2<T, PREC, WS>);
   const int g3 = occupancy_grid((const void *)bicg_k3<T, PREC>);
   SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
-    T *p_old = (it & 1) ? pB : pA, *p_new = (it & 1) ? pA : pB;
-    T *v_old = (it & 1) ? vB : vA, *v_new = (it & 1) ? vA : vB;
     cudaEvent_t ev;
     profiler().begin(0, it, s, &ev);
-    SLA_LAUNCH((bicg_k1<T, PREC, WS>), g1, kBlock, 0, s, A, r, rhat, p_old, v_old, dinv, p_new, v_new,
-               st, part[1]);
+    SLA_LAUNCH((bicg_k1<T, PREC, WS>), g1, kBlock, 0, s, A, r, rhat, q, dinv, p, v, st, part[1]);
     profiler().end(0, s, ev);
     profiler().begin(1, it, s, &ev);
-    SLA_LAUNCH((bicg_k2<T, PREC, WS>), g2, kBlock, 0, s, A, r, v_new, dinv, t, st, part[2]);
+    SLA_LAUNCH((bicg_k2<T, PREC, WS>), g2, kBlock, 0, s, A, r, v, dinv, t, st, part[2]);
     profiler().end(1, s, ev);
     profiler().begin(2, it, s, &ev);
-    SLA_LAUNCH((bicg_k3<T, PREC>), g3, kBlock, 0, s, n, x, r, rhat, p_new, v_new, t, dinv, st,
+    SLA_LAUNCH((bicg_k3<T, PREC>), g3, kBlock, 0, s, n, x, r, rhat, p, v, t, dinv, q, st,
                part[3]);
     profiler().end(2, s, ev);
     return SLA_OK;

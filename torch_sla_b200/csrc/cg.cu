@@ -22,6 +22,8 @@
 
 #include <cooperative_groups.h>
 
+#include <type_traits>
+
 #include "solver.cuh"
 
 namespace sla {
@@ -195,16 +197,34 @@ cg_spmv_split_kernel(Sell<T> A, const T *__restrict__ p, T *__restrict__ Ap, CgS
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   PlainGather<T> g{p};
   double acc[1] = {0.0};
-  for_each_slice<WS, true>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-    const int64_t slot = s * 32 + lane;
-    if (slot < A.n_slots) {
-      const int64_t row = slot_row(A, slot);
-      const T pn = __ldg(p + row);
-      Ap[row] = sum;
-      acc[0] += (double)pn * (double)sum;
-    }
-  });
+  if constexpr (std::is_same_v<T, float> && kSolverRowsX2<WS>) {
+    // float32 7-wide views: two rows per lane (p 8-byte aligned: checked
+    // by the launch)
+    for_each_slice_x2(A.n_slices, warp, nwarps, lane, [&](int64_t s, int hl) {
+      int64_t r0, r1;
+      float s0, s1;
+      sell_rows_x2<WS>(A, s, hl, p, r0, r1, s0, s1);
+      if (r0 >= 0) {
+        Ap[r0] = s0;
+        acc[0] += (double)__ldg(p + r0) * (double)s0;
+      }
+      if (r1 >= 0) {
+        Ap[r1] = s1;
+        acc[0] += (double)__ldg(p + r1) * (double)s1;
+      }
+    });
+  } else {
+    for_each_slice<WS, true>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+      T sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
+      const int64_t slot = s * 32 + lane;
+      if (slot < A.n_slots) {
+        const int64_t row = slot_row(A, slot);
+        const T pn = __ldg(p + row);
+        Ap[row] = sum;
+        acc[0] += (double)pn * (double)sum;
+      }
+    });
+  }
   if (last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem) && threadIdx.x == 0) {
     st->pAp = acc[0];
     st->alpha = st->rz / acc[0];

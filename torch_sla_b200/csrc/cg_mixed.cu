@@ -194,16 +194,33 @@ mx_spmv_split_kernel(Sell<float> A, const float *__restrict__ p32, const double 
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   PlainGather<float> g{p32};
   double acc[1] = {0.0};
-  for_each_slice<WS, true>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
-    const float sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
-    const int64_t slot = s * 32 + lane;
-    if (slot < A.n_slots) {
-      const int64_t row = slot_row(A, slot);
-      const double ap = (double)sum;
-      Ap[row] = ap;
-      acc[0] += __ldg(p + row) * ap;
-    }
-  });
+  if constexpr (kSolverRowsX2<WS>) {
+    // 7-wide views: two rows per lane (p32 8-byte aligned: workspace)
+    for_each_slice_x2(A.n_slices, warp, nwarps, lane, [&](int64_t s, int hl) {
+      int64_t r0, r1;
+      float s0, s1;
+      sell_rows_x2<WS>(A, s, hl, p32, r0, r1, s0, s1);
+      if (r0 >= 0) {
+        Ap[r0] = (double)s0;
+        acc[0] += __ldg(p + r0) * (double)s0;
+      }
+      if (r1 >= 0) {
+        Ap[r1] = (double)s1;
+        acc[0] += __ldg(p + r1) * (double)s1;
+      }
+    });
+  } else {
+    for_each_slice<WS, true>(A, warp, nwarps, lane, [&](int64_t s, int32_t sbase, int swidth) {
+      const float sum = sell_row_at<WS>(A, s, sbase, swidth, lane, g);
+      const int64_t slot = s * 32 + lane;
+      if (slot < A.n_slots) {
+        const int64_t row = slot_row(A, slot);
+        const double ap = (double)sum;
+        Ap[row] = ap;
+        acc[0] += __ldg(p + row) * ap;
+      }
+    });
+  }
   if (last_block_sum<1, kBlock>(acc, partials, &st->counter[1], smem) && threadIdx.x == 0) {
     st->pAp = acc[0];
     if (acc[0] <= 0.0) {

@@ -116,7 +116,10 @@ struct Carver {
   size_t cap;
   size_t off = 0;
   bool ok = true;
-  Carver(void *b, size_t c) : base((char *)b), cap(c) {}
+  // the carved arrays are 256-byte aligned offsets from the base, so the
+  // base must be 16-byte aligned for the vector loads (cudaMalloc and
+  // torch allocations are 256-byte aligned)
+  Carver(void *b, size_t c) : base((char *)b), cap(c), ok(((uintptr_t)b & 15u) == 0) {}
   template <typename U>
   U *take(size_t count) {
     size_t bytes = align_up(count * sizeof(U));

@@ -288,6 +288,7 @@ static int csr_build_impl(const int64_t *row, const int64_t *col, const T *val, 
   w.rowstart = c.take<int64_t>(n_rows + 1);
   w.rp64 = c.take<int64_t>(n_rows + 1);
   w.scan = (char *)c.base + c.off;
+  if (!c.ok) return SLA_ERR_WORKSPACE;
   SLA_CUDA_TRY(cudaMemsetAsync(w.counts, 0, sizeof(int32_t) * (n_rows + 1), s));
   SLA_CUDA_TRY(cudaMemsetAsync(w.cursor, 0, sizeof(int32_t) * (n_rows + 1), s));
   SLA_CUDA_TRY(cudaMemsetAsync(w.flags, 0, sizeof(int32_t) * 8, s));
@@ -614,6 +615,7 @@ int sla_sell_layout(const int32_t *rowptr, const int32_t *row_ids, int64_t n_slo
   int64_t *len = c.take<int64_t>(n_slices + 1);
   int64_t *ptr64 = c.take<int64_t>(n_slices + 1);
   int32_t *wmax = c.take<int32_t>(1);
+  if (!c.ok) return SLA_ERR_WORKSPACE;
   char *scan = c.base + c.off;
   SLA_CUDA_TRY(cudaMemsetAsync(len, 0, sizeof(int64_t) * (n_slices + 1), s));
   SLA_CUDA_TRY(cudaMemsetAsync(wmax, 0, sizeof(int32_t), s));
@@ -700,6 +702,7 @@ int sla_sell_diag_probe(const int32_t *rowptr, const int32_t *colind, const int3
   Carver c(workspace, workspace_bytes);
   int32_t *gtab = c.take<int32_t>(kDiagTable);
   int *overflow = c.take<int>(1);
+  if (!c.ok) return SLA_ERR_WORKSPACE;
   SLA_LAUNCH(diag_table_init_kernel, 1, kDiagTable, 0, s, gtab, overflow);
   if (n_slots > 0) {
     if (!colind) return SLA_ERR_INVALID;

@@ -283,4 +283,109 @@ struct PlainGather {
   __device__ __forceinline__ T operator()(int32_t c) const { return __ldg(x + c); }
 };
 
+// ---------------------------------------------- float32, two rows per lane
+// 4-byte values leave a one-row-per-lane warp with 128 B loads; here
+// half-warp h of a warp takes slice 2 pr + h and lane l of the half its slots
+// 2l and 2l + 1, whose entries j sit side by side in the SELL layout: one
+// 8-byte load fetches both values (and both columns of an explicit view),
+// 256 B per warp load as for fp64. Where the two gathered columns are
+// adjacent and the first is even, one 8-byte load fetches both x values.
+// Each row sums its entries in ascending j with the same FMAs as
+// sell_row_at, so per-row results are unchanged; the row-to-thread mapping
+// is the same for the diagonal-offset and the explicit 7-wide view of a
+// matrix, so dot products reduced over it agree between the two views.
+// x must be 8-byte aligned. Used for uniform views of at most eight
+// entries per row (one load batch); the solver kernels take it for the
+// 7-wide views only, whose diagonal-offset and explicit forms both qualify.
+template <int WS>
+constexpr bool kRowsX2 = WS > 0 && ws_width(WS) <= kRowBatch;
+template <int WS>
+constexpr bool kSolverRowsX2 = WS == kDiagSpec + 7 || WS == 7;
+
+template <int WS>
+__device__ __forceinline__ void sell_rows_x2(const Sell<float> &A, int64_t s, int hl,
+                                             const float *__restrict__ x, int64_t &r0,
+                                             int64_t &r1, float &s0, float &s1) {
+  constexpr int W = ws_width(WS);
+  const int64_t slot0 = s * 32 + 2 * hl;
+  const bool ok0 = slot0 < A.n_slots, ok1 = slot0 + 1 < A.n_slots;
+  const bool ids = A.row_ids != nullptr;
+  const int64_t a0 = ids ? (ok0 ? (int64_t)__ldg(A.row_ids + slot0) : 0) : A.row_base + slot0;
+  const int64_t a1 = ids ? (ok1 ? (int64_t)__ldg(A.row_ids + slot0 + 1) : 0) : a0 + 1;
+  r0 = ok0 ? a0 : -1;
+  r1 = ok1 ? a1 : -1;
+  const int64_t e0 = s * 32 * W + 2 * hl;
+  float2 v[W];
+#pragma unroll
+  for (int j = 0; j < W; ++j) v[j] = __ldcs(reinterpret_cast<const float2 *>(A.val + e0 + 32 * j));
+  float x0[W], x1[W];
+  if constexpr (WS > kDiagSpec) {
+    if (!ids) {
+      // consecutive rows: the two columns of entry j are adjacent. (The
+      // parity test is per lane on purpose: the same test written on the
+      // warp-uniform row_base + off[j] measured 123 us against 97 us for
+      // the float32 SpMV at 256^3.)
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const int64_t c0 = a0 + A.off[j], c1 = c0 + 1;
+        const bool in0 = ok0 && c0 >= 0 && c0 < A.n_cols;
+        const bool in1 = ok1 && c1 >= 0 && c1 < A.n_cols;
+        if (in0 && in1 && (c0 & 1) == 0) {
+          const float2 xv = __ldg(reinterpret_cast<const float2 *>(x + c0));
+          x0[j] = xv.x;
+          x1[j] = xv.y;
+        } else {
+          x0[j] = in0 ? __ldg(x + c0) : 0.f;
+          x1[j] = in1 ? __ldg(x + c1) : 0.f;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const int64_t c0 = a0 + A.off[j], c1 = a1 + A.off[j];
+        const bool in0 = ok0 && c0 >= 0 && c0 < A.n_cols;
+        const bool in1 = ok1 && c1 >= 0 && c1 < A.n_cols;
+        x0[j] = in0 ? __ldg(x + c0) : 0.f;
+        x1[j] = in1 ? __ldg(x + c1) : 0.f;
+      }
+    }
+  } else {
+    int2 c[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) c[j] = __ldcs(reinterpret_cast<const int2 *>(A.col + e0 + 32 * j));
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      const int32_t c0 = ok0 ? c[j].x : -1, c1 = ok1 ? c[j].y : -1;
+      if (c0 >= 0 && c1 == c0 + 1 && (c0 & 1) == 0) {
+        const float2 xv = __ldg(reinterpret_cast<const float2 *>(x + c0));
+        x0[j] = xv.x;
+        x1[j] = xv.y;
+      } else {
+        x0[j] = c0 >= 0 ? __ldg(x + c0) : 0.f;
+        x1[j] = c1 >= 0 ? __ldg(x + c1) : 0.f;
+      }
+    }
+  }
+  s0 = 0.f;
+  s1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    s0 = fmaf(v[j].x, x0[j], s0);
+    s1 = fmaf(v[j].y, x1[j], s1);
+  }
+}
+
+// Walk of the slice pairs of a warp: body(s, hl) for the slice of this
+// lane's half-warp, skipping a last odd slice's missing partner.
+template <typename Body>
+__device__ __forceinline__ void for_each_slice_x2(int64_t n_slices, int64_t warp, int64_t nwarps,
+                                                  int lane, Body body) {
+  const int h = lane >> 4, hl = lane & 15;
+  const int64_t npairs = (n_slices + 1) >> 1;
+  for (int64_t pr = warp; pr < npairs; pr += nwarps) {
+    const int64_t s = 2 * pr + h;
+    if (s < n_slices) body(s, hl);
+  }
+}
+
 }  // namespace sla

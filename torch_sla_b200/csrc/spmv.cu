@@ -23,61 +23,26 @@ __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks) spmv_kernel(Sell<T> A,
   });
 }
 
-// float32 diagonal-offset SpMV, two rows per lane: half-warp h of a warp
-// takes slice 2 pr + h, and lane l of the half rows 2l and 2l + 1 of it. The
-// two rows' values of entry j are adjacent, so one 8-byte load fetches both
-// (256 B per warp load, the width of an fp64 view's loads, where the
-// one-row-per-lane kernel issues 128 B loads); where row + off[j] is even
-// the two gathered x values are adjacent and 8-byte aligned as well (one
-// load), otherwise they are gathered separately. Each row still sums its W
-// entries in ascending j with the same FMAs, so y equals spmv_kernel's.
-// Views without row ids; x and y 8-byte aligned.
-template <int W>
+// float32 SpMV on uniform views of at most eight entries per row, two rows
+// per lane (sell_rows_x2): 8-byte value (and column) loads, paired aligned
+// gathers. Same per-row sums as spmv_kernel. x and y 8-byte aligned.
+template <int WS>
 __global__ void __launch_bounds__(kBlock, kSpmvMinBlocks)
-spmv_diag_f32x2_kernel(Sell<float> A, const float *__restrict__ x, float *__restrict__ y) {
+spmv_x2_kernel(Sell<float> A, const float *__restrict__ x, float *__restrict__ y) {
   const int lane = threadIdx.x & 31;
-  const int h = lane >> 4, hl = lane & 15;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const int64_t npairs = (A.n_slices + 1) >> 1;
-  for (int64_t pr = warp; pr < npairs; pr += nwarps) {
-    const int64_t s = 2 * pr + h;
-    if (s >= A.n_slices) continue;
-    const int64_t slot0 = s * 32 + 2 * hl;
-    const bool ok0 = slot0 < A.n_slots, ok1 = slot0 + 1 < A.n_slots;
-    const int64_t r0 = A.row_base + slot0;
-    const float *__restrict__ vp = A.val + s * 32 * W + 2 * hl;
-    float2 v[W];
-#pragma unroll
-    for (int j = 0; j < W; ++j) v[j] = __ldcs(reinterpret_cast<const float2 *>(vp + 32 * j));
-    float x0[W], x1[W];
-#pragma unroll
-    for (int j = 0; j < W; ++j) {
-      const int64_t c0 = r0 + A.off[j], c1 = c0 + 1;
-      const bool in0 = ok0 && c0 >= 0 && c0 < A.n_cols;
-      const bool in1 = ok1 && c1 >= 0 && c1 < A.n_cols;
-      if (in0 && in1 && (c0 & 1) == 0) {
-        const float2 xv = __ldg(reinterpret_cast<const float2 *>(x + c0));
-        x0[j] = xv.x;
-        x1[j] = xv.y;
-      } else {
-        x0[j] = in0 ? __ldg(x + c0) : 0.f;
-        x1[j] = in1 ? __ldg(x + c1) : 0.f;
-      }
-    }
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < W; ++j) {
-      s0 = fmaf(v[j].x, x0[j], s0);
-      s1 = fmaf(v[j].y, x1[j], s1);
-    }
-    if (ok0 && ok1 && (r0 & 1) == 0) {
+  for_each_slice_x2(A.n_slices, warp, nwarps, lane, [&](int64_t s, int hl) {
+    int64_t r0, r1;
+    float s0, s1;
+    sell_rows_x2<WS>(A, s, hl, x, r0, r1, s0, s1);
+    if (r0 >= 0 && r1 == r0 + 1 && (r0 & 1) == 0) {
       *reinterpret_cast<float2 *>(y + r0) = make_float2(s0, s1);
     } else {
-      if (ok0) y[r0] = s0;
-      if (ok1) y[r0 + 1] = s1;
+      if (r0 >= 0) y[r0] = s0;
+      if (r1 >= 0) y[r1] = s1;
     }
-  }
+  });
 }
 
 // y[r] for the CSR rows listed in `rows`, one warp per row: lane l takes the
@@ -125,21 +90,19 @@ int spmv_launch(const sla_sell_t *A, const void *x, void *y, cudaStream_t s) {
   // one wave of resident blocks (fp32 views fit five 256-thread blocks per
   // SM), never more blocks than warps have slices
   if constexpr (std::is_same_v<T, float>) {
-    // float32 diagonal views of 5 or 7 diagonals: two rows per lane
-    if (a.n_diags == 5 || a.n_diags == 7) {
-      if (!a.row_ids && aligned8(x, y)) {
-        const int64_t want = ((a.n_slices + 1) / 2 + kWarps - 1) / kWarps;
-        if (a.n_diags == 7) {
-          const int g = occupancy_grid((const void *)spmv_diag_f32x2_kernel<7>);
-          SLA_LAUNCH(spmv_diag_f32x2_kernel<7>, want < g ? (int)want : g, kBlock, 0, s, a,
+    // float32 views of at most eight entries per row: two rows per lane
+    if (aligned8(x, y)) {
+      bool done = false;
+      SLA_WS_DISPATCH(width_spec(A), {
+        if constexpr (kRowsX2<WS>) {
+          const int g = occupancy_grid((const void *)spmv_x2_kernel<WS>);
+          const int64_t want = ((a.n_slices + 1) / 2 + kWarps - 1) / kWarps;
+          SLA_LAUNCH(spmv_x2_kernel<WS>, want < g ? (int)want : g, kBlock, 0, s, a,
                      (const float *)x, (float *)y);
-        } else {
-          const int g = occupancy_grid((const void *)spmv_diag_f32x2_kernel<5>);
-          SLA_LAUNCH(spmv_diag_f32x2_kernel<5>, want < g ? (int)want : g, kBlock, 0, s, a,
-                     (const float *)x, (float *)y);
+          done = true;
         }
-        return SLA_OK;
-      }
+      });
+      if (done) return SLA_OK;
     }
   }
   SLA_WS_DISPATCH(width_spec(A), {
