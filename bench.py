@@ -316,9 +316,13 @@ def float32_pcg7(v, r, c, sh, b_host, dev, m, local):
     ms, its, _ = timed(lambda: PB._pcg_core(A, b, None, Mj.dinv, 0.0, RTOL, 10000,
                                             sell=sell)[1].iterations, 2, dev, local)
     ka_ms, ka_n = L.profile_read(0)
+    kb_ms, kb_n = L.profile_read(1)
+    kp_ms, kp_n = L.profile_read(2)
     L.profile_enable(False)
     out = {"iterations_per_solve": its[0], "iterations_per_s": round(sum(its) / (ms / 1e3), 1),
-           "format": fm["format"]}
+           "format": fm["format"],
+           "update_kernel_ms": round(kb_ms / max(kb_n, 1), 5),
+           "pform_kernel_ms": round(kp_ms / max(kp_n, 1), 5)}
     out["roofline"] = roofline("cg_spmv_split_kernel (float32)",
                                matrix_bytes(A.csr.nnz, n, V=4) + 2 * 4 * n, ka_ms, ka_n,
                                f"cg_spmv_split_kernel@pcg7-f32:{m}", fm["matrix_bytes"] + 2 * 4 * n)

@@ -266,6 +266,41 @@ def test_bicgstab_vs_oracle_larger(dev):
     assert rel(x, xo) < 1e-6
 
 
+def test_bicgstab_guess_float32_and_views(dev):
+    """K3 stores q = p - omega v for the next K1 (rounded as the reference's
+    p - omega * v), so the first iteration must see q = 0 whatever x0 is.
+    With an initial guess: iterations within the oracle's rounding envelope
+    and the true residual at rtol. float32: the true residual at the float32
+    floor. The diagonal-offset and explicit views of the matrix give the same
+    iterates bit for bit (same sums, same orders)."""
+    v, r, c, sh = P.convdiff_3d_upwind(16)
+    b = P.rhs_uniform01(sh[0], 5)
+    x0 = 0.1 * P.rhs_normal(sh[0], 6)
+    lo, hi, _ = rounding_envelope(K.pbicgstab, v, r, c, sh, b, x0=x0, atol=0.0, rtol=1e-9,
+                                  precond="jacobi")
+    x, it, _ = T.pbicgstab_solve(*cu(v, r, c, dev=dev), sh, b.to(dev), x0=x0.to(dev), atol=0.0,
+                                 rtol=1e-9, preconditioner="jacobi")
+    assert math.floor(0.97 * lo) <= it <= math.ceil(1.03 * hi), (it, lo, hi)
+    A = T.SparseTensor(*cu(v, r, c, dev=dev), sh)
+    bd = b.to(dev)
+    assert float((bd - A @ x).norm() / bd.norm()) < 2e-9
+    # float32
+    xf, itf, _ = T.pbicgstab_solve(*cu(v.float(), r, c, dev=dev), sh, b.float().to(dev),
+                                   atol=0.0, rtol=1e-5, preconditioner="jacobi")
+    Af = T.SparseTensor(*cu(v, r, c, dev=dev), sh)
+    assert xf.dtype == torch.float32
+    assert float((bd - Af @ xf.double()).norm() / bd.norm()) < 1e-4
+    # both views, bit for bit
+    out = []
+    for diagonal in (True, False):
+        Am = PB.CachedSparseMatrix(*cu(v, r, c, dev=dev), sh)
+        Am.csr._sell = Am.csr.sell(diagonal=diagonal)
+        M = PB.get_preconditioner(Am, "jacobi", method="bicgstab")
+        out.append(PB._bicgstab_core(Am, bd, None, M.dinv, 0.0, 1e-9, 10000))
+    assert out[0][1].iterations == out[1][1].iterations
+    assert torch.equal(out[0][0], out[1][0])
+
+
 # ---------------------------------------------------------------- batched
 def test_batched_cg_matches_reference(dev, golden):
     case = golden["batched_d2d12"]

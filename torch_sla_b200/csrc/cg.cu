@@ -148,9 +148,12 @@ cg_spmv_kernel(Sell<T> A, const T *__restrict__ r, const T *__restrict__ dinv,
   }
 }
 
-template <typename T> struct Pair;
-template <> struct Pair<double> { using type = double2; };
-template <> struct Pair<float> { using type = float2; };
+// 16-byte vector of a streaming pass: two doubles or four floats.
+template <typename T> struct Vec16;
+template <> struct Vec16<double> { using type = double2; static constexpr int E = 2; };
+template <> struct Vec16<float> { using type = float4; static constexpr int E = 4; };
+template <typename T, typename V>
+__device__ __forceinline__ T &lane_of(V &v, int u) { return reinterpret_cast<T *>(&v)[u]; }
 
 // Split K_A (kCgSplit): p_new = p_old*beta + M^{-1} r is formed once per row
 // by cg_pform_kernel (a streaming pass) and K_A is a plain SpMV over p_new
@@ -169,18 +172,20 @@ cg_pform_kernel(int64_t n, const T *__restrict__ r, const T *__restrict__ dinv,
   auto pf = [&](T pc, T rc, T dc) { return add_rn(mul_rn(pc, beta), PREC ? mul_rn(dc, rc) : rc); };
   int64_t tail = 0;
   if (VEC) {
-    using V = typename Pair<T>::type;
-    const int64_t n2 = n >> 1;
-    for (int64_t i = tid; i < n2; i += stride) {
-      const V rv = __ldcs((const V *)r + i), pv = __ldcs((const V *)p_old + i);
+    using V = typename Vec16<T>::type;
+    constexpr int E = Vec16<T>::E;
+    const int64_t nv = n / E;
+    for (int64_t i = tid; i < nv; i += stride) {
+      V rv = __ldcs((const V *)r + i), pv = __ldcs((const V *)p_old + i);
       V dv = rv;
       if (PREC) dv = __ldg((const V *)dinv + i);
       V out;
-      out.x = pf(pv.x, rv.x, dv.x);
-      out.y = pf(pv.y, rv.y, dv.y);
+#pragma unroll
+      for (int u = 0; u < E; ++u)
+        lane_of<T>(out, u) = pf(lane_of<T>(pv, u), lane_of<T>(rv, u), lane_of<T>(dv, u));
       ((V *)p_new)[i] = out;
     }
-    tail = n2 * 2;
+    tail = nv * E;
   }
   for (int64_t i = tail + tid; i < n; i += stride)
     p_new[i] = pf(p_old[i], r[i], PREC ? dinv[i] : T(0));
@@ -303,26 +308,28 @@ cg_update_kernel(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__res
     return add_rn(add_rn(xi, mul_rn(alpha_prev, pp)), mul_rn(alpha, pc));
   };
   if (VEC) {
-    using V = typename Pair<T>::type;
-    const int64_t n2 = n >> 1;
-    for (int64_t i = tid; i < n2; i += stride) {
+    using V = typename Vec16<T>::type;
+    constexpr int E = Vec16<T>::E;
+    const int64_t nv = n / E;
+    for (int64_t i = tid; i < nv; i += stride) {
       V rv = ((V *)r)[i];
-      const V av = __ldcs((const V *)Ap + i);
+      V av = __ldcs((const V *)Ap + i);
       V dv = av;
       if (PREC) dv = __ldg((const V *)dinv + i);
       if (XU) {
         V xv = ((V *)x)[i];
-        const V pv = __ldcs((const V *)p + i), qv = __ldcs((const V *)p_prev + i);
-        xv.x = xstep(xv.x, qv.x, pv.x);
-        xv.y = xstep(xv.y, qv.y, pv.y);
+        V pv = __ldcs((const V *)p + i), qv = __ldcs((const V *)p_prev + i);
+#pragma unroll
+        for (int u = 0; u < E; ++u)
+          lane_of<T>(xv, u) = xstep(lane_of<T>(xv, u), lane_of<T>(qv, u), lane_of<T>(pv, u));
         ((V *)x)[i] = xv;
       }
-      cg_rupd<T, PREC>(rv.x, av.x, dv.x, alpha, acc);
-      cg_rupd<T, PREC>(rv.y, av.y, dv.y, alpha, acc);
+#pragma unroll
+      for (int u = 0; u < E; ++u)
+        cg_rupd<T, PREC>(lane_of<T>(rv, u), lane_of<T>(av, u), lane_of<T>(dv, u), alpha, acc);
       ((V *)r)[i] = rv;
     }
-    if ((n & 1) && tid == 0) {
-      const int64_t i = n - 1;
+    for (int64_t i = nv * E + tid; i < n; i += stride) {
       if (XU) x[i] = xstep(x[i], p_prev[i], p[i]);
       T ri = r[i];
       cg_rupd<T, PREC>(ri, Ap[i], PREC ? dinv[i] : T(0), alpha, acc);
