@@ -159,7 +159,13 @@ bicg_k2(Sell<T> A, const T *__restrict__ r, const T *__restrict__ v, const T *__
   }
 }
 
-template <typename T, bool PREC>
+template <typename T> struct Vec16;
+template <> struct Vec16<double> { using type = double2; static constexpr int E = 2; };
+template <> struct Vec16<float> { using type = float4; static constexpr int E = 4; };
+template <typename T, typename V>
+__device__ __forceinline__ T &lane_of(V &v, int u) { return reinterpret_cast<T *>(&v)[u]; }
+
+template <typename T, bool PREC, bool VEC>
 __global__ void __launch_bounds__(kBlock)
 bicg_k3(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ rhat,
         const T *__restrict__ p, const T *__restrict__ v, const T *__restrict__ t,
@@ -169,24 +175,62 @@ bicg_k3(int64_t n, T *__restrict__ x, T *__restrict__ r, const T *__restrict__ r
   const int mode = st->mode;
   const T alpha = (T)st->alpha, omega = (T)st->omega;
   double acc[2] = {0.0, 0.0};
-  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (; i < n; i += stride) {
-    const T pi = p[i];
-    T ph = PREC ? mul_rn(dinv[i], pi) : pi;
-    T xi = add_rn(x[i], mul_rn(alpha, ph));
+  // one element: x += alpha M^{-1} p [+ omega M^{-1} s], r = s - omega t,
+  // q = p - omega v
+  auto elem = [&](T pi, T di, T &xi, T ri, T vi, T ti, T rh, T &qi, T &r_out) {
+    T ph = PREC ? mul_rn(di, pi) : pi;
+    xi = add_rn(xi, mul_rn(alpha, ph));
     if (mode == 0) {
-      const T vi = v[i];
-      q[i] = sub_rn(pi, mul_rn(omega, vi));
-      T si = sub_rn(r[i], mul_rn(alpha, vi));
-      T sh = PREC ? mul_rn(dinv[i], si) : si;
+      qi = sub_rn(pi, mul_rn(omega, vi));
+      T si = sub_rn(ri, mul_rn(alpha, vi));
+      T sh = PREC ? mul_rn(di, si) : si;
       xi = add_rn(xi, mul_rn(omega, sh));
-      T ri = sub_rn(si, mul_rn(omega, t[i]));
-      r[i] = ri;
-      acc[0] += (double)ri * (double)ri;
-      acc[1] += (double)rhat[i] * (double)ri;
+      r_out = sub_rn(si, mul_rn(omega, ti));
+      acc[0] += (double)r_out * (double)r_out;
+      acc[1] += (double)rh * (double)r_out;
     }
+  };
+  int64_t tail = 0;
+  if (VEC) {
+    // 16-byte vectors (all pointers checked aligned by the launch)
+    using V = typename Vec16<T>::type;
+    constexpr int E = Vec16<T>::E;
+    const int64_t nv = n / E;
+    for (int64_t i = tid; i < nv; i += stride) {
+      V pv = __ldcs((const V *)p + i), xv = ((V *)x)[i];
+      V dv = pv, rv = pv, vv = pv, tv = pv, hv = pv, qv = pv, ro = pv;
+      if (PREC) dv = __ldg((const V *)dinv + i);
+      if (mode == 0) {
+        rv = ((V *)r)[i];
+        vv = __ldcs((const V *)v + i);
+        tv = __ldcs((const V *)t + i);
+        hv = __ldg((const V *)rhat + i);
+      }
+#pragma unroll
+      for (int u = 0; u < E; ++u)
+        elem(lane_of<T>(pv, u), lane_of<T>(dv, u), lane_of<T>(xv, u), lane_of<T>(rv, u),
+             lane_of<T>(vv, u), lane_of<T>(tv, u), lane_of<T>(hv, u), lane_of<T>(qv, u),
+             lane_of<T>(ro, u));
+      ((V *)x)[i] = xv;
+      if (mode == 0) {
+        ((V *)q)[i] = qv;
+        ((V *)r)[i] = ro;
+      }
+    }
+    tail = nv * E;
+  }
+  for (int64_t i = tail + tid; i < n; i += stride) {
+    T xi = x[i], qi = T(0), ro = T(0);
+    const bool full = mode == 0;
+    elem(p[i], PREC ? dinv[i] : T(0), xi, full ? r[i] : T(0), full ? v[i] : T(0),
+         full ? t[i] : T(0), full ? rhat[i] : T(0), qi, ro);
     x[i] = xi;
+    if (full) {
+      q[i] = qi;
+      r[i] = ro;
+    }
   }
   if (last_block_sum<2, kBlock>(acc, partials, &st->counter[3], smem) && threadIdx.x == 0) {
     const long long it = st->iter + 1;
@@ -232,7 +276,9 @@ static int bicg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool
              q, st, part[0], atol, rtol);
   const int g1 = occupancy_grid((const void *)bicg_k1<T, PREC, WS>);
   const int g2 = occupancy_grid((const void *)bicg_k2<T, PREC, WS>);
-  const int g3 = occupancy_grid((const void *)bicg_k3<T, PREC>);
+  const bool vec = aligned16(x, r, rhat, p, q, v, t) && (!PREC || aligned16(dinv));
+  const int g3 = vec ? occupancy_grid((const void *)bicg_k3<T, PREC, true>)
+                     : occupancy_grid((const void *)bicg_k3<T, PREC, false>);
   SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
     cudaEvent_t ev;
     profiler().begin(0, it, s, &ev);
@@ -242,8 +288,12 @@ static int bicg_impl(const sla_sell_t *Ad, const T *dinv, const T *b, T *x, bool
     SLA_LAUNCH((bicg_k2<T, PREC, WS>), g2, kBlock, 0, s, A, r, v, dinv, t, st, part[2]);
     profiler().end(1, s, ev);
     profiler().begin(2, it, s, &ev);
-    SLA_LAUNCH((bicg_k3<T, PREC>), g3, kBlock, 0, s, n, x, r, rhat, p, v, t, dinv, q, st,
-               part[3]);
+    if (vec)
+      SLA_LAUNCH((bicg_k3<T, PREC, true>), g3, kBlock, 0, s, n, x, r, rhat, p, v, t, dinv, q, st,
+                 part[3]);
+    else
+      SLA_LAUNCH((bicg_k3<T, PREC, false>), g3, kBlock, 0, s, n, x, r, rhat, p, v, t, dinv, q, st,
+                 part[3]);
     profiler().end(2, s, ev);
     return SLA_OK;
   }));
