@@ -6,6 +6,7 @@ import torch
 
 import torch_sla_b200 as T
 from oracle import krylov as K
+from torch_sla_b200 import _lib as L
 from torch_sla_b200 import problems as P
 from torch_sla_b200._csr import DeviceCSR, spmv
 from torch_sla_b200.backends import pytorch_backend as PB
@@ -108,6 +109,39 @@ def test_diag_view_pcg_bitwise(dev, kind, flags):
         out.append((x, info.iterations))
     assert out[0][1] == out[1][1]
     assert torch.equal(out[0][0], out[1][0])
+
+
+@pytest.mark.parametrize("grid", [(20, 17, 33), (16, 10, 7)])
+def test_float32_pcg_two_rows_per_lane_views(dev, grid):
+    """float32 PCG and mixed-precision PCG on 7-point grids whose slice
+    count is odd (351 and 35: the last slice pair of the
+    two-rows-per-lane K_A has one slice): the diagonal-offset and explicit
+    views share the row-to-thread mapping, so the iterates agree bit for
+    bit; the float32 solve stays within 1e-4 of the float64 solution and
+    the mixed-precision one within 1e-6 of the oracle's mixed-precision
+    PCG."""
+    v, r, c, sh = P.poisson_3d_7pt(grid)
+    b = P.rhs_normal(sh[0], 8)
+    out, mixed = [], []
+    for diagonal in (True, False):
+        A = PB.CachedSparseMatrix(v.float().to(dev), r.to(dev), c.to(dev), sh)
+        A.csr._sell = A.csr.sell(diagonal=diagonal)
+        assert A.sell().diagonal_offsets == diagonal
+        M = PB.get_preconditioner(A, "jacobi")
+        x, info = PB._pcg_core(A, b.float().to(dev), None, M.dinv, 0.0, 1e-6, 5000,
+                               flags=L.SLA_PCG_STREAMED)
+        out.append((x, info.iterations))
+        res = PB.pcg_solve_mixed_precision(A, b.float().to(dev), atol=0.0, rtol=1e-9,
+                                           preconditioner=PB.Float32Preconditioner(M))
+        mixed.append((res.x, res.num_iters))
+    assert out[0][1] == out[1][1] and torch.equal(out[0][0], out[1][0])
+    assert mixed[0][1] == mixed[1][1] and torch.equal(mixed[0][0], mixed[1][0])
+    xo = K.pcg(v, r, c, sh, b, atol=0.0, rtol=1e-10, precond="jacobi")[0]
+    e = float((out[0][0].double().cpu() - xo).abs().max() / xo.abs().max())
+    assert e < 1e-4, e
+    xm = K.pcg_mixed(v.float(), r, c, sh, b.float(), atol=0.0, rtol=1e-9, precond="jacobi")[0]
+    em = float((mixed[0][0].cpu() - xm).abs().max() / xm.abs().max())
+    assert em < 1e-6, em
 
 
 def test_diag_view_bicgstab_bitwise(dev):

@@ -87,8 +87,8 @@ template <typename T>
 int spmv_launch(const sla_sell_t *A, const void *x, void *y, cudaStream_t s) {
   Sell<T> a = make_sell<T>(A);
   if (a.n_slices == 0) return SLA_OK;
-  // one wave of resident blocks (fp32 views fit five 256-thread blocks per
-  // SM), never more blocks than warps have slices
+  // one wave of resident blocks, never more blocks than warps have slices
+  // (slice pairs for the two-rows-per-lane kernel)
   if constexpr (std::is_same_v<T, float>) {
     // float32 views of at most eight entries per row: two rows per lane
     if (aligned8(x, y)) {
