@@ -168,15 +168,51 @@ mx_spmv_kernel(Sell<float> A, const double *__restrict__ r, const void *dinv,
 // rounding once per row; the SpMV then gathers the float32 copy (4 bytes
 // per entry instead of r, p_old and the inverse diagonal). Same values as
 // the gather above: (float)p of the same float64 p.
+// z = M r for two consecutive rows 2k, 2k + 1 (8- / 16-byte loads of the
+// inverse diagonal); same roundings as mx_z.
 template <int MODE>
+__device__ __forceinline__ double2 mx_z2(double2 r, const void *dinv, int64_t k) {
+  if constexpr (MODE == 0) {
+    return make_double2((double)__double2float_rn(r.x), (double)__double2float_rn(r.y));
+  } else if constexpr (MODE == 1) {
+    const float2 d = __ldg((const float2 *)dinv + k);
+    return make_double2((double)__fmul_rn(d.x, __double2float_rn(r.x)),
+                        (double)__fmul_rn(d.y, __double2float_rn(r.y)));
+  } else if constexpr (MODE == 2) {
+    const double2 d = __ldg((const double2 *)dinv + k);
+    return make_double2(__dmul_rn(d.x, r.x), __dmul_rn(d.y, r.y));
+  } else {
+    return r;
+  }
+}
+
+// VEC: two rows per thread step with 16-byte loads of r and p_old and
+// 16- / 8-byte stores of p and its float32 copy (pointers checked by the
+// launch).
+template <int MODE, bool VEC>
 __global__ void __launch_bounds__(kBlock)
 mx_pform_kernel(int64_t n, const double *__restrict__ r, const void *dinv,
                 const double *__restrict__ p_old, double *__restrict__ p_new,
                 float *__restrict__ p32, const MixState *st) {
   if (*(volatile const int *)&st->done) return;
   const MxPGather<MODE> g{r, dinv, p_old, st->beta};
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t tail = 0;
+  if (VEC) {
+    const double beta = st->beta;
+    const int64_t n2 = n >> 1;
+    for (int64_t k = tid; k < n2; k += stride) {
+      const double2 rv = __ldcs((const double2 *)r + k), pv = __ldcs((const double2 *)p_old + k);
+      const double2 z = mx_z2<MODE>(rv, dinv, k);
+      const double2 out = make_double2(__dadd_rn(__dmul_rn(pv.x, beta), z.x),
+                                       __dadd_rn(__dmul_rn(pv.y, beta), z.y));
+      ((double2 *)p_new)[k] = out;
+      ((float2 *)p32)[k] = make_float2(__double2float_rn(out.x), __double2float_rn(out.y));
+    }
+    tail = n2 * 2;
+  }
+  for (int64_t i = tail + tid; i < n; i += stride) {
     const double pv = g.p((int32_t)i);
     p_new[i] = pv;
     p32[i] = __double2float_rn(pv);
@@ -356,15 +392,22 @@ static int pcg_mixed_impl(const sla_sell_t *Ad, const void *dinv, int b_dtype, c
                guess ? Ap : nullptr, dinv, r, pA, st, part0, atol, rtol);
   const int grid_a = kCgSplit ? spmv_grid()
                               : occupancy_grid((const void *)mx_spmv_kernel<MODE, WS>);
-  const int grid_p = occupancy_grid((const void *)mx_pform_kernel<MODE>);
+  const int grid_p = occupancy_grid((const void *)mx_pform_kernel<MODE, true>);
   const bool vec = aligned16(x, r, pA, pB, Ap);
+  const bool vec_p = aligned16(r, pA, pB) && aligned8(p32) &&
+                     (MODE == 1 ? aligned8(dinv) : MODE == 2 ? aligned16(dinv) : true);
   SLA_TRY(run_chunked(maxiter, 8, &st->done, s, [&](int64_t it) -> int {
     double *p_old = (it & 1) ? pB : pA;
     double *p_new = (it & 1) ? pA : pB;
     cudaEvent_t ev;
     if (kCgSplit) {
       profiler().begin(2, it, s, &ev);
-      SLA_LAUNCH((mx_pform_kernel<MODE>), grid_p, kBlock, 0, s, n, r, dinv, p_old, p_new, p32, st);
+      if (vec_p)
+        SLA_LAUNCH((mx_pform_kernel<MODE, true>), grid_p, kBlock, 0, s, n, r, dinv, p_old, p_new,
+                   p32, st);
+      else
+        SLA_LAUNCH((mx_pform_kernel<MODE, false>), grid_p, kBlock, 0, s, n, r, dinv, p_old, p_new,
+                   p32, st);
       profiler().end(2, s, ev);
       profiler().begin(0, it, s, &ev);
       SLA_LAUNCH((mx_spmv_split_kernel<WS>), grid_a, kBlock, 0, s, A, (const float *)p32,
