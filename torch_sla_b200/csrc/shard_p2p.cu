@@ -167,7 +167,8 @@ __device__ __forceinline__ bool p2p_allreduce(const P2PDev<T> &P, int point, int
     P2PHeader *h = P.hdr[threadIdx.x];
 #pragma unroll
     for (int i = 0; i < NV; ++i) h->red_val[par][point][P.me][i] = v[i];
-    __threadfence_system();
+    // the release store orders this thread's value stores before the flag
+    // at system scope (no separate fence)
     st_release_sys(&h->red_flag[par][point][P.me], seq);
     if (!wait_seq(&P.local->red_flag[par][point][threadIdx.x], seq, P.wait_ns)) s_ok = 0;
   }
