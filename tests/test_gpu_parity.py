@@ -49,6 +49,45 @@ def test_csr_build_matches_torch(dev, n, nnz, long_row):
     assert rel(csr.vals, ref.values()) < 1e-14
 
 
+@pytest.mark.parametrize("case", ["sorted", "sorted_gaps", "one_swap", "duplicate", "bad_index"])
+def test_csr_build_sorted_input(dev, case):
+    """COO whose (row, col) keys strictly increase takes the copy-through
+    path; the same entries with one adjacent pair swapped, or with one
+    duplicate, take the sort/merge path. Both must give torch's CSR, the
+    identity maps (src_index[t] = t, seg_ptr[e] = e) on the sorted path, and
+    an index outside the shape is refused on either."""
+    g = torch.Generator().manual_seed(17)
+    n = 500
+    dense = torch.rand(n, n, generator=g) < 0.02
+    if case == "sorted_gaps":
+        dense[:7] = False       # empty leading rows
+        dense[200:260] = False  # an empty run in the middle
+        dense[-5:] = False      # empty trailing rows
+    r, c = dense.nonzero(as_tuple=True)  # row-major: strictly increasing keys
+    v = torch.randn(r.numel(), generator=g, dtype=torch.float64)
+    if case == "one_swap":
+        r, c, v = r.clone(), c.clone(), v.clone()
+        r[[10, 11]], c[[10, 11]], v[[10, 11]] = r[[11, 10]], c[[11, 10]], v[[11, 10]]
+    elif case == "duplicate":
+        r, c = torch.cat([r, r[5:6]]), torch.cat([c, c[5:6]])
+        v = torch.cat([v, torch.tensor([0.25], dtype=torch.float64)])
+    elif case == "bad_index":
+        c = c.clone()
+        c[-1] = n
+        with pytest.raises(ValueError):
+            DeviceCSR(*cu(v, r, c, dev=dev), (n, n))
+        return
+    ref = K.csr(v, r, c, (n, n))
+    csr = DeviceCSR(*cu(v, r, c, dev=dev), (n, n), keep_map=True)
+    assert torch.equal(csr.rowptr.cpu().long(), ref.crow_indices())
+    assert torch.equal(csr.colind.cpu().long(), ref.col_indices())
+    assert rel(csr.vals, ref.values()) < 1e-15
+    if case in ("sorted", "sorted_gaps"):
+        m = r.numel()
+        assert torch.equal(csr.src_index.cpu(), torch.arange(m))
+        assert torch.equal(csr.seg_ptr.cpu().long(), torch.arange(m + 1))
+
+
 def test_csr_build_rejects_bad_index(dev):
     r = torch.tensor([0, 1, 5], device=dev)
     c = torch.tensor([0, 1, 1], device=dev)

@@ -2,7 +2,9 @@
 // diagonal.
 //
 // COO -> CSR (replaces torch.sparse_coo_tensor(...).to_sparse_csr() in
-// CachedSparseMatrix, backends/pytorch_backend.py:138-142): bucket entries by
+// CachedSparseMatrix, backends/pytorch_backend.py:138-142). Input whose
+// (row, col) keys strictly increase is copied through (see the sorted fast
+// path below); otherwise: bucket entries by
 // row with an atomic histogram + exclusive scan, sort each row by
 // (col, input position) so duplicates are merged in input order, then emit
 // int32 CSR. Rows of <= 32 entries sort in registers of one thread, rows of
@@ -247,6 +249,59 @@ __global__ void row_emit_kernel(const int64_t *__restrict__ rowstart, const int6
   if (blockIdx.x == 0 && threadIdx.x == 0 && seg_ptr) seg_ptr[rp64[n_rows]] = (int32_t)nnz;
 }
 
+// ------------------------------------------- already-sorted COO fast path
+// A COO whose (row, col) keys strictly increase is already in CSR order with
+// no duplicates: the CSR is the narrowed input, row pointers come from the
+// row boundaries, and the sort/merge passes (which would reproduce exactly
+// these arrays) are skipped. flags[0]: an index outside the shape;
+// flags[2]: some key does not exceed its predecessor.
+__global__ void coo_sorted_check_kernel(const int64_t *__restrict__ row,
+                                        const int64_t *__restrict__ col, int64_t nnz,
+                                        int64_t n_rows, int64_t n_cols,
+                                        int32_t *__restrict__ flags) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  bool bad = false, unsorted = false;
+  for (; i < nnz; i += stride) {
+    const int64_t r = row[i], c = col[i];
+    if (r < 0 || r >= n_rows || c < 0 || c >= n_cols) { bad = true; continue; }
+    if (i > 0) {
+      const int64_t rp = row[i - 1], cp = col[i - 1];
+      if (rp > r || (rp == r && cp >= c)) unsorted = true;
+    }
+  }
+  if (bad) atomicOr(flags, 1);
+  if (unsorted) atomicOr(flags + 2, 1);
+}
+
+// rowptr[r] = number of entries of rows < r, written at each row boundary
+// (positions 0 .. nnz; the rows of a gap between two boundaries are empty).
+__global__ void sorted_rowptr_kernel(const int64_t *__restrict__ row, int64_t nnz, int64_t n_rows,
+                                     int32_t *__restrict__ rowptr) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i <= nnz; i += stride) {
+    const int64_t prev = i == 0 ? -1 : row[i - 1];
+    const int64_t cur = i == nnz ? n_rows : row[i];
+    for (int64_t r = prev + 1; r <= cur; ++r) rowptr[r] = (int32_t)i;
+  }
+}
+
+template <typename T>
+__global__ void sorted_emit_kernel(const int64_t *__restrict__ col, const T *__restrict__ val,
+                                   int64_t nnz, int32_t *__restrict__ colind, T *__restrict__ vals,
+                                   int64_t *__restrict__ src_index, int32_t *__restrict__ seg_ptr) {
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (; i < nnz; i += stride) {
+    colind[i] = (int32_t)col[i];
+    if (vals) vals[i] = val ? val[i] : T(0);
+    if (src_index) src_index[i] = i;
+    if (seg_ptr) seg_ptr[i] = (int32_t)i;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && seg_ptr) seg_ptr[nnz] = (int32_t)nnz;
+}
+
 struct CsrWs {
   int32_t *counts, *cursor, *tcol, *tidx, *ucount, *long_rows, *flags;
   int64_t *rowstart, *rp64;
@@ -289,9 +344,25 @@ static int csr_build_impl(const int64_t *row, const int64_t *col, const T *val, 
   w.rp64 = c.take<int64_t>(n_rows + 1);
   w.scan = (char *)c.base + c.off;
   if (!c.ok) return SLA_ERR_WORKSPACE;
+  SLA_CUDA_TRY(cudaMemsetAsync(w.flags, 0, sizeof(int32_t) * 8, s));
+  if (nnz > 0) {
+    SLA_LAUNCH(coo_sorted_check_kernel, grid_for(nnz), kBlock, 0, s, row, col, nnz, n_rows,
+               n_cols, w.flags);
+    int32_t f[3] = {0, 0, 0};
+    SLA_CUDA_TRY(cudaMemcpyAsync(f, w.flags, sizeof(f), cudaMemcpyDeviceToHost, s));
+    SLA_CUDA_TRY(cudaStreamSynchronize(s));
+    if (f[0]) return SLA_ERR_INDEX;
+    if (!f[2]) {
+      SLA_LAUNCH(sorted_rowptr_kernel, grid_for(nnz + 1), kBlock, 0, s, row, nnz, n_rows, rowptr);
+      SLA_LAUNCH(sorted_emit_kernel<T>, grid_for(nnz), kBlock, 0, s, col, val, nnz, colind, vals,
+                 src_index, seg_ptr);
+      *nnz_out = nnz;
+      return SLA_OK;
+    }
+    SLA_CUDA_TRY(cudaMemsetAsync(w.flags, 0, sizeof(int32_t) * 8, s));
+  }
   SLA_CUDA_TRY(cudaMemsetAsync(w.counts, 0, sizeof(int32_t) * (n_rows + 1), s));
   SLA_CUDA_TRY(cudaMemsetAsync(w.cursor, 0, sizeof(int32_t) * (n_rows + 1), s));
-  SLA_CUDA_TRY(cudaMemsetAsync(w.flags, 0, sizeof(int32_t) * 8, s));
   if (nnz > 0)
     SLA_LAUNCH(coo_count_kernel, grid_for(nnz), kBlock, 0, s, row, col, nnz, n_rows, n_cols,
                w.counts, w.flags);
