@@ -144,6 +144,33 @@ def test_float32_pcg_two_rows_per_lane_views(dev, grid):
     assert em < 1e-6, em
 
 
+def test_float32_two_rows_per_lane_permuted_view(dev):
+    """A float32 7-point matrix on an explicit view of all rows in a seeded
+    random order (row ids, uniform width 7): the two-rows-per-lane SpMV and
+    K_A read each lane's rows through the row ids (no pair loads across
+    non-adjacent rows). The SpMV gives the row-order view's sums bit for
+    bit; float32 PCG on it reaches the same solution within float32
+    rounding."""
+    v, r, c, sh = P.poisson_3d_7pt((20, 17, 33))
+    v = v.float()
+    n = sh[0]
+    csr = DeviceCSR(v.to(dev), r.to(dev), c.to(dev), sh)
+    plain = csr.sell(diagonal=False, sigma=1)
+    perm = torch.randperm(n, generator=torch.Generator().manual_seed(21)).to(torch.int32)
+    shuf = csr.sell(row_ids=perm.to(dev), diagonal=False)
+    assert shuf.row_ids is not None and shuf.uniform_width == 7 and plain.uniform_width == 7
+    x = P.rhs_normal(n, 4, torch.float32).to(dev)
+    assert torch.equal(spmv(shuf, x, n), spmv(plain, x, n))
+    A = PB.CachedSparseMatrix(v.to(dev), r.to(dev), c.to(dev), sh)
+    M = PB.get_preconditioner(A, "jacobi")
+    b = P.rhs_normal(n, 5, torch.float32).to(dev)
+    xs, info_s = PB._pcg_core(A, b, None, M.dinv, 0.0, 1e-6, 5000, L.SLA_PCG_STREAMED, sell=shuf)
+    xp, info_p = PB._pcg_core(A, b, None, M.dinv, 0.0, 1e-6, 5000, L.SLA_PCG_STREAMED,
+                              sell=plain)
+    assert abs(info_s.iterations - info_p.iterations) <= 1
+    assert float((xs - xp).abs().max() / xp.abs().max()) < 1e-4
+
+
 def test_diag_view_bicgstab_bitwise(dev):
     v, r, c, sh = _matrix("cd")
     b = P.rhs_uniform01(sh[0], 3).to(dev)
