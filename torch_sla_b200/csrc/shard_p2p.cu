@@ -118,14 +118,20 @@ __device__ __forceinline__ void p2p_count(const P2PDev<T> &P, int slot, unsigned
   if (P.timers && threadIdx.x == 0) atomicAdd(P.timers + slot, v);
 }
 
-// This block's share of the halo values of all neighbours, then the arrival
-// signal from the last block to finish (all threads of the block call it).
+// The first kHaloBlocks blocks store the halo values of all neighbours
+// (the other blocks skip the system fence the stores need), then the last
+// of them to finish raises the arrival flags (all threads of a block call
+// it).
+constexpr int kHaloBlocks = 64;
+
 template <typename T, typename PV>
 __device__ __forceinline__ void p2p_send_halo(const P2PDev<T> &P, const int32_t *__restrict__ idx,
                                               const PV &pval, unsigned long long seq) {
+  const unsigned senders = gridDim.x < kHaloBlocks ? gridDim.x : kHaloBlocks;
+  if (blockIdx.x >= senders) return;
   const long long ns = P.send_off[P.n_nb];
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < ns;
-       i += (long long)gridDim.x * blockDim.x) {
+       i += (long long)senders * blockDim.x) {
     int nb = 0;
     while (i >= P.send_off[nb + 1]) ++nb;
     P.dst[nb][i - P.send_off[nb]] = pval(idx[i]);
@@ -134,7 +140,7 @@ __device__ __forceinline__ void p2p_send_halo(const P2PDev<T> &P, const int32_t 
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned t = atomicAdd(&P.local->send_count, 1u);
-    if (t == gridDim.x - 1) {
+    if (t == senders - 1) {
       P.local->send_count = 0u;
       __threadfence_system();
       for (int nb = 0; nb < P.n_nb; ++nb) st_release_sys(&P.hdr[P.nb_rank[nb]]->arrive[P.me], seq);
