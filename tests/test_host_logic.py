@@ -265,3 +265,64 @@ def test_patch_install_into_reference():
                          env={**os.environ, "PYTHONDONTWRITEBYTECODE": "1"}, timeout=300)
     assert out.returncode == 0, out.stderr[-2000:]
     assert int(out.stdout.strip().splitlines()[-1]) >= 8
+
+
+SIG_SCRIPT = r"""
+import importlib, inspect, json, sys
+sys.path.insert(0, sys.argv[1])
+names = json.loads(sys.argv[2])
+out = {}
+for mod, fns in names.items():
+    m = importlib.import_module(mod)
+    for f in fns:
+        sig = inspect.signature(getattr(m, f))
+        out[mod + "." + f] = [(p.name, repr(p.default) if p.default is not inspect._empty else None,
+                               str(p.kind)) for p in sig.parameters.values()]
+print(json.dumps(out))
+"""
+
+PUBLIC = {
+    "backends.pytorch_backend": ["pcg_solve_optimized", "pcg_solve_fused", "pbicgstab_solve",
+                                 "pytorch_solve", "batched_cg_same_pattern", "batched_pcg_solve",
+                                 "batched_cg_solve", "get_preconditioner",
+                                 "pcg_solve_mixed_precision", "pcg_solve", "cg_solve",
+                                 "bicgstab_solve", "sparse_matvec", "extract_diagonal"],
+    "linear_solve": ["spsolve"],
+    "batch_solve": ["spsolve_batch_same_layout"],
+    "distributed.solve": ["cg_shard", "bicgstab_shard", "make_preconditioner"],
+    "distributed.matvec": ["halo_exchange", "shard_matvec", "shard_rmatvec",
+                           "reverse_halo_exchange"],
+    "partition": ["partition_simple", "build_partition", "find_halo_nodes"],
+}
+
+
+def test_public_signatures_accept_every_reference_call():
+    """Every public function of the mirror takes torch-sla's parameters in
+    torch-sla's order and kind with torch-sla's defaults (read from the
+    installed package; a parameter torch-sla requires may have a default
+    here); parameters the mirror adds come last and have defaults, so any
+    call written against torch-sla binds the same way."""
+    import json
+    import subprocess
+    import sys
+    from conftest import torch_sla_path
+    ref = torch_sla_path()
+    if ref is None:
+        pytest.skip("torch-sla not found (set TORCH_SLA_REF or install it into baseline/_ref)")
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sigs = {}
+    for pkg, path in (("torch_sla", ref), ("torch_sla_b200", repo)):
+        names = {f"{pkg}.{m}": fns for m, fns in PUBLIC.items()}
+        out = subprocess.run([sys.executable, "-c", SIG_SCRIPT, path, json.dumps(names)],
+                             capture_output=True, text=True, cwd="/tmp", timeout=300,
+                             env={**os.environ, "PYTHONDONTWRITEBYTECODE": "1"})
+        assert out.returncode == 0, out.stderr[-2000:]
+        sigs[pkg] = {k.split(".", 1)[1]: v
+                     for k, v in json.loads(out.stdout.strip().splitlines()[-1]).items()}
+    for name, theirs in sigs["torch_sla"].items():
+        mine = sigs["torch_sla_b200"][name]
+        assert len(mine) >= len(theirs), (name, theirs, mine)
+        for (tn, td, tk), (mn, md, mk) in zip(theirs, mine):
+            assert (tn, tk) == (mn, mk), (name, theirs, mine)
+            assert td is None or td == md, (name, tn, td, md)
+        assert all(default is not None for _, default, _ in mine[len(theirs):]), (name, mine)
