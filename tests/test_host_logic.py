@@ -275,7 +275,10 @@ out = {}
 for mod, fns in names.items():
     m = importlib.import_module(mod)
     for f in fns:
-        sig = inspect.signature(getattr(m, f))
+        obj = m
+        for part in f.split("."):
+            obj = getattr(obj, part)
+        sig = inspect.signature(obj)
         out[mod + "." + f] = [(p.name, repr(p.default) if p.default is not inspect._empty else None,
                                str(p.kind)) for p in sig.parameters.values()]
 print(json.dumps(out))
