@@ -128,7 +128,7 @@ template <typename T, typename PV>
 __device__ __forceinline__ void p2p_send_halo(const P2PDev<T> &P, const int32_t *__restrict__ idx,
                                               const PV &pval, unsigned long long seq) {
   const unsigned senders = gridDim.x < kHaloBlocks ? gridDim.x : kHaloBlocks;
-  if (blockIdx.x >= senders) return;
+  if (P.n_nb == 0 || blockIdx.x >= senders) return;  // no neighbour waits on this rank
   const long long ns = P.send_off[P.n_nb];
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < ns;
        i += (long long)senders * blockDim.x) {
